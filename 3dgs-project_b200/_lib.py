@@ -1,0 +1,102 @@
+"""ctypes binding of libsplat_b200.so (the C ABI declared in include/splat_b200.h).
+
+The library is loaded on first use and never replaced by anything else: if it is missing, or a
+tensor handed to it is not a CUDA tensor, the call raises. There is no CPU path.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().with_name("libsplat_b200.so")
+ABI_VERSION = 1
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_LL = ctypes.c_longlong
+_SZ = ctypes.c_size_t
+
+# name -> (restype, argtypes)
+_SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "splat_last_error": (ctypes.c_char_p, []),
+    "splat_abi_version": (_I, []),
+    "splat_scan_workspace_size": (_SZ, [_LL]),
+    "splat_scan_exclusive_u32": (_I, [_P, _P, _LL, _P, _P, _SZ, _P]),
+    "splat_sort_workspace_size": (_SZ, [_LL, _I]),
+    "splat_radix_sort_pairs": (_I, [_P, _P, _P, _P, _LL, _I, _I, _I, _P, _SZ, _P]),
+    "gs2d_bin_count_workspace_size": (_SZ, [_I]),
+    "gs2d_bin_fill_workspace_size": (_SZ, [_LL, _I, _I]),
+    "gs2d_bin_count": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _SZ, _P]),
+    "gs2d_bin_fill": (_I, [_P, _I, _I, _I, _LL, _P, _SZ, _P, _SZ, _P, _P, _P, _P, _P, _P]),
+    "gs2d_forward": (_I, [_P] * 8 + [_I, _LL, _I, _I, _I, _I] + [_P] * 5),
+    "gs2d_backward_pixel": (_I, [_P] * 7 + [_I, _LL, _I, _I] + [_P] * 8),
+    "gs2d_backward_splat": (_I, [_P] * 8 + [_I, _I, _LL, _I, _I] + [_P] * 8),
+}
+
+_lib: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and type the shared library; raise if it is missing or of another ABI."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"{LIB_PATH.name} is not built; run `python 3dgs-project_b200/build.py` "
+                "(or __graft_entry__.build()) first")
+        lib = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        if lib.splat_abi_version() != ABI_VERSION:
+            raise RuntimeError(f"{LIB_PATH.name} has ABI {lib.splat_abi_version()}, expected {ABI_VERSION}")
+        _lib = lib
+    return _lib
+
+
+def call(name: str, *args) -> None:
+    """Call one status-returning entry point; a non-zero status becomes RuntimeError(message)."""
+    lib = load()
+    status = getattr(lib, name)(*args)
+    if status != 0:
+        msg = lib.splat_last_error().decode(errors="replace")
+        raise RuntimeError(f"{name}: {msg} (status {status})")
+
+
+def query(name: str, *args) -> int:
+    return int(getattr(load(), name)(*args))
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    """Device address of a CUDA tensor (None passes NULL)."""
+    if t is None:
+        return None
+    return t.data_ptr()
+
+
+def stream_of(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def check_cuda(name: str, t: torch.Tensor, dtype: torch.dtype | None = None) -> torch.Tensor:
+    """The reference's CHECK_INPUT (toy2d/csrc/rasterize.cu:355-358): CUDA, contiguous, dtype."""
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a tensor")
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor")
+    if dtype is not None and t.dtype != dtype:
+        raise RuntimeError(f"{name} has the wrong dtype ({t.dtype}, expected {dtype})")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+    return t
+
+
+def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGNATURES)

@@ -1,0 +1,51 @@
+// sort.cuh - device-wide exclusive scan and stable LSD radix sort (internal API).
+//
+// Both are written for this library instead of calling CUB: the scan feeds the tile-instance and
+// bucket offsets, the sort orders the 64-bit (tile | depth) instance keys. Neither spins on flags
+// set by other blocks (reduce-then-scan, one histogram / scan / scatter triple per 8-bit digit), so
+// no launch can wait forever on another block.
+#pragma once
+
+#include "common.cuh"
+
+namespace splat {
+
+constexpr int kScanThreads = 1024;
+constexpr int kScanItems = 4;
+constexpr int kScanTile = kScanThreads * kScanItems;  // 4096 values per scan block
+
+constexpr int kSortThreads = 256;
+constexpr int kSortRounds = 16;
+constexpr int kSortTile = kSortThreads * kSortRounds;  // 4096 pairs per sort block
+constexpr int kRadixBits = 8;
+constexpr int kRadix = 1 << kRadixBits;
+
+// Workspace needed by scan_exclusive_u32 for n values.
+size_t scan_workspace_bytes(long long n);
+
+// out[i] = in[0] + ... + in[i-1]; *total (device pointer, may be null) = sum of all n values.
+// in and out may alias.
+int scan_exclusive_u32(const uint32_t* in, uint32_t* out, long long n, uint32_t* total, void* ws,
+                       size_t ws_bytes, cudaStream_t stream);
+
+template <typename K>
+size_t sort_workspace_bytes(long long n);
+
+// Stable sort of (key, value) pairs by key bits [begin_bit, end_bit). keys_in/vals_in are not
+// modified; results land in keys_out/vals_out (which must not alias the inputs).
+template <typename K>
+int radix_sort_pairs(const K* keys_in, const uint32_t* vals_in, K* keys_out, uint32_t* vals_out,
+                     long long n, int begin_bit, int end_bit, void* ws, size_t ws_bytes,
+                     cudaStream_t stream);
+
+// Number of significant bits needed to represent v (0 for v == 0).
+inline int bit_width(unsigned long long v) {
+    int b = 0;
+    while (v) {
+        ++b;
+        v >>= 1;
+    }
+    return b;
+}
+
+}  // namespace splat

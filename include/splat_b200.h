@@ -1,0 +1,102 @@
+/* splat_b200.h - C ABI of libsplat_b200.so, the B200 (sm_100a) Gaussian-splatting rasterizer.
+ *
+ * Conventions shared by every entry point:
+ *   - all array arguments are DEVICE pointers (cudaMalloc'd or torch-owned), contiguous, in the
+ *     dtype the name says; sizes are plain ints; no torch or CUDA types appear in the signatures
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream); every launch goes
+ *     on that stream and no entry point synchronises with the host
+ *   - the return value is a status: SPLAT_OK (0) or one of the SPLAT_ERR_* codes; a failing call
+ *     leaves a one-line message that splat_last_error() returns (thread-local)
+ *   - entry points never launch a grid of zero blocks; empty inputs return SPLAT_OK with outputs
+ *     zero-filled where the reference returns zeros
+ *   - outputs are written, not accumulated: gradient buffers are cleared by the call itself
+ *   - `workspace` buffers are caller-owned scratch of at least the queried size
+ *
+ * Each declaration names the reference interface it replaces (asadrizvi64/3dgs-project, path:line).
+ */
+#ifndef SPLAT_B200_H
+#define SPLAT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SPLAT_ABI_VERSION 1
+
+#define SPLAT_OK 0
+#define SPLAT_ERR_ARG 1      /* bad shape, size or pointer */
+#define SPLAT_ERR_CUDA 2     /* a CUDA call or launch failed */
+#define SPLAT_ERR_OVERFLOW 3 /* a size bound was exceeded */
+#define SPLAT_ERR_TIMEOUT 4  /* a bounded device-side wait gave up */
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* splat_last_error(void);
+/* SPLAT_ABI_VERSION of the loaded library. */
+int splat_abi_version(void);
+
+/* ---------------------------------------------------------------------------------------------
+ * Device-wide primitives (replace the CUB DeviceScan / DeviceRadixSort calls inside Faster-GS's
+ * forward, whose call sites phase2/fastergs_readback.patch:46-89 shows)
+ * ------------------------------------------------------------------------------------------- */
+size_t splat_scan_workspace_size(long long n);
+/* out[i] = sum(in[0..i)); *total (device, may be NULL) = sum of all n. in and out may alias. */
+int splat_scan_exclusive_u32(const uint32_t* in, uint32_t* out, long long n, uint32_t* total, void* workspace,
+                             size_t workspace_bytes, void* stream);
+size_t splat_sort_workspace_size(long long n, int key_bytes);
+/* Stable LSD radix sort of (key, uint32 value) pairs by key bits [begin_bit, end_bit); key_bytes 4 or 8.
+ * Inputs are left untouched; outputs must not alias them. */
+int splat_radix_sort_pairs(const void* keys_in, const uint32_t* vals_in, void* keys_out, uint32_t* vals_out,
+                           long long n, int key_bytes, int begin_bit, int end_bit, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * gs2d: toy2d 2D Gaussian rasterizer (replaces toy2d/csrc/rasterize.cu:366-454 and the device
+ * binning of toy2d/gs2d/binning.py:35-88). means f32[N,2], conic f32[N,3] (A,B,C), color f32[N,3],
+ * opacity f32[N], bg f32[3] (device: no host copy, unlike rasterize.cu:360-364). num_instances = M is
+ * the length of point_list; ranges and ids are clamped to [0, M] and [0, N) on the device, so an
+ * inconsistent table gives wrong pixels but never an out-of-bounds access.
+ * ------------------------------------------------------------------------------------------- */
+size_t gs2d_bin_count_workspace_size(int n);
+size_t gs2d_bin_fill_workspace_size(long long num_instances, int H, int W);
+/* Binning phase 1 (binning.py:44-67): rect i32[N,4] (xmin, ymin, xmax, ymax in tiles, max exclusive),
+ * order i64[N] (stable depth argsort; depth is f32[N] or f64[N] when depth_is_f64), and the number of
+ * (tile, Gaussian) instances M written to *num_instances (device u32). radii i32[N]. */
+int gs2d_bin_count(const float* means, const int32_t* radii, const void* depth, int depth_is_f64, int n, int H,
+                   int W, int32_t* rect, int64_t* order, uint32_t* num_instances, void* count_workspace,
+                   size_t count_workspace_bytes, void* stream);
+/* Binning phase 2 (binning.py:69-88), given M read back by the host and the phase-1 workspace:
+ * point_list i32[M], ranges i32[T,2], bucket_offsets i32[T], bucket_to_tile i32[capacity >= M/32 + T]
+ * (first num_buckets entries valid) and *num_buckets (device u32). */
+int gs2d_bin_fill(const int32_t* rect, int n, int H, int W, long long num_instances, void* count_workspace,
+                  size_t count_workspace_bytes, void* fill_workspace, size_t fill_workspace_bytes,
+                  int32_t* point_list, int32_t* ranges, int32_t* bucket_offsets, int32_t* bucket_to_tile,
+                  uint32_t* num_buckets, void* stream);
+/* rasterize.cu:366-394 `forward`: out f32[3,H,W], final_T f32[H,W], n_contrib i32[H,W],
+ * bucket_state f32[num_buckets,256,4] = (T, C) when save_buckets (untouched entries keep the caller's
+ * zero fill, as in the reference). */
+int gs2d_forward(const float* means, const float* conic, const float* color, const float* opacity, const float* bg,
+                 const int32_t* ranges, const int32_t* point_list, const int32_t* bucket_offsets, int N,
+                 long long num_instances, int num_buckets, int H, int W, int save_buckets, float* out,
+                 float* final_T, int32_t* n_contrib, float* bucket_state, void* stream);
+/* rasterize.cu:396-417 `backward_pixel`: dmeans f32[N,2], dconic f32[N,3], dcolor f32[N,3], dopacity f32[N]. */
+int gs2d_backward_pixel(const float* means, const float* conic, const float* color, const float* opacity,
+                        const float* bg, const int32_t* ranges, const int32_t* point_list, int N,
+                        long long num_instances, int H, int W, const float* final_T, const int32_t* n_contrib,
+                        const float* dL_dout, float* dmeans, float* dconic, float* dcolor, float* dopacity,
+                        void* stream);
+/* rasterize.cu:419-448 `backward_splat` (warp per 32-splat bucket; zero gradients when num_buckets == 0). */
+int gs2d_backward_splat(const float* means, const float* conic, const float* color, const float* opacity,
+                        const int32_t* ranges, const int32_t* point_list, const int32_t* bucket_offsets,
+                        const int32_t* bucket_to_tile, int num_buckets, int N, long long num_instances, int H,
+                        int W, const float* out, const int32_t* n_contrib, const float* bucket_state,
+                        const float* dL_dout, float* dmeans, float* dconic, float* dcolor, float* dopacity,
+                        void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* SPLAT_B200_H */

@@ -1,0 +1,77 @@
+"""Builds the CPU checkers (TEST INFRASTRUCTURE, never linked into the product).
+
+    python oracle/build.py [--reference <root>]
+
+  oracle/liboracle.so        the C++ restatement of the 3DGS path (oracle/gs3d_oracle.cpp), OpenMP,
+                             compiled with -ffp-contract=off so float32 rounding follows the source
+  oracle/_ref/libsplat2d_ref.so   the reference's own splat2d CPU code (phase0/csrc/macrotile/
+                             splat2d_cpu.cpp, compiled in place from the reference tree with g++)
+                             behind oracle/splat2d_ref_capi.cpp; built only where the reference
+                             tree exists (REFERENCE_ROOT or --reference)
+
+Built files are git-ignored; they travel to the GPU box with the working tree.
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+REF_OUT = HERE / "_ref"
+CXX = os.environ.get("CXX", "g++")
+FLAGS = ["-O2", "-std=c++17", "-fPIC", "-shared", "-ffp-contract=off", "-fno-fast-math"]
+
+
+def _compile(out: Path, sources: list[Path], flags: list[str], extra_inputs: list[Path] = ()) -> Path:
+    inputs = list(sources) + list(extra_inputs)
+    stamp = out.with_suffix(out.suffix + ".stamp")
+    h = hashlib.sha256(" ".join(flags).encode())
+    for p in inputs:
+        h.update(p.read_bytes())
+    digest = h.hexdigest()
+    if out.exists() and stamp.exists() and stamp.read_text() == digest:
+        return out
+    cmd = [CXX, *flags, *map(str, sources), "-o", str(out)]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"oracle build failed:\n{' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+    stamp.write_text(digest)
+    return out
+
+
+def reference_root(arg: str | None = None) -> Path | None:
+    root = arg or os.environ.get("REFERENCE_ROOT")
+    if root is None:
+        guess = Path("/") / "root" / "reference"
+        root = str(guess) if guess.is_dir() else None
+    return Path(root) if root and Path(root).is_dir() else None
+
+
+def build(reference: str | None = None) -> None:
+    srcs = sorted(HERE.glob("*.cpp"))
+    mine = [p for p in srcs if not p.name.endswith("_ref_capi.cpp")]
+    if mine:
+        _compile(HERE / "liboracle.so", mine, FLAGS + ["-fopenmp"], list(HERE.glob("*.h")))
+    ref = reference_root(reference)
+    if ref is not None:
+        mt = ref / "phase0" / "csrc" / "macrotile"
+        if (mt / "splat2d_cpu.cpp").exists():
+            REF_OUT.mkdir(exist_ok=True)
+            _compile(REF_OUT / "libsplat2d_ref.so", [HERE / "splat2d_ref_capi.cpp", mt / "splat2d_cpu.cpp"],
+                     FLAGS + [f"-I{mt}"], [mt / "splat2d_common.h"])
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference")
+    a = ap.parse_args()
+    build(a.reference)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,40 @@
+"""The C ABI: the built library loads (no GPU needed) and exports every symbol include/*.h declares."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+from gs_b200 import _lib
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_functions() -> set[str]:
+    names = set()
+    for h in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        for m in re.finditer(r"\b([A-Za-z_][A-Za-z0-9_]*)\s*\(", text):
+            name = m.group(1)
+            if name.startswith(("splat_", "gs2d_", "splat2d_", "gs3d_", "adam_")):
+                names.add(name)
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(_lib.LIB_PATH))
+    missing = [n for n in sorted(declared_functions()) if not hasattr(lib, n)]
+    assert not missing, f"declared but not exported: {missing}"
+
+
+def test_python_binding_covers_the_header():
+    assert declared_functions() == set(_lib.exported_symbols())
+
+
+def test_abi_version_and_error_channel():
+    lib = _lib.load()
+    assert lib.splat_abi_version() == _lib.ABI_VERSION
+    # an argument error is reported without touching the GPU
+    status = lib.splat_radix_sort_pairs(None, None, None, None, 10, 3, 0, 8, None, 0, None)
+    assert status == 1
+    assert b"key_bytes" in lib.splat_last_error()
