@@ -33,6 +33,15 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gs2d_forward": (_I, [_P] * 8 + [_I, _LL, _I, _I, _I, _I] + [_P] * 5),
     "gs2d_backward_pixel": (_I, [_P] * 7 + [_I, _LL, _I, _I] + [_P] * 8),
     "gs2d_backward_splat": (_I, [_P] * 8 + [_I, _I, _LL, _I, _I] + [_P] * 8),
+    "splat2d_bin_count_workspace_size": (_SZ, [_I]),
+    "splat2d_bin_fill_workspace_size": (_SZ, [_LL, _I, _I]),
+    "splat2d_bin_count": (_I, [_I, _P, _P, _P, _I, _I, _I, _P, _P, _SZ, _P]),
+    "splat2d_bin_fill": (_I, [_I, _I, _I, _LL, _P, _SZ, _P, _SZ, _P, _P, _P, _P, _P, _P]),
+    "splat2d_forward": (_I, [_I] + [_P] * 8 + [_I, _LL, _I, _I, _I] + [_P] * 6),
+    "splat2d_backward": (_I, [_I, _I] + [_P] * 9 + [_I, _LL, _I, _I, _I] + [_P] * 9),
+    "splat2d_set_counting": (_I, [_I]),
+    "splat2d_reset_counters": (_I, []),
+    "splat2d_get_counters": (_I, [_P]),
 }
 
 _lib: ctypes.CDLL | None = None

