@@ -32,7 +32,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gs2d_bin_fill": (_I, [_P, _I, _I, _I, _LL, _P, _SZ, _P, _SZ, _P, _P, _P, _P, _P, _P]),
     "gs2d_forward": (_I, [_P] * 8 + [_I, _LL, _I, _I, _I, _I] + [_P] * 5),
     "gs2d_backward_pixel": (_I, [_P] * 7 + [_I, _LL, _I, _I] + [_P] * 8),
-    "gs2d_backward_splat": (_I, [_P] * 8 + [_I, _I, _LL, _I, _I] + [_P] * 8),
+    "gs2d_backward_splat": (_I, [_P] * 8 + [_I, _I, _LL, _I, _I] + [_P] * 9),
     "splat2d_bin_count_workspace_size": (_SZ, [_I]),
     "splat2d_bin_fill_workspace_size": (_SZ, [_LL, _I, _I]),
     "splat2d_bin_count": (_I, [_I, _P, _P, _P, _I, _I, _I, _P, _P, _SZ, _P]),
@@ -69,7 +69,10 @@ def load() -> ctypes.CDLL:
 def call(name: str, *args) -> None:
     """Call one status-returning entry point; a non-zero status becomes RuntimeError(message)."""
     lib = load()
-    status = getattr(lib, name)(*args)
+    fn = getattr(lib, name)
+    if len(args) != len(fn.argtypes):  # ctypes would pass surplus arguments unconverted
+        raise TypeError(f"{name} takes {len(fn.argtypes)} arguments, got {len(args)}")
+    status = fn(*args)
     if status != 0:
         msg = lib.splat_last_error().decode(errors="replace")
         raise RuntimeError(f"{name}: {msg} (status {status})")

@@ -38,3 +38,43 @@ def test_abi_version_and_error_channel():
     status = lib.splat_radix_sort_pairs(None, None, None, None, 10, 3, 0, 8, None, 0, None)
     assert status == 1
     assert b"key_bytes" in lib.splat_last_error()
+
+
+def _prototypes() -> dict[str, tuple[str, list[str]]]:
+    """name -> (return type, [parameter types]) parsed from the header's prototypes."""
+    out = {}
+    for h in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        text = re.sub(r"#[^\n]*", "", text)
+        for m in re.finditer(r"([A-Za-z_][A-Za-z0-9_ \*]*?)\b([A-Za-z_][A-Za-z0-9_]*)\s*\(([^;{}]*?)\)\s*;", text):
+            ret, name, params = m.group(1).strip(), m.group(2), m.group(3).strip()
+            plist = [] if params in ("", "void") else [p.strip() for p in params.split(",")]
+            out[name] = (ret, plist)
+    return out
+
+
+def _kind(decl: str):
+    if "*" in decl:
+        return ctypes.c_void_p
+    if "size_t" in decl:
+        return ctypes.c_size_t
+    if "long long" in decl:
+        return ctypes.c_longlong
+    if re.search(r"\bint\b", decl):
+        return ctypes.c_int
+    raise AssertionError(f"unclassified parameter {decl!r}")
+
+
+def test_ctypes_signatures_match_the_header():
+    """Every argtypes list has the header's arity and kinds (a short list truncates the stream handle)."""
+    protos = _prototypes()
+    for name, (res, args) in _lib._SIGNATURES.items():
+        ret, params = protos[name]
+        want = [_kind(p) for p in params]
+        assert args == want, f"{name}: ctypes {args} vs header {want}"
+        if "*" in ret:
+            assert res == ctypes.c_char_p, name
+        elif "size_t" in ret:
+            assert res == ctypes.c_size_t, name
+        else:
+            assert res == ctypes.c_int, name
