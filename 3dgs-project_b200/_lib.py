@@ -42,6 +42,15 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "splat2d_set_counting": (_I, [_I]),
     "splat2d_reset_counters": (_I, []),
     "splat2d_get_counters": (_I, [_P]),
+    "gs3d_primitive_buffer_size": (_SZ, [_I]),
+    "gs3d_tile_buffer_size": (_SZ, [_I, _I]),
+    "gs3d_instance_buffer_size": (_SZ, [_LL]),
+    "gs3d_bucket_bound": (_LL, [_LL, _I, _I]),
+    "gs3d_bucket_buffer_size": (_SZ, [_LL]),
+    "gs3d_backward_workspace_size": (_SZ, [_I]),
+    "gs3d_preprocess": (_I, [_P] * 6 + [_I, _P, _P, _SZ, _P, _P]),
+    "gs3d_render": (_I, [_I, _LL, _P, _P, _SZ, _P, _SZ, _P, _SZ, _P, _SZ, _LL, _P, _P]),
+    "gs3d_backward": (_I, [_P] * 7 + [_I, _LL, _P] + [_P, _SZ] * 4 + [_LL, _P, _SZ] + [_P] * 7),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -1,0 +1,552 @@
+// gs3d_backward.cu - 3DGS backward: per-Gaussian warp-bucketed blend backward, then the preprocess
+// backward to the six parameter gradients.
+//
+// k_blend_backward: one warp per (tile, 32-splat bucket). Lane l owns the 8 pixels r*32 + l of the
+// 16x16 tile (column l % 16, rows 2r + l / 16). From the bucket's (C, T) checkpoint each pixel keeps
+// T and rho = G . (image - C) (image with background), so that
+//     dL/dalpha_j = T_j (G . c_j) - rho_after_j / max(1 - alpha_j, 1e-6),  rho_after_j = rho_j - T_j alpha_j (G . c_j)
+// (the formulation of phase1/fastergs_macro.patch:22-31,186-198), and replays the bucket's splats in
+// front-to-back order up to the pixel's last contributor. Row bands whose culling rectangle misses
+// the splat are skipped by the whole warp. Per splat the lanes' nine sums (mean2d 2, conic 3,
+// opacity, colour 3) are reduced with shuffles and lane 0 issues three vector atomics (float2,
+// float4, float4) instead of nine scalar ones. Buckets past the tile's last contributor exit at once.
+//
+// k_preprocess_backward: one thread per Gaussian recomputes the projection and chains
+// (dL/dmean2d, dL/dconic, dL/dopacity, dL/dcolour) to means, scales, rotations, opacity logits,
+// sh0 and sh_rest. SH rows are read and their gradients written per warp through shared memory with
+// 16-byte accesses (the coalesced layout of upstream/sh_coalesced_loads.patch:12-52). Gaussians
+// that were not visible get zero gradients.
+#include "gs3d_common.cuh"
+
+namespace splat {
+namespace gs3d {
+
+constexpr int kBwdWarps = 4;
+constexpr int kPxPerLane = kTilePixels / 32;  // 8
+constexpr int kPbThreads = 128;
+constexpr int kPbWarps = kPbThreads / 32;
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct GradAcc {
+    float2* mean2d;  // [N] dL/dmean2d
+    float4* conic_o;  // [N] (dL/dA, dL/dB, dL/dC, dL/dopacity)
+    float4* color;   // [N] dL/d max(colour, 0), w unused
+};
+
+inline GradAcc carve_grad(Carver& c, int n) {
+    const size_t nn = static_cast<size_t>(n < 1 ? 1 : n);
+    GradAcc g;
+    g.mean2d = c.take<float2>(nn);
+    g.conic_o = c.take<float4>(nn);
+    g.color = c.take<float4>(nn);
+    return g;
+}
+
+__global__ void __launch_bounds__(32 * kBwdWarps) k_blend_backward(
+    Cam cam, const uint32_t* __restrict__ counters, const uint32_t* __restrict__ bucket_tile,
+    const uint2* __restrict__ ranges, const uint32_t* __restrict__ bstart, const uint32_t* __restrict__ max_contrib,
+    const uint32_t* __restrict__ point_list, const float2* __restrict__ mean2d, const float4* __restrict__ conic_o,
+    const float4* __restrict__ color_z, const ushort4* __restrict__ rect, const float* __restrict__ grad_image,
+    const float* __restrict__ image, const uint32_t* __restrict__ n_contrib, const float4* __restrict__ ckpt, int n,
+    int m, long long bcap, GradAcc acc) {
+    __shared__ float2 s_mean[kBwdWarps][kBucket];
+    __shared__ float4 s_con[kBwdWarps][kBucket];
+    __shared__ float4 s_col[kBwdWarps][kBucket];
+    __shared__ ushort4 s_rect[kBwdWarps][kBucket];
+    __shared__ uint32_t s_id[kBwdWarps][kBucket];
+    __shared__ float3 s_grad[kBwdWarps][kTilePixels];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long b = static_cast<long long>(blockIdx.x) * kBwdWarps + warp;
+    const long long nbuckets = min(static_cast<long long>(counters[1]), bcap);
+    if (b >= nbuckets) return;  // whole warp; warps never synchronise with each other
+    const int T_tiles = cam.tiles_x * cam.tiles_y;
+    const uint32_t tile = bucket_tile[b];
+    if (tile >= static_cast<uint32_t>(T_tiles)) return;
+    uint2 rg = ranges[tile];
+    rg.y = min(rg.y, static_cast<uint32_t>(m));
+    rg.x = min(rg.x, rg.y);
+    const long long bucket_start = (b - static_cast<long long>(bstart[tile])) * kBucket;
+    const long long tile_last = min(static_cast<long long>(max_contrib[tile]), static_cast<long long>(rg.y - rg.x));
+    if (bucket_start < 0 || bucket_start >= tile_last) return;
+    const int bsize = static_cast<int>(min(static_cast<long long>(kBucket), tile_last - bucket_start));
+
+    const int tx0 = (tile % cam.tiles_x) * kTile, ty0 = (tile / cam.tiles_x) * kTile;
+    if (lane < bsize) {
+        const int g = min(static_cast<int>(point_list[rg.x + bucket_start + lane]), n - 1);
+        s_id[warp][lane] = g;
+        s_mean[warp][lane] = mean2d[g];
+        const float4 co = conic_o[g];
+        s_con[warp][lane] = make_float4(-0.5f * kLog2e * co.x, -kLog2e * co.y, -0.5f * kLog2e * co.z, co.w);
+        const float4 cz = color_z[g];
+        s_col[warp][lane] = make_float4(fmaxf(cz.x, 0.f), fmaxf(cz.y, 0.f), fmaxf(cz.z, 0.f), 0.f);
+        s_rect[warp][lane] = rect[g];
+    }
+
+    const int x = tx0 + (lane & 15);
+    const int y0 = ty0 + (lane >> 4);
+    const float pxf = static_cast<float>(x) + 0.5f;
+    const size_t HW = static_cast<size_t>(cam.width) * cam.height;
+    const float4* ck = ckpt + b * kTilePixels;
+    float T[kPxPerLane], rho[kPxPerLane];
+    int lim[kPxPerLane];
+#pragma unroll
+    for (int r = 0; r < kPxPerLane; ++r) {
+        const int y = y0 + 2 * r;
+        float3 G = make_float3(0.f, 0.f, 0.f);
+        T[r] = 0.f;
+        rho[r] = 0.f;
+        lim[r] = 0;
+        if (x < cam.width && y < cam.height) {
+            const int pix = y * cam.width + x;
+            lim[r] = static_cast<int>(static_cast<long long>(n_contrib[pix]) - bucket_start);
+            if (lim[r] > 0) {
+                G = make_float3(grad_image[pix], grad_image[HW + pix], grad_image[2 * HW + pix]);
+                const float4 st = ck[r * 32 + lane];
+                T[r] = st.w;
+                rho[r] = G.x * (image[pix] - st.x) + G.y * (image[HW + pix] - st.y) + G.z * (image[2 * HW + pix] - st.z);
+            }
+        }
+        s_grad[warp][r * 32 + lane] = G;
+    }
+    __syncwarp();
+
+    for (int j = 0; j < bsize; ++j) {
+        const float2 mm = s_mean[warp][j];
+        const float4 co = s_con[warp][j];
+        const float4 c = s_col[warp][j];
+        const ushort4 rc = s_rect[warp][j];
+        float g_mx = 0.f, g_my = 0.f, g_a = 0.f, g_b = 0.f, g_c = 0.f, g_o = 0.f, g_r = 0.f, g_g = 0.f, g_bl = 0.f;
+        bool used = false;
+        const bool col_hit = x >= rc.x && x <= rc.z;
+#pragma unroll
+        for (int r = 0; r < kPxPerLane; ++r) {
+            const int yb = ty0 + 2 * r;  // rows yb, yb + 1 of this band
+            if (rc.y > yb + 1 || rc.w < yb) continue;  // warp-uniform
+            if (!col_hit || j >= lim[r]) continue;
+            const float dx = mm.x - pxf, dy = mm.y - (static_cast<float>(y0 + 2 * r) + 0.5f);
+            const float q2 = dx * (co.x * dx + co.y * dy) + co.z * dy * dy;
+            const float G = exp2f(fminf(q2, 0.f));
+            const float alpha = co.w * G;
+            if (alpha < kAlphaMin) continue;
+            used = true;
+            const float3 gp = s_grad[warp][r * 32 + lane];
+            const float w = alpha * T[r];
+            const float dot_c = gp.x * c.x + gp.y * c.y + gp.z * c.z;
+            g_r += w * gp.x;
+            g_g += w * gp.y;
+            g_bl += w * gp.z;
+            rho[r] -= w * dot_c;
+            const float one_minus = 1.f - alpha;
+            const float dL_dalpha = T[r] * dot_c - rho[r] * __frcp_rn(fmaxf(one_minus, kOneMinusAlphaEps));
+            g_o += G * dL_dalpha;
+            const float h = alpha * dL_dalpha * kLn2;  // dL/dq2
+            g_mx += h * (2.f * co.x * dx + co.y * dy);
+            g_my += h * (co.y * dx + 2.f * co.z * dy);
+            g_a += h * dx * dx;
+            g_b += h * dx * dy;
+            g_c += h * dy * dy;
+            T[r] *= one_minus;
+        }
+        if (__ballot_sync(kFullMask, used) == 0u) continue;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            g_mx += __shfl_down_sync(kFullMask, g_mx, o);
+            g_my += __shfl_down_sync(kFullMask, g_my, o);
+            g_a += __shfl_down_sync(kFullMask, g_a, o);
+            g_b += __shfl_down_sync(kFullMask, g_b, o);
+            g_c += __shfl_down_sync(kFullMask, g_c, o);
+            g_o += __shfl_down_sync(kFullMask, g_o, o);
+            g_r += __shfl_down_sync(kFullMask, g_r, o);
+            g_g += __shfl_down_sync(kFullMask, g_g, o);
+            g_bl += __shfl_down_sync(kFullMask, g_bl, o);
+        }
+        if (lane == 0) {
+            const int g = s_id[warp][j];
+            // back from the exp2-scaled conic (q2 = log2(e) * power) to (A, B, C)
+            atomicAdd(acc.mean2d + g, make_float2(g_mx, g_my));
+            atomicAdd(acc.conic_o + g, make_float4(-0.5f * kLog2e * g_a, -kLog2e * g_b, -0.5f * kLog2e * g_c, g_o));
+            atomicAdd(acc.color + g, make_float4(g_r, g_g, g_bl, 0.f));
+        }
+    }
+}
+
+struct PParams {
+    const float* means;
+    const float* scales;
+    const float* rotations;
+    const float* opacities;
+    const float* sh_rest;
+    const float* w2c;
+    const float* cam_pos;
+    int n;
+};
+
+struct Grads {
+    float* means;
+    float* scales;
+    float* rotations;
+    float* opacities;
+    float* sh0;
+    float* sh_rest;
+};
+
+__device__ __forceinline__ void sh_backward(float x, float y, float z, int bases, const float* v, float& gx, float& gy,
+                                            float& gz) {
+    // v[k] = sum over channels of dL/dcolour * coefficient k; returns dL/d(direction)
+    gx = gy = gz = 0.f;
+    if (bases > 1) {
+        gy += -kSH1 * v[1];
+        gz += kSH1 * v[2];
+        gx += -kSH1 * v[3];
+    }
+    if (bases > 4) {
+        const float xx = x * x, yy = y * y, zz = z * z;
+        gx += kSH2_0 * y * v[4];
+        gy += kSH2_0 * x * v[4];
+        gy += kSH2_1 * z * v[5];
+        gz += kSH2_1 * y * v[5];
+        gx += -2.f * kSH2_2 * x * v[6];
+        gy += -2.f * kSH2_2 * y * v[6];
+        gz += 4.f * kSH2_2 * z * v[6];
+        gx += kSH2_3 * z * v[7];
+        gz += kSH2_3 * x * v[7];
+        gx += 2.f * kSH2_4 * x * v[8];
+        gy += -2.f * kSH2_4 * y * v[8];
+        if (bases > 9) {
+            gx += 6.f * kSH3_0 * x * y * v[9];
+            gy += kSH3_0 * (3.f * xx - 3.f * yy) * v[9];
+            gx += kSH3_1 * y * z * v[10];
+            gy += kSH3_1 * x * z * v[10];
+            gz += kSH3_1 * x * y * v[10];
+            gx += -2.f * kSH3_2 * x * y * v[11];
+            gy += kSH3_2 * (4.f * zz - xx - 3.f * yy) * v[11];
+            gz += 8.f * kSH3_2 * y * z * v[11];
+            gx += -6.f * kSH3_3 * x * z * v[12];
+            gy += -6.f * kSH3_3 * y * z * v[12];
+            gz += kSH3_3 * (6.f * zz - 3.f * xx - 3.f * yy) * v[12];
+            gx += kSH3_4 * (4.f * zz - 3.f * xx - yy) * v[13];
+            gy += -2.f * kSH3_4 * x * y * v[13];
+            gz += 8.f * kSH3_4 * x * z * v[13];
+            gx += 2.f * kSH3_5 * x * z * v[14];
+            gy += -2.f * kSH3_5 * y * z * v[14];
+            gz += kSH3_5 * (xx - yy) * v[14];
+            gx += kSH3_6 * (3.f * xx - 3.f * yy) * v[15];
+            gy += -6.f * kSH3_6 * x * y * v[15];
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kPbThreads) k_preprocess_backward(PParams P, Cam cam, PrimBuffers pb, GradAcc acc,
+                                                                    Grads out) {
+    extern __shared__ __align__(16) float s_sh[];  // [kPbWarps][32 * rest_bases * 3]
+    const int i = blockIdx.x * kPbThreads + threadIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (i - lane >= P.n) return;  // whole warp past the end
+    const bool valid = i < P.n;
+    const bool vis = valid && pb.n_touched[i] > 0;
+    const int rest3 = cam.rest_bases * 3;
+    float* sh = s_sh + warp * 32 * rest3;
+    const int first = i - lane;
+    const int cnt = min(32, P.n - first);
+    const int nfl = cnt * rest3;
+    const bool vec = ((reinterpret_cast<uintptr_t>(P.sh_rest + static_cast<size_t>(first) * rest3) |
+                       reinterpret_cast<uintptr_t>(out.sh_rest + static_cast<size_t>(first) * rest3)) & 15u) == 0;
+    const unsigned any_vis = __ballot_sync(kFullMask, vis);
+    if (any_vis && cam.active_sh_bases > 1 && rest3 > 0) {
+        const float* src = P.sh_rest + static_cast<size_t>(first) * rest3;
+        int done = 0;
+        if (vec) {
+            const int n4 = nfl / 4;
+            for (int k = lane; k < n4; k += 32)
+                reinterpret_cast<float4*>(sh)[k] = __ldg(reinterpret_cast<const float4*>(src) + k);
+            done = n4 * 4;
+        }
+        for (int k = done + lane; k < nfl; k += 32) sh[k] = __ldg(src + k);
+    }
+    __syncwarp();
+
+    float* my_sh = sh + lane * rest3;  // this Gaussian's coefficients, overwritten by their gradients
+    if (vis) {
+        float w2c[12];
+#pragma unroll
+        for (int k = 0; k < 12; ++k) w2c[k] = __ldg(P.w2c + k);
+        const float px = P.means[3 * i], py = P.means[3 * i + 1], pz = P.means[3 * i + 2];
+        const float xc = w2c[0] * px + w2c[1] * py + w2c[2] * pz + w2c[3];
+        const float yc = w2c[4] * px + w2c[5] * py + w2c[6] * pz + w2c[7];
+        const float zc = w2c[8] * px + w2c[9] * py + w2c[10] * pz + w2c[11];
+
+        const float2 gm = acc.mean2d[i];
+        const float4 gco = acc.conic_o[i];
+        const float4 gcl = acc.color[i];
+        const float4 cz = pb.color_z[i];
+        const float gr = cz.x >= 0.f ? gcl.x : 0.f, gg = cz.y >= 0.f ? gcl.y : 0.f, gb = cz.z >= 0.f ? gcl.z : 0.f;
+
+        // ---- SH: colour = sum_k basis_k(d) sh_k + 0.5, d = (p - cam) / |p - cam|
+        float ux = px - __ldg(P.cam_pos), uy = py - __ldg(P.cam_pos + 1), uz = pz - __ldg(P.cam_pos + 2);
+        const float inv_len = rsqrtf(ux * ux + uy * uy + uz * uz);
+        const float dx = ux * inv_len, dy = uy * inv_len, dz = uz * inv_len;
+        float bas[16];
+        sh_basis(dx, dy, dz, cam.active_sh_bases, bas);
+        out.sh0[3 * i] = bas[0] * gr;
+        out.sh0[3 * i + 1] = bas[0] * gg;
+        out.sh0[3 * i + 2] = bas[0] * gb;
+        float v[16];
+        v[0] = 0.f;
+        const int nb = min(cam.active_sh_bases, cam.rest_bases + 1);
+        for (int k = 1; k < nb; ++k) {
+            const float cr = my_sh[3 * (k - 1)], cg = my_sh[3 * (k - 1) + 1], cb = my_sh[3 * (k - 1) + 2];
+            v[k] = gr * cr + gg * cg + gb * cb;
+            my_sh[3 * (k - 1)] = bas[k] * gr;
+            my_sh[3 * (k - 1) + 1] = bas[k] * gg;
+            my_sh[3 * (k - 1) + 2] = bas[k] * gb;
+        }
+        for (int k = nb; k < 16; ++k) v[k] = 0.f;
+        for (int k = max(nb, 1); k <= cam.rest_bases; ++k) {
+            my_sh[3 * (k - 1)] = 0.f;
+            my_sh[3 * (k - 1) + 1] = 0.f;
+            my_sh[3 * (k - 1) + 2] = 0.f;
+        }
+        float gdx, gdy, gdz;
+        sh_backward(dx, dy, dz, nb, v, gdx, gdy, gdz);
+        const float dd = gdx * dx + gdy * dy + gdz * dz;
+        float gpx = (gdx - dx * dd) * inv_len, gpy = (gdy - dy * dd) * inv_len, gpz = (gdz - dz * dd) * inv_len;
+
+        // ---- recompute the projection
+        const float4 q = make_float4(P.rotations[4 * i], P.rotations[4 * i + 1], P.rotations[4 * i + 2],
+                                     P.rotations[4 * i + 3]);
+        float nsq;
+        const Mat3 R = quat_to_rot(q, nsq);
+        const float s[3] = {expf(P.scales[3 * i]), expf(P.scales[3 * i + 1]), expf(P.scales[3 * i + 2])};
+        float M[3][3];
+#pragma unroll
+        for (int r = 0; r < 3; ++r)
+#pragma unroll
+            for (int c = 0; c < 3; ++c) M[r][c] = R.m[r][c] * s[c];
+        float S3[3][3];
+#pragma unroll
+        for (int r = 0; r < 3; ++r)
+#pragma unroll
+            for (int c = 0; c < 3; ++c) S3[r][c] = M[r][0] * M[c][0] + M[r][1] * M[c][1] + M[r][2] * M[c][2];
+        float T1[3][3], Sc[3][3];
+#pragma unroll
+        for (int r = 0; r < 3; ++r)
+#pragma unroll
+            for (int c = 0; c < 3; ++c)
+                T1[r][c] = w2c[4 * r] * S3[0][c] + w2c[4 * r + 1] * S3[1][c] + w2c[4 * r + 2] * S3[2][c];
+#pragma unroll
+        for (int r = 0; r < 3; ++r)
+#pragma unroll
+            for (int c = 0; c < 3; ++c)
+                Sc[r][c] = T1[r][0] * w2c[4 * c] + T1[r][1] * w2c[4 * c + 1] + T1[r][2] * w2c[4 * c + 2];
+        const float inv_z = 1.f / zc;
+        const float lox = -1.3f * cam.cx / cam.fx, hix = 1.3f * (cam.width - cam.cx) / cam.fx;
+        const float loy = -1.3f * cam.cy / cam.fy, hiy = 1.3f * (cam.height - cam.cy) / cam.fy;
+        const float rx = xc * inv_z, ry = yc * inv_z;
+        const float tx = fminf(fmaxf(rx, lox), hix), ty = fminf(fmaxf(ry, loy), hiy);
+        const bool free_x = rx >= lox && rx <= hix, free_y = ry >= loy && ry <= hiy;
+        const float j00 = cam.fx * inv_z, j02 = -cam.fx * tx * inv_z;
+        const float j11 = cam.fy * inv_z, j12 = -cam.fy * ty * inv_z;
+        const float a = j00 * (j00 * Sc[0][0] + j02 * Sc[0][2]) + j02 * (j00 * Sc[2][0] + j02 * Sc[2][2]);
+        const float b = j00 * (j11 * Sc[0][1] + j12 * Sc[0][2]) + j02 * (j11 * Sc[2][1] + j12 * Sc[2][2]);
+        const float c = j11 * (j11 * Sc[1][1] + j12 * Sc[1][2]) + j12 * (j11 * Sc[2][1] + j12 * Sc[2][2]);
+        const float ad = a + kDilation, cd = c + kDilation;
+        const float det = ad * cd - b * b;
+        const float inv_det = 1.f / det;
+        const float A = cd * inv_det, B = -b * inv_det, C = ad * inv_det;
+        const float sig = 1.f / (1.f + expf(-P.opacities[i]));
+
+        // ---- opacity (and the antialiasing factor f = sqrt(det(Sigma2) / det(Sigma2 + 0.3 I)))
+        float ga = 0.f, gb2 = 0.f, gc = 0.f;  // dL/d(a, b, c) of Sigma2 (b = the off-diagonal value)
+        float f = 1.f;
+        if (cam.proper_aa) {
+            const float det0 = a * c - b * b;
+            const float ratio = det0 * inv_det;
+            if (ratio > 0.f) {
+                f = sqrtf(ratio);
+                const float dL_dratio = gco.w * sig * 0.5f / f;
+                const float id2 = inv_det * inv_det;
+                ga += dL_dratio * (c * det - det0 * cd) * id2;
+                gc += dL_dratio * (a * det - det0 * ad) * id2;
+                gb2 += dL_dratio * (-2.f * b * (det - det0)) * id2;
+            } else {
+                f = 0.f;
+            }
+        }
+        out.opacities[i] = gco.w * f * sig * (1.f - sig);
+
+        // ---- conic = inverse of [[ad, b], [b, cd]]: dL/dS = -K G K with G = [[gA, gB/2], [gB/2, gC]]
+        {
+            const float g0 = gco.x, g1 = 0.5f * gco.y, g2 = gco.z;
+            const float k00 = A * g0 + B * g1, k01 = A * g1 + B * g2, k10 = B * g0 + C * g1, k11 = B * g1 + C * g2;
+            const float p00 = k00 * A + k01 * B, p01 = k00 * B + k01 * C, p11 = k10 * B + k11 * C;
+            ga += -p00;
+            gc += -p11;
+            gb2 += -2.f * p01;
+        }
+
+        // ---- Sigma2 = J Sc J^T: dL/dSc = J^T G2 J, dL/dJ = 2 G2 J Sc, G2 = [[ga, gb2/2], [gb2/2, gc]]
+        const float G2[2][2] = {{ga, 0.5f * gb2}, {0.5f * gb2, gc}};
+        const float J[2][3] = {{j00, 0.f, j02}, {0.f, j11, j12}};
+        float GJ[2][3];
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+            for (int k = 0; k < 3; ++k) GJ[r][k] = G2[r][0] * J[0][k] + G2[r][1] * J[1][k];
+        float gSc[3][3];
+#pragma unroll
+        for (int r = 0; r < 3; ++r)
+#pragma unroll
+            for (int k = 0; k < 3; ++k) gSc[r][k] = J[0][r] * GJ[0][k] + J[1][r] * GJ[1][k];
+        float gJ[2][3];
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+            for (int k = 0; k < 3; ++k)
+                gJ[r][k] = 2.f * (GJ[r][0] * Sc[0][k] + GJ[r][1] * Sc[1][k] + GJ[r][2] * Sc[2][k]);
+
+        // ---- J and mean2d to camera coordinates
+        const float iz2 = inv_z * inv_z;
+        float gxc = cam.fx * inv_z * gm.x;
+        float gyc = cam.fy * inv_z * gm.y;
+        float gzc = -cam.fx * xc * iz2 * gm.x - cam.fy * yc * iz2 * gm.y;
+        gzc += -cam.fx * iz2 * gJ[0][0] - cam.fy * iz2 * gJ[1][1];
+        // j02 = -fx tx / z with tx = x / z inside the clamp window, constant outside
+        gzc += gJ[0][2] * (cam.fx * tx * iz2 + (free_x ? -cam.fx * inv_z * xc * iz2 : 0.f));
+        gxc += free_x ? gJ[0][2] * (-cam.fx * iz2) : 0.f;
+        gzc += gJ[1][2] * (cam.fy * ty * iz2 + (free_y ? -cam.fy * inv_z * yc * iz2 : 0.f));
+        gyc += free_y ? gJ[1][2] * (-cam.fy * iz2) : 0.f;
+        gpx += w2c[0] * gxc + w2c[4] * gyc + w2c[8] * gzc;
+        gpy += w2c[1] * gxc + w2c[5] * gyc + w2c[9] * gzc;
+        gpz += w2c[2] * gxc + w2c[6] * gyc + w2c[10] * gzc;
+        out.means[3 * i] = gpx;
+        out.means[3 * i + 1] = gpy;
+        out.means[3 * i + 2] = gpz;
+
+        // ---- Sc = Wr S3 Wr^T: dL/dS3 = Wr^T gSc Wr; S3 = M M^T: dL/dM = 2 dL/dS3 M
+        float t1[3][3], gS3[3][3];
+#pragma unroll
+        for (int r = 0; r < 3; ++r)
+#pragma unroll
+            for (int k = 0; k < 3; ++k) t1[r][k] = w2c[r] * gSc[0][k] + w2c[4 + r] * gSc[1][k] + w2c[8 + r] * gSc[2][k];
+#pragma unroll
+        for (int r = 0; r < 3; ++r)
+#pragma unroll
+            for (int k = 0; k < 3; ++k) gS3[r][k] = t1[r][0] * w2c[k] + t1[r][1] * w2c[4 + k] + t1[r][2] * w2c[8 + k];
+        float gM[3][3];
+#pragma unroll
+        for (int r = 0; r < 3; ++r)
+#pragma unroll
+            for (int k = 0; k < 3; ++k)
+                gM[r][k] = 2.f * (gS3[r][0] * M[0][k] + gS3[r][1] * M[1][k] + gS3[r][2] * M[2][k]);
+        float gR[3][3];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            const float gs = gM[0][k] * R.m[0][k] + gM[1][k] * R.m[1][k] + gM[2][k] * R.m[2][k];
+            out.scales[3 * i + k] = gs * s[k];
+#pragma unroll
+            for (int r = 0; r < 3; ++r) gR[r][k] = gM[r][k] * s[k];
+        }
+        // ---- rotation of the normalised quaternion (w, x, y, z), then the normalisation
+        const float inv_n = rsqrtf(fmaxf(nsq, 1e-30f));
+        const float w = q.x * inv_n, qx = q.y * inv_n, qy = q.z * inv_n, qz = q.w * inv_n;
+        const float gw = 2.f * (-qz * gR[0][1] + qy * gR[0][2] + qz * gR[1][0] - qx * gR[1][2] - qy * gR[2][0] +
+                                qx * gR[2][1]);
+        const float gx = 2.f * (qy * gR[0][1] + qz * gR[0][2] + qy * gR[1][0] - 2.f * qx * gR[1][1] - w * gR[1][2] +
+                                qz * gR[2][0] + w * gR[2][1] - 2.f * qx * gR[2][2]);
+        const float gy = 2.f * (-2.f * qy * gR[0][0] + qx * gR[0][1] + w * gR[0][2] + qx * gR[1][0] + qz * gR[1][2] -
+                                w * gR[2][0] + qz * gR[2][1] - 2.f * qy * gR[2][2]);
+        const float gz = 2.f * (-2.f * qz * gR[0][0] - w * gR[0][1] + qx * gR[0][2] + w * gR[1][0] -
+                                2.f * qz * gR[1][1] + qy * gR[1][2] + qx * gR[2][0] + qy * gR[2][1]);
+        const float qd = gw * w + gx * qx + gy * qy + gz * qz;
+        out.rotations[4 * i] = (gw - w * qd) * inv_n;
+        out.rotations[4 * i + 1] = (gx - qx * qd) * inv_n;
+        out.rotations[4 * i + 2] = (gy - qy * qd) * inv_n;
+        out.rotations[4 * i + 3] = (gz - qz * qd) * inv_n;
+    } else if (valid) {
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            out.means[3 * i + k] = 0.f;
+            out.scales[3 * i + k] = 0.f;
+            out.sh0[3 * i + k] = 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) out.rotations[4 * i + k] = 0.f;
+        out.opacities[i] = 0.f;
+        if (rest3 > 0 && any_vis && cam.active_sh_bases > 1)
+            for (int k = 0; k < rest3; ++k) my_sh[k] = 0.f;
+    }
+    __syncwarp();
+    // write the warp's SH-rest gradients as one contiguous block
+    if (rest3 > 0) {
+        float* dst = out.sh_rest + static_cast<size_t>(first) * rest3;
+        const bool staged = any_vis && cam.active_sh_bases > 1;
+        int done = 0;
+        if (vec) {
+            const int n4 = nfl / 4;
+            for (int k = lane; k < n4; k += 32)
+                reinterpret_cast<float4*>(dst)[k] = staged ? reinterpret_cast<const float4*>(sh)[k]
+                                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+            done = n4 * 4;
+        }
+        for (int k = done + lane; k < nfl; k += 32) dst[k] = staged ? sh[k] : 0.f;
+    }
+}
+
+}  // namespace gs3d
+}  // namespace splat
+
+using namespace splat;
+using namespace splat::gs3d;
+
+extern "C" {
+
+size_t gs3d_backward_workspace_size(int n) {
+    Carver c(nullptr, 0);
+    carve_grad(c, n);
+    return c.used + 256;
+}
+
+int gs3d_backward(const float* grad_image, const float* image, const float* means, const float* scales,
+                  const float* rotations, const float* opacities, const float* sh_rest, int n, long long num_instances,
+                  const gs3d_settings* settings, void* prim_buf, size_t prim_bytes_, void* tile_buf,
+                  size_t tile_bytes_, void* inst_buf, size_t inst_bytes_, void* bucket_buf, size_t bucket_bytes_,
+                  long long bucket_capacity, void* workspace, size_t workspace_bytes, float* grad_means,
+                  float* grad_scales, float* grad_rotations, float* grad_opacities, float* grad_sh0,
+                  float* grad_sh_rest, void* stream) {
+    Cam cam;
+    SPLAT_TRY(fill_cam(settings, cam));
+    const long long m = num_instances;
+    const int T = cam.tiles_x * cam.tiles_y;
+    SPLAT_REQUIRE(n >= 0 && m >= 0 && m < (1ll << 31), "gs3d_backward: bad sizes n=%d M=%lld", n, m);
+    SPLAT_REQUIRE(prim_bytes_ >= prim_bytes(n) && tile_bytes_ >= tile_bytes(cam.width, cam.height) &&
+                      inst_bytes_ >= inst_bytes(m) && bucket_capacity >= bucket_bound(m, T) &&
+                      bucket_bytes_ >= bucket_bytes(bucket_capacity) &&
+                      workspace_bytes >= gs3d_backward_workspace_size(n),
+                  "gs3d_backward: a buffer is smaller than its size query");
+    if (n == 0) return SPLAT_OK;
+    cudaStream_t st = as_stream(stream);
+    Carver cp(prim_buf, prim_bytes_), ct(tile_buf, tile_bytes_), ci(inst_buf, inst_bytes_),
+        cb(bucket_buf, bucket_bytes_), cw(workspace, workspace_bytes);
+    PrimBuffers pb = carve_prim(cp, n);
+    TileBuffers tb = carve_tile(ct, cam.width, cam.height);
+    InstBuffers ib = carve_inst(ci, m);
+    BucketBuffers bb = carve_bucket(cb, bucket_capacity);
+    GradAcc acc = carve_grad(cw, n);
+    const size_t acc_bytes = cw.used;
+    SPLAT_CUDA(cudaMemsetAsync(workspace, 0, acc_bytes, st));
+    if (m > 0) {
+        k_blend_backward<<<div_up(bucket_capacity, kBwdWarps), 32 * kBwdWarps, 0, st>>>(
+            cam, pb.counters, bb.tile, tb.ranges, tb.bstart, tb.max_contrib, ib.point_list, pb.mean2d, pb.conic_o,
+            pb.color_z, pb.rect, grad_image, image, tb.n_contrib, bb.ckpt, n, static_cast<int>(m), bucket_capacity,
+            acc);
+        SPLAT_TRY(check_launch("gs3d_blend_backward"));
+    }
+    PParams P{means, scales, rotations, opacities, sh_rest, settings->w2c, settings->cam_position, n};
+    Grads g{grad_means, grad_scales, grad_rotations, grad_opacities, grad_sh0, grad_sh_rest};
+    const size_t smem = static_cast<size_t>(kPbWarps) * 32 * cam.rest_bases * 3 * sizeof(float);
+    k_preprocess_backward<<<div_up(n, kPbThreads), kPbThreads, smem, st>>>(P, cam, pb, acc, g);
+    return check_launch("gs3d_preprocess_backward");
+}
+
+}  // extern "C"

@@ -1,0 +1,281 @@
+// gs3d_common.cuh - the 3DGS rasterization rules and buffer layouts shared by the forward and
+// backward kernels.
+//
+// The rules are this library's restatement of Faster-GS's (nerficg-project/faster-gaussian-splatting
+// @ c60ea26, not vendored in the reference; its blend rules are visible in
+// phase1/fastergs_macro.patch:174-211 and upstream/upstream_main_kernels.patch:9-13,100-103):
+//   * camera: x_c = w2c[:3,:3] p + w2c[:3,3]; visible if near <= z <= far
+//   * Sigma3 = R S S^T R^T (R from the normalised quaternion (w, x, y, z), S = diag(exp(scales)))
+//   * EWA: Sigma2 = J W Sigma3 W^T J^T with J the projection Jacobian at the clamped
+//     x/z in [-1.3 cx/fx, 1.3 (W-cx)/fx] (and likewise y), low-pass dilation +0.3 on the diagonal;
+//     proper antialiasing scales opacity by sqrt(det(Sigma2) / det(Sigma2 + 0.3 I))
+//   * mean2d = (fx x/z + cx, fy y/z + cy) in pixel units, pixel (i, j) has its centre at (i+0.5, j+0.5)
+//   * colour = real SH of degree <= 3 in the view direction (p - cam_position) / |.|, + 0.5; the
+//     blend uses max(colour, 0) and the gradient passes where colour >= 0
+//   * opacity = sigmoid(logit); a Gaussian with opacity < 1/255 can never reach the alpha cut-off
+//   * blend: G = exp2(min(q2, 0)) with q2 = log2(e) * (-0.5 d^T conic d), d = mean2d - centre;
+//     alpha = opacity G; skipped if alpha < 1/255; C += T alpha c; T *= 1 - alpha; the pixel
+//     stops after the splat that drops T below 1e-4; image = C + T bg
+//   * a Gaussian is listed in a 16x16 tile iff the ellipse alpha >= 1/255 (q <= 2 ln(255 opacity))
+//     meets the tile's pixel-centre rectangle (exact rectangle minimum of the quadratic form)
+//   * tile lists are ordered by the 64-bit key (tile << 32 | float bits of z), ties by Gaussian index
+#pragma once
+
+#include "common.cuh"
+#include "sort.cuh"
+
+namespace splat {
+namespace gs3d {
+
+constexpr int kTile = 16;
+constexpr int kTilePixels = kTile * kTile;
+constexpr int kBucket = 32;
+constexpr float kAlphaMin = 1.0f / 255.0f;
+constexpr float kTMin = 1e-4f;
+constexpr float kOneMinusAlphaEps = 1e-6f;
+constexpr float kDilation = 0.3f;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kCullMargin = 0.01f;  // log-domain margin of the per-warp culling rectangle
+
+// Real spherical-harmonics constants (degrees 0-3), the published values used by 3DGS.
+constexpr float kSH0 = 0.28209479177387814f;
+constexpr float kSH1 = 0.4886025119029199f;
+constexpr float kSH2_0 = 1.0925484305920792f;
+constexpr float kSH2_1 = -1.0925484305920792f;
+constexpr float kSH2_2 = 0.31539156525252005f;
+constexpr float kSH2_3 = -1.0925484305920792f;
+constexpr float kSH2_4 = 0.5462742152960396f;
+constexpr float kSH3_0 = -0.5900435899266435f;
+constexpr float kSH3_1 = 2.890611442640554f;
+constexpr float kSH3_2 = -0.4570457994644658f;
+constexpr float kSH3_3 = 0.3731763325901154f;
+constexpr float kSH3_4 = -0.4570457994644658f;
+constexpr float kSH3_5 = 1.445305721320277f;
+constexpr float kSH3_6 = -0.5900435899266435f;
+
+// Camera and image, passed by value to every kernel.
+struct Cam {
+    float fx, fy, cx, cy, near_plane, far_plane;
+    int width, height, tiles_x, tiles_y;
+    int active_sh_bases;  // 1, 4, 9 or 16
+    int rest_bases;       // coefficients per Gaussian in sh_rest (15 for degree 3)
+    int proper_aa;
+};
+
+// ---------------------------------------------------------------------------------------------
+// Per-Gaussian ("primitive") buffer, sized by N
+// ---------------------------------------------------------------------------------------------
+struct PrimBuffers {
+    float2* mean2d;        // pixel units
+    float4* conic_o;       // (A, B, C, opacity); power = -0.5 (A dx^2 + 2B dx dy + C dy^2)
+    float4* color_z;       // (r, g, b) unclamped SH colour, w = camera depth z
+    ushort4* rect;         // culling rectangle in pixels (x0, y0, x1, y1), inclusive, with margin
+    float* thr;            // ln(255 opacity): the ellipse q <= 2 thr holds every alpha >= 1/255
+    uint32_t* n_touched;   // listed tiles (0 = not visible)
+    uint32_t* offsets;     // exclusive prefix of n_touched
+    uint32_t* counters;    // [0] = instance count M, [1] = bucket count B
+    void* scan_ws;
+    size_t scan_bytes;
+};
+
+// Per-tile and per-pixel buffer, sized by the image
+struct TileBuffers {
+    uint2* ranges;          // [T] (start, end) into the instance list
+    uint32_t* nb;           // [T + 1] buckets per tile
+    uint32_t* bstart;       // [T + 1] first bucket of each tile (exclusive prefix of nb)
+    uint32_t* max_contrib;  // [T] max over the tile's pixels of n_contrib
+    float* final_T;         // [H * W]
+    uint32_t* n_contrib;    // [H * W] list position of the last contributor + 1
+    void* scan_ws;
+    size_t scan_bytes;
+};
+
+// Per-instance buffer, sized by M
+struct InstBuffers {
+    unsigned long long* keys;
+    uint32_t* vals;
+    unsigned long long* keys_sorted;
+    uint32_t* point_list;  // sorted Gaussian ids
+    void* sort_ws;
+    size_t sort_bytes;
+};
+
+// Per-bucket buffer, sized by the bucket bound floor((M + 31 T) / 32) + 1
+struct BucketBuffers {
+    uint32_t* tile;  // [B] tile of each bucket
+    float4* ckpt;    // [B * 256] (C.r, C.g, C.b, T) at the bucket start, per tile pixel
+};
+
+inline long long bucket_bound(long long m, int T) { return (m + 31ll * T) / 32 + 1; }
+
+// Validates the settings and fills the kernel-side camera (gs3d_forward.cu).
+int fill_cam(const gs3d_settings* s, Cam& cam);
+
+inline PrimBuffers carve_prim(Carver& c, int n) {
+    PrimBuffers b;
+    const size_t nn = static_cast<size_t>(n < 1 ? 1 : n);
+    b.mean2d = c.take<float2>(nn);
+    b.conic_o = c.take<float4>(nn);
+    b.color_z = c.take<float4>(nn);
+    b.rect = c.take<ushort4>(nn);
+    b.thr = c.take<float>(nn);
+    b.n_touched = c.take<uint32_t>(nn);
+    b.offsets = c.take<uint32_t>(nn);
+    b.counters = c.take<uint32_t>(4);
+    b.scan_bytes = scan_workspace_bytes(static_cast<long long>(nn));
+    b.scan_ws = c.take<unsigned char>(b.scan_bytes);
+    return b;
+}
+
+inline TileBuffers carve_tile(Carver& c, int W, int H) {
+    const int T = ((W + kTile - 1) / kTile) * ((H + kTile - 1) / kTile);
+    TileBuffers b;
+    b.ranges = c.take<uint2>(T);
+    b.nb = c.take<uint32_t>(T + 1);
+    b.bstart = c.take<uint32_t>(T + 1);
+    b.max_contrib = c.take<uint32_t>(T);
+    b.final_T = c.take<float>(static_cast<size_t>(W) * H);
+    b.n_contrib = c.take<uint32_t>(static_cast<size_t>(W) * H);
+    b.scan_bytes = scan_workspace_bytes(T + 1);
+    b.scan_ws = c.take<unsigned char>(b.scan_bytes);
+    return b;
+}
+
+inline InstBuffers carve_inst(Carver& c, long long m) {
+    const size_t mm = static_cast<size_t>(m < 1 ? 1 : m);
+    InstBuffers b;
+    b.keys = c.take<unsigned long long>(mm);
+    b.vals = c.take<uint32_t>(mm);
+    b.keys_sorted = c.take<unsigned long long>(mm);
+    b.point_list = c.take<uint32_t>(mm);
+    b.sort_bytes = sort_workspace_bytes<unsigned long long>(static_cast<long long>(mm));
+    b.sort_ws = c.take<unsigned char>(b.sort_bytes);
+    return b;
+}
+
+inline BucketBuffers carve_bucket(Carver& c, long long bcap) {
+    BucketBuffers b;
+    b.tile = c.take<uint32_t>(static_cast<size_t>(bcap < 1 ? 1 : bcap));
+    b.ckpt = c.take<float4>(static_cast<size_t>(bcap < 1 ? 1 : bcap) * kTilePixels);
+    return b;
+}
+
+inline size_t prim_bytes(int n) {
+    Carver c(nullptr, 0);
+    carve_prim(c, n);
+    return c.used + 256;
+}
+inline size_t tile_bytes(int W, int H) {
+    Carver c(nullptr, 0);
+    carve_tile(c, W, H);
+    return c.used + 256;
+}
+inline size_t inst_bytes(long long m) {
+    Carver c(nullptr, 0);
+    carve_inst(c, m);
+    return c.used + 256;
+}
+inline size_t bucket_bytes(long long bcap) {
+    Carver c(nullptr, 0);
+    carve_bucket(c, bcap);
+    return c.used + 256;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Device math
+// ---------------------------------------------------------------------------------------------
+struct Mat3 {
+    float m[3][3];
+};
+
+// Rotation of the normalised quaternion q = (w, x, y, z); returns |q|^2 for the backward.
+__device__ __forceinline__ Mat3 quat_to_rot(float4 q, float& norm_sq) {
+    norm_sq = q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w;
+    const float inv = rsqrtf(fmaxf(norm_sq, 1e-30f));
+    const float w = q.x * inv, x = q.y * inv, y = q.z * inv, z = q.w * inv;
+    Mat3 R;
+    R.m[0][0] = 1.f - 2.f * (y * y + z * z);
+    R.m[0][1] = 2.f * (x * y - w * z);
+    R.m[0][2] = 2.f * (x * z + w * y);
+    R.m[1][0] = 2.f * (x * y + w * z);
+    R.m[1][1] = 1.f - 2.f * (x * x + z * z);
+    R.m[1][2] = 2.f * (y * z - w * x);
+    R.m[2][0] = 2.f * (x * z - w * y);
+    R.m[2][1] = 2.f * (y * z + w * x);
+    R.m[2][2] = 1.f - 2.f * (x * x + y * y);
+    return R;
+}
+
+// SH basis values b[0..15] (b[0] = SH0) for the unit direction (x, y, z).
+__device__ __forceinline__ void sh_basis(float x, float y, float z, int bases, float* b) {
+    b[0] = kSH0;
+    if (bases > 1) {
+        b[1] = -kSH1 * y;
+        b[2] = kSH1 * z;
+        b[3] = -kSH1 * x;
+    }
+    if (bases > 4) {
+        const float xx = x * x, yy = y * y, zz = z * z;
+        b[4] = kSH2_0 * x * y;
+        b[5] = kSH2_1 * y * z;
+        b[6] = kSH2_2 * (2.f * zz - xx - yy);
+        b[7] = kSH2_3 * x * z;
+        b[8] = kSH2_4 * (xx - yy);
+        if (bases > 9) {
+            b[9] = kSH3_0 * y * (3.f * xx - yy);
+            b[10] = kSH3_1 * x * y * z;
+            b[11] = kSH3_2 * y * (4.f * zz - xx - yy);
+            b[12] = kSH3_3 * z * (2.f * zz - 3.f * xx - 3.f * yy);
+            b[13] = kSH3_4 * x * (4.f * zz - xx - yy);
+            b[14] = kSH3_5 * z * (xx - yy);
+            b[15] = kSH3_6 * x * (xx - 3.f * yy);
+        }
+    }
+}
+
+// q(d) = A dx^2 + 2 B dx dy + C dy^2, every operation rounded separately (no contraction), so the
+// count pass, the write pass and the C oracle all get the same bits.
+__device__ __forceinline__ float quad_form(float A, float B, float C, float dx, float dy) {
+    const float t0 = __fmul_rn(__fmul_rn(A, dx), dx);
+    const float t1 = __fmul_rn(__fmul_rn(__fmul_rn(2.f, B), dx), dy);
+    const float t2 = __fmul_rn(__fmul_rn(C, dy), dy);
+    return __fadd_rn(__fadd_rn(t0, t1), t2);
+}
+
+// Minimum over the axis-aligned rectangle [x0, x1] x [y0, y1] (offsets from the mean) of the
+// positive-definite q: 0 when the mean lies inside, else the smaller minimum over the (at most two)
+// edges that face the mean, each a clamped 1D quadratic.
+__device__ __forceinline__ float rect_min_quadratic(float A, float B, float C, float x0, float x1, float y0,
+                                                    float y1) {
+    const bool in_x = x0 <= 0.f && 0.f <= x1;
+    const bool in_y = y0 <= 0.f && 0.f <= y1;
+    if (in_x && in_y) return 0.f;
+    float best = 3.0e38f;
+    if (!in_x) {
+        const float dx = x0 > 0.f ? x0 : x1;
+        const float dy = fminf(fmaxf(__fdiv_rn(__fmul_rn(-B, dx), C), y0), y1);
+        best = fminf(best, quad_form(A, B, C, dx, dy));
+    }
+    if (!in_y) {
+        const float dy = y0 > 0.f ? y0 : y1;
+        const float dx = fminf(fmaxf(__fdiv_rn(__fmul_rn(-B, dy), A), x0), x1);
+        best = fminf(best, quad_form(A, B, C, dx, dy));
+    }
+    return best;
+}
+
+// Does the ellipse q <= 2 thr around (mx, my) reach a pixel centre of tile (tx, ty)? (The pixel-
+// centre rectangle is tested as a continuous rectangle, which can only add tiles, never drop one.)
+__device__ __forceinline__ bool tile_hit(float mx, float my, float A, float B, float C, float thr, int tx, int ty,
+                                         int W, int H) {
+    const float px0 = static_cast<float>(tx * kTile) + 0.5f;
+    const float px1 = static_cast<float>(min((tx + 1) * kTile, W)) - 0.5f;
+    const float py0 = static_cast<float>(ty * kTile) + 0.5f;
+    const float py1 = static_cast<float>(min((ty + 1) * kTile, H)) - 0.5f;
+    const float q = rect_min_quadratic(A, B, C, __fsub_rn(px0, mx), __fsub_rn(px1, mx), __fsub_rn(py0, my),
+                                       __fsub_rn(py1, my));
+    return q <= __fmul_rn(2.f, thr);
+}
+
+}  // namespace gs3d
+}  // namespace splat

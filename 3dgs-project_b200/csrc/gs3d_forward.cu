@@ -1,0 +1,451 @@
+// gs3d_forward.cu - 3DGS forward: preprocess, key duplication, 64-bit key sort, tile ranges and
+// buckets, front-to-back blend (rules in gs3d_common.cuh).
+//
+// Launch sequence of one forward (all on the caller's stream):
+//   gs3d_preprocess   k_preprocess (1 thread per Gaussian; SH rows loaded per warp with 16-byte
+//                     loads through shared memory), scan of the tile counts -> M on the device
+//   (host reads M once to size the instance buffer; the bucket buffer is sized by a bound)
+//   gs3d_render       k_duplicate, radix sort of (tile << 32 | depth bits, id) over 32 + tile bits,
+//                     k_ranges, k_bucket_counts + scan, k_bucket_tiles, k_blend
+// k_blend: one 256-thread block per 16x16 tile; each warp owns an 8x4 subtile and walks the
+// tile list in 32-splat buckets staged in shared memory, skipping (by ballot) the splats whose
+// culling rectangle misses its subtile - a rectangle that holds every pixel with alpha >= 1/255,
+// so the skip changes no result. The (C, T) state of every pixel is saved at each bucket start for
+// the backward; a block stops once every pixel has stopped.
+#include "gs3d_common.cuh"
+
+namespace splat {
+namespace gs3d {
+
+constexpr int kPreThreads = 128;
+constexpr int kPreWarps = kPreThreads / 32;
+constexpr int kMaxRestBases = 15;
+
+struct Params {
+    const float* means;      // [N, 3]
+    const float* scales;     // [N, 3] log scales
+    const float* rotations;  // [N, 4] (w, x, y, z), not normalised
+    const float* opacities;  // [N] logits
+    const float* sh0;        // [N, 3]
+    const float* sh_rest;    // [N, rest_bases, 3]
+    const float* w2c;        // [4, 4] row-major
+    const float* cam_pos;    // [3]
+    int n;
+};
+
+__global__ void __launch_bounds__(kPreThreads) k_preprocess(Params P, Cam cam, PrimBuffers pb) {
+    extern __shared__ __align__(16) float s_sh[];  // [kPreWarps][32 * rest_bases * 3]
+    const int i = blockIdx.x * kPreThreads + threadIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const bool valid = i < P.n;
+    const int rest3 = cam.rest_bases * 3;
+
+    float w2c[12];
+#pragma unroll
+    for (int k = 0; k < 12; ++k) w2c[k] = __ldg(P.w2c + k);
+
+    float px = 0.f, py = 0.f, pz = 0.f;
+    if (valid) {
+        px = P.means[3 * i];
+        py = P.means[3 * i + 1];
+        pz = P.means[3 * i + 2];
+    }
+    const float xc = w2c[0] * px + w2c[1] * py + w2c[2] * pz + w2c[3];
+    const float yc = w2c[4] * px + w2c[5] * py + w2c[6] * pz + w2c[7];
+    const float zc = w2c[8] * px + w2c[9] * py + w2c[10] * pz + w2c[11];
+    bool vis = valid && zc >= cam.near_plane && zc <= cam.far_plane;
+
+    float mx = 0.f, my = 0.f, A = 0.f, B = 0.f, C = 0.f, o = 0.f, thr = 0.f;
+    int rx0 = 0, ry0 = 0, rx1 = -1, ry1 = -1;
+    uint32_t touched = 0;
+    if (vis) {
+        const float4 q = make_float4(P.rotations[4 * i], P.rotations[4 * i + 1], P.rotations[4 * i + 2],
+                                     P.rotations[4 * i + 3]);
+        float nsq;
+        const Mat3 R = quat_to_rot(q, nsq);
+        const float s[3] = {expf(P.scales[3 * i]), expf(P.scales[3 * i + 1]), expf(P.scales[3 * i + 2])};
+        float M[3][3];
+#pragma unroll
+        for (int r = 0; r < 3; ++r)
+#pragma unroll
+            for (int c = 0; c < 3; ++c) M[r][c] = R.m[r][c] * s[c];
+        float S3[3][3];
+#pragma unroll
+        for (int r = 0; r < 3; ++r)
+#pragma unroll
+            for (int c = 0; c < 3; ++c) S3[r][c] = M[r][0] * M[c][0] + M[r][1] * M[c][1] + M[r][2] * M[c][2];
+        // camera-space covariance Sc = Wr S3 Wr^T
+        float T1[3][3], Sc[3][3];
+#pragma unroll
+        for (int r = 0; r < 3; ++r)
+#pragma unroll
+            for (int c = 0; c < 3; ++c)
+                T1[r][c] = w2c[4 * r] * S3[0][c] + w2c[4 * r + 1] * S3[1][c] + w2c[4 * r + 2] * S3[2][c];
+#pragma unroll
+        for (int r = 0; r < 3; ++r)
+#pragma unroll
+            for (int c = 0; c < 3; ++c)
+                Sc[r][c] = T1[r][0] * w2c[4 * c] + T1[r][1] * w2c[4 * c + 1] + T1[r][2] * w2c[4 * c + 2];
+        const float inv_z = 1.f / zc;
+        const float tx = fminf(fmaxf(xc * inv_z, -1.3f * cam.cx / cam.fx), 1.3f * (cam.width - cam.cx) / cam.fx);
+        const float ty = fminf(fmaxf(yc * inv_z, -1.3f * cam.cy / cam.fy), 1.3f * (cam.height - cam.cy) / cam.fy);
+        const float j00 = cam.fx * inv_z, j02 = -cam.fx * tx * inv_z;
+        const float j11 = cam.fy * inv_z, j12 = -cam.fy * ty * inv_z;
+        // Sigma2 = J Sc J^T with J = [[j00, 0, j02], [0, j11, j12]]
+        const float a = j00 * (j00 * Sc[0][0] + j02 * Sc[0][2]) + j02 * (j00 * Sc[2][0] + j02 * Sc[2][2]);
+        const float b = j00 * (j11 * Sc[0][1] + j12 * Sc[0][2]) + j02 * (j11 * Sc[2][1] + j12 * Sc[2][2]);
+        const float c = j11 * (j11 * Sc[1][1] + j12 * Sc[1][2]) + j12 * (j11 * Sc[2][1] + j12 * Sc[2][2]);
+        const float ad = a + kDilation, cd = c + kDilation;
+        const float det = ad * cd - b * b;
+        o = 1.f / (1.f + expf(-P.opacities[i]));
+        if (cam.proper_aa) o *= sqrtf(fmaxf((a * c - b * b) / det, 0.f));
+        mx = cam.fx * xc * inv_z + cam.cx;
+        my = cam.fy * yc * inv_z + cam.cy;
+        vis = det > 0.f && o * 255.f >= 1.f && isfinite(mx) && isfinite(my);
+        if (vis) {
+            const float inv_det = 1.f / det;
+            A = cd * inv_det;
+            B = -b * inv_det;
+            C = ad * inv_det;
+            thr = logf(255.f * o);
+            const float r2 = 2.f * (thr + kCullMargin);
+            const float ex = sqrtf(r2 * ad), ey = sqrtf(r2 * cd);
+            const float fx0 = ceilf(mx - ex - 0.5f) - 1.f, fx1 = floorf(mx + ex - 0.5f) + 1.f;
+            const float fy0 = ceilf(my - ey - 0.5f) - 1.f, fy1 = floorf(my + ey - 0.5f) + 1.f;
+            vis = fx1 >= 0.f && fy1 >= 0.f && fx0 <= cam.width - 1 && fy0 <= cam.height - 1;
+            if (vis) {
+                rx0 = static_cast<int>(fmaxf(fx0, 0.f));
+                ry0 = static_cast<int>(fmaxf(fy0, 0.f));
+                rx1 = static_cast<int>(fminf(fx1, static_cast<float>(cam.width - 1)));
+                ry1 = static_cast<int>(fminf(fy1, static_cast<float>(cam.height - 1)));
+                for (int tyi = ry0 / kTile; tyi <= ry1 / kTile; ++tyi)
+                    for (int txi = rx0 / kTile; txi <= rx1 / kTile; ++txi)
+                        touched += tile_hit(mx, my, A, B, C, thr, txi, tyi, cam.width, cam.height) ? 1u : 0u;
+                vis = touched > 0;
+            }
+        }
+    }
+
+    // colour: the warp's SH rows are one contiguous block (its first Gaussian is a multiple of 32)
+    float3 col = make_float3(0.f, 0.f, 0.f);
+    const unsigned any_vis = __ballot_sync(kFullMask, vis);
+    if (any_vis) {
+        float* sh = s_sh + warp * 32 * rest3;
+        const int first = i - lane;
+        const int cnt = min(32, P.n - first);
+        const int nfl = cnt * rest3;
+        const float* src = P.sh_rest + static_cast<size_t>(first) * rest3;
+        if (cam.active_sh_bases > 1 && rest3 > 0) {
+            int done = 0;
+            if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+                const int n4 = nfl / 4;
+                for (int k = lane; k < n4; k += 32)
+                    reinterpret_cast<float4*>(sh)[k] = __ldg(reinterpret_cast<const float4*>(src) + k);
+                done = n4 * 4;
+            }
+            for (int k = done + lane; k < nfl; k += 32) sh[k] = __ldg(src + k);
+        }
+        __syncwarp();
+        if (vis) {
+            float dx = px - __ldg(P.cam_pos), dy = py - __ldg(P.cam_pos + 1), dz = pz - __ldg(P.cam_pos + 2);
+            const float inv_len = rsqrtf(dx * dx + dy * dy + dz * dz);
+            dx *= inv_len;
+            dy *= inv_len;
+            dz *= inv_len;
+            float bas[16];
+            sh_basis(dx, dy, dz, cam.active_sh_bases, bas);
+            col.x = bas[0] * P.sh0[3 * i] + 0.5f;
+            col.y = bas[0] * P.sh0[3 * i + 1] + 0.5f;
+            col.z = bas[0] * P.sh0[3 * i + 2] + 0.5f;
+            const float* mine = sh + lane * rest3;
+            for (int k = 1; k < cam.active_sh_bases && k <= cam.rest_bases; ++k) {
+                col.x += bas[k] * mine[3 * (k - 1)];
+                col.y += bas[k] * mine[3 * (k - 1) + 1];
+                col.z += bas[k] * mine[3 * (k - 1) + 2];
+            }
+        }
+    }
+    if (!valid) return;
+    pb.n_touched[i] = touched;
+    if (!vis) return;
+    pb.mean2d[i] = make_float2(mx, my);
+    pb.conic_o[i] = make_float4(A, B, C, o);
+    pb.color_z[i] = make_float4(col.x, col.y, col.z, zc);
+    pb.rect[i] = make_ushort4(static_cast<unsigned short>(rx0), static_cast<unsigned short>(ry0),
+                              static_cast<unsigned short>(rx1), static_cast<unsigned short>(ry1));
+    pb.thr[i] = thr;
+}
+
+// One (key, id) per listed tile; never more than the counted n_touched (a shortfall, which the
+// shared tile test rules out, is padded with keys past the last tile).
+__global__ void k_duplicate(int n, Cam cam, PrimBuffers pb, InstBuffers ib) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const uint32_t cnt = pb.n_touched[i];
+    if (cnt == 0) return;
+    const float2 m = pb.mean2d[i];
+    const float4 co = pb.conic_o[i];
+    const float thr = pb.thr[i];
+    const ushort4 r = pb.rect[i];
+    const unsigned long long zbits = __float_as_uint(pb.color_z[i].w);
+    const uint32_t off = pb.offsets[i];
+    uint32_t k = 0;
+    for (int ty = r.y / kTile; ty <= r.w / kTile && k < cnt; ++ty)
+        for (int tx = r.x / kTile; tx <= r.z / kTile && k < cnt; ++tx)
+            if (tile_hit(m.x, m.y, co.x, co.y, co.z, thr, tx, ty, cam.width, cam.height)) {
+                const unsigned long long tile = static_cast<unsigned long long>(ty) * cam.tiles_x + tx;
+                ib.keys[off + k] = (tile << 32) | zbits;
+                ib.vals[off + k] = static_cast<uint32_t>(i);
+                ++k;
+            }
+    const unsigned long long pad = static_cast<unsigned long long>(cam.tiles_x) * cam.tiles_y << 32;
+    for (; k < cnt; ++k) {
+        ib.keys[off + k] = pad | 0xffffffffull;
+        ib.vals[off + k] = static_cast<uint32_t>(i);
+    }
+}
+
+__global__ void k_ranges(const unsigned long long* __restrict__ keys, int m, int T, uint2* __restrict__ ranges) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= m) return;
+    const unsigned long long t = keys[i] >> 32;
+    if (t >= static_cast<unsigned long long>(T)) return;
+    if (i == 0 || (keys[i - 1] >> 32) != t) ranges[t].x = i;
+    if (i == m - 1 || (keys[i + 1] >> 32) != t) ranges[t].y = i + 1;
+}
+
+__global__ void k_bucket_counts(const uint2* __restrict__ ranges, int T, uint32_t* __restrict__ nb) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t > T) return;
+    nb[t] = t < T ? (ranges[t].y - ranges[t].x + kBucket - 1) / kBucket : 0u;
+}
+
+__global__ void k_bucket_tiles(const uint32_t* __restrict__ nb, const uint32_t* __restrict__ bstart, int T,
+                               long long bcap, uint32_t* __restrict__ bucket_tile) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T) return;
+    const uint32_t s = bstart[t];
+    for (uint32_t k = 0; k < nb[t] && s + k < bcap; ++k) bucket_tile[s + k] = t;
+}
+
+__global__ void __launch_bounds__(kTilePixels) k_blend(Cam cam, const uint2* __restrict__ ranges,
+                                                       const uint32_t* __restrict__ bstart,
+                                                       const uint32_t* __restrict__ point_list,
+                                                       const float2* __restrict__ mean2d,
+                                                       const float4* __restrict__ conic_o,
+                                                       const float4* __restrict__ color_z,
+                                                       const ushort4* __restrict__ rect, const float* __restrict__ bg,
+                                                       float* __restrict__ image, float* __restrict__ final_T,
+                                                       uint32_t* __restrict__ n_contrib,
+                                                       uint32_t* __restrict__ max_contrib, float4* __restrict__ ckpt,
+                                                       int n, int m, long long bcap) {
+    __shared__ float2 s_mean[kTilePixels];
+    __shared__ float4 s_con[kTilePixels];
+    __shared__ float4 s_col[kTilePixels];
+    __shared__ ushort4 s_rect[kTilePixels];
+    __shared__ uint32_t s_max[kTilePixels / 32];
+
+    const int tile = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tx0 = (tile % cam.tiles_x) * kTile, ty0 = (tile / cam.tiles_x) * kTile;
+    const int sx0 = tx0 + (warp & 1) * 8, sy0 = ty0 + (warp >> 1) * 4;  // this warp's 8x4 subtile
+    const int x = sx0 + (lane & 7), y = sy0 + (lane >> 3);
+    const int local = (y - ty0) * kTile + (x - tx0);
+    const bool inside = x < cam.width && y < cam.height;
+    const float pxf = static_cast<float>(x) + 0.5f, pyf = static_cast<float>(y) + 0.5f;
+
+    uint2 rg = ranges[tile];
+    rg.y = min(rg.y, static_cast<uint32_t>(m));
+    rg.x = min(rg.x, rg.y);
+    const int count = static_cast<int>(rg.y - rg.x);
+    const long long b0 = bstart[tile];
+
+    float Cr = 0.f, Cg = 0.f, Cb = 0.f, T = 1.f;
+    uint32_t last = 0;
+    bool done = !inside;
+    for (int base = 0; base < count; base += kTilePixels) {
+        if (__syncthreads_count(!done) == 0) break;
+        const int k = static_cast<int>(rg.x) + base + tid;
+        if (k < static_cast<int>(rg.y)) {
+            const int g = min(static_cast<int>(point_list[k]), n - 1);
+            s_mean[tid] = mean2d[g];
+            const float4 co = conic_o[g];
+            s_con[tid] = make_float4(-0.5f * kLog2e * co.x, -kLog2e * co.y, -0.5f * kLog2e * co.z, co.w);
+            const float4 cz = color_z[g];
+            s_col[tid] = make_float4(fmaxf(cz.x, 0.f), fmaxf(cz.y, 0.f), fmaxf(cz.z, 0.f), 0.f);
+            s_rect[tid] = rect[g];
+        }
+        __syncthreads();
+        const int in_batch = min(kTilePixels, count - base);
+        for (int j0 = 0; j0 < in_batch; j0 += kBucket) {
+            const long long bucket = b0 + ((base + j0) >> 5);
+            if (bucket < bcap) ckpt[bucket * kTilePixels + local] = make_float4(Cr, Cg, Cb, T);
+            if (__all_sync(kFullMask, done)) continue;
+            const int cnt = min(kBucket, in_batch - j0);
+            bool hit = false;
+            if (lane < cnt) {
+                const ushort4 r = s_rect[j0 + lane];
+                hit = r.x <= sx0 + 7 && r.z >= sx0 && r.y <= sy0 + 3 && r.w >= sy0;
+            }
+            unsigned pending = __ballot_sync(kFullMask, hit);
+            while (pending) {
+                const int j = j0 + __ffs(pending) - 1;
+                pending &= pending - 1;
+                if (!done) {
+                    const float2 mm = s_mean[j];
+                    const float4 co = s_con[j];
+                    const float dx = mm.x - pxf, dy = mm.y - pyf;
+                    const float q2 = dx * (co.x * dx + co.y * dy) + co.z * dy * dy;
+                    const float alpha = co.w * exp2f(fminf(q2, 0.f));
+                    if (alpha >= kAlphaMin) {
+                        const float4 c = s_col[j];
+                        const float w = alpha * T;
+                        Cr += w * c.x;
+                        Cg += w * c.y;
+                        Cb += w * c.z;
+                        T *= 1.f - alpha;
+                        last = static_cast<uint32_t>(base + j + 1);
+                        done = T < kTMin;
+                    }
+                }
+                if (__all_sync(kFullMask, done)) break;
+            }
+        }
+        __syncthreads();
+    }
+    const uint32_t wmax = __reduce_max_sync(kFullMask, last);
+    if (lane == 0) s_max[warp] = wmax;
+    __syncthreads();
+    if (tid == 0) {
+        uint32_t mxv = 0;
+#pragma unroll
+        for (int w = 0; w < kTilePixels / 32; ++w) mxv = max(mxv, s_max[w]);
+        max_contrib[tile] = mxv;
+    }
+    if (inside) {
+        const int pix = y * cam.width + x;
+        const size_t HW = static_cast<size_t>(cam.width) * cam.height;
+        image[pix] = Cr + T * __ldg(bg);
+        image[HW + pix] = Cg + T * __ldg(bg + 1);
+        image[2 * HW + pix] = Cb + T * __ldg(bg + 2);
+        final_T[pix] = T;
+        n_contrib[pix] = last;
+    }
+}
+
+int fill_cam(const gs3d_settings* s, Cam& cam) {
+    SPLAT_REQUIRE(s != nullptr, "gs3d: settings missing");
+    SPLAT_REQUIRE(s->width > 0 && s->height > 0 && s->width <= 65535 && s->height <= 65535,
+                  "gs3d: image size %dx%d out of range", s->width, s->height);
+    SPLAT_REQUIRE(s->active_sh_bases >= 1 && s->active_sh_bases <= 16, "gs3d: active_sh_bases %d not in [1, 16]",
+                  s->active_sh_bases);
+    SPLAT_REQUIRE(s->rest_bases >= 0 && s->rest_bases <= kMaxRestBases, "gs3d: rest_bases %d not in [0, 15]",
+                  s->rest_bases);
+    SPLAT_REQUIRE(s->fx > 0.f && s->fy > 0.f, "gs3d: focal lengths must be positive");
+    SPLAT_REQUIRE(s->w2c && s->cam_position && s->bg, "gs3d: w2c, cam_position and bg are required");
+    cam.fx = s->fx;
+    cam.fy = s->fy;
+    cam.cx = s->cx;
+    cam.cy = s->cy;
+    cam.near_plane = s->near_plane;
+    cam.far_plane = s->far_plane;
+    cam.width = s->width;
+    cam.height = s->height;
+    cam.tiles_x = (s->width + kTile - 1) / kTile;
+    cam.tiles_y = (s->height + kTile - 1) / kTile;
+    cam.active_sh_bases = s->active_sh_bases;
+    cam.rest_bases = s->rest_bases;
+    cam.proper_aa = s->proper_antialiasing;
+    return SPLAT_OK;
+}
+
+}  // namespace gs3d
+}  // namespace splat
+
+using namespace splat;
+using namespace splat::gs3d;
+
+extern "C" {
+
+size_t gs3d_primitive_buffer_size(int n) { return prim_bytes(n); }
+size_t gs3d_tile_buffer_size(int width, int height) { return tile_bytes(width, height); }
+size_t gs3d_instance_buffer_size(long long num_instances) { return inst_bytes(num_instances); }
+long long gs3d_bucket_bound(long long num_instances, int width, int height) {
+    const int T = ((width + kTile - 1) / kTile) * ((height + kTile - 1) / kTile);
+    return bucket_bound(num_instances, T);
+}
+size_t gs3d_bucket_buffer_size(long long bucket_capacity) { return bucket_bytes(bucket_capacity); }
+
+int gs3d_preprocess(const float* means, const float* scales, const float* rotations, const float* opacities,
+                    const float* sh0, const float* sh_rest, int n, const gs3d_settings* settings, void* prim_buf,
+                    size_t prim_bytes_, uint32_t* num_instances, void* stream) {
+    Cam cam;
+    SPLAT_TRY(fill_cam(settings, cam));
+    SPLAT_REQUIRE(n >= 0 && n < (1 << 30), "gs3d_preprocess: n=%d out of range", n);
+    SPLAT_REQUIRE(prim_bytes_ >= prim_bytes(n), "gs3d_preprocess: primitive buffer too small");
+    cudaStream_t st = as_stream(stream);
+    Carver c(prim_buf, prim_bytes_);
+    PrimBuffers pb = carve_prim(c, n);
+    if (n == 0) {
+        SPLAT_CUDA(cudaMemsetAsync(pb.counters, 0, 4 * sizeof(uint32_t), st));
+        if (num_instances) SPLAT_CUDA(cudaMemsetAsync(num_instances, 0, sizeof(uint32_t), st));
+        return SPLAT_OK;
+    }
+    Params P{means, scales, rotations, opacities, sh0, sh_rest, settings->w2c, settings->cam_position, n};
+    const size_t smem = static_cast<size_t>(kPreWarps) * 32 * cam.rest_bases * 3 * sizeof(float);
+    static bool configured = false;
+    if (!configured) {
+        SPLAT_CUDA(cudaFuncSetAttribute(k_preprocess, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        kPreWarps * 32 * kMaxRestBases * 3 * static_cast<int>(sizeof(float))));
+        configured = true;
+    }
+    k_preprocess<<<div_up(n, kPreThreads), kPreThreads, smem, st>>>(P, cam, pb);
+    SPLAT_TRY(check_launch("gs3d_preprocess"));
+    SPLAT_TRY(scan_exclusive_u32(pb.n_touched, pb.offsets, n, pb.counters, pb.scan_ws, pb.scan_bytes, st));
+    if (num_instances)
+        SPLAT_CUDA(cudaMemcpyAsync(num_instances, pb.counters, sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
+    return SPLAT_OK;
+}
+
+int gs3d_render(int n, long long num_instances, const gs3d_settings* settings, void* prim_buf, size_t prim_bytes_,
+                void* tile_buf, size_t tile_bytes_, void* inst_buf, size_t inst_bytes_, void* bucket_buf,
+                size_t bucket_bytes_, long long bucket_capacity, float* image, void* stream) {
+    Cam cam;
+    SPLAT_TRY(fill_cam(settings, cam));
+    const long long m = num_instances;
+    const int T = cam.tiles_x * cam.tiles_y;
+    SPLAT_REQUIRE(n >= 0 && m >= 0 && m < (1ll << 31), "gs3d_render: bad sizes n=%d M=%lld", n, m);
+    SPLAT_REQUIRE(n > 0 || m == 0, "gs3d_render: instances without Gaussians");
+    SPLAT_REQUIRE(prim_bytes_ >= prim_bytes(n) && tile_bytes_ >= tile_bytes(cam.width, cam.height) &&
+                      inst_bytes_ >= inst_bytes(m) && bucket_capacity >= bucket_bound(m, T) &&
+                      bucket_bytes_ >= bucket_bytes(bucket_capacity),
+                  "gs3d_render: a buffer is smaller than its size query");
+    cudaStream_t st = as_stream(stream);
+    Carver cp(prim_buf, prim_bytes_), ct(tile_buf, tile_bytes_), ci(inst_buf, inst_bytes_),
+        cb(bucket_buf, bucket_bytes_);
+    PrimBuffers pb = carve_prim(cp, n);
+    TileBuffers tb = carve_tile(ct, cam.width, cam.height);
+    InstBuffers ib = carve_inst(ci, m);
+    BucketBuffers bb = carve_bucket(cb, bucket_capacity);
+    SPLAT_CUDA(cudaMemsetAsync(tb.ranges, 0, sizeof(uint2) * T, st));
+    if (m > 0) {
+        k_duplicate<<<div_up(n, 256), 256, 0, st>>>(n, cam, pb, ib);
+        SPLAT_TRY(check_launch("gs3d_duplicate"));
+        const int tile_bits = bit_width(static_cast<unsigned long long>(T));
+        SPLAT_TRY(radix_sort_pairs<unsigned long long>(ib.keys, ib.vals, ib.keys_sorted, ib.point_list, m, 0,
+                                                       32 + tile_bits, ib.sort_ws, ib.sort_bytes, st));
+        k_ranges<<<div_up(m, 256), 256, 0, st>>>(ib.keys_sorted, static_cast<int>(m), T, tb.ranges);
+        SPLAT_TRY(check_launch("gs3d_ranges"));
+    }
+    k_bucket_counts<<<div_up(T + 1, 256), 256, 0, st>>>(tb.ranges, T, tb.nb);
+    SPLAT_TRY(check_launch("gs3d_bucket_counts"));
+    SPLAT_TRY(scan_exclusive_u32(tb.nb, tb.bstart, T + 1, pb.counters + 1, tb.scan_ws, tb.scan_bytes, st));
+    k_bucket_tiles<<<div_up(T, 256), 256, 0, st>>>(tb.nb, tb.bstart, T, bucket_capacity, bb.tile);
+    SPLAT_TRY(check_launch("gs3d_bucket_tiles"));
+    k_blend<<<T, kTilePixels, 0, st>>>(cam, tb.ranges, tb.bstart, ib.point_list, pb.mean2d, pb.conic_o, pb.color_z,
+                                       pb.rect, settings->bg, image, tb.final_T, tb.n_contrib, tb.max_contrib, bb.ckpt,
+                                       n < 1 ? 1 : n, static_cast<int>(m), bucket_capacity);
+    return check_launch("gs3d_blend");
+}
+
+}  // extern "C"

@@ -1,0 +1,273 @@
+"""3DGS rasterization over libsplat_b200.so, shaped like the reference's 3DGS boundary.
+
+Faster-GS-compatible (the calls of phase1/tests/test_parity.py:82-98 and cluster/tests/test_lean_adam.py:109-123):
+    image, prim_buf, tile_buf, inst_buf, bucket_buf, n_instances, n_buckets, selector = forward(
+        means, scales, rotations, opacities, sh0, sh_rest, *settings.as_tuple())
+    grads = backward(densification_info, grad_image, image, means, scales, rotations, opacities, sh_rest,
+                     prim_buf, tile_buf, inst_buf, bucket_buf, *settings.as_tuple(), n_instances, n_buckets, selector)
+    image = diff_rasterize(means, scales, rotations, opacities, sh0, sh_rest, densification_info, settings)
+graphdeco-style (requested by the benchmark spec): rasterize_gaussians(means3D, scales, rotations, opacities, shs,
+    viewmatrix, projmatrix, ...) with activated inputs, mapped onto the same kernels.
+
+The rasterization rules are Faster-GS's (alpha = opacity * G with no 0.99 clamp, a pixel stops after the splat that
+drops T below 1e-4, (1 - alpha) floored at 1e-6 in the backward); they are listed in csrc/gs3d_common.cuh.
+One host read per forward (the instance count, to size the instance buffer); the bucket buffer is sized by a bound
+and ``n_buckets`` returns that bound, as phase2/tests/test_readback_equiv.py:100-104 allows.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Any, NamedTuple
+
+import torch
+
+from . import _lib as L
+
+TILE = 16
+
+
+class _Settings(ctypes.Structure):
+    """Mirror of gs3d_settings in include/splat_b200.h."""
+
+    _fields_ = [("w2c", ctypes.c_void_p), ("cam_position", ctypes.c_void_p), ("bg", ctypes.c_void_p),
+                ("active_sh_bases", ctypes.c_int), ("rest_bases", ctypes.c_int), ("width", ctypes.c_int),
+                ("height", ctypes.c_int), ("fx", ctypes.c_float), ("fy", ctypes.c_float), ("cx", ctypes.c_float),
+                ("cy", ctypes.c_float), ("near_plane", ctypes.c_float), ("far_plane", ctypes.c_float),
+                ("proper_antialiasing", ctypes.c_int)]
+
+
+class RasterizerSettings(NamedTuple):
+    """Faster-GS's RasterizerSettings (field names as used in cluster/tests/test_lean_adam.py:119-121)."""
+
+    w2c: torch.Tensor
+    cam_position: torch.Tensor
+    bg_color: torch.Tensor
+    active_sh_bases: int
+    width: int
+    height: int
+    focal_x: float
+    focal_y: float
+    center_x: float
+    center_y: float
+    near_plane: float
+    far_plane: float
+    proper_antialiasing: bool
+
+    def as_tuple(self) -> tuple:
+        return tuple(self)
+
+
+def _settings(dev, w2c, cam_position, bg, active_sh_bases, width, height, fx, fy, cx, cy, near, far, aa, rest_bases,
+              keep: list):
+    w2c = w2c.detach().to(device=dev, dtype=torch.float32).contiguous()
+    cam = cam_position.detach().to(device=dev, dtype=torch.float32).contiguous()
+    bgd = bg.detach().to(device=dev, dtype=torch.float32).contiguous()
+    if w2c.numel() != 16 or cam.numel() != 3 or bgd.numel() != 3:
+        raise RuntimeError("w2c must be [4, 4], cam_position and bg_color [3]")
+    keep += [w2c, cam, bgd]
+    return _Settings(w2c.data_ptr(), cam.data_ptr(), bgd.data_ptr(), int(active_sh_bases), int(rest_bases),
+                     int(width), int(height), float(fx), float(fy), float(cx), float(cy), float(near), float(far),
+                     int(bool(aa)))
+
+
+def _check_params(means, scales, rotations, opacities, sh0, sh_rest):
+    n = means.shape[0]
+    shapes = {"means": (means, (n, 3)), "scales": (scales, (n, 3)), "rotations": (rotations, (n, 4))}
+    for name, (t, shp) in shapes.items():
+        L.check_cuda(name, t, torch.float32)
+        if tuple(t.shape) != shp:
+            raise RuntimeError(f"{name} must be {list(shp)}, got {list(t.shape)}")
+    for name, t in (("opacities", opacities), ("sh0", sh0), ("sh_rest", sh_rest)):
+        L.check_cuda(name, t, torch.float32)
+    if opacities.numel() != n:
+        raise RuntimeError("opacities must hold N values")
+    if sh0.numel() != 3 * n:
+        raise RuntimeError("sh0 must be [N, 1, 3]")
+    if sh_rest.numel() % (3 * max(n, 1)) != 0 or (n and sh_rest.shape[0] != n):
+        raise RuntimeError("sh_rest must be [N, rest_bases, 3]")
+    return n, (sh_rest.numel() // (3 * n) if n else 0)
+
+
+@torch.no_grad()
+def forward(means, scales, rotations, opacities, sh0, sh_rest, w2c, cam_position, bg_color, active_sh_bases, width,
+            height, focal_x, focal_y, center_x, center_y, near_plane, far_plane, proper_antialiasing):
+    """Faster-GS `_C.forward`: (image[3,H,W], prim_buf, tile_buf, inst_buf, bucket_buf, n_instances, n_buckets, 0)."""
+    n, rest = _check_params(means, scales, rotations, opacities, sh0, sh_rest)
+    dev = means.device
+    keep: list = []
+    s = _settings(dev, w2c, cam_position, bg_color, active_sh_bases, width, height, focal_x, focal_y, center_x,
+                  center_y, near_plane, far_plane, proper_antialiasing, rest, keep)
+    stream = L.stream_of(means)
+    prim = torch.empty(L.query("gs3d_primitive_buffer_size", n), dtype=torch.uint8, device=dev)
+    tile = torch.empty(L.query("gs3d_tile_buffer_size", width, height), dtype=torch.uint8, device=dev)
+    count = torch.zeros(1, dtype=torch.int32, device=dev)
+    L.call("gs3d_preprocess", L.ptr(means), L.ptr(scales), L.ptr(rotations), L.ptr(opacities), L.ptr(sh0),
+           L.ptr(sh_rest), n, ctypes.byref(s), L.ptr(prim), prim.numel(), L.ptr(count), stream)
+    m = int(count.item())  # the one host read of a forward
+    bcap = int(L.load().gs3d_bucket_bound(m, width, height))
+    inst = torch.empty(L.query("gs3d_instance_buffer_size", m), dtype=torch.uint8, device=dev)
+    bucket = torch.empty(L.query("gs3d_bucket_buffer_size", bcap), dtype=torch.uint8, device=dev)
+    image = torch.empty(3, height, width, dtype=torch.float32, device=dev)
+    L.call("gs3d_render", n, m, ctypes.byref(s), L.ptr(prim), prim.numel(), L.ptr(tile), tile.numel(), L.ptr(inst),
+           inst.numel(), L.ptr(bucket), bucket.numel(), bcap, L.ptr(image), stream)
+    return image, prim, tile, inst, bucket, m, bcap, 0
+
+
+@torch.no_grad()
+def backward(densification_info, grad_image, image, means, scales, rotations, opacities, sh_rest, prim_buf,
+             tile_buf, inst_buf, bucket_buf, w2c, cam_position, bg_color, active_sh_bases, width, height, focal_x,
+             focal_y, center_x, center_y, near_plane, far_plane, proper_antialiasing, n_instances, n_buckets,
+             selector, *mode):
+    """Faster-GS `_C.backward` (the trailing blend-backward mode of the phase1 patch is accepted and ignored:
+    there is one blend backward here). Returns (means, scales, rotations, opacities[N,1], sh0[N,1,3], sh_rest)."""
+    n = means.shape[0]
+    rest = sh_rest.shape[1] if sh_rest.dim() == 3 else 0
+    dev = means.device
+    keep: list = []
+    s = _settings(dev, w2c, cam_position, bg_color, active_sh_bases, width, height, focal_x, focal_y, center_x,
+                  center_y, near_plane, far_plane, proper_antialiasing, rest, keep)
+    g_img = grad_image.detach().to(torch.float32).contiguous()
+    ws = torch.empty(L.query("gs3d_backward_workspace_size", n), dtype=torch.uint8, device=dev)
+    grads = (torch.empty(n, 3, device=dev), torch.empty(n, 3, device=dev), torch.empty(n, 4, device=dev),
+             torch.empty(n, 1, device=dev), torch.empty(n, 1, 3, device=dev), torch.empty(n, rest, 3, device=dev))
+    L.call("gs3d_backward", L.ptr(g_img), L.ptr(image), L.ptr(means), L.ptr(scales), L.ptr(rotations),
+           L.ptr(opacities), L.ptr(sh_rest), n, int(n_instances), ctypes.byref(s), L.ptr(prim_buf), prim_buf.numel(),
+           L.ptr(tile_buf), tile_buf.numel(), L.ptr(inst_buf), inst_buf.numel(), L.ptr(bucket_buf), bucket_buf.numel(),
+           int(n_buckets), L.ptr(ws), ws.numel(), *map(L.ptr, grads), L.stream_of(means))
+    return grads
+
+
+class _Rasterize(torch.autograd.Function):
+    """The autograd function behind diff_rasterize (phase1/fastergs_macro.patch:565-594 shows its backward)."""
+
+    @staticmethod
+    def forward(ctx: Any, means, scales, rotations, opacities, sh0, sh_rest, densification_info,
+                settings: RasterizerSettings):
+        params = [t.contiguous() for t in (means, scales, rotations, opacities, sh0, sh_rest)]
+        image, prim, tile, inst, bucket, m, nb, sel = forward(*params, *settings.as_tuple())
+        ctx.settings = settings
+        ctx.buffer_state = (m, nb, sel)
+        ctx.densification_info = densification_info
+        ctx.shapes = (opacities.shape, sh0.shape, sh_rest.shape)
+        ctx.save_for_backward(image, params[0], params[1], params[2], params[3], params[5], prim, tile, inst, bucket)
+        return image
+
+    @staticmethod
+    def backward(ctx: Any, grad_image):
+        image, means, scales, rotations, opacities, sh_rest, prim, tile, inst, bucket = ctx.saved_tensors
+        g = backward(ctx.densification_info, grad_image, image, means, scales, rotations, opacities, sh_rest, prim,
+                     tile, inst, bucket, *ctx.settings.as_tuple(), *ctx.buffer_state)
+        op_shape, sh0_shape, rest_shape = ctx.shapes
+        return (g[0], g[1], g[2], g[3].reshape(op_shape), g[4].reshape(sh0_shape), g[5].reshape(rest_shape), None,
+                None)
+
+
+def diff_rasterize(means, scales, rotations, opacities, sh0, sh_rest, densification_info,
+                   settings: RasterizerSettings) -> torch.Tensor:
+    """Differentiable render of one view: image [3, H, W]."""
+    return _Rasterize.apply(means, scales, rotations, opacities, sh0, sh_rest, densification_info, settings)
+
+
+def rasterize_gaussians(means3D, scales, rotations, opacities, shs, viewmatrix, projmatrix, bg, tanfovx, tanfovy,
+                        image_height, image_width, sh_degree, campos, scale_modifier=1.0, near_plane=0.2,
+                        far_plane=1000.0):
+    """graphdeco-style entry: activated inputs (scales > 0, opacities in (0, 1), any quaternions, shs [N, K, 3]);
+    viewmatrix is the transposed world-to-view matrix as graphdeco passes it (p_view = p_h @ viewmatrix).
+    projmatrix is accepted for signature compatibility; the pinhole model uses tanfovx / tanfovy.
+    Returns (image [3, H, W], radii int32 [N]: half the culling rectangle's larger side, 0 = not visible)."""
+    W, H = int(image_width), int(image_height)
+    fx = W / (2.0 * float(tanfovx))
+    fy = H / (2.0 * float(tanfovy))
+    w2c = viewmatrix.transpose(0, 1).contiguous()
+    bases = (int(sh_degree) + 1) ** 2
+    settings = RasterizerSettings(w2c, campos, bg, bases, W, H, fx, fy, W / 2.0, H / 2.0, near_plane, far_plane,
+                                  False)
+    log_scales = torch.log(scales * scale_modifier)
+    logits = torch.logit(opacities.reshape(-1, 1).clamp(1e-7, 1 - 1e-7))
+    sh0, sh_rest = shs[:, :1].contiguous(), shs[:, 1:].contiguous()
+    image = diff_rasterize(means3D, log_scales, rotations, logits, sh0, sh_rest, torch.empty(0), settings)
+    with torch.no_grad():
+        prim = _last_visibility(means3D, log_scales, rotations, logits, sh0, sh_rest, settings)
+    return image, prim
+
+
+@torch.no_grad()
+def _last_visibility(means, scales, rotations, opacities, sh0, sh_rest, settings):
+    """Per-Gaussian screen radius from a preprocess pass (rasterize_gaussians' second output)."""
+    n, rest = _check_params(means.contiguous(), scales.contiguous(), rotations.contiguous(), opacities.contiguous(),
+                            sh0, sh_rest)
+    dev = means.device
+    keep: list = []
+    s = _settings(dev, *settings.as_tuple()[:3], settings.active_sh_bases, settings.width, settings.height,
+                  settings.focal_x, settings.focal_y, settings.center_x, settings.center_y, settings.near_plane,
+                  settings.far_plane, settings.proper_antialiasing, rest, keep)
+    prim = torch.empty(L.query("gs3d_primitive_buffer_size", n), dtype=torch.uint8, device=dev)
+    L.call("gs3d_preprocess", L.ptr(means.contiguous()), L.ptr(scales.contiguous()), L.ptr(rotations.contiguous()),
+           L.ptr(opacities.contiguous()), L.ptr(sh0), L.ptr(sh_rest), n, ctypes.byref(s), L.ptr(prim), prim.numel(),
+           None, L.stream_of(means))
+    v = primitive_views(prim, n)
+    r = v["rect"].to(torch.int32)
+    radii = torch.maximum(r[:, 2] - r[:, 0], r[:, 3] - r[:, 1]).div(2, rounding_mode="floor") + 1
+    return torch.where(v["n_touched"] > 0, radii, torch.zeros_like(radii))
+
+
+def _align(x: int) -> int:
+    return (x + 255) & ~255
+
+
+def primitive_views(prim_buf: torch.Tensor, n: int) -> dict[str, torch.Tensor]:
+    """Typed views into a primitive buffer (the layout of carve_prim in csrc/gs3d_common.cuh):
+    mean2d [N,2], conic_o [N,4] (A, B, C, opacity), color_z [N,4] (r, g, b, depth), rect [N,4] (int16 pixels),
+    thr [N], n_touched [N] (int32), offsets [N]. Valid for Gaussians with n_touched > 0."""
+    nn = max(n, 1)
+    off = 0
+    out = {}
+    for name, elem, width, dtype in (("mean2d", 8, 2, torch.float32), ("conic_o", 16, 4, torch.float32),
+                                     ("color_z", 16, 4, torch.float32), ("rect", 8, 4, torch.int16),
+                                     ("thr", 4, 1, torch.float32), ("n_touched", 4, 1, torch.int32),
+                                     ("offsets", 4, 1, torch.int32)):
+        off = _align(off)
+        t = prim_buf[off:off + elem * nn].view(dtype)
+        out[name] = t.view(nn, width)[:n] if width > 1 else t[:n]
+        off += elem * nn
+    out["rect"] = out["rect"].to(torch.int32) & 0xFFFF
+    return out
+
+
+def n_touched_tiles(prim_buf: torch.Tensor, n: int) -> torch.Tensor:
+    """Faster-GS `_C.n_touched_tiles` (cluster/patches/fastergs_lean_adam.patch:316-323): int32 [N], > 0 = visible."""
+    return primitive_views(prim_buf, n)["n_touched"].clone()
+
+
+def tile_views(tile_buf: torch.Tensor, width: int, height: int) -> dict[str, torch.Tensor]:
+    """ranges [T,2], buckets per tile [T+1], first bucket [T+1], max_contrib [T], final_T [H,W], n_contrib [H,W]."""
+    T = ((width + TILE - 1) // TILE) * ((height + TILE - 1) // TILE)
+    off = 0
+    out = {}
+    for name, count, dtype, shape in (("ranges", 2 * T, torch.int32, (T, 2)), ("nb", T + 1, torch.int32, (T + 1,)),
+                                      ("bstart", T + 1, torch.int32, (T + 1,)),
+                                      ("max_contrib", T, torch.int32, (T,)),
+                                      ("final_T", width * height, torch.float32, (height, width)),
+                                      ("n_contrib", width * height, torch.int32, (height, width))):
+        off = _align(off)
+        out[name] = tile_buf[off:off + 4 * count].view(dtype).view(shape)
+        off += 4 * count
+    return out
+
+
+def instance_views(inst_buf: torch.Tensor, m: int) -> dict[str, torch.Tensor]:
+    """keys (unsorted), vals, keys_sorted [M] (int64 views of the uint64 keys), point_list [M] (int32)."""
+    mm = max(m, 1)
+    off = 0
+    out = {}
+    for name, elem, dtype in (("keys", 8, torch.int64), ("vals", 4, torch.int32), ("keys_sorted", 8, torch.int64),
+                              ("point_list", 4, torch.int32)):
+        off = _align(off)
+        out[name] = inst_buf[off:off + elem * mm].view(dtype)[:m]
+        off += elem * mm
+    return out
+
+
+def focal_from_fov(fov_y_deg: float, height: int) -> float:
+    return 0.5 * height / math.tan(math.radians(fov_y_deg) / 2.0)

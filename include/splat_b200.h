@@ -136,6 +136,60 @@ int splat2d_set_counting(int on);
 int splat2d_reset_counters(void);
 int splat2d_get_counters(long long* out3);
 
+/* ---------------------------------------------------------------------------------------------
+ * gs3d: 3DGS rasterization, the Faster-GS `_C.forward` / `_C.backward` pair
+ * (phase1/tests/test_parity.py:82-98 shows the calls; phase1/fastergs_macro.patch:403-452 and
+ * upstream/upstream_main_kernels.patch:228-252 the backward's outputs). Parameters: means f32[N,3],
+ * scales f32[N,3] (log), rotations f32[N,4] (w,x,y,z), opacities f32[N] (logits), sh0 f32[N,3],
+ * sh_rest f32[N,rest_bases,3]. The four opaque buffers mirror Faster-GS's primitive / tile / instance /
+ * bucket byte blobs; each is caller-allocated from its size query.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct gs3d_settings {
+    const float* w2c;          /* device f32[4,4], row-major world-to-camera */
+    const float* cam_position; /* device f32[3] */
+    const float* bg;           /* device f32[3] background colour */
+    int active_sh_bases;       /* 1, 4, 9 or 16 */
+    int rest_bases;            /* sh_rest.shape[1] (15 for degree 3) */
+    int width;
+    int height;
+    float fx;
+    float fy;
+    float cx;
+    float cy;
+    float near_plane;
+    float far_plane;
+    int proper_antialiasing;
+} gs3d_settings;
+
+size_t gs3d_primitive_buffer_size(int n);
+size_t gs3d_tile_buffer_size(int width, int height);
+size_t gs3d_instance_buffer_size(long long num_instances);
+/* Upper bound on the bucket count, floor((M + 31 T) / 32) + 1 (the bound of
+ * phase2/tests/test_readback_equiv.py:100, for 16x16 tiles): sizes the bucket buffer without a host read. */
+long long gs3d_bucket_bound(long long num_instances, int width, int height);
+size_t gs3d_bucket_buffer_size(long long bucket_capacity);
+size_t gs3d_backward_workspace_size(int n);
+/* Forward, phase 1: projection, SH colour, conic, culling rectangle, exact listed-tile count and depth
+ * per Gaussian, and the instance count M (device u32 *num_instances, may be NULL). */
+int gs3d_preprocess(const float* means, const float* scales, const float* rotations, const float* opacities,
+                    const float* sh0, const float* sh_rest, int n, const gs3d_settings* settings, void* prim_buf,
+                    size_t prim_bytes, uint32_t* num_instances, void* stream);
+/* Forward, phase 2 (M read back by the host): duplication, 64-bit (tile | depth) key sort, tile ranges,
+ * buckets, blend. image f32[3,H,W]; per-pixel final T and contributor counts stay in tile_buf. */
+int gs3d_render(int n, long long num_instances, const gs3d_settings* settings, void* prim_buf, size_t prim_bytes,
+                void* tile_buf, size_t tile_bytes, void* inst_buf, size_t inst_bytes, void* bucket_buf,
+                size_t bucket_bytes, long long bucket_capacity, float* image, void* stream);
+/* Backward: grad_image f32[3,H,W] -> grad_means f32[N,3], grad_scales f32[N,3], grad_rotations f32[N,4],
+ * grad_opacities f32[N], grad_sh0 f32[N,3], grad_sh_rest f32[N,rest_bases,3] (zeros for Gaussians that
+ * were not visible). The bucket count is read on the device, so no host sync happens. */
+int gs3d_backward(const float* grad_image, const float* image, const float* means, const float* scales,
+                  const float* rotations, const float* opacities, const float* sh_rest, int n, long long num_instances,
+                  const gs3d_settings* settings, void* prim_buf, size_t prim_bytes, void* tile_buf,
+                  size_t tile_bytes, void* inst_buf, size_t inst_bytes, void* bucket_buf, size_t bucket_bytes,
+                  long long bucket_capacity, void* workspace, size_t workspace_bytes, float* grad_means,
+                  float* grad_scales, float* grad_rotations, float* grad_opacities, float* grad_sh0,
+                  float* grad_sh_rest, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -76,5 +76,7 @@ def test_ctypes_signatures_match_the_header():
             assert res == ctypes.c_char_p, name
         elif "size_t" in ret:
             assert res == ctypes.c_size_t, name
+        elif "long long" in ret:
+            assert res == ctypes.c_longlong, name
         else:
             assert res == ctypes.c_int, name
