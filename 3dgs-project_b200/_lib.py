@@ -51,6 +51,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gs3d_preprocess": (_I, [_P] * 6 + [_I, _P, _P, _SZ, _P, _P]),
     "gs3d_render": (_I, [_I, _LL, _P, _P, _SZ, _P, _SZ, _P, _SZ, _P, _SZ, _LL, _P, _P]),
     "gs3d_backward": (_I, [_P] * 7 + [_I, _LL, _P] + [_P, _SZ] * 4 + [_LL, _P, _SZ] + [_P] * 7),
+    "adam_step_multi": (_I, [_I, _P, _I, ctypes.c_float, ctypes.c_float, ctypes.c_float, _P]),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -411,10 +411,11 @@ __global__ void __launch_bounds__(kPbThreads) k_preprocess_backward(PParams P, C
         float gyc = cam.fy * inv_z * gm.y;
         float gzc = -cam.fx * xc * iz2 * gm.x - cam.fy * yc * iz2 * gm.y;
         gzc += -cam.fx * iz2 * gJ[0][0] - cam.fy * iz2 * gJ[1][1];
-        // j02 = -fx tx / z with tx = x / z inside the clamp window, constant outside
-        gzc += gJ[0][2] * (cam.fx * tx * iz2 + (free_x ? -cam.fx * inv_z * xc * iz2 : 0.f));
+        // j02 = -fx tx / z with tx = x / z inside the clamp window (dtx/dz = -x / z^2), constant outside:
+        // dj02/dz = fx tx / z^2 - (fx / z) dtx/dz, dj02/dx = -(fx / z) dtx/dx
+        gzc += gJ[0][2] * (cam.fx * tx * iz2 + (free_x ? cam.fx * inv_z * xc * iz2 : 0.f));
         gxc += free_x ? gJ[0][2] * (-cam.fx * iz2) : 0.f;
-        gzc += gJ[1][2] * (cam.fy * ty * iz2 + (free_y ? -cam.fy * inv_z * yc * iz2 : 0.f));
+        gzc += gJ[1][2] * (cam.fy * ty * iz2 + (free_y ? cam.fy * inv_z * yc * iz2 : 0.f));
         gyc += free_y ? gJ[1][2] * (-cam.fy * iz2) : 0.f;
         gpx += w2c[0] * gxc + w2c[4] * gyc + w2c[8] * gzc;
         gpy += w2c[1] * gxc + w2c[5] * gyc + w2c[9] * gzc;

@@ -118,9 +118,10 @@ def forward(means, scales, rotations, opacities, sh0, sh_rest, w2c, cam_position
 def backward(densification_info, grad_image, image, means, scales, rotations, opacities, sh_rest, prim_buf,
              tile_buf, inst_buf, bucket_buf, w2c, cam_position, bg_color, active_sh_bases, width, height, focal_x,
              focal_y, center_x, center_y, near_plane, far_plane, proper_antialiasing, n_instances, n_buckets,
-             selector, *mode):
+             selector, *mode, out: tuple | None = None):
     """Faster-GS `_C.backward` (the trailing blend-backward mode of the phase1 patch is accepted and ignored:
-    there is one blend backward here). Returns (means, scales, rotations, opacities[N,1], sh0[N,1,3], sh_rest)."""
+    there is one blend backward here). Returns (means, scales, rotations, opacities[N,1], sh0[N,1,3], sh_rest).
+    ``out`` may supply the six contiguous float32 result tensors (e.g. views of one flat gradient buffer)."""
     n = means.shape[0]
     rest = sh_rest.shape[1] if sh_rest.dim() == 3 else 0
     dev = means.device
@@ -129,8 +130,15 @@ def backward(densification_info, grad_image, image, means, scales, rotations, op
                   center_y, near_plane, far_plane, proper_antialiasing, rest, keep)
     g_img = grad_image.detach().to(torch.float32).contiguous()
     ws = torch.empty(L.query("gs3d_backward_workspace_size", n), dtype=torch.uint8, device=dev)
-    grads = (torch.empty(n, 3, device=dev), torch.empty(n, 3, device=dev), torch.empty(n, 4, device=dev),
-             torch.empty(n, 1, device=dev), torch.empty(n, 1, 3, device=dev), torch.empty(n, rest, 3, device=dev))
+    if out is not None:
+        grads = tuple(out)
+        for t, numel in zip(grads, (3 * n, 3 * n, 4 * n, n, 3 * n, 3 * rest * n)):
+            L.check_cuda("out", t, torch.float32)
+            if t.numel() != numel:
+                raise RuntimeError("out tensors must match the parameter shapes")
+    else:
+        grads = (torch.empty(n, 3, device=dev), torch.empty(n, 3, device=dev), torch.empty(n, 4, device=dev),
+                 torch.empty(n, 1, device=dev), torch.empty(n, 1, 3, device=dev), torch.empty(n, rest, 3, device=dev))
     L.call("gs3d_backward", L.ptr(g_img), L.ptr(image), L.ptr(means), L.ptr(scales), L.ptr(rotations),
            L.ptr(opacities), L.ptr(sh_rest), n, int(n_instances), ctypes.byref(s), L.ptr(prim_buf), prim_buf.numel(),
            L.ptr(tile_buf), tile_buf.numel(), L.ptr(inst_buf), inst_buf.numel(), L.ptr(bucket_buf), bucket_buf.numel(),

@@ -1,0 +1,351 @@
+"""Benchmark of the 3DGS training step on B200, one process per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c3|c4|c2]
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \
+        bench.py --gpus N --steps K --warmup W
+
+Workload (default c3): the scene of config C3 - 3M Gaussians from 64 isotropic clusters, SH degree 3, seeded
+synthetic parameters (no dataset is available) - rendered at 1920x1080 / 60 deg. One step on each rank is the
+training step of one view: forward, backward with dL/dimage ~ N(0, 1e-3), (N > 1: one NCCL all-reduce of the flat
+59-float-per-Gaussian gradient), fused Adam over the six parameter groups. Each rank renders its own view (a
+seeded camera at radius 12), so the work per GPU is fixed as N grows (weak scaling) and
+    value = N * K / (max over ranks of the device time of K steps)  [views/s],  ms_per_step = that time / K.
+The Gaussian state (2.8 GB with moments) is far larger than the 126 MB L2, so no flush is needed between steps.
+``e2e`` runs the same step through the public API (diff_rasterize + autograd + FusedAdam) with the upstream
+gradient copied from pinned host memory every step and the loss read back.
+
+--impl reference times the CPU restatement of the same step (oracle/liboracle.so, OpenMP over all host cores)
+on rank 0 only, over a bounded sample (a horizontal band of the image), and reports the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+from __graft_entry__ import load_package  # noqa: E402
+
+load_package()
+from gs_b200 import adam as gs_adam  # noqa: E402
+from gs_b200 import gs3d, scenes  # noqa: E402
+
+METRIC = "fwd+bwd ms/iter (3M Gaussians, 1080p, SH3); train views/s at 1/2/4/8 B200"
+LRS = {"means": 1.6e-4, "scales": 5e-3, "rotations": 1e-3, "opacities": 5e-2, "sh0": 2.5e-3, "sh_rest": 2.5e-3}
+NAMES = ("means", "scales", "rotations", "opacities", "sh0", "sh_rest")
+WIDTHS = (3, 3, 4, 1, 3, 45)  # floats per Gaussian in each group: 59 in total
+
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.rows = []
+        if self.proc is None:
+            return False
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        for line in out.splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+        return False
+
+    def summary(self) -> dict:
+        rows = getattr(self, "rows", [])
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        for r in rows:
+            for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def setup_dist(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def scene_for(workload: str, rank: int, world: int):
+    if workload == "c3":
+        sc = scenes.gs3d_config("c3", seed=0)
+        if rank > 0:  # another seeded view at the same radius
+            g = torch.Generator().manual_seed(5000 + rank)
+            d = torch.randn(3, generator=g)
+            d = d / d.norm() * 12.0
+            sc["cameras"] = [scenes.camera(1920, 1080, tuple(d.tolist()))]
+        return sc, sc["cameras"][:1]
+    if workload == "c4":
+        sc = scenes.gs3d_config("c4", seed=0)
+        cams = sc["cameras"]
+        return sc, [cams[k] for k in range(rank, len(cams), world)]
+    if workload == "c2":
+        sc = scenes.gs3d_config("c2", seed=0)
+        return sc, sc["cameras"]
+    raise ValueError(workload)
+
+
+class Trainer:
+    """Replicated Gaussians, flat gradient buffer, Adam state; one training step per call."""
+
+    def __init__(self, sc: dict, dev, world: int):
+        self.dev = dev
+        self.world = world
+        self.params = [sc[k].to(dev).contiguous() for k in NAMES]
+        self.bases = sc["active_sh_bases"]
+        n = self.params[0].shape[0]
+        self.n = n
+        self.flat = torch.zeros(59 * n, device=dev)
+        self.grads, off = [], 0
+        for p, w in zip(self.params, WIDTHS):
+            self.grads.append(self.flat[off:off + w * n].view(p.shape))
+            off += w * n
+        self.m = [torch.zeros_like(p) for p in self.params]
+        self.v = [torch.zeros_like(p) for p in self.params]
+        self.t = 0
+        self.ev = {k: [] for k in ("fwd", "bwd", "comm", "adam")}
+
+    def step(self, cam: dict, dout: torch.Tensor, timed: bool):
+        s = scenes.settings_tuple(cam, self.bases, self.dev)
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(5)] if timed else None
+        if timed:
+            e[0].record()
+        image, prim, tile, inst, bucket, m, nb, sel = gs3d.forward(*self.params, *s)
+        if timed:
+            e[1].record()
+        gs3d.backward(None, dout, image, self.params[0], self.params[1], self.params[2], self.params[3],
+                      self.params[5], prim, tile, inst, bucket, *s, m, nb, sel, out=self.grads)
+        if timed:
+            e[2].record()
+        if self.world > 1:
+            torch.distributed.all_reduce(self.flat)
+        if timed:
+            e[3].record()
+        self.t += 1
+        gs_adam.adam_step([(p, g, mm, vv, LRS[nm]) for p, g, mm, vv, nm in
+                           zip(self.params, self.grads, self.m, self.v, NAMES)], self.t, eps=1e-15)
+        if timed:
+            e[4].record()
+            for k, (a, b) in zip(("fwd", "bwd", "comm", "adam"), zip(e[:-1], e[1:])):
+                self.ev[k].append((a, b))
+        return m
+
+
+def run_ours(args) -> None:
+    world, rank, local = setup_dist(args.gpus)
+    dev = torch.device("cuda", local)
+    sc, cams = scene_for(args.workload, rank, world)
+    cam = cams[0]
+    tr = Trainer(sc, dev, world)
+    g = torch.Generator().manual_seed(77 + rank)
+    H, W = cam["height"], cam["width"]
+    dout = (1e-3 * torch.randn(3, H, W, generator=g)).to(dev)
+    views_per_step = len(cams)
+
+    def one_step(timed):
+        insts = []
+        for c in cams:
+            insts.append(tr.step(c, dout, timed))
+        return insts
+
+    for _ in range(args.warmup):
+        one_step(False)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        t0 = time.perf_counter()
+        start.record()
+        insts = []
+        for _ in range(args.steps):
+            insts += one_step(True)
+        end.record()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+    if world > 1:
+        torch.distributed.barrier()
+    ms = start.elapsed_time(end)
+    ms_t = torch.tensor([ms], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    stage = {k: sum(a.elapsed_time(b) for a, b in v) / max(len(v), 1) for k, v in tr.ev.items()}
+
+    # end to end through the public API: pinned host upstream gradient in, loss out, every step
+    e2e = run_e2e(sc, cams, dev, world, args, tr)
+
+    if rank == 0:
+        value = world * views_per_step * args.steps / (ms_max / 1000.0)
+        n = tr.n
+        m_avg = float(np.mean(insts)) if insts else 0.0
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "views/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config-shaped)",
+            "config": {"workload": f"{args.workload}: 3DGS training step of one {W}x{H} view per GPU per step, "
+                                   f"{n} Gaussians, SH3; fwd + bwd + grad all-reduce (N>1) + fused Adam",
+                       "gaussians": n, "width": W, "height": H, "views_per_gpu_per_step": views_per_step,
+                       "instances_per_view": round(m_avg), "l2": "state (2.8 GB) larger than L2; no flush",
+                       "parallelism": f"dp{world} (views)"},
+            "stage_ms": {k: round(v, 4) for k, v in stage.items()},
+            "fwd_bwd_ms": round(stage["fwd"] + stage["bwd"], 4),
+            "wall_s": round(wall, 3),
+            "clocks": clk.summary(),
+            "e2e": e2e,
+            "gpu_launches": None,
+        }
+        line.update(roofline_and_counts(args, tr, stage, m_avg))
+        line["cpu_baseline"] = cpu_baseline(args, sc, cam) if not args.no_cpu_baseline else None
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
+    leaves = [p.clone().requires_grad_(True) for p in tr.params]
+    opt = gs_adam.FusedAdam([{"params": [p], "lr": LRS[nm]} for p, nm in zip(leaves, NAMES)], lr=0.0, eps=1e-15)
+    cam = cams[0]
+    H, W = cam["height"], cam["width"]
+    host = (1e-3 * torch.randn(3, H, W, generator=torch.Generator().manual_seed(99))).pin_memory()
+    settings = gs3d.RasterizerSettings(*scenes.settings_tuple(cam, tr.bases, dev))
+    flat_grads = None
+
+    def step():
+        dout = host.to(dev, non_blocking=True)
+        img = gs3d.diff_rasterize(*leaves, torch.empty(0), settings)
+        loss = (img * dout).sum()
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        if world > 1:
+            for p in leaves:
+                torch.distributed.all_reduce(p.grad)
+        opt.step()
+        return loss.detach().to("cpu", non_blocking=False)
+
+    for _ in range(max(1, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([a.elapsed_time(b)], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+    del flat_grads
+    return {"value": round(world * args.steps / (float(ms.item()) / 1000.0), 3), "unit": "views/s",
+            "h2d_bytes_per_step": int(host.numel() * 4), "d2h_bytes_per_step": 4}
+
+
+def roofline_and_counts(args, tr: Trainer, stage: dict, m_avg: float) -> dict:
+    """Filled in from the per-stage times; the dominant stage's algorithmic bytes per launch over its time."""
+    peaks_path = ROOT / "MEASURED_PEAKS.json"
+    hbm = None
+    src = "fallback"
+    if peaks_path.exists():
+        hbm = json.loads(peaks_path.read_text()).get("hbm_gbs")
+        src = "measured"
+    if hbm is None:
+        hbm = 6650.0
+    n = tr.n
+    bwd_bytes = 236.0 * n + 250.0 * n  # preprocess backward dominates the backward's DRAM traffic
+    ach = bwd_bytes / (stage["bwd"] / 1000.0) / 1e9 if stage["bwd"] > 0 else 0.0
+    return {"roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(ach / hbm, 4), "traffic": None, "kernel": "backward (blend + preprocess)",
+                         "peak_source": src}}
+
+
+def cpu_baseline(args, sc, cam):
+    try:
+        from oracle import gs3d_cpu
+    except Exception as exc:  # the C restatement is built by __graft_entry__.build()
+        return {"value": None, "unit": "views/s", "cores": os.cpu_count(), "kind": "port",
+                "sample": f"unavailable: {exc}"}
+    return gs3d_cpu.time_training_step(sc, cam, budget_s=args.cpu_budget)
+
+
+def run_reference(args) -> None:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    sc, cams = scene_for(args.workload, 0, 1)
+    res = cpu_baseline(args, sc, cams[0])
+    value = res.get("value")
+    line = {"metric": METRIC, "value": value, "unit": "views/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": (1000.0 / value) if value else None, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config-shaped)",
+            "config": {"workload": f"{args.workload}: CPU restatement of the 3DGS training step on a bounded sample",
+                       "parallelism": "host threads"},
+            "impl": "reference", "cpu_baseline": res,
+            "e2e": {"value": value, "unit": "views/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["c3", "c4", "c2"], default="c3")
+    ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for the baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -190,6 +190,23 @@ int gs3d_backward(const float* grad_image, const float* image, const float* mean
                   float* grad_scales, float* grad_rotations, float* grad_opacities, float* grad_sh0,
                   float* grad_sh_rest, void* stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * Fused Adam (replaces the per-group `_C.adam_step` launches of Faster-GS's FusedAdam,
+ * cluster/patches/fastergs_lean_adam.patch:251-307, with one launch over every group).
+ * ------------------------------------------------------------------------------------------- */
+#define SPLAT_ADAM_MAX_GROUPS 8
+typedef struct adam_group {
+    float* param;          /* device f32[n], updated in place */
+    const float* grad;     /* device f32[n] */
+    float* exp_avg;        /* device f32[n] first moment */
+    float* exp_avg_sq;     /* device f32[n] second moment */
+    long long n;
+    float lr;
+} adam_group;
+/* One Adam step (step = t >= 1) over `count` groups (host array, at most SPLAT_ADAM_MAX_GROUPS). */
+int adam_step_multi(int count, const adam_group* groups, int step, float beta1, float beta2, float eps,
+                    void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif
