@@ -60,4 +60,6 @@ def test_fused_adam_optimizer_matches_torch_adam(cuda):
     assert sa.keys() == sb.keys()
     for k in sa:
         assert set(sa[k]) == set(sb[k])
-        assert torch.allclose(sa[k]["exp_avg_sq"], sb[k]["exp_avg_sq"], rtol=1e-5, atol=1e-12)
+        # the reference's fmaf(beta2, v - g^2, g^2) weighs g^2 by 1 - float(0.999), torch by float(1 - 0.999):
+        # 1.3e-5 apart
+        assert torch.allclose(sa[k]["exp_avg_sq"], sb[k]["exp_avg_sq"], rtol=5e-5, atol=1e-12)
