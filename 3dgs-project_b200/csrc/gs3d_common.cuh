@@ -17,7 +17,7 @@
 //     alpha = opacity G; skipped if alpha < 1/255; C += T alpha c; T *= 1 - alpha; the pixel
 //     stops after the splat that drops T below 1e-4; image = C + T bg
 //   * a Gaussian is listed in a 16x16 tile iff the ellipse alpha >= 1/255 (q <= 2 ln(255 opacity))
-//     meets the tile's pixel-centre rectangle (exact rectangle minimum of the quadratic form)
+//     meets the tile's pixel-centre rectangle (closed-form x-extent per tile row, below)
 //   * tile lists are ordered by the 64-bit key (tile << 32 | float bits of z), ties by Gaussian index
 #pragma once
 
@@ -72,10 +72,16 @@ struct PrimBuffers {
     ushort4* rect;         // culling rectangle in pixels (x0, y0, x1, y1), inclusive, with margin
     float* thr;            // ln(255 opacity): the ellipse q <= 2 thr holds every alpha >= 1/255
     uint32_t* n_touched;   // listed tiles (0 = not visible)
-    uint32_t* offsets;     // exclusive prefix of n_touched
+    uint32_t* depth_key;   // float bits of z (visible), 0xffffffff (not visible)
+    uint32_t* ids;         // 0..N-1
+    uint32_t* depth_key_sorted;
+    uint32_t* order;       // Gaussian ids in (depth, id) order: the depth passes of the 64-bit key sort
+    uint32_t* offsets;     // exclusive prefix of n_touched, in that order
     uint32_t* counters;    // [0] = instance count M, [1] = bucket count B
     void* scan_ws;
     size_t scan_bytes;
+    void* sort_ws;
+    size_t sort_bytes;
 };
 
 // Per-tile and per-pixel buffer, sized by the image
@@ -90,12 +96,13 @@ struct TileBuffers {
     size_t scan_bytes;
 };
 
-// Per-instance buffer, sized by M
+// Per-instance buffer, sized by M. Instances are written in depth order, so a stable sort on the tile
+// alone finishes the LSD sort of the 64-bit (tile << 32 | depth) keys.
 struct InstBuffers {
-    unsigned long long* keys;
-    uint32_t* vals;
-    unsigned long long* keys_sorted;
-    uint32_t* point_list;  // sorted Gaussian ids
+    uint32_t* keys;         // tile index, generation (depth) order
+    uint32_t* vals;         // Gaussian id
+    uint32_t* keys_sorted;  // tile index, final order
+    uint32_t* point_list;   // sorted Gaussian ids
     void* sort_ws;
     size_t sort_bytes;
 };
@@ -120,10 +127,16 @@ inline PrimBuffers carve_prim(Carver& c, int n) {
     b.rect = c.take<ushort4>(nn);
     b.thr = c.take<float>(nn);
     b.n_touched = c.take<uint32_t>(nn);
+    b.depth_key = c.take<uint32_t>(nn);
+    b.ids = c.take<uint32_t>(nn);
+    b.depth_key_sorted = c.take<uint32_t>(nn);
+    b.order = c.take<uint32_t>(nn);
     b.offsets = c.take<uint32_t>(nn);
     b.counters = c.take<uint32_t>(4);
     b.scan_bytes = scan_workspace_bytes(static_cast<long long>(nn));
     b.scan_ws = c.take<unsigned char>(b.scan_bytes);
+    b.sort_bytes = sort_workspace_bytes<uint32_t>(static_cast<long long>(nn));
+    b.sort_ws = c.take<unsigned char>(b.sort_bytes);
     return b;
 }
 
@@ -144,11 +157,11 @@ inline TileBuffers carve_tile(Carver& c, int W, int H) {
 inline InstBuffers carve_inst(Carver& c, long long m) {
     const size_t mm = static_cast<size_t>(m < 1 ? 1 : m);
     InstBuffers b;
-    b.keys = c.take<unsigned long long>(mm);
+    b.keys = c.take<uint32_t>(mm);
     b.vals = c.take<uint32_t>(mm);
-    b.keys_sorted = c.take<unsigned long long>(mm);
+    b.keys_sorted = c.take<uint32_t>(mm);
     b.point_list = c.take<uint32_t>(mm);
-    b.sort_bytes = sort_workspace_bytes<unsigned long long>(static_cast<long long>(mm));
+    b.sort_bytes = sort_workspace_bytes<uint32_t>(static_cast<long long>(mm));
     b.sort_ws = c.take<unsigned char>(b.sort_bytes);
     return b;
 }
@@ -233,48 +246,60 @@ __device__ __forceinline__ void sh_basis(float x, float y, float z, int bases, f
     }
 }
 
-// q(d) = A dx^2 + 2 B dx dy + C dy^2, every operation rounded separately (no contraction), so the
-// count pass, the write pass and the C oracle all get the same bits.
-__device__ __forceinline__ float quad_form(float A, float B, float C, float dx, float dy) {
-    const float t0 = __fmul_rn(__fmul_rn(A, dx), dx);
-    const float t1 = __fmul_rn(__fmul_rn(__fmul_rn(2.f, B), dx), dy);
-    const float t2 = __fmul_rn(__fmul_rn(C, dy), dy);
-    return __fadd_rn(__fadd_rn(t0, t1), t2);
+// ---------------------------------------------------------------------------------------------
+// Listing test: which tiles the ellipse q = A dx^2 + 2B dx dy + C dy^2 <= R = 2 thr (every pixel
+// with alpha >= 1/255) reaches, each tile taken as the continuous rectangle of its pixel centres.
+// Per tile row, the ellipse's x-extent over the row band is found in closed form (the rightmost /
+// leftmost point on the band: x(dy) = (-B dy +- sqrt(A R - D dy^2)) / A is concave / convex, so its
+// extreme on the band is at the clamped stationary dy = -+B sqrt(R / (D C)), D = AC - B^2), and the
+// tiles whose centre range meets that interval are listed. Every operation is rounded on its own
+// (no fused multiply-add), so the count pass, the write pass and the numpy oracle agree bit for bit.
+// ---------------------------------------------------------------------------------------------
+struct Ellipse {
+    float mx, my, A, B, R, D, ey, s;
+};
+
+__device__ __forceinline__ Ellipse make_ellipse(float mx, float my, float A, float B, float C, float thr) {
+    Ellipse e;
+    e.mx = mx;
+    e.my = my;
+    e.A = A;
+    e.B = B;
+    e.R = __fmul_rn(2.f, thr);
+    e.D = __fsub_rn(__fmul_rn(A, C), __fmul_rn(B, B));
+    e.ey = __fsqrt_rn(__fdiv_rn(__fmul_rn(A, e.R), e.D));
+    e.s = __fsqrt_rn(__fdiv_rn(e.R, __fmul_rn(e.D, C)));
+    return e;
 }
 
-// Minimum over the axis-aligned rectangle [x0, x1] x [y0, y1] (offsets from the mean) of the
-// positive-definite q: 0 when the mean lies inside, else the smaller minimum over the (at most two)
-// edges that face the mean, each a clamped 1D quadratic.
-__device__ __forceinline__ float rect_min_quadratic(float A, float B, float C, float x0, float x1, float y0,
-                                                    float y1) {
-    const bool in_x = x0 <= 0.f && 0.f <= x1;
-    const bool in_y = y0 <= 0.f && 0.f <= y1;
-    if (in_x && in_y) return 0.f;
-    float best = 3.0e38f;
-    if (!in_x) {
-        const float dx = x0 > 0.f ? x0 : x1;
-        const float dy = fminf(fmaxf(__fdiv_rn(__fmul_rn(-B, dx), C), y0), y1);
-        best = fminf(best, quad_form(A, B, C, dx, dy));
-    }
-    if (!in_y) {
-        const float dy = y0 > 0.f ? y0 : y1;
-        const float dx = fminf(fmaxf(__fdiv_rn(__fmul_rn(-B, dy), A), x0), x1);
-        best = fminf(best, quad_form(A, B, C, dx, dy));
-    }
-    return best;
+// First and last tile row the ellipse can reach (empty when lo > hi).
+__device__ __forceinline__ int2 ellipse_rows(const Ellipse& e, int H, int tiles_y) {
+    const float top = __fsub_rn(e.my, e.ey), bot = __fadd_rn(e.my, e.ey);
+    if (!(bot >= 0.5f && top <= static_cast<float>(H) - 0.5f)) return make_int2(1, 0);
+    const int lo = max(static_cast<int>(ceilf(__fdiv_rn(__fsub_rn(top, 15.5f), 16.f))), 0);
+    const int hi = min(static_cast<int>(floorf(__fdiv_rn(__fsub_rn(bot, 0.5f), 16.f))), tiles_y - 1);
+    return make_int2(lo, hi);
 }
 
-// Does the ellipse q <= 2 thr around (mx, my) reach a pixel centre of tile (tx, ty)? (The pixel-
-// centre rectangle is tested as a continuous rectangle, which can only add tiles, never drop one.)
-__device__ __forceinline__ bool tile_hit(float mx, float my, float A, float B, float C, float thr, int tx, int ty,
-                                         int W, int H) {
-    const float px0 = static_cast<float>(tx * kTile) + 0.5f;
-    const float px1 = static_cast<float>(min((tx + 1) * kTile, W)) - 0.5f;
-    const float py0 = static_cast<float>(ty * kTile) + 0.5f;
-    const float py1 = static_cast<float>(min((ty + 1) * kTile, H)) - 0.5f;
-    const float q = rect_min_quadratic(A, B, C, __fsub_rn(px0, mx), __fsub_rn(px1, mx), __fsub_rn(py0, my),
-                                       __fsub_rn(py1, my));
-    return q <= __fmul_rn(2.f, thr);
+__device__ __forceinline__ float ellipse_x(const Ellipse& e, float dy, float sign) {
+    const float disc = fmaxf(__fsub_rn(__fmul_rn(e.A, e.R), __fmul_rn(__fmul_rn(e.D, dy), dy)), 0.f);
+    return __fdiv_rn(__fadd_rn(__fmul_rn(-e.B, dy), __fmul_rn(sign, __fsqrt_rn(disc))), e.A);
+}
+
+// Listed tiles [x, y] of tile row ty (empty when x > y).
+__device__ __forceinline__ int2 ellipse_row_tiles(const Ellipse& e, int ty, int W, int H, int tiles_x) {
+    const float y0 = static_cast<float>(ty * kTile) + 0.5f;
+    const float y1 = static_cast<float>(min(ty * kTile + kTile, H)) - 0.5f;
+    const float lo = fmaxf(__fsub_rn(y0, e.my), -e.ey), hi = fminf(__fsub_rn(y1, e.my), e.ey);
+    if (!(lo <= hi)) return make_int2(1, 0);
+    const float dyr = fminf(fmaxf(__fmul_rn(-e.B, e.s), lo), hi);
+    const float dyl = fminf(fmaxf(__fmul_rn(e.B, e.s), lo), hi);
+    const float xr = __fadd_rn(e.mx, ellipse_x(e, dyr, 1.f));
+    const float xl = __fadd_rn(e.mx, ellipse_x(e, dyl, -1.f));
+    if (!(xr >= 0.5f && xl <= static_cast<float>(W) - 0.5f)) return make_int2(1, 0);
+    const int tlo = max(static_cast<int>(ceilf(__fdiv_rn(__fsub_rn(xl, 15.5f), 16.f))), 0);
+    const int thi = min(static_cast<int>(floorf(__fdiv_rn(__fsub_rn(xr, 0.5f), 16.f))), tiles_x - 1);
+    return make_int2(tlo, thi);
 }
 
 }  // namespace gs3d

@@ -3,10 +3,14 @@
 //
 // Launch sequence of one forward (all on the caller's stream):
 //   gs3d_preprocess   k_preprocess (1 thread per Gaussian; SH rows loaded per warp with 16-byte
-//                     loads through shared memory), scan of the tile counts -> M on the device
+//                     loads through shared memory; listed tiles counted row by row in closed form),
+//                     radix sort of the Gaussians by depth bits (the four depth-digit passes of the
+//                     64-bit (tile << 32 | depth) key sort, done on N Gaussians instead of M
+//                     instances), tile counts gathered in that order and scanned -> M on the device
 //   (host reads M once to size the instance buffer; the bucket buffer is sized by a bound)
-//   gs3d_render       k_duplicate, radix sort of (tile << 32 | depth bits, id) over 32 + tile bits,
-//                     k_ranges, k_bucket_counts + scan, k_bucket_tiles, k_blend
+//   gs3d_render       k_duplicate in depth order, stable radix sort on the tile digits (completing
+//                     the LSD sort of the 64-bit keys: same order, ties by Gaussian id), k_ranges,
+//                     k_bucket_counts + scan, k_bucket_tiles, k_blend
 // k_blend: one 256-thread block per 16x16 tile; each warp owns an 8x4 subtile and walks the
 // tile list in 32-splat buckets staged in shared memory, skipping (by ballot) the splats whose
 // culling rectangle misses its subtile - a rectangle that holds every pixel with alpha >= 1/255,
@@ -118,9 +122,12 @@ __global__ void __launch_bounds__(kPreThreads) k_preprocess(Params P, Cam cam, P
                 ry0 = static_cast<int>(fmaxf(fy0, 0.f));
                 rx1 = static_cast<int>(fminf(fx1, static_cast<float>(cam.width - 1)));
                 ry1 = static_cast<int>(fminf(fy1, static_cast<float>(cam.height - 1)));
-                for (int tyi = ry0 / kTile; tyi <= ry1 / kTile; ++tyi)
-                    for (int txi = rx0 / kTile; txi <= rx1 / kTile; ++txi)
-                        touched += tile_hit(mx, my, A, B, C, thr, txi, tyi, cam.width, cam.height) ? 1u : 0u;
+                const Ellipse e = make_ellipse(mx, my, A, B, C, thr);
+                const int2 rows = ellipse_rows(e, cam.height, cam.tiles_y);
+                for (int tyi = rows.x; tyi <= rows.y; ++tyi) {
+                    const int2 t = ellipse_row_tiles(e, tyi, cam.width, cam.height, cam.tiles_x);
+                    touched += static_cast<uint32_t>(max(t.y - t.x + 1, 0));
+                }
                 vis = touched > 0;
             }
         }
@@ -167,6 +174,10 @@ __global__ void __launch_bounds__(kPreThreads) k_preprocess(Params P, Cam cam, P
     }
     if (!valid) return;
     pb.n_touched[i] = touched;
+    pb.ids[i] = static_cast<uint32_t>(i);
+    // order-preserving bits of the depth (z > 0 in practice, negative z handled too); not visible = last
+    const uint32_t zb = __float_as_uint(zc);
+    pb.depth_key[i] = vis ? ((zb & 0x80000000u) ? ~zb : (zb | 0x80000000u)) : 0xffffffffu;
     if (!vis) return;
     pb.mean2d[i] = make_float2(mx, my);
     pb.conic_o[i] = make_float4(A, B, C, o);
@@ -176,42 +187,50 @@ __global__ void __launch_bounds__(kPreThreads) k_preprocess(Params P, Cam cam, P
     pb.thr[i] = thr;
 }
 
-// One (key, id) per listed tile; never more than the counted n_touched (a shortfall, which the
-// shared tile test rules out, is padded with keys past the last tile).
+// Tile counts in depth order (the input of the offsets scan).
+__global__ void k_gather_counts(const uint32_t* __restrict__ order, const uint32_t* __restrict__ n_touched, int n,
+                                uint32_t* __restrict__ counts_sorted) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= n) return;
+    counts_sorted[r] = n_touched[min(order[r], static_cast<uint32_t>(n - 1))];
+}
+
+// One (tile, id) per listed tile, Gaussians taken in (depth, id) order so that the stable tile sort that
+// follows completes the LSD sort of the 64-bit (tile << 32 | depth) keys. Never more than the counted
+// n_touched per Gaussian (a shortfall, which the shared row test rules out, is padded past the last tile).
 __global__ void k_duplicate(int n, Cam cam, PrimBuffers pb, InstBuffers ib) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= n) return;
+    const uint32_t i = pb.order[r];
+    if (i >= static_cast<uint32_t>(n)) return;
     const uint32_t cnt = pb.n_touched[i];
     if (cnt == 0) return;
     const float2 m = pb.mean2d[i];
     const float4 co = pb.conic_o[i];
-    const float thr = pb.thr[i];
-    const ushort4 r = pb.rect[i];
-    const unsigned long long zbits = __float_as_uint(pb.color_z[i].w);
-    const uint32_t off = pb.offsets[i];
+    const Ellipse e = make_ellipse(m.x, m.y, co.x, co.y, co.z, pb.thr[i]);
+    const uint32_t off = pb.offsets[r];
     uint32_t k = 0;
-    for (int ty = r.y / kTile; ty <= r.w / kTile && k < cnt; ++ty)
-        for (int tx = r.x / kTile; tx <= r.z / kTile && k < cnt; ++tx)
-            if (tile_hit(m.x, m.y, co.x, co.y, co.z, thr, tx, ty, cam.width, cam.height)) {
-                const unsigned long long tile = static_cast<unsigned long long>(ty) * cam.tiles_x + tx;
-                ib.keys[off + k] = (tile << 32) | zbits;
-                ib.vals[off + k] = static_cast<uint32_t>(i);
-                ++k;
-            }
-    const unsigned long long pad = static_cast<unsigned long long>(cam.tiles_x) * cam.tiles_y << 32;
+    const int2 rows = ellipse_rows(e, cam.height, cam.tiles_y);
+    for (int ty = rows.x; ty <= rows.y && k < cnt; ++ty) {
+        const int2 t = ellipse_row_tiles(e, ty, cam.width, cam.height, cam.tiles_x);
+        for (int tx = t.x; tx <= t.y && k < cnt; ++tx, ++k) {
+            ib.keys[off + k] = static_cast<uint32_t>(ty * cam.tiles_x + tx);
+            ib.vals[off + k] = i;
+        }
+    }
     for (; k < cnt; ++k) {
-        ib.keys[off + k] = pad | 0xffffffffull;
-        ib.vals[off + k] = static_cast<uint32_t>(i);
+        ib.keys[off + k] = static_cast<uint32_t>(cam.tiles_x * cam.tiles_y);
+        ib.vals[off + k] = i;
     }
 }
 
-__global__ void k_ranges(const unsigned long long* __restrict__ keys, int m, int T, uint2* __restrict__ ranges) {
+__global__ void k_ranges(const uint32_t* __restrict__ keys, int m, int T, uint2* __restrict__ ranges) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= m) return;
-    const unsigned long long t = keys[i] >> 32;
-    if (t >= static_cast<unsigned long long>(T)) return;
-    if (i == 0 || (keys[i - 1] >> 32) != t) ranges[t].x = i;
-    if (i == m - 1 || (keys[i + 1] >> 32) != t) ranges[t].y = i + 1;
+    const uint32_t t = keys[i];
+    if (t >= static_cast<uint32_t>(T)) return;
+    if (i == 0 || keys[i - 1] != t) ranges[t].x = i;
+    if (i == m - 1 || keys[i + 1] != t) ranges[t].y = i + 1;
 }
 
 __global__ void k_bucket_counts(const uint2* __restrict__ ranges, int T, uint32_t* __restrict__ nb) {
@@ -401,7 +420,12 @@ int gs3d_preprocess(const float* means, const float* scales, const float* rotati
     }
     k_preprocess<<<div_up(n, kPreThreads), kPreThreads, smem, st>>>(P, cam, pb);
     SPLAT_TRY(check_launch("gs3d_preprocess"));
-    SPLAT_TRY(scan_exclusive_u32(pb.n_touched, pb.offsets, n, pb.counters, pb.scan_ws, pb.scan_bytes, st));
+    // the depth-digit passes of the (tile << 32 | depth) key sort, on the Gaussians before duplication
+    SPLAT_TRY(radix_sort_pairs<uint32_t>(pb.depth_key, pb.ids, pb.depth_key_sorted, pb.order, n, 0, 32, pb.sort_ws,
+                                         pb.sort_bytes, st));
+    k_gather_counts<<<div_up(n, 256), 256, 0, st>>>(pb.order, pb.n_touched, n, pb.offsets);
+    SPLAT_TRY(check_launch("gs3d_gather_counts"));
+    SPLAT_TRY(scan_exclusive_u32(pb.offsets, pb.offsets, n, pb.counters, pb.scan_ws, pb.scan_bytes, st));
     if (num_instances)
         SPLAT_CUDA(cudaMemcpyAsync(num_instances, pb.counters, sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
     return SPLAT_OK;
@@ -431,9 +455,10 @@ int gs3d_render(int n, long long num_instances, const gs3d_settings* settings, v
     if (m > 0) {
         k_duplicate<<<div_up(n, 256), 256, 0, st>>>(n, cam, pb, ib);
         SPLAT_TRY(check_launch("gs3d_duplicate"));
+        // the tile-digit passes (the pad key T needs bit_width(T) bits)
         const int tile_bits = bit_width(static_cast<unsigned long long>(T));
-        SPLAT_TRY(radix_sort_pairs<unsigned long long>(ib.keys, ib.vals, ib.keys_sorted, ib.point_list, m, 0,
-                                                       32 + tile_bits, ib.sort_ws, ib.sort_bytes, st));
+        SPLAT_TRY(radix_sort_pairs<uint32_t>(ib.keys, ib.vals, ib.keys_sorted, ib.point_list, m, 0, tile_bits,
+                                             ib.sort_ws, ib.sort_bytes, st));
         k_ranges<<<div_up(m, 256), 256, 0, st>>>(ib.keys_sorted, static_cast<int>(m), T, tb.ranges);
         SPLAT_TRY(check_launch("gs3d_ranges"));
     }

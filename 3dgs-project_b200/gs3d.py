@@ -227,13 +227,16 @@ def _align(x: int) -> int:
 def primitive_views(prim_buf: torch.Tensor, n: int) -> dict[str, torch.Tensor]:
     """Typed views into a primitive buffer (the layout of carve_prim in csrc/gs3d_common.cuh):
     mean2d [N,2], conic_o [N,4] (A, B, C, opacity), color_z [N,4] (r, g, b, depth), rect [N,4] (int16 pixels),
-    thr [N], n_touched [N] (int32), offsets [N]. Valid for Gaussians with n_touched > 0."""
+    thr [N], n_touched [N] (int32), depth_key / ids / depth_key_sorted [N], order [N] (ids in depth order),
+    offsets [N] (instance offsets in that order). Per-Gaussian values are valid where n_touched > 0."""
     nn = max(n, 1)
     off = 0
     out = {}
     for name, elem, width, dtype in (("mean2d", 8, 2, torch.float32), ("conic_o", 16, 4, torch.float32),
                                      ("color_z", 16, 4, torch.float32), ("rect", 8, 4, torch.int16),
                                      ("thr", 4, 1, torch.float32), ("n_touched", 4, 1, torch.int32),
+                                     ("depth_key", 4, 1, torch.int32), ("ids", 4, 1, torch.int32),
+                                     ("depth_key_sorted", 4, 1, torch.int32), ("order", 4, 1, torch.int32),
                                      ("offsets", 4, 1, torch.int32)):
         off = _align(off)
         t = prim_buf[off:off + elem * nn].view(dtype)
@@ -264,16 +267,22 @@ def tile_views(tile_buf: torch.Tensor, width: int, height: int) -> dict[str, tor
     return out
 
 
-def instance_views(inst_buf: torch.Tensor, m: int) -> dict[str, torch.Tensor]:
-    """keys (unsorted), vals, keys_sorted [M] (int64 views of the uint64 keys), point_list [M] (int32)."""
+def instance_views(inst_buf: torch.Tensor, m: int, prim_buf: torch.Tensor | None = None,
+                   n: int = 0) -> dict[str, torch.Tensor]:
+    """tiles (generation order), vals, tiles_sorted, point_list [M] (int32). With the primitive buffer, also
+    keys_sorted: the 64-bit (tile << 32 | order-preserving depth bits) keys in sorted order (as int64)."""
     mm = max(m, 1)
     off = 0
     out = {}
-    for name, elem, dtype in (("keys", 8, torch.int64), ("vals", 4, torch.int32), ("keys_sorted", 8, torch.int64),
-                              ("point_list", 4, torch.int32)):
+    for name in ("tiles", "vals", "tiles_sorted", "point_list"):
         off = _align(off)
-        out[name] = inst_buf[off:off + elem * mm].view(dtype)[:m]
-        off += elem * mm
+        out[name] = inst_buf[off:off + 4 * mm].view(torch.int32)[:m]
+        off += 4 * mm
+    if prim_buf is not None:
+        z = primitive_views(prim_buf, n)["color_z"][:, 3].contiguous()
+        zb = z.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+        zk = torch.where(zb >= 2 ** 31, zb ^ 0xFFFFFFFF, zb | 2 ** 31)
+        out["keys_sorted"] = (out["tiles_sorted"].to(torch.int64) << 32) | zk[out["point_list"].long()]
     return out
 
 

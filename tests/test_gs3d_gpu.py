@@ -48,13 +48,18 @@ def test_binning_bit_exact(name, cuda):
     pv = gs3d.primitive_views(prim, n)
     vis = (pv["n_touched"] > 0).cpu().numpy()
     ref = O.bin_instances(pv["mean2d"].cpu().numpy(), pv["conic_o"].cpu().numpy(), pv["thr"].cpu().numpy(),
-                          pv["rect"].cpu().numpy(), pv["color_z"][:, 3].cpu().numpy(), vis, W, H)
+                          pv["color_z"][:, 3].cpu().numpy(), vis, W, H)
     n_touched, keys, ids, keys_sorted, point_list, ranges, buckets = ref
     assert np.array_equal(pv["n_touched"].cpu().numpy(), n_touched)
     assert m == keys.size
-    iv = gs3d.instance_views(inst, m)
+    iv = gs3d.instance_views(inst, m, prim, n)
     assert np.array_equal(iv["keys_sorted"].cpu().numpy().view(np.uint64), keys_sorted)
     assert np.array_equal(iv["point_list"].cpu().numpy(), point_list)
+    # the depth passes: Gaussians ordered by (depth, id), the ones not visible last
+    order = pv["order"].cpu().numpy()
+    zk = O.depth_order_key(pv["color_z"][:, 3].cpu().numpy())
+    zk = np.where(vis, zk.astype(np.uint64), np.uint64(0xFFFFFFFF))
+    assert np.array_equal(order, np.argsort(zk, kind="stable"))
     tv = gs3d.tile_views(tile, W, H)
     assert np.array_equal(tv["ranges"].cpu().numpy(), ranges)
     assert np.array_equal(tv["nb"].cpu().numpy()[:-1], buckets)
