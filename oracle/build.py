@@ -22,7 +22,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 REF_OUT = HERE / "_ref"
-CXX = os.environ.get("CXX", "g++")
+CXX = os.environ.get("ORACLE_CXX", "g++")  # the PATH g++ (the image's $CXX wrapper lacks libgomp)
 FLAGS = ["-O2", "-std=c++17", "-fPIC", "-shared", "-ffp-contract=off", "-fno-fast-math"]
 
 
