@@ -1,0 +1,115 @@
+"""Multi-process host logic of the data-parallel step, on CPU with gloo (world size 2).
+
+Checks the view sharding, that one all-reduce of the flat buffer sums every group's gradients, and that the
+replicas stay identical after the same Adam step; a rank that raises is seen by the other as a failed
+collective (short process-group timeout), not as a hang.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from __graft_entry__ import load_package  # spawned ranks re-import this module: register the package first
+
+load_package()
+from gs_b200 import dist as gdist  # noqa: E402
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _init(rank, world, port, timeout_s=60):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
+
+
+def _worker(rank, world, port, q):
+    try:
+        _init(rank, world, port)
+        n = 37
+        views = list(range(8))
+        mine = gdist.shard_views(views, rank, world)
+        g = gdist.FlatGradients(n, 15)
+        torch.manual_seed(100 + rank)
+        per_view = []
+        for v in mine:
+            torch.manual_seed(1000 + v)
+            grads = [torch.randn(v.shape) for v in g.views]
+            per_view.append(grads)
+            g.add_(grads)
+        g.all_reduce()
+        # the expected sum over all 8 views, computed locally
+        expect = [torch.zeros_like(v) for v in g.views]
+        for v in views:
+            torch.manual_seed(1000 + v)
+            for e, t in zip(expect, [torch.randn(x.shape) for x in g.views]):
+                e.add_(t)
+        ok_sum = all(torch.allclose(a, b, atol=1e-5) for a, b in zip(g.views, expect))
+        # same Adam-like update on both ranks keeps the replicas equal
+        p = torch.ones(n, 3)
+        p -= 0.1 * g.views[0].sign()
+        gathered = [torch.zeros_like(p) for _ in range(world)]
+        dist.all_gather(gathered, p)
+        q.put((rank, mine, ok_sum, all(torch.equal(gathered[0], x) for x in gathered)))
+        dist.destroy_process_group()
+    except Exception as exc:  # report instead of hanging the parent
+        q.put((rank, None, False, repr(exc)))
+
+
+def test_two_ranks_shard_views_and_sum_gradients():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res[0][1] == [0, 2, 4, 6] and res[1][1] == [1, 3, 5, 7]
+    assert all(r[2] for r in res), res
+    assert all(r[3] is True for r in res), res
+
+
+def _dying_worker(rank, world, port, q):
+    _init(rank, world, port, timeout_s=5)
+    if rank == 1:
+        dist.destroy_process_group()
+        raise SystemExit(3)  # leaves between steps, before the collective
+    t = torch.ones(4)
+    try:
+        dist.all_reduce(t)
+        q.put((rank, "completed"))
+    except Exception as exc:
+        q.put((rank, type(exc).__name__))
+
+
+def test_a_rank_that_leaves_makes_the_collective_fail_not_hang():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dying_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    rank, outcome = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert rank == 0 and outcome != "completed"
+
+
+def test_shard_views_rejects_bad_ranks():
+    with pytest.raises(ValueError):
+        gdist.shard_views([1, 2], 2, 2)
+    assert gdist.shard_views(list(range(8)), 3, 8) == [3]
