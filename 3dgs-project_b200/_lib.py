@@ -6,11 +6,13 @@ tensor handed to it is not a CUDA tensor, the call raises. There is no CPU path.
 from __future__ import annotations
 
 import ctypes
+import os
 from pathlib import Path
 
 import torch
 
-LIB_PATH = Path(__file__).resolve().with_name("libsplat_b200.so")
+# SPLAT_B200_LIB may name another build of the same library (e.g. a tuning variant); it is still this C ABI.
+LIB_PATH = Path(os.environ.get("SPLAT_B200_LIB", Path(__file__).resolve().with_name("libsplat_b200.so")))
 ABI_VERSION = 1
 
 _P = ctypes.c_void_p

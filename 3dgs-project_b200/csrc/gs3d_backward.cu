@@ -22,6 +22,9 @@ namespace splat {
 namespace gs3d {
 
 constexpr int kBwdWarps = 4;
+#ifndef SPLAT_BWD_MIN_BLOCKS
+#define SPLAT_BWD_MIN_BLOCKS 7  // 72 registers, no spills: 28 warps per SM instead of 20
+#endif
 constexpr int kPxPerLane = kTilePixels / 32;  // 8
 constexpr int kPbThreads = 128;
 constexpr int kPbWarps = kPbThreads / 32;
@@ -42,7 +45,7 @@ inline GradAcc carve_grad(Carver& c, int n) {
     return g;
 }
 
-__global__ void __launch_bounds__(32 * kBwdWarps) k_blend_backward(
+__global__ void __launch_bounds__(32 * kBwdWarps, SPLAT_BWD_MIN_BLOCKS) k_blend_backward(
     Cam cam, const uint32_t* __restrict__ counters, const uint32_t* __restrict__ bucket_tile,
     const uint2* __restrict__ ranges, const uint32_t* __restrict__ bstart, const uint32_t* __restrict__ max_contrib,
     const uint32_t* __restrict__ point_list, const float2* __restrict__ mean2d, const float4* __restrict__ conic_o,
@@ -54,7 +57,7 @@ __global__ void __launch_bounds__(32 * kBwdWarps) k_blend_backward(
     __shared__ float4 s_col[kBwdWarps][kBucket];
     __shared__ ushort4 s_rect[kBwdWarps][kBucket];
     __shared__ uint32_t s_id[kBwdWarps][kBucket];
-    __shared__ float3 s_grad[kBwdWarps][kTilePixels];
+    __shared__ float4 s_grad[kBwdWarps][kTilePixels];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long long b = static_cast<long long>(blockIdx.x) * kBwdWarps + warp;
@@ -89,19 +92,24 @@ __global__ void __launch_bounds__(32 * kBwdWarps) k_blend_backward(
     const size_t HW = static_cast<size_t>(cam.width) * cam.height;
     const float4* ck = ckpt + b * kTilePixels;
     float T[kPxPerLane], rho[kPxPerLane];
-    int lim[kPxPerLane];
+    // per pixel, how many of this bucket's splats it used in the forward, clamped to [0, 32], 8 bits each
+    uint32_t lim_lo = 0u, lim_hi = 0u;
 #pragma unroll
     for (int r = 0; r < kPxPerLane; ++r) {
         const int y = y0 + 2 * r;
-        float3 G = make_float3(0.f, 0.f, 0.f);
+        float4 G = make_float4(0.f, 0.f, 0.f, 0.f);
         T[r] = 0.f;
         rho[r] = 0.f;
-        lim[r] = 0;
         if (x < cam.width && y < cam.height) {
             const int pix = y * cam.width + x;
-            lim[r] = static_cast<int>(static_cast<long long>(n_contrib[pix]) - bucket_start);
-            if (lim[r] > 0) {
-                G = make_float3(grad_image[pix], grad_image[HW + pix], grad_image[2 * HW + pix]);
+            const long long used_here = static_cast<long long>(n_contrib[pix]) - bucket_start;
+            if (used_here > 0) {
+                const uint32_t l = static_cast<uint32_t>(min(used_here, 32ll));
+                if (r < 4)
+                    lim_lo |= l << (8 * r);
+                else
+                    lim_hi |= l << (8 * (r - 4));
+                G = make_float4(grad_image[pix], grad_image[HW + pix], grad_image[2 * HW + pix], 0.f);
                 const float4 st = ck[r * 32 + lane];
                 T[r] = st.w;
                 rho[r] = G.x * (image[pix] - st.x) + G.y * (image[HW + pix] - st.y) + G.z * (image[2 * HW + pix] - st.z);
@@ -116,21 +124,22 @@ __global__ void __launch_bounds__(32 * kBwdWarps) k_blend_backward(
         const float4 co = s_con[warp][j];
         const float4 c = s_col[warp][j];
         const ushort4 rc = s_rect[warp][j];
-        float g_mx = 0.f, g_my = 0.f, g_a = 0.f, g_b = 0.f, g_c = 0.f, g_o = 0.f, g_r = 0.f, g_g = 0.f, g_bl = 0.f;
+        // per-lane sums over its pixels: h = dL/dq2 moments (for mean2d and conic), opacity, colour
+        float s_x = 0.f, s_y = 0.f, s_xx = 0.f, s_xy = 0.f, s_yy = 0.f, g_o = 0.f, g_r = 0.f, g_g = 0.f, g_bl = 0.f;
         bool used = false;
         const bool col_hit = x >= rc.x && x <= rc.z;
 #pragma unroll
         for (int r = 0; r < kPxPerLane; ++r) {
             const int yb = ty0 + 2 * r;  // rows yb, yb + 1 of this band
             if (rc.y > yb + 1 || rc.w < yb) continue;  // warp-uniform
-            if (!col_hit || j >= lim[r]) continue;
+            const uint32_t l = ((r < 4 ? lim_lo : lim_hi) >> (8 * (r & 3))) & 0xffu;
+            if (!col_hit || static_cast<uint32_t>(j) >= l) continue;
             const float dx = mm.x - pxf, dy = mm.y - (static_cast<float>(y0 + 2 * r) + 0.5f);
-            const float q2 = dx * (co.x * dx + co.y * dy) + co.z * dy * dy;
-            const float G = exp2f(fminf(q2, 0.f));
+            const float G = hw_exp2(fminf(blend_q2(co.x, co.y, co.z, dx, dy), 0.f));
             const float alpha = co.w * G;
             if (alpha < kAlphaMin) continue;
             used = true;
-            const float3 gp = s_grad[warp][r * 32 + lane];
+            const float4 gp = s_grad[warp][r * 32 + lane];
             const float w = alpha * T[r];
             const float dot_c = gp.x * c.x + gp.y * c.y + gp.z * c.z;
             g_r += w * gp.x;
@@ -138,24 +147,25 @@ __global__ void __launch_bounds__(32 * kBwdWarps) k_blend_backward(
             g_bl += w * gp.z;
             rho[r] -= w * dot_c;
             const float one_minus = 1.f - alpha;
-            const float dL_dalpha = T[r] * dot_c - rho[r] * __frcp_rn(fmaxf(one_minus, kOneMinusAlphaEps));
+            const float dL_dalpha = T[r] * dot_c - __fdividef(rho[r], fmaxf(one_minus, kOneMinusAlphaEps));
             g_o += G * dL_dalpha;
             const float h = alpha * dL_dalpha * kLn2;  // dL/dq2
-            g_mx += h * (2.f * co.x * dx + co.y * dy);
-            g_my += h * (co.y * dx + 2.f * co.z * dy);
-            g_a += h * dx * dx;
-            g_b += h * dx * dy;
-            g_c += h * dy * dy;
+            const float hx = h * dx, hy = h * dy;
+            s_x += hx;
+            s_y += hy;
+            s_xx += hx * dx;
+            s_xy += hx * dy;
+            s_yy += hy * dy;
             T[r] *= one_minus;
         }
         if (__ballot_sync(kFullMask, used) == 0u) continue;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
-            g_mx += __shfl_down_sync(kFullMask, g_mx, o);
-            g_my += __shfl_down_sync(kFullMask, g_my, o);
-            g_a += __shfl_down_sync(kFullMask, g_a, o);
-            g_b += __shfl_down_sync(kFullMask, g_b, o);
-            g_c += __shfl_down_sync(kFullMask, g_c, o);
+            s_x += __shfl_down_sync(kFullMask, s_x, o);
+            s_y += __shfl_down_sync(kFullMask, s_y, o);
+            s_xx += __shfl_down_sync(kFullMask, s_xx, o);
+            s_xy += __shfl_down_sync(kFullMask, s_xy, o);
+            s_yy += __shfl_down_sync(kFullMask, s_yy, o);
             g_o += __shfl_down_sync(kFullMask, g_o, o);
             g_r += __shfl_down_sync(kFullMask, g_r, o);
             g_g += __shfl_down_sync(kFullMask, g_g, o);
@@ -163,9 +173,11 @@ __global__ void __launch_bounds__(32 * kBwdWarps) k_blend_backward(
         }
         if (lane == 0) {
             const int g = s_id[warp][j];
-            // back from the exp2-scaled conic (q2 = log2(e) * power) to (A, B, C)
-            atomicAdd(acc.mean2d + g, make_float2(g_mx, g_my));
-            atomicAdd(acc.conic_o + g, make_float4(-0.5f * kLog2e * g_a, -kLog2e * g_b, -0.5f * kLog2e * g_c, g_o));
+            // q2 = a2 dx^2 + b2 dx dy + c2 dy^2: dq2/dmx = 2 a2 dx + b2 dy, dq2/dmy = b2 dx + 2 c2 dy; then back
+            // from the exp2-scaled conic (a2, b2, c2) = log2(e) (-0.5 A, -B, -0.5 C) to (A, B, C)
+            atomicAdd(acc.mean2d + g, make_float2(2.f * co.x * s_x + co.y * s_y, co.y * s_x + 2.f * co.z * s_y));
+            atomicAdd(acc.conic_o + g,
+                      make_float4(-0.5f * kLog2e * s_xx, -kLog2e * s_xy, -0.5f * kLog2e * s_yy, g_o));
             atomicAdd(acc.color + g, make_float4(g_r, g_g, g_bl, 0.f));
         }
     }

@@ -247,6 +247,22 @@ __device__ __forceinline__ void sh_basis(float x, float y, float z, int bases, f
 }
 
 // ---------------------------------------------------------------------------------------------
+// Blend evaluation shared by the forward and the backward, with explicit fused multiply-adds so both
+// kernels take the same alpha >= 1/255 decisions bit for bit. (a2, b2, c2) is the conic scaled by
+// log2(e) (-0.5 A, -B, -0.5 C), so q2 = log2(e) * power and G = 2^min(q2, 0). The hardware ex2 is used:
+// below 2^-126 it flushes to 0, where alpha is far under the 1/255 cut-off anyway.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ float hw_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float blend_q2(float a2, float b2, float c2, float dx, float dy) {
+    return __fmaf_rn(dx, __fmaf_rn(a2, dx, __fmul_rn(b2, dy)), __fmul_rn(c2, __fmul_rn(dy, dy)));
+}
+
+// ---------------------------------------------------------------------------------------------
 // Listing test: which tiles the ellipse q = A dx^2 + 2B dx dy + C dy^2 <= R = 2 thr (every pixel
 // with alpha >= 1/255) reaches, each tile taken as the continuous rectangle of its pixel centres.
 // Per tile row, the ellipse's x-extent over the row band is found in closed form (the rightmost /
@@ -256,9 +272,11 @@ __device__ __forceinline__ void sh_basis(float x, float y, float z, int bases, f
 // (no fused multiply-add), so the count pass, the write pass and the numpy oracle agree bit for bit.
 // ---------------------------------------------------------------------------------------------
 struct Ellipse {
-    float mx, my, A, B, R, D, ey, s;
+    float mx, my, A, B, R, D, ey, s, inv_a;
 };
 
+// Reciprocals are taken once per Gaussian (correctly rounded), the per-row work is products, sums and two
+// square roots; divisions by 16 are products by 1/16 (exact).
 __device__ __forceinline__ Ellipse make_ellipse(float mx, float my, float A, float B, float C, float thr) {
     Ellipse e;
     e.mx = mx;
@@ -267,8 +285,10 @@ __device__ __forceinline__ Ellipse make_ellipse(float mx, float my, float A, flo
     e.B = B;
     e.R = __fmul_rn(2.f, thr);
     e.D = __fsub_rn(__fmul_rn(A, C), __fmul_rn(B, B));
-    e.ey = __fsqrt_rn(__fdiv_rn(__fmul_rn(A, e.R), e.D));
-    e.s = __fsqrt_rn(__fdiv_rn(e.R, __fmul_rn(e.D, C)));
+    const float inv_d = __frcp_rn(e.D);
+    e.ey = __fsqrt_rn(__fmul_rn(__fmul_rn(A, e.R), inv_d));
+    e.s = __fsqrt_rn(__fmul_rn(__fmul_rn(e.R, inv_d), __frcp_rn(C)));
+    e.inv_a = __frcp_rn(A);
     return e;
 }
 
@@ -276,14 +296,14 @@ __device__ __forceinline__ Ellipse make_ellipse(float mx, float my, float A, flo
 __device__ __forceinline__ int2 ellipse_rows(const Ellipse& e, int H, int tiles_y) {
     const float top = __fsub_rn(e.my, e.ey), bot = __fadd_rn(e.my, e.ey);
     if (!(bot >= 0.5f && top <= static_cast<float>(H) - 0.5f)) return make_int2(1, 0);
-    const int lo = max(static_cast<int>(ceilf(__fdiv_rn(__fsub_rn(top, 15.5f), 16.f))), 0);
-    const int hi = min(static_cast<int>(floorf(__fdiv_rn(__fsub_rn(bot, 0.5f), 16.f))), tiles_y - 1);
+    const int lo = max(static_cast<int>(ceilf(__fmul_rn(__fsub_rn(top, 15.5f), 0.0625f))), 0);
+    const int hi = min(static_cast<int>(floorf(__fmul_rn(__fsub_rn(bot, 0.5f), 0.0625f))), tiles_y - 1);
     return make_int2(lo, hi);
 }
 
 __device__ __forceinline__ float ellipse_x(const Ellipse& e, float dy, float sign) {
     const float disc = fmaxf(__fsub_rn(__fmul_rn(e.A, e.R), __fmul_rn(__fmul_rn(e.D, dy), dy)), 0.f);
-    return __fdiv_rn(__fadd_rn(__fmul_rn(-e.B, dy), __fmul_rn(sign, __fsqrt_rn(disc))), e.A);
+    return __fmul_rn(__fadd_rn(__fmul_rn(-e.B, dy), __fmul_rn(sign, __fsqrt_rn(disc))), e.inv_a);
 }
 
 // Listed tiles [x, y] of tile row ty (empty when x > y).
@@ -297,8 +317,8 @@ __device__ __forceinline__ int2 ellipse_row_tiles(const Ellipse& e, int ty, int 
     const float xr = __fadd_rn(e.mx, ellipse_x(e, dyr, 1.f));
     const float xl = __fadd_rn(e.mx, ellipse_x(e, dyl, -1.f));
     if (!(xr >= 0.5f && xl <= static_cast<float>(W) - 0.5f)) return make_int2(1, 0);
-    const int tlo = max(static_cast<int>(ceilf(__fdiv_rn(__fsub_rn(xl, 15.5f), 16.f))), 0);
-    const int thi = min(static_cast<int>(floorf(__fdiv_rn(__fsub_rn(xr, 0.5f), 16.f))), tiles_x - 1);
+    const int tlo = max(static_cast<int>(ceilf(__fmul_rn(__fsub_rn(xl, 15.5f), 0.0625f))), 0);
+    const int thi = min(static_cast<int>(floorf(__fmul_rn(__fsub_rn(xr, 0.5f), 0.0625f))), tiles_x - 1);
     return make_int2(tlo, thi);
 }
 

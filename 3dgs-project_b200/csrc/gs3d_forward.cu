@@ -307,15 +307,13 @@ __global__ void __launch_bounds__(kTilePixels) k_blend(Cam cam, const uint2* __r
                 hit = r.x <= sx0 + 7 && r.z >= sx0 && r.y <= sy0 + 3 && r.w >= sy0;
             }
             unsigned pending = __ballot_sync(kFullMask, hit);
-            while (pending) {
-                const int j = j0 + __ffs(pending) - 1;
-                pending &= pending - 1;
-                if (!done) {
+            if (!done) {
+                while (pending) {
+                    const int j = j0 + __ffs(pending) - 1;
+                    pending &= pending - 1;
                     const float2 mm = s_mean[j];
                     const float4 co = s_con[j];
-                    const float dx = mm.x - pxf, dy = mm.y - pyf;
-                    const float q2 = dx * (co.x * dx + co.y * dy) + co.z * dy * dy;
-                    const float alpha = co.w * exp2f(fminf(q2, 0.f));
+                    const float alpha = co.w * hw_exp2(fminf(blend_q2(co.x, co.y, co.z, mm.x - pxf, mm.y - pyf), 0.f));
                     if (alpha >= kAlphaMin) {
                         const float4 c = s_col[j];
                         const float w = alpha * T;
@@ -324,10 +322,12 @@ __global__ void __launch_bounds__(kTilePixels) k_blend(Cam cam, const uint2* __r
                         Cb += w * c.z;
                         T *= 1.f - alpha;
                         last = static_cast<uint32_t>(base + j + 1);
-                        done = T < kTMin;
+                        if (T < kTMin) {
+                            done = true;
+                            break;
+                        }
                     }
                 }
-                if (__all_sync(kFullMask, done)) break;
             }
         }
         __syncthreads();

@@ -125,7 +125,7 @@ void quat_rot(const float* q, float R[3][3], float& nsq) {
 
 // Listing test (every operation rounded on its own; the file is built with -ffp-contract=off).
 struct Ell {
-    float mx, my, A, B, R, D, ey, s;
+    float mx, my, A, B, R, D, ey, s, inv_a;
 };
 
 Ell make_ell(float mx, float my, float A, float B, float C, float thr) {
@@ -136,8 +136,10 @@ Ell make_ell(float mx, float my, float A, float B, float C, float thr) {
     e.B = B;
     e.R = 2.f * thr;
     e.D = A * C - B * B;
-    e.ey = sqrtf((A * e.R) / e.D);
-    e.s = sqrtf(e.R / (e.D * C));
+    const float inv_d = 1.f / e.D;
+    e.ey = sqrtf((A * e.R) * inv_d);
+    e.s = sqrtf((e.R * inv_d) * (1.f / C));
+    e.inv_a = 1.f / A;
     return e;
 }
 
@@ -148,13 +150,14 @@ void ell_rows(const Ell& e, int H, int tiles_y, int& lo, int& hi) {
         hi = 0;
         return;
     }
-    lo = std::max(static_cast<int>(std::max(ceilf((top - 15.5f) / 16.f), -1.f)), 0);
-    hi = std::min(static_cast<int>(std::min(floorf((bot - 0.5f) / 16.f), static_cast<float>(tiles_y))), tiles_y - 1);
+    lo = std::max(static_cast<int>(std::max(ceilf((top - 15.5f) * 0.0625f), -1.f)), 0);
+    hi = std::min(static_cast<int>(std::min(floorf((bot - 0.5f) * 0.0625f), static_cast<float>(tiles_y))),
+                  tiles_y - 1);
 }
 
 float ell_x(const Ell& e, float dy, float sign) {
     const float disc = std::max(e.A * e.R - (e.D * dy) * dy, 0.f);
-    return ((-e.B) * dy + sign * sqrtf(disc)) / e.A;
+    return ((-e.B) * dy + sign * sqrtf(disc)) * e.inv_a;
 }
 
 void ell_row_tiles(const Ell& e, int ty, int W, int H, int tiles_x, int& tlo, int& thi) {
@@ -169,8 +172,9 @@ void ell_row_tiles(const Ell& e, int ty, int W, int H, int tiles_x, int& tlo, in
     const float xr = e.mx + ell_x(e, dyr, 1.f);
     const float xl = e.mx + ell_x(e, dyl, -1.f);
     if (!(xr >= 0.5f && xl <= static_cast<float>(W) - 0.5f)) return;
-    tlo = std::max(static_cast<int>(std::max(ceilf((xl - 15.5f) / 16.f), -1.f)), 0);
-    thi = std::min(static_cast<int>(std::min(floorf((xr - 0.5f) / 16.f), static_cast<float>(tiles_x))), tiles_x - 1);
+    tlo = std::max(static_cast<int>(std::max(ceilf((xl - 15.5f) * 0.0625f), -1.f)), 0);
+    thi = std::min(static_cast<int>(std::min(floorf((xr - 0.5f) * 0.0625f), static_cast<float>(tiles_x))),
+                   tiles_x - 1);
 }
 
 uint32_t depth_order_key(float z) {
@@ -365,7 +369,7 @@ void gs3o_blend(gs3o_ctx* c, int row0, int row1) {
                     const float* co = &c->conic_o[4 * g];
                     const float dx = c->mean2d[2 * g] - pxf, dy = c->mean2d[2 * g + 1] - pyf;
                     const float a2 = -0.5f * kLog2e * co[0], b2 = -kLog2e * co[1], c2 = -0.5f * kLog2e * co[2];
-                    const float q2 = dx * (a2 * dx + b2 * dy) + c2 * dy * dy;
+                    const float q2 = fmaf(dx, fmaf(a2, dx, b2 * dy), c2 * (dy * dy));  // the device's blend_q2
                     const float alpha = co[3] * exp2f(std::min(q2, 0.f));
                     if (alpha < kAlphaMin) continue;
                     const float w = alpha * T;
@@ -413,7 +417,7 @@ void gs3o_blend_backward(gs3o_ctx* c, const float* grad_image, int row0, int row
                     // same float evaluation as the forward, so the same splats pass
                     const float dxf = c->mean2d[2 * g] - (float)pxf, dyf = c->mean2d[2 * g + 1] - (float)pyf;
                     const float a2 = -0.5f * kLog2e * co[0], b2 = -kLog2e * co[1], c2 = -0.5f * kLog2e * co[2];
-                    const float q2 = dxf * (a2 * dxf + b2 * dyf) + c2 * dyf * dyf;
+                    const float q2 = fmaf(dxf, fmaf(a2, dxf, b2 * dyf), c2 * (dyf * dyf));
                     const float Gs = exp2f(std::min(q2, 0.f));
                     const float alpha_f = co[3] * Gs;
                     if (alpha_f < kAlphaMin) continue;

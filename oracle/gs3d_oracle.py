@@ -29,9 +29,9 @@ def depth_order_key(z) -> np.ndarray:
     return np.where(b & np.uint32(0x80000000), ~b, b | np.uint32(0x80000000)).astype(np.uint32)
 
 
-def _x_extent(A, B, R, D, dy, sign):
+def _x_extent(A, B, R, D, inv_a, dy, sign):
     disc = np.maximum((A * R) - ((D * dy) * dy), f32(0))
-    return ((-B) * dy + f32(sign) * np.sqrt(disc)) / A
+    return ((-B) * dy + f32(sign) * np.sqrt(disc)) * inv_a
 
 
 def listed_tiles(mx, my, A, B, C, thr, W: int, H: int):
@@ -41,13 +41,15 @@ def listed_tiles(mx, my, A, B, C, thr, W: int, H: int):
     tiles_x, tiles_y = (W + TILE - 1) // TILE, (H + TILE - 1) // TILE
     R = f32(2) * thr
     D = (A * C) - (B * B)
+    sixteenth = f32(0.0625)
     with np.errstate(all="ignore"):
-        ey = np.sqrt((A * R) / D)
-        s = np.sqrt(R / (D * C))
+        inv_d, inv_c, inv_a = f32(1) / D, f32(1) / C, f32(1) / A  # correctly rounded reciprocals
+        ey = np.sqrt((A * R) * inv_d)
+        s = np.sqrt((R * inv_d) * inv_c)
         top, bot = my - ey, my + ey
         ok = (bot >= f32(0.5)) & (top <= f32(H) - f32(0.5))
-        rlo = np.maximum(np.ceil((top - f32(15.5)) / f32(16)), -1).astype(np.int64)
-        rhi = np.minimum(np.floor((bot - f32(0.5)) / f32(16)), tiles_y).astype(np.int64)
+        rlo = np.maximum(np.ceil((top - f32(15.5)) * sixteenth), -1).astype(np.int64)
+        rhi = np.minimum(np.floor((bot - f32(0.5)) * sixteenth), tiles_y).astype(np.int64)
     rlo = np.maximum(rlo, 0)
     rhi = np.minimum(rhi, tiles_y - 1)
     nrows = np.where(ok, np.maximum(rhi - rlo + 1, 0), 0)
@@ -60,11 +62,11 @@ def listed_tiles(mx, my, A, B, C, thr, W: int, H: int):
         hi = np.minimum(y1 - my[g], ey[g])
         dyr = np.minimum(np.maximum((-B[g]) * s[g], lo), hi)
         dyl = np.minimum(np.maximum(B[g] * s[g], lo), hi)
-        xr = mx[g] + _x_extent(A[g], B[g], R[g], D[g], dyr, 1.0)
-        xl = mx[g] + _x_extent(A[g], B[g], R[g], D[g], dyl, -1.0)
+        xr = mx[g] + _x_extent(A[g], B[g], R[g], D[g], inv_a[g], dyr, 1.0)
+        xl = mx[g] + _x_extent(A[g], B[g], R[g], D[g], inv_a[g], dyl, -1.0)
         row_ok = (lo <= hi) & (xr >= f32(0.5)) & (xl <= f32(W) - f32(0.5))
-        tlo = np.maximum(np.ceil((xl - f32(15.5)) / f32(16)), -1).astype(np.int64)
-        thi = np.minimum(np.floor((xr - f32(0.5)) / f32(16)), tiles_x).astype(np.int64)
+        tlo = np.maximum(np.ceil((xl - f32(15.5)) * sixteenth), -1).astype(np.int64)
+        thi = np.minimum(np.floor((xr - f32(0.5)) * sixteenth), tiles_x).astype(np.int64)
     tlo = np.maximum(tlo, 0)
     thi = np.minimum(thi, tiles_x - 1)
     ncols = np.where(row_ok, np.maximum(thi - tlo + 1, 0), 0)
