@@ -133,29 +133,42 @@ __device__ __forceinline__ uint32_t digit_of(K key, int shift, uint32_t mask) {
     return static_cast<uint32_t>(key >> shift) & mask;
 }
 
+// Lanes of the warp whose digit equals this lane's (among the lanes in `valid`): one ballot per digit bit.
+__device__ __forceinline__ unsigned digit_peers(uint32_t d, int bits, unsigned valid) {
+    unsigned peers = valid;
+#pragma unroll
+    for (int b = 0; b < kRadixBits; ++b) {
+        if (b < bits) {
+            const bool set = (d >> b) & 1u;
+            const unsigned m = __ballot_sync(kFullMask, set);
+            peers &= set ? m : ~m;
+        }
+    }
+    return peers;
+}
+
+// Per-warp privatised counters in shared memory (no cross-warp contention), summed at the end.
 template <typename K>
 __global__ void __launch_bounds__(kSortThreads) k_sort_hist(const K* __restrict__ keys, long long n, int shift,
                                                             uint32_t mask, uint32_t* __restrict__ hist,
                                                             int nblocks) {
-    __shared__ uint32_t s_hist[kRadix];
-    for (int d = threadIdx.x; d < kRadix; d += kSortThreads) s_hist[d] = 0u;
+    constexpr int kWarps = kSortThreads / 32;
+    __shared__ uint32_t s_hist[kWarps][kRadix];
+    const int warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) s_hist[w][threadIdx.x] = 0u;
     __syncthreads();
     const long long base = static_cast<long long>(blockIdx.x) * kSortTile;
-    const int lane = threadIdx.x & 31;
 #pragma unroll 4
     for (int r = 0; r < kSortRounds; ++r) {
         const long long i = base + r * kSortThreads + threadIdx.x;
-        const bool ok = i < n;
-        const unsigned okm = __ballot_sync(kFullMask, ok);
-        if (ok) {
-            const uint32_t d = digit_of(keys[i], shift, mask);
-            const unsigned peers = __match_any_sync(okm, d);
-            if ((peers & ((1u << lane) - 1u)) == 0u) atomicAdd(&s_hist[d], static_cast<uint32_t>(__popc(peers)));
-        }
+        if (i < n) atomicAdd(&s_hist[warp][digit_of(keys[i], shift, mask)], 1u);
     }
     __syncthreads();
-    for (int d = threadIdx.x; d < kRadix; d += kSortThreads)
-        hist[static_cast<long long>(d) * nblocks + blockIdx.x] = s_hist[d];
+    uint32_t total = 0u;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) total += s_hist[w][threadIdx.x];
+    hist[static_cast<long long>(threadIdx.x) * nblocks + blockIdx.x] = total;
 }
 
 template <typename K>
@@ -184,6 +197,7 @@ __global__ void __launch_bounds__(kSortThreads) k_sort_scatter(const K* __restri
     __shared__ uint32_t s_warp[33];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int bits = __popc(mask);
     s_base[tid] = 0u;
     s_goff[tid] = offsets[static_cast<long long>(tid) * nblocks + blockIdx.x];
 #pragma unroll
@@ -209,7 +223,9 @@ __global__ void __launch_bounds__(kSortThreads) k_sort_scatter(const K* __restri
             key[r] = keys_in[base + li];
             val[r] = vals_in[base + li];
             d = digit_of(key[r], shift, mask);
-            const unsigned peers = __match_any_sync(okm, d);
+        }
+        const unsigned peers = digit_peers(d, bits, okm);
+        if (ok) {
             lane_rank = __popc(peers & ((1u << lane) - 1u));
             if (lane_rank == 0u) cnt[warp * kRadix + d] = __popc(peers);
         }

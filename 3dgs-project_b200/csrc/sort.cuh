@@ -15,7 +15,10 @@ constexpr int kScanItems = 4;
 constexpr int kScanTile = kScanThreads * kScanItems;  // 4096 values per scan block
 
 constexpr int kSortThreads = 256;
-constexpr int kSortRounds = 16;
+#ifndef SPLAT_SORT_ROUNDS
+#define SPLAT_SORT_ROUNDS 16
+#endif
+constexpr int kSortRounds = SPLAT_SORT_ROUNDS;
 constexpr int kSortTile = kSortThreads * kSortRounds;  // 4096 pairs per sort block
 constexpr int kRadixBits = 8;
 constexpr int kRadix = 1 << kRadixBits;
