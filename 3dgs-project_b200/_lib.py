@@ -24,10 +24,12 @@ _SZ = ctypes.c_size_t
 _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "splat_last_error": (ctypes.c_char_p, []),
     "splat_abi_version": (_I, []),
+    "splat_launch_count": (_LL, []),
     "splat_scan_workspace_size": (_SZ, [_LL]),
     "splat_scan_exclusive_u32": (_I, [_P, _P, _LL, _P, _P, _SZ, _P]),
     "splat_sort_workspace_size": (_SZ, [_LL, _I]),
     "splat_radix_sort_pairs": (_I, [_P, _P, _P, _P, _LL, _I, _I, _I, _P, _SZ, _P]),
+    "splat_check_device_waits": (_I, []),
     "gs2d_bin_count_workspace_size": (_SZ, [_I]),
     "gs2d_bin_fill_workspace_size": (_SZ, [_LL, _I, _I]),
     "gs2d_bin_count": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _SZ, _P]),
@@ -53,6 +55,8 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gs3d_preprocess": (_I, [_P] * 6 + [_I, _P, _P, _SZ, _P, _P]),
     "gs3d_render": (_I, [_I, _LL, _P, _P, _SZ, _P, _SZ, _P, _SZ, _P, _SZ, _LL, _P, _P]),
     "gs3d_backward": (_I, [_P] * 7 + [_I, _LL, _P] + [_P, _SZ] * 4 + [_LL, _P, _SZ] + [_P] * 7),
+    "gs3d_backward_blend": (_I, [_P, _P, _I, _LL, _P] + [_P, _SZ] * 4 + [_LL, _P, _SZ, _P]),
+    "gs3d_backward_preprocess": (_I, [_P] * 5 + [_I, _P, _P, _SZ, _P, _SZ] + [_P] * 7),
     "adam_step_multi": (_I, [_I, _P, _I, ctypes.c_float, ctypes.c_float, ctypes.c_float, _P]),
 }
 
@@ -88,6 +92,13 @@ def call(name: str, *args) -> None:
     if status != 0:
         msg = lib.splat_last_error().decode(errors="replace")
         raise RuntimeError(f"{name}: {msg} (status {status})")
+
+
+def check_device_waits(device: torch.device) -> None:
+    """Raise if a bounded device-side wait (radix sort look-back) gave up on ``device`` since the last check.
+    Costs one small synchronous copy; call it where the host already waits for the device."""
+    with torch.cuda.device(device):
+        call("splat_check_device_waits")
 
 
 def query(name: str, *args) -> int:

@@ -1,11 +1,16 @@
-// common.cu - error reporting shared by all entry points.
+// common.cu - error reporting and the launch counter shared by all entry points.
+#include <atomic>
+
 #include "common.cuh"
 
 namespace splat {
 
 namespace {
 thread_local char g_error[1024] = "";
-}
+std::atomic<long long> g_launches{0};
+}  // namespace
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 void set_error(const char* fmt, ...) {
     va_list ap;
@@ -42,5 +47,7 @@ extern "C" {
 const char* splat_last_error(void) { return splat::g_error; }
 
 int splat_abi_version(void) { return SPLAT_ABI_VERSION; }
+
+long long splat_launch_count(void) { return splat::g_launches.load(std::memory_order_relaxed); }
 
 }  // extern "C"

@@ -49,6 +49,9 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 // Number of SMs of the current device (cached per device id).
 int sm_count();
 
+// Counts one kernel launch of this library (every launch site calls it; read by splat_launch_count).
+void note_launch();
+
 constexpr unsigned int kFullMask = 0xffffffffu;
 
 // ---- workspace carving: one caller-owned byte buffer split into 256-byte aligned pieces ----

@@ -589,6 +589,7 @@ int gs2d_bin_count(const float* means, const int32_t* radii, const void* depth, 
     const unsigned int blocks = div_up(n, 256);
     k_bin_rect<<<blocks, 256, 0, st>>>(means, radii, depth, depth_is_f64, n, tiles_x, tiles_y,
                                        reinterpret_cast<int4*>(rect), s.counts, s.dkey64, s.dkey32, s.ids);
+    note_launch();
     SPLAT_TRY(check_launch("gs2d_bin_rect"));
     if (depth_is_f64)
         SPLAT_TRY(radix_sort_pairs<unsigned long long>(s.dkey64, s.ids, s.dkey64_sorted, s.ids_sorted, n, 0, 64,
@@ -597,6 +598,7 @@ int gs2d_bin_count(const float* means, const int32_t* radii, const void* depth, 
         SPLAT_TRY(radix_sort_pairs<uint32_t>(s.dkey32, s.ids, s.dkey32_sorted, s.ids_sorted, n, 0, 32, s.sort_ws,
                                              s.sort_ws_bytes, st));
     k_bin_rank<<<blocks, 256, 0, st>>>(s.ids_sorted, n, order, s.rank);
+    note_launch();
     SPLAT_TRY(check_launch("gs2d_bin_rank"));
     SPLAT_TRY(scan_exclusive_u32(s.counts, s.offsets, n, num_instances, s.scan_ws, s.scan_ws_bytes, st));
     return SPLAT_OK;
@@ -622,21 +624,26 @@ int gs2d_bin_fill(const int32_t* rect, int n, int H, int W, long long m, void* c
     if (m > 0) {
         k_bin_duplicate<<<div_up(n, 256), 256, 0, st>>>(reinterpret_cast<const int4*>(rect), s.counts, s.offsets,
                                                         s.rank, n, tiles_x, rank_bits, f.keys, f.vals);
+        note_launch();
         SPLAT_TRY(check_launch("gs2d_bin_duplicate"));
         SPLAT_TRY(radix_sort_pairs<unsigned long long>(f.keys, f.vals, f.keys_sorted, f.vals_sorted, m, 0,
                                                        rank_bits + tile_bits, f.sort_ws, f.sort_ws_bytes, st));
         k_bin_runs<<<div_up(m, 256), 256, 0, st>>>(f.keys_sorted, f.vals_sorted, static_cast<int>(m), rank_bits,
                                                    f.first, f.last, point_list);
+        note_launch();
         SPLAT_TRY(check_launch("gs2d_bin_runs"));
     }
     k_bin_tile_counts<<<div_up(T, 256), 256, 0, st>>>(f.first, f.last, T, f.count, f.nb);
+    note_launch();
     SPLAT_TRY(check_launch("gs2d_bin_tile_counts"));
     SPLAT_TRY(scan_exclusive_u32(f.count, f.start, T, nullptr, f.scan_ws, f.scan_ws_bytes, st));
     SPLAT_TRY(scan_exclusive_u32(f.nb, f.bstart, T, num_buckets, f.scan_ws, f.scan_ws_bytes, st));
     k_bin_ranges<<<div_up(T, 256), 256, 0, st>>>(f.count, f.start, f.bstart, T, ranges, bucket_offsets);
+    note_launch();
     SPLAT_TRY(check_launch("gs2d_bin_ranges"));
     if (bucket_to_tile) {
         k_bin_bucket_tiles<<<div_up(T, 256), 256, 0, st>>>(f.nb, f.bstart, T, bucket_to_tile);
+        note_launch();
         SPLAT_TRY(check_launch("gs2d_bin_bucket_tiles"));
     }
     return SPLAT_OK;
@@ -657,6 +664,7 @@ int gs2d_forward(const float* means, const float* conic, const float* color, con
         reinterpret_cast<const int2*>(ranges), point_list, means, conic, color, opacity, bg, N,
         static_cast<int>(num_instances), num_buckets, W, H, tiles_x, out, final_T, n_contrib, bucket_offsets,
         (save_buckets && num_buckets > 0) ? reinterpret_cast<float4*>(bucket_state) : nullptr);
+    note_launch();
     return check_launch("gs2d_forward");
 }
 
@@ -677,6 +685,7 @@ int gs2d_backward_pixel(const float* means, const float* conic, const float* col
     k_backward_pixel<<<dim3(tiles_x, tiles_y), kBlock, 0, st>>>(
         reinterpret_cast<const int2*>(ranges), point_list, means, conic, color, opacity, bg, N,
         static_cast<int>(num_instances), W, H, tiles_x, final_T, n_contrib, dL_dout, dmeans, dconic, dcolor, dopacity);
+    note_launch();
     return check_launch("gs2d_backward_pixel");
 }
 
@@ -701,6 +710,7 @@ int gs2d_backward_splat(const float* means, const float* conic, const float* col
         color, opacity, N, static_cast<int>(num_instances), W, H, tiles_x, out, n_contrib, dL_dout,
         reinterpret_cast<const float4*>(bucket_state), dmeans,
         dconic, dcolor, dopacity);
+    note_launch();
     return check_launch("gs2d_backward_splat");
 }
 

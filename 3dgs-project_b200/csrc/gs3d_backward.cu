@@ -520,13 +520,11 @@ size_t gs3d_backward_workspace_size(int n) {
     return c.used + 256;
 }
 
-int gs3d_backward(const float* grad_image, const float* image, const float* means, const float* scales,
-                  const float* rotations, const float* opacities, const float* sh_rest, int n, long long num_instances,
-                  const gs3d_settings* settings, void* prim_buf, size_t prim_bytes_, void* tile_buf,
-                  size_t tile_bytes_, void* inst_buf, size_t inst_bytes_, void* bucket_buf, size_t bucket_bytes_,
-                  long long bucket_capacity, void* workspace, size_t workspace_bytes, float* grad_means,
-                  float* grad_scales, float* grad_rotations, float* grad_opacities, float* grad_sh0,
-                  float* grad_sh_rest, void* stream) {
+int gs3d_backward_blend(const float* grad_image, const float* image, int n, long long num_instances,
+                        const gs3d_settings* settings, void* prim_buf, size_t prim_bytes_, void* tile_buf,
+                        size_t tile_bytes_, void* inst_buf, size_t inst_bytes_, void* bucket_buf,
+                        size_t bucket_bytes_, long long bucket_capacity, void* workspace, size_t workspace_bytes,
+                        void* stream) {
     Cam cam;
     SPLAT_TRY(fill_cam(settings, cam));
     const long long m = num_instances;
@@ -546,20 +544,53 @@ int gs3d_backward(const float* grad_image, const float* image, const float* mean
     InstBuffers ib = carve_inst(ci, m);
     BucketBuffers bb = carve_bucket(cb, bucket_capacity);
     GradAcc acc = carve_grad(cw, n);
-    const size_t acc_bytes = cw.used;
-    SPLAT_CUDA(cudaMemsetAsync(workspace, 0, acc_bytes, st));
+    SPLAT_CUDA(cudaMemsetAsync(workspace, 0, cw.used, st));
     if (m > 0) {
         k_blend_backward<<<div_up(bucket_capacity, kBwdWarps), 32 * kBwdWarps, 0, st>>>(
             cam, pb.counters, bb.tile, tb.ranges, tb.bstart, tb.max_contrib, ib.point_list, pb.mean2d, pb.conic_o,
             pb.color_z, pb.rect, grad_image, image, tb.n_contrib, bb.ckpt, n, static_cast<int>(m), bucket_capacity,
             acc);
+        note_launch();
         SPLAT_TRY(check_launch("gs3d_blend_backward"));
     }
+    return SPLAT_OK;
+}
+
+int gs3d_backward_preprocess(const float* means, const float* scales, const float* rotations,
+                             const float* opacities, const float* sh_rest, int n, const gs3d_settings* settings,
+                             void* prim_buf, size_t prim_bytes_, void* workspace, size_t workspace_bytes,
+                             float* grad_means, float* grad_scales, float* grad_rotations, float* grad_opacities,
+                             float* grad_sh0, float* grad_sh_rest, void* stream) {
+    Cam cam;
+    SPLAT_TRY(fill_cam(settings, cam));
+    SPLAT_REQUIRE(n >= 0, "gs3d_backward: bad size n=%d", n);
+    SPLAT_REQUIRE(prim_bytes_ >= prim_bytes(n) && workspace_bytes >= gs3d_backward_workspace_size(n),
+                  "gs3d_backward: a buffer is smaller than its size query");
+    if (n == 0) return SPLAT_OK;
+    Carver cp(prim_buf, prim_bytes_), cw(workspace, workspace_bytes);
+    PrimBuffers pb = carve_prim(cp, n);
+    GradAcc acc = carve_grad(cw, n);
     PParams P{means, scales, rotations, opacities, sh_rest, settings->w2c, settings->cam_position, n};
     Grads g{grad_means, grad_scales, grad_rotations, grad_opacities, grad_sh0, grad_sh_rest};
     const size_t smem = static_cast<size_t>(kPbWarps) * 32 * cam.rest_bases * 3 * sizeof(float);
-    k_preprocess_backward<<<div_up(n, kPbThreads), kPbThreads, smem, st>>>(P, cam, pb, acc, g);
+    k_preprocess_backward<<<div_up(n, kPbThreads), kPbThreads, smem, as_stream(stream)>>>(P, cam, pb, acc, g);
+    note_launch();
     return check_launch("gs3d_preprocess_backward");
+}
+
+int gs3d_backward(const float* grad_image, const float* image, const float* means, const float* scales,
+                  const float* rotations, const float* opacities, const float* sh_rest, int n, long long num_instances,
+                  const gs3d_settings* settings, void* prim_buf, size_t prim_bytes_, void* tile_buf,
+                  size_t tile_bytes_, void* inst_buf, size_t inst_bytes_, void* bucket_buf, size_t bucket_bytes_,
+                  long long bucket_capacity, void* workspace, size_t workspace_bytes, float* grad_means,
+                  float* grad_scales, float* grad_rotations, float* grad_opacities, float* grad_sh0,
+                  float* grad_sh_rest, void* stream) {
+    SPLAT_TRY(gs3d_backward_blend(grad_image, image, n, num_instances, settings, prim_buf, prim_bytes_, tile_buf,
+                                  tile_bytes_, inst_buf, inst_bytes_, bucket_buf, bucket_bytes_, bucket_capacity,
+                                  workspace, workspace_bytes, stream));
+    return gs3d_backward_preprocess(means, scales, rotations, opacities, sh_rest, n, settings, prim_buf,
+                                    prim_bytes_, workspace, workspace_bytes, grad_means, grad_scales, grad_rotations,
+                                    grad_opacities, grad_sh0, grad_sh_rest, stream);
 }
 
 }  // extern "C"

@@ -419,11 +419,13 @@ int gs3d_preprocess(const float* means, const float* scales, const float* rotati
         configured = true;
     }
     k_preprocess<<<div_up(n, kPreThreads), kPreThreads, smem, st>>>(P, cam, pb);
+    note_launch();
     SPLAT_TRY(check_launch("gs3d_preprocess"));
     // the depth-digit passes of the (tile << 32 | depth) key sort, on the Gaussians before duplication
     SPLAT_TRY(radix_sort_pairs<uint32_t>(pb.depth_key, pb.ids, pb.depth_key_sorted, pb.order, n, 0, 32, pb.sort_ws,
                                          pb.sort_bytes, st));
     k_gather_counts<<<div_up(n, 256), 256, 0, st>>>(pb.order, pb.n_touched, n, pb.offsets);
+    note_launch();
     SPLAT_TRY(check_launch("gs3d_gather_counts"));
     SPLAT_TRY(scan_exclusive_u32(pb.offsets, pb.offsets, n, pb.counters, pb.scan_ws, pb.scan_bytes, st));
     if (num_instances)
@@ -454,22 +456,27 @@ int gs3d_render(int n, long long num_instances, const gs3d_settings* settings, v
     SPLAT_CUDA(cudaMemsetAsync(tb.ranges, 0, sizeof(uint2) * T, st));
     if (m > 0) {
         k_duplicate<<<div_up(n, 256), 256, 0, st>>>(n, cam, pb, ib);
+        note_launch();
         SPLAT_TRY(check_launch("gs3d_duplicate"));
         // the tile-digit passes (the pad key T needs bit_width(T) bits)
         const int tile_bits = bit_width(static_cast<unsigned long long>(T));
         SPLAT_TRY(radix_sort_pairs<uint32_t>(ib.keys, ib.vals, ib.keys_sorted, ib.point_list, m, 0, tile_bits,
                                              ib.sort_ws, ib.sort_bytes, st));
         k_ranges<<<div_up(m, 256), 256, 0, st>>>(ib.keys_sorted, static_cast<int>(m), T, tb.ranges);
+        note_launch();
         SPLAT_TRY(check_launch("gs3d_ranges"));
     }
     k_bucket_counts<<<div_up(T + 1, 256), 256, 0, st>>>(tb.ranges, T, tb.nb);
+    note_launch();
     SPLAT_TRY(check_launch("gs3d_bucket_counts"));
     SPLAT_TRY(scan_exclusive_u32(tb.nb, tb.bstart, T + 1, pb.counters + 1, tb.scan_ws, tb.scan_bytes, st));
     k_bucket_tiles<<<div_up(T, 256), 256, 0, st>>>(tb.nb, tb.bstart, T, bucket_capacity, bb.tile);
+    note_launch();
     SPLAT_TRY(check_launch("gs3d_bucket_tiles"));
     k_blend<<<T, kTilePixels, 0, st>>>(cam, tb.ranges, tb.bstart, ib.point_list, pb.mean2d, pb.conic_o, pb.color_z,
                                        pb.rect, settings->bg, image, tb.final_T, tb.n_contrib, tb.max_contrib, bb.ckpt,
                                        n < 1 ? 1 : n, static_cast<int>(m), bucket_capacity);
+    note_launch();
     return check_launch("gs3d_blend");
 }
 

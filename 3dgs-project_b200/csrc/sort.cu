@@ -1,14 +1,22 @@
 // sort.cu - device-wide exclusive scan and stable LSD radix sort.
 //
 // Scan: reduce-then-scan in three launches (block sums, one-block scan of the sums, block scans
-// plus offsets). Radix sort: per 8-bit digit a histogram launch (warp-aggregated shared-memory
-// counters), a scan of the digit-major [digit][block] count table, and a scatter launch that ranks
-// the block's 4096 pairs stably in shared memory (match.any per warp, warp-ordered prefix per digit)
-// and writes them out digit run by digit run, so consecutive threads store consecutive addresses.
+// plus offsets). Radix sort: one launch counts the digits of every pass in a single read of the keys,
+// one block turns the counts into each digit's first output slot, then one launch per 8-bit digit
+// ranks each tile of pairs stably in shared memory (ballot-based digit peers per warp, warp-ordered
+// prefix per digit), finds the tile's global offsets by decoupled look-back over the counts the
+// earlier tiles publish, and writes the pairs out digit run by digit run, so consecutive threads store
+// consecutive addresses.
+#include <algorithm>
+
 #include "sort.cuh"
 
 namespace splat {
 namespace {
+
+// Bounded device-side waits that gave up (look-back of the radix sort), per device; read and cleared by
+// splat_check_device_waits.
+__device__ unsigned int g_wait_timeouts = 0u;
 
 __device__ __forceinline__ uint32_t warp_inclusive_scan(uint32_t v, int lane) {
 #pragma unroll
@@ -147,111 +155,212 @@ __device__ __forceinline__ unsigned digit_peers(uint32_t d, int bits, unsigned v
     return peers;
 }
 
-// Per-warp privatised counters in shared memory (no cross-warp contention), summed at the end.
+// Digit counts of every pass in one read of the keys: per-warp shared counters (dynamic shared memory,
+// [passes][warp][digit]), loads batched kHistUnroll deep, then one global atomic per (pass, digit) and block.
+constexpr int kHistUnroll = 4;
+
 template <typename K>
-__global__ void __launch_bounds__(kSortThreads) k_sort_hist(const K* __restrict__ keys, long long n, int shift,
-                                                            uint32_t mask, uint32_t* __restrict__ hist,
-                                                            int nblocks) {
+__global__ void __launch_bounds__(kSortThreads) k_sort_global_hist(const K* __restrict__ keys, long long n,
+                                                                   int begin_bit, int end_bit, int passes,
+                                                                   uint32_t* __restrict__ hist) {
     constexpr int kWarps = kSortThreads / 32;
-    __shared__ uint32_t s_hist[kWarps][kRadix];
-    const int warp = threadIdx.x >> 5;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) s_hist[w][threadIdx.x] = 0u;
+    extern __shared__ uint32_t s_whist[];
+    uint32_t* mine = s_whist + (threadIdx.x >> 5) * kRadix;
+    for (int i = threadIdx.x; i < passes * kWarps * kRadix; i += kSortThreads) s_whist[i] = 0u;
     __syncthreads();
-    const long long base = static_cast<long long>(blockIdx.x) * kSortTile;
-#pragma unroll 4
-    for (int r = 0; r < kSortRounds; ++r) {
-        const long long i = base + r * kSortThreads + threadIdx.x;
-        if (i < n) atomicAdd(&s_hist[warp][digit_of(keys[i], shift, mask)], 1u);
+    const long long stride = static_cast<long long>(gridDim.x) * kSortThreads;
+    auto count = [&](K k) {
+        for (int p = 0; p < passes; ++p) {
+            const int shift = begin_bit + p * kRadixBits;
+            const uint32_t mask = (1u << min(kRadixBits, end_bit - shift)) - 1u;
+            atomicAdd(&mine[p * kWarps * kRadix + digit_of(k, shift, mask)], 1u);
+        }
+    };
+    long long i = static_cast<long long>(blockIdx.x) * kSortThreads + threadIdx.x;
+    for (; i + (kHistUnroll - 1) * stride < n; i += kHistUnroll * stride) {
+        K k[kHistUnroll];
+#pragma unroll
+        for (int u = 0; u < kHistUnroll; ++u) k[u] = keys[i + u * stride];
+#pragma unroll
+        for (int u = 0; u < kHistUnroll; ++u) count(k[u]);
     }
+    for (; i < n; i += stride) count(keys[i]);
     __syncthreads();
-    uint32_t total = 0u;
+    for (int p = 0; p < passes; ++p) {
+        uint32_t total = 0u;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) total += s_hist[w][threadIdx.x];
-    hist[static_cast<long long>(threadIdx.x) * nblocks + blockIdx.x] = total;
+        for (int w = 0; w < kWarps; ++w) total += s_whist[(p * kWarps + w) * kRadix + threadIdx.x];
+        if (total) atomicAdd(&hist[p * kRadix + threadIdx.x], total);
+    }
+}
+
+constexpr size_t global_hist_smem_bytes(int passes) {
+    return static_cast<size_t>(passes) * (kSortThreads / 32) * kRadix * sizeof(uint32_t);
+}
+
+// hist[p][d] -> first output slot of digit d in pass p (exclusive prefix), one block.
+__global__ void __launch_bounds__(kSortThreads) k_sort_digit_base(uint32_t* __restrict__ hist, int passes) {
+    __shared__ uint32_t s_warp[33];
+    for (int p = 0; p < passes; ++p) {
+        uint32_t total;
+        const uint32_t v = hist[p * kRadix + threadIdx.x];
+        hist[p * kRadix + threadIdx.x] = block_exclusive_scan(v, s_warp, total);
+    }
+}
+
+// Look-back status words, one per (tile, digit): two flag bits over a 30-bit count.
+constexpr uint32_t kAggregateFlag = 1u << 30;  // count of this tile alone
+constexpr uint32_t kPrefixFlag = 2u << 30;     // count of this tile and every tile before it
+constexpr uint32_t kFlagMask = 3u << 30;
+constexpr uint32_t kCountMask = kAggregateFlag - 1u;
+// Polls of one digit's look-back before it gives up (about a second with the back-off below; a tile
+// normally waits a few microseconds).
+constexpr int kLookbackPollLimit = 1 << 20;
+#ifndef SPLAT_LOOKBACK_WINDOW
+#define SPLAT_LOOKBACK_WINDOW 4
+#endif
+constexpr int kLookbackWindow = SPLAT_LOOKBACK_WINDOW;  // earlier tiles' status words fetched per round trip
+
+__device__ __forceinline__ uint32_t load_status(const uint32_t* p) {
+    return *reinterpret_cast<const volatile uint32_t*>(p);
+}
+
+__device__ __forceinline__ void store_status(uint32_t* p, uint32_t v) {
+    *reinterpret_cast<volatile uint32_t*>(p) = v;
 }
 
 template <typename K>
 constexpr size_t scatter_smem_bytes() {
     return kSortTile * sizeof(K) + kSortTile * sizeof(uint32_t) +
-           (2 * (kSortThreads / 32) * kRadix + 3 * kRadix) * sizeof(uint32_t);
+           ((kSortThreads / 32) * kRadix + 2 * kRadix) * sizeof(uint32_t);
 }
 
+// Number of earlier pairs of digit `tid` over all tiles before `tile`: walks back over the status words,
+// kLookbackWindow tiles per round trip, summing counts up to and including the first inclusive prefix.
+__device__ __forceinline__ uint32_t look_back(const uint32_t* status, long long tile, int tid) {
+    uint32_t excl = 0u;
+    long long j = tile - 1;
+    int polls = 0;
+    while (true) {
+        uint32_t st[kLookbackWindow];
+#pragma unroll
+        for (int q = 0; q < kLookbackWindow; ++q)
+            st[q] = j - q >= 0 ? load_status(status + (j - q) * kRadix + tid) : 0u;
+        int used = 0;
+        bool done = false;
+#pragma unroll
+        for (int q = 0; q < kLookbackWindow; ++q) {
+            // stop at the first tile that has published nothing yet; tile 0 always publishes a prefix,
+            // so no entry past it (j - q < 0) is ever consumed
+            if (done || used < q || !(st[q] & kFlagMask)) continue;
+            excl += st[q] & kCountMask;
+            used = q + 1;
+            done = (st[q] & kPrefixFlag) != 0u;
+        }
+        if (done) break;
+        j -= used;
+        if (used == 0) {
+            if (++polls >= kLookbackPollLimit) {
+                atomicAdd(&g_wait_timeouts, 1u);
+                break;
+            }
+            if (polls > 32) __nanosleep(64);
+        }
+    }
+    return excl;
+}
+
+// One digit pass in one launch. Tiles are taken in launch order from a ticket counter. Warp w of a tile
+// owns the tile's pairs [w * 32 * kSortRounds, (w + 1) * 32 * kSortRounds) and ranks them round by round
+// against its own per-digit counters (ballot-based peers, no atomics, no block barrier); one block
+// barrier later the per-warp counts give each warp's base per digit and the tile's per-digit totals. The
+// totals are published, and the number of earlier pairs of each digit is found by looking back over the
+// totals of the tiles before (stopping at the first tile that has published an inclusive prefix). A tile
+// only waits on tiles that took their ticket earlier, which are running; every wait is bounded, and on
+// timeout the wait counter is raised and the pass completes (with wrong offsets) instead of hanging.
+// Pairs are then placed in digit order in shared memory and written out digit run by digit run.
 template <typename K>
-__global__ void __launch_bounds__(kSortThreads) k_sort_scatter(const K* __restrict__ keys_in,
+__global__ void __launch_bounds__(kSortThreads, kSortMinBlocks) k_sort_scatter(const K* __restrict__ keys_in,
                                                                const uint32_t* __restrict__ vals_in,
                                                                K* __restrict__ keys_out,
                                                                uint32_t* __restrict__ vals_out, long long n,
                                                                int shift, uint32_t mask,
-                                                               const uint32_t* __restrict__ offsets,
-                                                               int nblocks) {
+                                                               const uint32_t* __restrict__ digit_base,
+                                                               uint32_t* __restrict__ status,
+                                                               uint32_t* __restrict__ ticket) {
     static_assert(kRadix == kSortThreads, "one thread per digit");
     constexpr int kWarps = kSortThreads / 32;
+    constexpr int kWarpItems = 32 * kSortRounds;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     K* s_keys = reinterpret_cast<K*>(smem_raw);
     uint32_t* s_vals = reinterpret_cast<uint32_t*>(s_keys + kSortTile);
-    uint32_t* s_cnt = s_vals + kSortTile;          // [2][kWarps][kRadix]
-    uint32_t* s_base = s_cnt + 2 * kWarps * kRadix;  // running count per digit
-    uint32_t* s_start = s_base + kRadix;             // first slot of each digit in the sorted tile
-    uint32_t* s_goff = s_start + kRadix;             // first global slot of each digit for this block
+    uint32_t* s_cnt = s_vals + kSortTile;          // [kWarps][kRadix]: running counts, then warp bases
+    uint32_t* s_start = s_cnt + kWarps * kRadix;   // first slot of each digit in the sorted tile
+    uint32_t* s_goff = s_start + kRadix;           // first global slot of each digit for this tile
     __shared__ uint32_t s_warp[33];
+    __shared__ uint32_t s_tile;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int bits = __popc(mask);
-    s_base[tid] = 0u;
-    s_goff[tid] = offsets[static_cast<long long>(tid) * nblocks + blockIdx.x];
+    if (tid == 0) s_tile = atomicAdd(ticket, 1u);
 #pragma unroll
-    for (int w = 0; w < 2 * kWarps; ++w) s_cnt[w * kRadix + tid] = 0u;
+    for (int w = 0; w < kWarps; ++w) s_cnt[w * kRadix + tid] = 0u;
     __syncthreads();
-
-    const long long base = static_cast<long long>(blockIdx.x) * kSortTile;
+    const long long tile = s_tile;
+    const long long base = tile * kSortTile;
     const int tile_n = static_cast<int>(min(static_cast<long long>(kSortTile), n - base));
+    const int wbase = warp * kWarpItems;
+
     K key[kSortRounds];
     uint32_t val[kSortRounds];
     uint32_t rank[kSortRounds];
 #pragma unroll
-    for (int r = 0; r < kSortRounds; ++r) {
-        uint32_t* cnt = s_cnt + (r & 1) * kWarps * kRadix;
-        uint32_t* cnt_prev = s_cnt + ((r + 1) & 1) * kWarps * kRadix;
-        const int li = r * kSortThreads + tid;
-        const bool ok = li < tile_n;
-        uint32_t d = 0u, lane_rank = 0u;
-        key[r] = K(0);
-        val[r] = 0u;
-        const unsigned okm = __ballot_sync(kFullMask, ok);
-        if (ok) {
-            key[r] = keys_in[base + li];
-            val[r] = vals_in[base + li];
-            d = digit_of(key[r], shift, mask);
-        }
-        const unsigned peers = digit_peers(d, bits, okm);
-        if (ok) {
-            lane_rank = __popc(peers & ((1u << lane) - 1u));
-            if (lane_rank == 0u) cnt[warp * kRadix + d] = __popc(peers);
-        }
-        __syncthreads();
-        {   // thread tid owns digit tid: warp-ordered exclusive prefix, then the running count
-            uint32_t run = s_base[tid];
+    for (int r = 0; r < kSortRounds; ++r) {  // every load in flight before the ranking starts
+        const int li = wbase + r * 32 + lane;
+        key[r] = li < tile_n ? keys_in[base + li] : K(0);
+        val[r] = li < tile_n ? vals_in[base + li] : 0u;
+    }
+    uint32_t* cnt = s_cnt + warp * kRadix;
+    const unsigned lanes_below = (1u << lane) - 1u;
 #pragma unroll
-            for (int w = 0; w < kWarps; ++w) {
-                const uint32_t c = cnt[w * kRadix + tid];
-                cnt[w * kRadix + tid] = run;
-                run += c;
-                cnt_prev[w * kRadix + tid] = 0u;  // every read of the previous round's table is done
-            }
-            s_base[tid] = run;
-        }
-        __syncthreads();
-        rank[r] = ok ? cnt[warp * kRadix + d] + lane_rank : 0u;
+    for (int r = 0; r < kSortRounds; ++r) {
+        const bool ok = wbase + r * 32 + lane < tile_n;
+        const unsigned okm = __ballot_sync(kFullMask, ok);
+        const uint32_t d = ok ? digit_of(key[r], shift, mask) : 0u;
+        const unsigned peers = digit_peers(d, bits, okm);
+        const uint32_t below = __popc(peers & lanes_below);
+        const uint32_t prior = ok ? cnt[d] : 0u;
+        __syncwarp();
+        if (ok && below == 0u) cnt[d] = prior + __popc(peers);
+        __syncwarp();
+        rank[r] = prior + below;
+    }
+    __syncthreads();
+    uint32_t count = 0u;  // thread tid owns digit tid: per-warp counts -> warp bases, tile total
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+        const uint32_t c = s_cnt[w * kRadix + tid];
+        s_cnt[w * kRadix + tid] = count;
+        count += c;
+    }
+    uint32_t* mine = status + tile * kRadix + tid;
+    if (tile == 0) {
+        store_status(mine, kPrefixFlag | count);
+        s_goff[tid] = digit_base[tid];
+    } else {
+        store_status(mine, kAggregateFlag | count);
+        const uint32_t excl = look_back(status, tile, tid);
+        store_status(mine, kPrefixFlag | (excl + count));
+        s_goff[tid] = digit_base[tid] + excl;
     }
     uint32_t btotal;
-    s_start[tid] = block_exclusive_scan(s_base[tid], s_warp, btotal);
+    s_start[tid] = block_exclusive_scan(count, s_warp, btotal);  // its barriers publish s_cnt and s_goff too
     __syncthreads();
 #pragma unroll
     for (int r = 0; r < kSortRounds; ++r) {
-        const int li = r * kSortThreads + tid;
-        if (li < tile_n) {
-            const uint32_t pos = s_start[digit_of(key[r], shift, mask)] + rank[r];
+        if (wbase + r * 32 + lane < tile_n) {
+            const uint32_t d = digit_of(key[r], shift, mask);
+            const uint32_t pos = s_start[d] + s_cnt[warp * kRadix + d] + rank[r];
             s_keys[pos] = key[r];
             s_vals[pos] = val[r];
         }
@@ -272,6 +381,8 @@ int configure_scatter() {
     if (!done) {
         SPLAT_CUDA(cudaFuncSetAttribute(k_sort_scatter<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(scatter_smem_bytes<K>())));
+        SPLAT_CUDA(cudaFuncSetAttribute(k_sort_global_hist<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(global_hist_smem_bytes(kMaxPasses))));
         done = true;
     }
     return SPLAT_OK;
@@ -295,11 +406,16 @@ int scan_exclusive_u32(const uint32_t* in, uint32_t* out, long long n, uint32_t*
     const unsigned int nb = div_up(n, kScanTile);
     uint32_t* partial = static_cast<uint32_t*>(ws);
     k_scan_reduce<<<nb, kScanThreads, 0, stream>>>(in, n, partial);
+    note_launch();
     k_scan_partials<<<1, kScanThreads, 0, stream>>>(partial, nb, total);
+    note_launch();
     k_scan_apply<<<nb, kScanThreads, 0, stream>>>(in, out, n, partial);
+    note_launch();
     return check_launch("scan_exclusive_u32");
 }
 
+// Workspace layout: alternate keys / values, then one zeroed block (digit counts of every pass, one tile
+// ticket per pass, look-back status words of every pass and tile).
 template <typename K>
 size_t sort_workspace_bytes(long long n) {
     if (n < 1) n = 1;
@@ -307,8 +423,8 @@ size_t sort_workspace_bytes(long long n) {
     Carver c(nullptr, 0);
     c.take<K>(n);
     c.take<uint32_t>(n);
-    c.take<uint32_t>(nb * kRadix);
-    c.take<unsigned char>(scan_workspace_bytes(nb * kRadix));
+    c.take<uint32_t>(kMaxPasses * kRadix + kMaxPasses);
+    c.take<uint32_t>(static_cast<size_t>(sizeof(K)) * nb * kRadix);
     return c.used + 256;
 }
 
@@ -318,7 +434,8 @@ int radix_sort_pairs(const K* keys_in, const uint32_t* vals_in, K* keys_out, uin
     constexpr int kKeyBits = static_cast<int>(sizeof(K) * 8);
     SPLAT_REQUIRE(0 <= begin_bit && begin_bit <= end_bit && end_bit <= kKeyBits, "bad bit range [%d, %d)",
                   begin_bit, end_bit);
-    SPLAT_REQUIRE(n >= 0 && n < (1ll << 31), "sort size %lld out of range", n);
+    SPLAT_REQUIRE(n >= 0 && n <= static_cast<long long>(kCountMask), "sort size %lld out of range (max %u)", n,
+                  kCountMask);
     if (n == 0) return SPLAT_OK;
     const int passes = (end_bit - begin_bit + kRadixBits - 1) / kRadixBits;
     if (passes == 0) {
@@ -329,12 +446,23 @@ int radix_sort_pairs(const K* keys_in, const uint32_t* vals_in, K* keys_out, uin
     SPLAT_REQUIRE(ws_bytes >= sort_workspace_bytes<K>(n), "sort workspace too small (%zu < %zu)", ws_bytes,
                   sort_workspace_bytes<K>(n));
     SPLAT_TRY(configure_scatter<K>());
-    const int nb = static_cast<int>(div_up(n, kSortTile));
+    const long long nb = div_up(n, kSortTile);
     Carver c(ws, ws_bytes);
     K* alt_keys = c.take<K>(n);
     uint32_t* alt_vals = c.take<uint32_t>(n);
-    uint32_t* hist = c.take<uint32_t>(static_cast<size_t>(nb) * kRadix);
-    void* scan_ws = c.take<unsigned char>(scan_workspace_bytes(static_cast<long long>(nb) * kRadix));
+    uint32_t* hist = c.take<uint32_t>(kMaxPasses * kRadix + kMaxPasses);
+    uint32_t* tickets = hist + kMaxPasses * kRadix;
+    uint32_t* status = c.take<uint32_t>(static_cast<size_t>(sizeof(K)) * nb * kRadix);
+    // hist, tickets and status are contiguous: one memset clears what this sort uses of them.
+    const size_t zero_bytes = reinterpret_cast<unsigned char*>(status + static_cast<size_t>(passes) * nb * kRadix) -
+                              reinterpret_cast<unsigned char*>(hist);
+    SPLAT_CUDA(cudaMemsetAsync(hist, 0, zero_bytes, stream));
+    const long long hist_blocks = std::min<long long>(div_up(n, kSortThreads * 8), 4ll * sm_count());
+    k_sort_global_hist<K><<<static_cast<unsigned>(hist_blocks), kSortThreads, global_hist_smem_bytes(passes),
+                            stream>>>(keys_in, n, begin_bit, end_bit, passes, hist);
+    note_launch();
+    k_sort_digit_base<<<1, kSortThreads, 0, stream>>>(hist, passes);
+    note_launch();
     const K* src_k = keys_in;
     const uint32_t* src_v = vals_in;
     for (int p = 0; p < passes; ++p) {
@@ -344,15 +472,25 @@ int radix_sort_pairs(const K* keys_in, const uint32_t* vals_in, K* keys_out, uin
         const bool to_out = ((passes - 1 - p) % 2) == 0;
         K* dst_k = to_out ? keys_out : alt_keys;
         uint32_t* dst_v = to_out ? vals_out : alt_vals;
-        k_sort_hist<K><<<nb, kSortThreads, 0, stream>>>(src_k, n, shift, mask, hist, nb);
-        SPLAT_TRY(scan_exclusive_u32(hist, hist, static_cast<long long>(nb) * kRadix, nullptr, scan_ws,
-                                     scan_workspace_bytes(static_cast<long long>(nb) * kRadix), stream));
-        k_sort_scatter<K><<<nb, kSortThreads, scatter_smem_bytes<K>(), stream>>>(src_k, src_v, dst_k, dst_v, n,
-                                                                                 shift, mask, hist, nb);
+        k_sort_scatter<K><<<static_cast<unsigned>(nb), kSortThreads, scatter_smem_bytes<K>(), stream>>>(
+            src_k, src_v, dst_k, dst_v, n, shift, mask, hist + p * kRadix,
+            status + static_cast<size_t>(p) * nb * kRadix, tickets + p);
+        note_launch();
         SPLAT_TRY(check_launch("radix_sort_pairs"));
         src_k = dst_k;
         src_v = dst_v;
     }
+    return SPLAT_OK;
+}
+
+int take_wait_timeouts(unsigned int* count) {
+    unsigned int h = 0u;
+    SPLAT_CUDA(cudaMemcpyFromSymbol(&h, g_wait_timeouts, sizeof(h)));
+    if (h) {
+        const unsigned int zero = 0u;
+        SPLAT_CUDA(cudaMemcpyToSymbol(g_wait_timeouts, &zero, sizeof(zero)));
+    }
+    *count = h;
     return SPLAT_OK;
 }
 
@@ -380,6 +518,18 @@ int splat_scan_exclusive_u32(const uint32_t* in, uint32_t* out, long long n, uin
 size_t splat_sort_workspace_size(long long n, int key_bytes) {
     return key_bytes == 8 ? splat::sort_workspace_bytes<unsigned long long>(n)
                           : splat::sort_workspace_bytes<uint32_t>(n);
+}
+
+int splat_check_device_waits(void) {
+    unsigned int n = 0u;
+    SPLAT_TRY(splat::take_wait_timeouts(&n));
+    if (n) {
+        splat::set_error("%u bounded device-side wait(s) gave up (radix sort look-back); results since the last "
+                         "check are unreliable",
+                         n);
+        return SPLAT_ERR_TIMEOUT;
+    }
+    return SPLAT_OK;
 }
 
 int splat_radix_sort_pairs(const void* keys_in, const uint32_t* vals_in, void* keys_out, uint32_t* vals_out,

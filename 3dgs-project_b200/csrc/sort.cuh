@@ -1,9 +1,10 @@
 // sort.cuh - device-wide exclusive scan and stable LSD radix sort (internal API).
 //
 // Both are written for this library instead of calling CUB: the scan feeds the tile-instance and
-// bucket offsets, the sort orders the 64-bit (tile | depth) instance keys. Neither spins on flags
-// set by other blocks (reduce-then-scan, one histogram / scan / scatter triple per 8-bit digit), so
-// no launch can wait forever on another block.
+// bucket offsets, the sort orders the (tile | depth) instance keys. The scan never waits on other
+// blocks (reduce-then-scan). The sort is single-sweep per 8-bit digit: its scatter blocks look back
+// over counts published by earlier blocks; every such wait is bounded, and a wait that gives up is
+// counted on the device and reported by splat_check_device_waits instead of hanging the launch.
 #pragma once
 
 #include "common.cuh"
@@ -19,9 +20,14 @@ constexpr int kSortThreads = 256;
 #define SPLAT_SORT_ROUNDS 16
 #endif
 constexpr int kSortRounds = SPLAT_SORT_ROUNDS;
-constexpr int kSortTile = kSortThreads * kSortRounds;  // 4096 pairs per sort block
+#ifndef SPLAT_SORT_MIN_BLOCKS
+#define SPLAT_SORT_MIN_BLOCKS 2
+#endif
+constexpr int kSortMinBlocks = SPLAT_SORT_MIN_BLOCKS;  // resident scatter blocks per SM to budget registers for
+constexpr int kSortTile = kSortThreads * kSortRounds;  // pairs per sort block
 constexpr int kRadixBits = 8;
 constexpr int kRadix = 1 << kRadixBits;
+constexpr int kMaxPasses = 64 / kRadixBits;
 
 // Workspace needed by scan_exclusive_u32 for n values.
 size_t scan_workspace_bytes(long long n);

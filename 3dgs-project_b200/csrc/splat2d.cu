@@ -533,6 +533,7 @@ int forward_impl(const void* means, const void* chol, const void* zl, const void
     kern<<<t.T, kBlock, 0, st>>>(t, static_cast<const S*>(means), static_cast<const S*>(chol),
                                  static_cast<const S*>(zl), static_cast<const S*>(colors), static_cast<S*>(image),
                                  static_cast<S*>(t_final), n_contrib, last_contrib, static_cast<S*>(ckpt));
+    note_launch();
     return check_launch("splat2d_forward");
 }
 
@@ -557,11 +558,13 @@ int backward_impl(int splat_mode, const void* grad_image, const void* means, con
         kern<<<div_up(B, kBwdWarps), 32 * kBwdWarps, 0, st>>>(
             t, gi, static_cast<const S*>(image), static_cast<const S*>(means), static_cast<const S*>(chol),
             static_cast<const S*>(zl), static_cast<const S*>(colors), static_cast<const S*>(ckpt), gm, gc, gz, gcol);
+        note_launch();
     } else {
         auto kern = g_counting ? k_backward_pixel<S, true> : k_backward_pixel<S, false>;
         kern<<<t.T, kBlock, 0, st>>>(t, gi, static_cast<const S*>(means), static_cast<const S*>(chol),
                                      static_cast<const S*>(zl), static_cast<const S*>(colors),
                                      static_cast<const S*>(t_final), last_contrib, gm, gc, gz, gcol);
+        note_launch();
     }
     return check_launch(splat_mode ? "splat2d_backward_splat" : "splat2d_backward_pixel");
 }
@@ -608,6 +611,8 @@ int splat2d_bin_count(int is_f64, const void* means, const void* chol, const voi
                                                              static_cast<const float*>(chol),
                                                              static_cast<const float*>(opacity_logit), n, H, W,
                                                              w.trect, w.counts);
+   
+        note_launch();
     SPLAT_TRY(check_launch("splat2d_bin_rect"));
     return scan_exclusive_u32(w.counts, w.offsets, n, num_instances, w.scan_ws, w.scan_bytes, st);
 }
@@ -631,19 +636,23 @@ int splat2d_bin_fill(int n, int H, int W, long long m, void* count_ws, size_t co
     if (m > 0) {
         s2::k_bin_duplicate<<<div_up(n, 256), 256, 0, st>>>(cw.trect, cw.counts, cw.offsets, n, tiles_x, id_bits,
                                                             f.keys, f.vals);
+        note_launch();
         SPLAT_TRY(check_launch("splat2d_bin_duplicate"));
         SPLAT_TRY(radix_sort_pairs<unsigned long long>(f.keys, f.vals, f.keys_sorted, f.vals_sorted, m, 0,
                                                        id_bits + tile_bits, f.sort_ws, f.sort_bytes, st));
         s2::k_bin_runs<<<div_up(m, 256), 256, 0, st>>>(f.keys_sorted, f.vals_sorted, static_cast<int>(m), id_bits,
                                                        f.first, f.last, tile_ids);
+        note_launch();
         SPLAT_TRY(check_launch("splat2d_bin_runs"));
     }
     s2::k_bin_counts<<<div_up(T + 1, 256), 256, 0, st>>>(f.first, f.last, T, f.cnt, f.nb);
+    note_launch();
     SPLAT_TRY(check_launch("splat2d_bin_counts"));
     SPLAT_TRY(scan_exclusive_u32(f.cnt, f.cstart, T + 1, nullptr, f.scan_ws, f.scan_bytes, st));
     SPLAT_TRY(scan_exclusive_u32(f.nb, f.bstart, T + 1, num_buckets, f.scan_ws, f.scan_bytes, st));
     s2::k_bin_tables<<<div_up(T + 1, 256), 256, 0, st>>>(f.cstart, f.nb, f.bstart, T, tile_offsets, bucket_offsets,
                                                          bucket_tile);
+    note_launch();
     return check_launch("splat2d_bin_tables");
 }
 

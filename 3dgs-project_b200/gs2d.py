@@ -123,6 +123,7 @@ def bin_gaussians(means: torch.Tensor, radii: torch.Tensor, depth: torch.Tensor,
     L.call("gs2d_bin_fill", L.ptr(rect), n, H, W, M, L.ptr(cws), cws.numel(), L.ptr(fws), fws.numel(),
            L.ptr(point_list), L.ptr(ranges), L.ptr(bucket_offsets), L.ptr(bucket_to_tile), L.ptr(counts[1:]), stream)
     B = int(counts[1].item())
+    L.check_device_waits(dev)
     return Bins(H, W, tiles_x, tiles_y, rect, order, point_list, ranges, bucket_offsets,
                 bucket_to_tile[:B].clone(), B)
 

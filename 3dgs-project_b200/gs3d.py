@@ -105,6 +105,7 @@ def forward(means, scales, rotations, opacities, sh0, sh_rest, w2c, cam_position
     L.call("gs3d_preprocess", L.ptr(means), L.ptr(scales), L.ptr(rotations), L.ptr(opacities), L.ptr(sh0),
            L.ptr(sh_rest), n, ctypes.byref(s), L.ptr(prim), prim.numel(), L.ptr(count), stream)
     m = int(count.item())  # the one host read of a forward
+    L.check_device_waits(dev)  # covers this depth sort and the previous forward's tile sort
     bcap = int(L.load().gs3d_bucket_bound(m, width, height))
     inst = torch.empty(L.query("gs3d_instance_buffer_size", m), dtype=torch.uint8, device=dev)
     bucket = torch.empty(L.query("gs3d_bucket_buffer_size", bcap), dtype=torch.uint8, device=dev)
@@ -118,10 +119,12 @@ def forward(means, scales, rotations, opacities, sh0, sh_rest, w2c, cam_position
 def backward(densification_info, grad_image, image, means, scales, rotations, opacities, sh_rest, prim_buf,
              tile_buf, inst_buf, bucket_buf, w2c, cam_position, bg_color, active_sh_bases, width, height, focal_x,
              focal_y, center_x, center_y, near_plane, far_plane, proper_antialiasing, n_instances, n_buckets,
-             selector, *mode, out: tuple | None = None):
+             selector, *mode, out: tuple | None = None, stage_event: torch.cuda.Event | None = None):
     """Faster-GS `_C.backward` (the trailing blend-backward mode of the phase1 patch is accepted and ignored:
     there is one blend backward here). Returns (means, scales, rotations, opacities[N,1], sh0[N,1,3], sh_rest).
-    ``out`` may supply the six contiguous float32 result tensors (e.g. views of one flat gradient buffer)."""
+    ``out`` may supply the six contiguous float32 result tensors (e.g. views of one flat gradient buffer).
+    It runs as its two launches (gs3d_backward_blend, gs3d_backward_preprocess); ``stage_event``, if given, is
+    recorded on the stream between them."""
     n = means.shape[0]
     rest = sh_rest.shape[1] if sh_rest.dim() == 3 else 0
     dev = means.device
@@ -139,10 +142,15 @@ def backward(densification_info, grad_image, image, means, scales, rotations, op
     else:
         grads = (torch.empty(n, 3, device=dev), torch.empty(n, 3, device=dev), torch.empty(n, 4, device=dev),
                  torch.empty(n, 1, device=dev), torch.empty(n, 1, 3, device=dev), torch.empty(n, rest, 3, device=dev))
-    L.call("gs3d_backward", L.ptr(g_img), L.ptr(image), L.ptr(means), L.ptr(scales), L.ptr(rotations),
-           L.ptr(opacities), L.ptr(sh_rest), n, int(n_instances), ctypes.byref(s), L.ptr(prim_buf), prim_buf.numel(),
-           L.ptr(tile_buf), tile_buf.numel(), L.ptr(inst_buf), inst_buf.numel(), L.ptr(bucket_buf), bucket_buf.numel(),
-           int(n_buckets), L.ptr(ws), ws.numel(), *map(L.ptr, grads), L.stream_of(means))
+    stream = L.stream_of(means)
+    L.call("gs3d_backward_blend", L.ptr(g_img), L.ptr(image), n, int(n_instances), ctypes.byref(s), L.ptr(prim_buf),
+           prim_buf.numel(), L.ptr(tile_buf), tile_buf.numel(), L.ptr(inst_buf), inst_buf.numel(), L.ptr(bucket_buf),
+           bucket_buf.numel(), int(n_buckets), L.ptr(ws), ws.numel(), stream)
+    if stage_event is not None:
+        stage_event.record(torch.cuda.current_stream(dev))
+    L.call("gs3d_backward_preprocess", L.ptr(means), L.ptr(scales), L.ptr(rotations), L.ptr(opacities),
+           L.ptr(sh_rest), n, ctypes.byref(s), L.ptr(prim_buf), prim_buf.numel(), L.ptr(ws), ws.numel(),
+           *map(L.ptr, grads), stream)
     return grads
 
 
@@ -228,7 +236,8 @@ def primitive_views(prim_buf: torch.Tensor, n: int) -> dict[str, torch.Tensor]:
     """Typed views into a primitive buffer (the layout of carve_prim in csrc/gs3d_common.cuh):
     mean2d [N,2], conic_o [N,4] (A, B, C, opacity), color_z [N,4] (r, g, b, depth), rect [N,4] (int16 pixels),
     thr [N], n_touched [N] (int32), depth_key / ids / depth_key_sorted [N], order [N] (ids in depth order),
-    offsets [N] (instance offsets in that order). Per-Gaussian values are valid where n_touched > 0."""
+    offsets [N] (instance offsets in that order), counters [4] (int32: instance count M, bucket count B). Per-Gaussian
+    values are valid where n_touched > 0."""
     nn = max(n, 1)
     off = 0
     out = {}
@@ -242,6 +251,8 @@ def primitive_views(prim_buf: torch.Tensor, n: int) -> dict[str, torch.Tensor]:
         t = prim_buf[off:off + elem * nn].view(dtype)
         out[name] = t.view(nn, width)[:n] if width > 1 else t[:n]
         off += elem * nn
+    off = _align(off)
+    out["counters"] = prim_buf[off:off + 16].view(torch.int32)
     out["rect"] = out["rect"].to(torch.int32) & 0xFFFF
     return out
 

@@ -214,6 +214,7 @@ def bin_tiles(means: Tensor, chol: Tensor, opacity_logit: Tensor, height: int, w
     L.call("splat2d_bin_fill", n, height, width, M, L.ptr(cws), cws.numel(), L.ptr(fws), fws.numel(),
            L.ptr(tile_offsets), L.ptr(tile_ids), L.ptr(bucket_offsets), L.ptr(bucket_tile), L.ptr(counts[1:]), stream)
     B = int(counts[1].item())
+    L.check_device_waits(dev)
     return TileBins(tile_offsets, tile_ids, bucket_offsets, bucket_tile[:B].clone(), tiles_x, tiles_y)
 
 

@@ -37,6 +37,7 @@ import torch  # noqa: E402
 from __graft_entry__ import load_package  # noqa: E402
 
 load_package()
+from gs_b200 import _lib as L  # noqa: E402
 from gs_b200 import adam as gs_adam  # noqa: E402
 from gs_b200 import gs3d, scenes  # noqa: E402
 
@@ -44,6 +45,9 @@ METRIC = "fwd+bwd ms/iter (3M Gaussians, 1080p, SH3); train views/s at 1/2/4/8 B
 LRS = {"means": 1.6e-4, "scales": 5e-3, "rotations": 1e-3, "opacities": 5e-2, "sh0": 2.5e-3, "sh_rest": 2.5e-3}
 NAMES = ("means", "scales", "rotations", "opacities", "sh0", "sh_rest")
 WIDTHS = (3, 3, 4, 1, 3, 45)  # floats per Gaussian in each group: 59 in total
+# dram__bytes_read.sum + dram__bytes_write.sum of one k_blend_backward launch on the C3 workload, from one ncu
+# capture (profiles/); None until captured.
+BLEND_BWD_TRAFFIC = None
 
 
 class Clocks:
@@ -145,20 +149,24 @@ class Trainer:
         self.m = [torch.zeros_like(p) for p in self.params]
         self.v = [torch.zeros_like(p) for p in self.params]
         self.t = 0
-        self.ev = {k: [] for k in ("fwd", "bwd", "comm", "adam")}
+        self.ev = {k: [] for k in ("fwd", "bwd", "comm", "adam", "blend_bwd")}
+        self.last = None
 
     def step(self, cam: dict, dout: torch.Tensor, timed: bool):
         s = scenes.settings_tuple(cam, self.bases, self.dev)
-        e = [torch.cuda.Event(enable_timing=True) for _ in range(5)] if timed else None
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(6)] if timed else None
         if timed:
             e[0].record()
         image, prim, tile, inst, bucket, m, nb, sel = gs3d.forward(*self.params, *s)
         if timed:
             e[1].record()
         gs3d.backward(None, dout, image, self.params[0], self.params[1], self.params[2], self.params[3],
-                      self.params[5], prim, tile, inst, bucket, *s, m, nb, sel, out=self.grads)
+                      self.params[5], prim, tile, inst, bucket, *s, m, nb, sel, out=self.grads,
+                      stage_event=e[5] if timed else None)
         if timed:
             e[2].record()
+            self.ev["blend_bwd"].append((e[1], e[5]))
+        self.last = (prim, m, cam)
         if self.world > 1:
             torch.distributed.all_reduce(self.flat)
         if timed:
@@ -198,12 +206,14 @@ def run_ours(args) -> None:
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
         t0 = time.perf_counter()
+        launches0 = L.query("splat_launch_count")
         start.record()
         insts = []
         for _ in range(args.steps):
             insts += one_step(True)
         end.record()
         torch.cuda.synchronize()
+        launches = L.query("splat_launch_count") - launches0
         wall = time.perf_counter() - t0
     if world > 1:
         torch.distributed.barrier()
@@ -213,6 +223,8 @@ def run_ours(args) -> None:
         torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
     ms_max = float(ms_t.item())
     stage = {k: sum(a.elapsed_time(b) for a, b in v) / max(len(v), 1) for k, v in tr.ev.items()}
+    prim, m_last, cam_last = tr.last
+    buckets_last = int(gs3d.primitive_views(prim, tr.n)["counters"][1].item())
 
     # end to end through the public API: pinned host upstream gradient in, loss out, every step
     e2e = run_e2e(sc, cams, dev, world, args, tr)
@@ -235,9 +247,9 @@ def run_ours(args) -> None:
             "wall_s": round(wall, 3),
             "clocks": clk.summary(),
             "e2e": e2e,
-            "gpu_launches": None,
+            "gpu_launches": launches,
         }
-        line.update(roofline_and_counts(args, tr, stage, m_avg))
+        line.update(roofline(tr, stage, m_last, buckets_last, W * H))
         line["cpu_baseline"] = cpu_baseline(args, sc, cam) if not args.no_cpu_baseline else None
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -284,22 +296,26 @@ def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
             "h2d_bytes_per_step": int(host.numel() * 4), "d2h_bytes_per_step": 4}
 
 
-def roofline_and_counts(args, tr: Trainer, stage: dict, m_avg: float) -> dict:
-    """Filled in from the per-stage times; the dominant stage's algorithmic bytes per launch over its time."""
+def roofline(tr: Trainer, stage: dict, m: int, buckets: int, pixels: int) -> dict:
+    """Roofline of the dominant kernel, the blend backward (k_blend_backward, with the clear of its
+    accumulators), timed live with CUDA events around its call in every timed step. Algorithmic bytes per
+    launch: checkpoints 16 B x 256 pixels x B buckets + 24 B per pixel (upstream gradient, image, final T /
+    contributor counts) + 40 B per instance (id, mean2d, conic + opacity, colour) + 36 B per Gaussian (the
+    accumulator clear). The bucket count B is read from the last step's counters."""
     peaks_path = ROOT / "MEASURED_PEAKS.json"
-    hbm = None
-    src = "fallback"
+    hbm, src = 6650.0, "fallback"
     if peaks_path.exists():
-        hbm = json.loads(peaks_path.read_text()).get("hbm_gbs")
-        src = "measured"
-    if hbm is None:
-        hbm = 6650.0
-    n = tr.n
-    bwd_bytes = 236.0 * n + 250.0 * n  # preprocess backward dominates the backward's DRAM traffic
-    ach = bwd_bytes / (stage["bwd"] / 1000.0) / 1e9 if stage["bwd"] > 0 else 0.0
+        v = json.loads(peaks_path.read_text()).get("hbm_gbs")
+        if v:
+            hbm, src = float(v), "measured"
+    algo = 16.0 * 256 * buckets + 24.0 * pixels + 40.0 * m + 36.0 * tr.n
+    t_ms = stage["blend_bwd"]
+    ach = algo / (t_ms / 1000.0) / 1e9 if t_ms > 0 else 0.0
     return {"roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(ach / hbm, 4), "traffic": None, "kernel": "backward (blend + preprocess)",
-                         "peak_source": src}}
+                         "frac": round(ach / hbm, 4), "traffic": BLEND_BWD_TRAFFIC,
+                         "kernel": "k_blend_backward (+ accumulator clear)", "kernel_ms": round(t_ms, 4),
+                         "algorithmic_bytes": int(algo), "buckets": buckets, "instances": m,
+                         "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src}}
 
 
 def cpu_baseline(args, sc, cam):

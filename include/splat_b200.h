@@ -36,6 +36,9 @@ extern "C" {
 const char* splat_last_error(void);
 /* SPLAT_ABI_VERSION of the loaded library. */
 int splat_abi_version(void);
+/* Kernels this library has launched in this process so far (all threads and devices). No counterpart in
+ * the reference; benchmarks read it before and after a timed region. */
+long long splat_launch_count(void);
 
 /* ---------------------------------------------------------------------------------------------
  * Device-wide primitives (replace the CUB DeviceScan / DeviceRadixSort calls inside Faster-GS's
@@ -46,11 +49,16 @@ size_t splat_scan_workspace_size(long long n);
 int splat_scan_exclusive_u32(const uint32_t* in, uint32_t* out, long long n, uint32_t* total, void* workspace,
                              size_t workspace_bytes, void* stream);
 size_t splat_sort_workspace_size(long long n, int key_bytes);
-/* Stable LSD radix sort of (key, uint32 value) pairs by key bits [begin_bit, end_bit); key_bytes 4 or 8.
- * Inputs are left untouched; outputs must not alias them. */
+/* Stable LSD radix sort of (key, uint32 value) pairs by key bits [begin_bit, end_bit); key_bytes 4 or 8,
+ * n < 2^30. Inputs are left untouched; outputs must not alias them. Its per-digit passes wait (bounded) on
+ * counts published by earlier blocks of the same launch; see splat_check_device_waits. */
 int splat_radix_sort_pairs(const void* keys_in, const uint32_t* vals_in, void* keys_out, uint32_t* vals_out,
                            long long n, int key_bytes, int begin_bit, int end_bit, void* workspace,
                            size_t workspace_bytes, void* stream);
+/* SPLAT_ERR_TIMEOUT if a bounded device-side wait on the current device gave up since the last call
+ * (results produced since then are unreliable), else SPLAT_OK. Synchronises the device; clears the count.
+ * No counterpart in the reference (CUB's single-sweep sort waits without a bound). */
+int splat_check_device_waits(void);
 
 /* ---------------------------------------------------------------------------------------------
  * gs2d: toy2d 2D Gaussian rasterizer (replaces toy2d/csrc/rasterize.cu:366-454 and the device
@@ -189,6 +197,19 @@ int gs3d_backward(const float* grad_image, const float* image, const float* mean
                   long long bucket_capacity, void* workspace, size_t workspace_bytes, float* grad_means,
                   float* grad_scales, float* grad_rotations, float* grad_opacities, float* grad_sh0,
                   float* grad_sh_rest, void* stream);
+/* gs3d_backward in its two launches (the reference's _C.backward runs both back to back): the blend
+ * backward accumulates the per-Gaussian 2D gradients (mean2d, conic, opacity, colour) into workspace,
+ * which it clears first; the preprocess backward turns them into the parameter gradients. Called in this
+ * order on one stream they give exactly gs3d_backward's results. */
+int gs3d_backward_blend(const float* grad_image, const float* image, int n, long long num_instances,
+                        const gs3d_settings* settings, void* prim_buf, size_t prim_bytes, void* tile_buf,
+                        size_t tile_bytes, void* inst_buf, size_t inst_bytes, void* bucket_buf, size_t bucket_bytes,
+                        long long bucket_capacity, void* workspace, size_t workspace_bytes, void* stream);
+int gs3d_backward_preprocess(const float* means, const float* scales, const float* rotations,
+                             const float* opacities, const float* sh_rest, int n, const gs3d_settings* settings,
+                             void* prim_buf, size_t prim_bytes, void* workspace, size_t workspace_bytes,
+                             float* grad_means, float* grad_scales, float* grad_rotations, float* grad_opacities,
+                             float* grad_sh0, float* grad_sh_rest, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
  * Fused Adam (replaces the per-group `_C.adam_step` launches of Faster-GS's FusedAdam,

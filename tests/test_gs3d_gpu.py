@@ -123,6 +123,30 @@ def test_deterministic_up_to_atomics(cuda):
     assert max(rel(a, b) for a, b in zip(outs[0][1], outs[1][1])) < 1e-6
 
 
+def test_single_call_backward_matches_split(cuda):
+    """gs3d_backward (one C call) gives the results of gs3d_backward_blend + gs3d_backward_preprocess, which the
+    Python mirror uses, up to the atomic-order noise."""
+    import ctypes
+
+    from gs_b200 import _lib as L
+
+    sc, cam, params, settings = _setup("partial_tiles", seed=5)
+    image, prim, tile, inst, bucket, m, nb, sel = gs3d.forward(*params, *settings)
+    dout = torch.randn_like(image)
+    split = gs3d.backward(None, dout, image, params[0], params[1], params[2], params[3], params[5], prim, tile, inst,
+                          bucket, *settings, m, nb, sel)
+    n = params[0].shape[0]
+    rest = params[5].shape[1]
+    keep: list = []
+    s = gs3d._settings(params[0].device, *settings, rest, keep)
+    ws = torch.empty(L.query("gs3d_backward_workspace_size", n), dtype=torch.uint8, device=cuda)
+    single = tuple(torch.empty_like(g) for g in split)
+    L.call("gs3d_backward", L.ptr(dout), L.ptr(image), *map(L.ptr, params[:4]), L.ptr(params[5]), n, m,
+           ctypes.byref(s), L.ptr(prim), prim.numel(), L.ptr(tile), tile.numel(), L.ptr(inst), inst.numel(),
+           L.ptr(bucket), bucket.numel(), nb, L.ptr(ws), ws.numel(), *map(L.ptr, single), L.stream_of(image))
+    assert max(rel(a, b) for a, b in zip(single, split)) < 1e-5  # float atomics: summation order differs
+
+
 def test_empty_scene(cuda):
     """All Gaussians behind the camera: no instances, zero gradients, no launch error (test_parity.py:143-153)."""
     sc, cam, params, settings = _setup("empty", seed=3)
