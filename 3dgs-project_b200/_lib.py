@@ -27,6 +27,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "splat_launch_count": (_LL, []),
     "splat_scan_workspace_size": (_SZ, [_LL]),
     "splat_scan_exclusive_u32": (_I, [_P, _P, _LL, _P, _P, _SZ, _P]),
+    "splat_scan_exclusive_u32_noalloc": (_I, [_P, _P, _LL, _P, _P]),
     "splat_sort_workspace_size": (_SZ, [_LL, _I]),
     "splat_radix_sort_pairs": (_I, [_P, _P, _P, _P, _LL, _I, _I, _I, _P, _SZ, _P]),
     "splat_check_device_waits": (_I, []),

@@ -8,6 +8,7 @@
 // earlier tiles publish, and writes the pairs out digit run by digit run, so consecutive threads store
 // consecutive addresses.
 #include <algorithm>
+#include <mutex>
 
 #include "sort.cuh"
 
@@ -494,6 +495,61 @@ int take_wait_timeouts(unsigned int* count) {
     return SPLAT_OK;
 }
 
+// ---- exclusive scan without a workspace: the block sums live in a fixed device array ----
+
+// 2^28 values -> 65,536 block sums of 4096 values: 256 KiB of device memory per device.
+constexpr long long kNoAllocScanMaxN = SPLAT_SCAN_NOALLOC_MAX_N;
+constexpr long long kNoAllocScanPartials = kNoAllocScanMaxN / kScanTile;
+static_assert(kNoAllocScanMaxN % kScanTile == 0, "whole scan blocks");
+static __device__ __align__(256) uint32_t g_noalloc_scan_partials[kNoAllocScanPartials];
+
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+uint32_t* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of g_noalloc_scan_partials on the current device, looked up on the first call per device.
+int noalloc_scan_partials(uint32_t** out) {
+    int dev = -1;
+    SPLAT_CUDA(cudaGetDevice(&dev));
+    SPLAT_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, "device %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        SPLAT_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scan_partials));
+        g_noalloc_ptr[dev] = static_cast<uint32_t*>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return SPLAT_OK;
+}
+
+}  // namespace
+
+int scan_exclusive_u32_noalloc(const uint32_t* in, uint32_t* out, long long n, uint32_t* total,
+                               cudaStream_t stream) {
+    if (n > kNoAllocScanMaxN) {
+        set_error("splat_scan_exclusive_u32_noalloc: n = %lld exceeds its maximum of %lld values (its fixed "
+                  "scratch holds %lld block sums); use splat_scan_exclusive_u32 with a workspace",
+                  n, kNoAllocScanMaxN, kNoAllocScanPartials);
+        return SPLAT_ERR_OVERFLOW;
+    }
+    if (n <= 0) {
+        if (total) SPLAT_CUDA(cudaMemsetAsync(total, 0, sizeof(uint32_t), stream));
+        return SPLAT_OK;
+    }
+    uint32_t* partial = nullptr;
+    SPLAT_TRY(noalloc_scan_partials(&partial));
+    const unsigned int nb = div_up(n, kScanTile);  // <= kNoAllocScanPartials
+    k_scan_reduce<<<nb, kScanThreads, 0, stream>>>(in, n, partial);
+    note_launch();
+    k_scan_partials<<<1, kScanThreads, 0, stream>>>(partial, nb, total);
+    note_launch();
+    k_scan_apply<<<nb, kScanThreads, 0, stream>>>(in, out, n, partial);
+    note_launch();
+    return check_launch("scan_exclusive_u32_noalloc");
+}
+
 template size_t sort_workspace_bytes<uint32_t>(long long);
 template size_t sort_workspace_bytes<unsigned long long>(long long);
 template int radix_sort_pairs<uint32_t>(const uint32_t*, const uint32_t*, uint32_t*, uint32_t*, long long, int,
@@ -513,6 +569,10 @@ size_t splat_scan_workspace_size(long long n) { return splat::scan_workspace_byt
 int splat_scan_exclusive_u32(const uint32_t* in, uint32_t* out, long long n, uint32_t* total, void* workspace,
                              size_t workspace_bytes, void* stream) {
     return splat::scan_exclusive_u32(in, out, n, total, workspace, workspace_bytes, splat::as_stream(stream));
+}
+
+int splat_scan_exclusive_u32_noalloc(const uint32_t* in, uint32_t* out, long long n, uint32_t* total, void* stream) {
+    return splat::scan_exclusive_u32_noalloc(in, out, n, total, splat::as_stream(stream));
 }
 
 size_t splat_sort_workspace_size(long long n, int key_bytes) {

@@ -37,6 +37,11 @@ size_t scan_workspace_bytes(long long n);
 int scan_exclusive_u32(const uint32_t* in, uint32_t* out, long long n, uint32_t* total, void* ws,
                        size_t ws_bytes, cudaStream_t stream);
 
+// scan_exclusive_u32 with its block sums in a fixed device array instead of a workspace (n at most
+// SPLAT_SCAN_NOALLOC_MAX_N); calls on one device share that array.
+int scan_exclusive_u32_noalloc(const uint32_t* in, uint32_t* out, long long n, uint32_t* total,
+                               cudaStream_t stream);
+
 template <typename K>
 size_t sort_workspace_bytes(long long n);
 

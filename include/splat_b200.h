@@ -48,6 +48,21 @@ size_t splat_scan_workspace_size(long long n);
 /* out[i] = sum(in[0..i)); *total (device, may be NULL) = sum of all n. in and out may alias. */
 int splat_scan_exclusive_u32(const uint32_t* in, uint32_t* out, long long n, uint32_t* total, void* workspace,
                              size_t workspace_bytes, void* stream);
+/* Exclusive scan that allocates nothing (no counterpart in the reference, whose entry points all take their
+ * scratch from PyTorch's caching allocator). Same results as splat_scan_exclusive_u32, without the workspace:
+ * its block sums live in one fixed device array of this library, SPLAT_SCAN_NOALLOC_MAX_N / 4096 uint32
+ * (256 KiB) per device. For callers that cannot allocate device memory: a host that holds only the input and
+ * output pointers and no device allocator (a C, cgo or JNI host driving buffers another framework owns), a
+ * process whose device memory is already fully reserved, and callers on a latency-critical stream, where
+ * cudaMalloc / cudaFree would synchronise the device.
+ *  - n > SPLAT_SCAN_NOALLOC_MAX_N returns SPLAT_ERR_OVERFLOW before any launch.
+ *  - The first call on each device looks up the array's address (cudaGetSymbolAddress on the current
+ *    device, which must be the device of in, out and stream); make that first call before any stream capture.
+ *  - Every call on a device uses the same array. Nothing in it has to start at zero (each call writes every
+ *    block sum it reads), but calls whose executions overlap in time (other streams, other host threads)
+ *    race on it and give wrong results: serialise them. */
+#define SPLAT_SCAN_NOALLOC_MAX_N (1LL << 28)
+int splat_scan_exclusive_u32_noalloc(const uint32_t* in, uint32_t* out, long long n, uint32_t* total, void* stream);
 size_t splat_sort_workspace_size(long long n, int key_bytes);
 /* Stable LSD radix sort of (key, uint32 value) pairs by key bits [begin_bit, end_bit); key_bytes 4 or 8,
  * n < 2^30. Inputs are left untouched; outputs must not alias them. Its per-digit passes wait (bounded) on
