@@ -13,7 +13,7 @@ import torch
 
 # SPLAT_B200_LIB may name another build of the same library (e.g. a tuning variant); it is still this C ABI.
 LIB_PATH = Path(os.environ.get("SPLAT_B200_LIB", Path(__file__).resolve().with_name("libsplat_b200.so")))
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -55,10 +55,11 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gs3d_backward_workspace_size": (_SZ, [_I]),
     "gs3d_preprocess": (_I, [_P] * 6 + [_I, _P, _P, _SZ, _P, _P]),
     "gs3d_render": (_I, [_I, _LL, _P, _P, _SZ, _P, _SZ, _P, _SZ, _P, _SZ, _LL, _P, _P]),
-    "gs3d_backward": (_I, [_P] * 7 + [_I, _LL, _P] + [_P, _SZ] * 4 + [_LL, _P, _SZ] + [_P] * 7),
-    "gs3d_backward_blend": (_I, [_P, _P, _I, _LL, _P] + [_P, _SZ] * 4 + [_LL, _P, _SZ, _P]),
-    "gs3d_backward_preprocess": (_I, [_P] * 5 + [_I, _P, _P, _SZ, _P, _SZ] + [_P] * 7),
-    "adam_step_multi": (_I, [_I, _P, _I, ctypes.c_float, ctypes.c_float, ctypes.c_float, _P]),
+    "gs3d_backward": (_I, [_P] * 7 + [_I, _LL, _P] + [_P, _SZ] * 4 + [_LL, _P, _SZ] + [_P] * 7 + [_I, _P]),
+    "gs3d_backward_blend": (_I, [_P, _P, _I, _LL, _P] + [_P, _SZ] * 4 + [_LL, _P, _SZ, _I, _P]),
+    "gs3d_backward_preprocess": (_I, [_P] * 5 + [_I, _P, _P, _SZ, _P, _SZ] + [_P] * 7 + [_I, _P]),
+    "adam_step_multi": (_I, [_I, _P, _I, ctypes.c_double, ctypes.c_double, ctypes.c_double, _P]),
+    "adam_step_multi_lean": (_I, [_I, _P, _I, ctypes.c_double, ctypes.c_double, ctypes.c_double, _P, _LL, _P]),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -1,5 +1,6 @@
 """FusedAdam: Faster-GS's optimizer interface (cluster/patches/fastergs_lean_adam.patch:251-307) with every
-parameter group updated by ONE launch of adam_step_multi (csrc/adam.cu) instead of one launch per group.
+parameter group updated by ONE launch of adam_step_multi (csrc/adam.cu) instead of one launch per group, and the
+lean options of that patch (visibility-sparse update, bfloat16 moments) through adam_step_multi_lean.
 
 State is the torch.optim.Adam layout ('step', 'exp_avg', 'exp_avg_sq' per parameter), so state_dict()
 round-trips with torch's Adam and with checkpoints written by the reference's trainer.
@@ -17,23 +18,54 @@ class _Group(ctypes.Structure):
     """Mirror of adam_group in include/splat_b200.h."""
 
     _fields_ = [("param", ctypes.c_void_p), ("grad", ctypes.c_void_p), ("exp_avg", ctypes.c_void_p),
-                ("exp_avg_sq", ctypes.c_void_p), ("n", ctypes.c_longlong), ("lr", ctypes.c_float)]
+                ("exp_avg_sq", ctypes.c_void_p), ("n", ctypes.c_longlong), ("lr", ctypes.c_double)]
+
+
+class _LeanGroup(ctypes.Structure):
+    """Mirror of adam_lean_group in include/splat_b200.h."""
+
+    _fields_ = [("param", ctypes.c_void_p), ("grad", ctypes.c_void_p), ("exp_avg", ctypes.c_void_p),
+                ("exp_avg_sq", ctypes.c_void_p), ("n", ctypes.c_longlong), ("lr", ctypes.c_double),
+                ("features", ctypes.c_int), ("lowp_moments", ctypes.c_int)]
 
 
 MAX_GROUPS = 8
 
 
 class FusedAdam(torch.optim.Adam):
-    """Adam over single-tensor parameter groups, all groups in one kernel launch per step."""
+    """Adam over single-tensor parameter groups, all groups in one kernel launch per step.
 
-    def __init__(self, params, lr, eps, betas=(0.9, 0.999)) -> None:
+    The options of the reference's lean optimizer (cluster/patches/fastergs_lean_adam.patch:251-307), both off by
+    default (then this is the original Faster-GS optimizer):
+      sparse              only primitives visible in the last differentiable forward (n_touched_tiles > 0, handed
+                          over by gs3d._Rasterize.last_visibility) are updated; the others keep their parameters
+                          and moments for that step
+      lowp_moment_groups  names of parameter groups whose exp_avg / exp_avg_sq are kept in bfloat16 (stochastic
+                          rounding on write)
+    """
+
+    def __init__(self, params, lr, eps, betas=(0.9, 0.999), sparse: bool = False,
+                 lowp_moment_groups: tuple = ()) -> None:
         super().__init__(params=params, lr=lr, eps=eps, betas=betas)
+        self.sparse = bool(sparse)
+        self.lowp_moment_groups = set(lowp_moment_groups)
+        self.lean = self.sparse or bool(self.lowp_moment_groups)
+        self.n_dense_fallbacks = 0
+        from . import gs3d
+
+        gs3d._Rasterize.track_visibility = self.sparse
 
     @torch.no_grad()
     def step(self, closure=None) -> None:  # noqa: D102
         if closure is not None:
             raise RuntimeError("FusedAdam does not take a closure")
+        visibility = None
+        if self.sparse:
+            from . import gs3d
+
+            visibility = gs3d._Rasterize.last_visibility
         by_key: dict[tuple, list] = {}
+        masks: dict[tuple, torch.Tensor | None] = {}
         for group in self.param_groups:
             if len(group["params"]) != 1:
                 raise RuntimeError("more than one tensor in group")
@@ -41,24 +73,50 @@ class FusedAdam(torch.optim.Adam):
             if param.grad is None or param.numel() == 0:
                 continue
             L.check_cuda("param", param, torch.float32)
+            lowp = group.get("name") in self.lowp_moment_groups
+            moment_dtype = torch.bfloat16 if lowp else param.dtype
             state = self.state[param]
             if len(state) == 0:
                 state["step"] = torch.tensor(0.0)
-                state["exp_avg"] = torch.zeros_like(param)
-                state["exp_avg_sq"] = torch.zeros_like(param)
+                state["exp_avg"] = torch.zeros_like(param, dtype=moment_dtype)
+                state["exp_avg_sq"] = torch.zeros_like(param, dtype=moment_dtype)
+            elif state["exp_avg"].dtype != moment_dtype:
+                # densification concatenates float32 zeros to the moments, which promotes them; convert back
+                state["exp_avg"] = state["exp_avg"].to(moment_dtype)
+                state["exp_avg_sq"] = state["exp_avg_sq"].to(moment_dtype)
             state["step"] += 1
             grad = param.grad if param.grad.is_contiguous() else param.grad.contiguous()
-            key = (int(state["step"].item()), *group["betas"], group["eps"], param.device)
-            by_key.setdefault(key, []).append(_Group(param.data_ptr(), grad.data_ptr(), state["exp_avg"].data_ptr(),
-                                                     state["exp_avg_sq"].data_ptr(), param.numel(),
-                                                     float(group["lr"])))
-            by_key[key][-1]._keep = grad
-        for (step, b1, b2, eps, dev), groups in by_key.items():
+            step = int(state["step"].item())
+            if not self.lean:
+                key = ("dense", step, *group["betas"], group["eps"], param.device)
+                entry = _Group(param.data_ptr(), grad.data_ptr(), state["exp_avg"].data_ptr(),
+                               state["exp_avg_sq"].data_ptr(), param.numel(), float(group["lr"]))
+            else:
+                vis = visibility
+                if vis is not None and vis.numel() != param.shape[0]:
+                    vis = None  # stale mask: this group falls back to the dense update
+                    self.n_dense_fallbacks += 1
+                key = ("lean", step, *group["betas"], group["eps"], param.device, None if vis is None else id(vis))
+                masks[key] = vis
+                entry = _LeanGroup(param.data_ptr(), grad.data_ptr(), state["exp_avg"].data_ptr(),
+                                   state["exp_avg_sq"].data_ptr(), param.numel(), float(group["lr"]),
+                                   param.numel() // max(param.shape[0], 1), int(lowp))
+            entry._keep = grad
+            by_key.setdefault(key, []).append(entry)
+        for key, groups in by_key.items():
+            kind, step, b1, b2, eps, dev = key[:6]
+            stream = torch.cuda.current_stream(dev).cuda_stream
             for s in range(0, len(groups), MAX_GROUPS):
                 chunk = groups[s:s + MAX_GROUPS]
-                arr = (_Group * len(chunk))(*chunk)
-                L.call("adam_step_multi", len(chunk), ctypes.addressof(arr), step, float(b1), float(b2), float(eps),
-                       torch.cuda.current_stream(dev).cuda_stream)
+                if kind == "dense":
+                    arr = (_Group * len(chunk))(*chunk)
+                    L.call("adam_step_multi", len(chunk), ctypes.addressof(arr), step, float(b1), float(b2),
+                           float(eps), stream)
+                else:
+                    vis = masks[key]
+                    arr = (_LeanGroup * len(chunk))(*chunk)
+                    L.call("adam_step_multi_lean", len(chunk), ctypes.addressof(arr), step, float(b1), float(b2),
+                           float(eps), L.ptr(vis), 0 if vis is None else vis.numel(), stream)
 
 
 def adam_step(groups: list[tuple], step: int, betas=(0.9, 0.999), eps: float = 1e-15) -> None:
@@ -69,3 +127,23 @@ def adam_step(groups: list[tuple], step: int, betas=(0.9, 0.999), eps: float = 1
                                    for p, g, m, v, lr in groups])
     L.call("adam_step_multi", len(groups), ctypes.addressof(arr), int(step), float(betas[0]), float(betas[1]),
            float(eps), L.stream_of(groups[0][0]))
+
+
+def adam_step_lean(groups: list[tuple], step: int, visibility: torch.Tensor | None = None, betas=(0.9, 0.999),
+                   eps: float = 1e-15) -> None:
+    """Functional lean form (the reference's `_C.adam_step_sparse` for several groups at once): groups =
+    [(param, grad, exp_avg, exp_avg_sq, lr), ...]; exp_avg / exp_avg_sq float32 or bfloat16 (stochastic rounding);
+    visibility int32 [n_primitives] on the GPU or None."""
+    if not groups:
+        return
+    entries = []
+    for p, g, m, v, lr in groups:
+        if m.dtype != v.dtype or m.dtype not in (torch.float32, torch.bfloat16):
+            raise RuntimeError("moments must share a dtype, float32 or bfloat16")
+        if visibility is not None and (visibility.dtype != torch.int32 or not visibility.is_cuda):
+            raise RuntimeError("visibility must be int32 [n_primitives] on CUDA")
+        entries.append(_LeanGroup(p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel(), float(lr),
+                                  p.numel() // max(p.shape[0], 1), int(m.dtype == torch.bfloat16)))
+    arr = (_LeanGroup * len(entries))(*entries)
+    L.call("adam_step_multi_lean", len(entries), ctypes.addressof(arr), int(step), float(betas[0]), float(betas[1]),
+           float(eps), L.ptr(visibility), 0 if visibility is None else visibility.numel(), L.stream_of(groups[0][0]))

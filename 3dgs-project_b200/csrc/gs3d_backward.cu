@@ -16,6 +16,8 @@
 // sh0 and sh_rest. SH rows are read and their gradients written per warp through shared memory with
 // 16-byte accesses (the coalesced layout of upstream/sh_coalesced_loads.patch:12-52). Gaussians
 // that were not visible get zero gradients.
+#include <algorithm>
+
 #include "gs3d_common.cuh"
 
 namespace splat {
@@ -23,7 +25,7 @@ namespace gs3d {
 
 constexpr int kBwdWarps = 4;
 #ifndef SPLAT_BWD_MIN_BLOCKS
-#define SPLAT_BWD_MIN_BLOCKS 7  // 72 registers, no spills: 28 warps per SM instead of 20
+#define SPLAT_BWD_MIN_BLOCKS 7  // 72 registers (4 bytes spilled): 28 warps per SM instead of 20
 #endif
 constexpr int kPxPerLane = kTilePixels / 32;  // 8
 constexpr int kPbThreads = 128;
@@ -31,27 +33,34 @@ constexpr int kPbWarps = kPbThreads / 32;
 constexpr float kLn2 = 0.6931471805599453f;
 
 struct GradAcc {
+    uint32_t* work;  // next entry of the replayed-bucket list for the blend backward's persistent warps
     float2* mean2d;  // [N] dL/dmean2d
     float4* conic_o;  // [N] (dL/dA, dL/dB, dL/dC, dL/dopacity)
     float4* color;   // [N] dL/d max(colour, 0), w unused
+    float2* mean2d_abs;  // [N] sums of |per-pixel dL/dmean2d| (cleared and written only for 3 densification rows)
 };
 
 inline GradAcc carve_grad(Carver& c, int n) {
     const size_t nn = static_cast<size_t>(n < 1 ? 1 : n);
     GradAcc g;
+    g.work = c.take<uint32_t>(1);
     g.mean2d = c.take<float2>(nn);
     g.conic_o = c.take<float4>(nn);
     g.color = c.take<float4>(nn);
+    g.mean2d_abs = c.take<float2>(nn);
     return g;
 }
 
+// kAbs: also accumulate the per-pixel absolute values of the mean2d gradient (the third densification row).
+template <bool kAbs>
 __global__ void __launch_bounds__(32 * kBwdWarps, SPLAT_BWD_MIN_BLOCKS) k_blend_backward(
-    Cam cam, const uint32_t* __restrict__ counters, const uint32_t* __restrict__ bucket_tile,
-    const uint2* __restrict__ ranges, const uint32_t* __restrict__ bstart, const uint32_t* __restrict__ max_contrib,
-    const uint32_t* __restrict__ point_list, const float2* __restrict__ mean2d, const float4* __restrict__ conic_o,
-    const float4* __restrict__ color_z, const ushort4* __restrict__ rect, const float* __restrict__ grad_image,
-    const float* __restrict__ image, const uint32_t* __restrict__ n_contrib, const float4* __restrict__ ckpt, int n,
-    int m, long long bcap, GradAcc acc) {
+    Cam cam, const uint32_t* __restrict__ counters, const uint32_t* __restrict__ reached, uint32_t* __restrict__ work,
+    const uint32_t* __restrict__ bucket_tile, const uint2* __restrict__ ranges, const uint32_t* __restrict__ bstart,
+    const uint32_t* __restrict__ max_contrib, const uint32_t* __restrict__ point_list,
+    const float2* __restrict__ mean2d, const float4* __restrict__ conic_o, const float4* __restrict__ color_z,
+    const ushort4* __restrict__ rect, const float* __restrict__ grad_image, const float* __restrict__ image,
+    const uint32_t* __restrict__ n_contrib, const float4* __restrict__ ckpt, int n, int m, long long bcap,
+    GradAcc acc) {
     __shared__ float2 s_mean[kBwdWarps][kBucket];
     __shared__ float4 s_con[kBwdWarps][kBucket];
     __shared__ float4 s_col[kBwdWarps][kBucket];
@@ -60,125 +69,145 @@ __global__ void __launch_bounds__(32 * kBwdWarps, SPLAT_BWD_MIN_BLOCKS) k_blend_
     __shared__ float4 s_grad[kBwdWarps][kTilePixels];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long long b = static_cast<long long>(blockIdx.x) * kBwdWarps + warp;
     const long long nbuckets = min(static_cast<long long>(counters[1]), bcap);
-    if (b >= nbuckets) return;  // whole warp; warps never synchronise with each other
+    const long long nwork = min(static_cast<long long>(counters[2]), bcap);
     const int T_tiles = cam.tiles_x * cam.tiles_y;
-    const uint32_t tile = bucket_tile[b];
-    if (tile >= static_cast<uint32_t>(T_tiles)) return;
-    uint2 rg = ranges[tile];
-    rg.y = min(rg.y, static_cast<uint32_t>(m));
-    rg.x = min(rg.x, rg.y);
-    const long long bucket_start = (b - static_cast<long long>(bstart[tile])) * kBucket;
-    const long long tile_last = min(static_cast<long long>(max_contrib[tile]), static_cast<long long>(rg.y - rg.x));
-    if (bucket_start < 0 || bucket_start >= tile_last) return;
-    const int bsize = static_cast<int>(min(static_cast<long long>(kBucket), tile_last - bucket_start));
+    // Persistent warps: each takes the next replayed bucket from the work counter until the list is done, so
+    // no warp is launched for a bucket past its tile's last contributor and heavy buckets do not leave a tail.
+    for (;;) {
+        uint32_t k = 0u;
+        if (lane == 0) k = atomicAdd(work, 1u);
+        k = __shfl_sync(kFullMask, k, 0);
+        if (k >= nwork) break;
+        const long long b = reached[k];
+        if (b >= nbuckets) continue;
+        const uint32_t tile = bucket_tile[b];
+        if (tile >= static_cast<uint32_t>(T_tiles)) continue;
+        uint2 rg = ranges[tile];
+        rg.y = min(rg.y, static_cast<uint32_t>(m));
+        rg.x = min(rg.x, rg.y);
+        const long long bucket_start = (b - static_cast<long long>(bstart[tile])) * kBucket;
+        const long long tile_last = min(static_cast<long long>(max_contrib[tile]), static_cast<long long>(rg.y - rg.x));
+        if (bucket_start < 0 || bucket_start >= tile_last) continue;
+        const int bsize = static_cast<int>(min(static_cast<long long>(kBucket), tile_last - bucket_start));
+        __syncwarp();  // this warp's staging below is rewritten only after every lane finished the previous bucket
 
-    const int tx0 = (tile % cam.tiles_x) * kTile, ty0 = (tile / cam.tiles_x) * kTile;
-    if (lane < bsize) {
-        const int g = min(static_cast<int>(point_list[rg.x + bucket_start + lane]), n - 1);
-        s_id[warp][lane] = g;
-        s_mean[warp][lane] = mean2d[g];
-        const float4 co = conic_o[g];
-        s_con[warp][lane] = make_float4(-0.5f * kLog2e * co.x, -kLog2e * co.y, -0.5f * kLog2e * co.z, co.w);
-        const float4 cz = color_z[g];
-        s_col[warp][lane] = make_float4(fmaxf(cz.x, 0.f), fmaxf(cz.y, 0.f), fmaxf(cz.z, 0.f), 0.f);
-        s_rect[warp][lane] = rect[g];
-    }
-
-    const int x = tx0 + (lane & 15);
-    const int y0 = ty0 + (lane >> 4);
-    const float pxf = static_cast<float>(x) + 0.5f;
-    const size_t HW = static_cast<size_t>(cam.width) * cam.height;
-    const float4* ck = ckpt + b * kTilePixels;
-    float T[kPxPerLane], rho[kPxPerLane];
-    // per pixel, how many of this bucket's splats it used in the forward, clamped to [0, 32], 8 bits each
-    uint32_t lim_lo = 0u, lim_hi = 0u;
-#pragma unroll
-    for (int r = 0; r < kPxPerLane; ++r) {
-        const int y = y0 + 2 * r;
-        float4 G = make_float4(0.f, 0.f, 0.f, 0.f);
-        T[r] = 0.f;
-        rho[r] = 0.f;
-        if (x < cam.width && y < cam.height) {
-            const int pix = y * cam.width + x;
-            const long long used_here = static_cast<long long>(n_contrib[pix]) - bucket_start;
-            if (used_here > 0) {
-                const uint32_t l = static_cast<uint32_t>(min(used_here, 32ll));
-                if (r < 4)
-                    lim_lo |= l << (8 * r);
-                else
-                    lim_hi |= l << (8 * (r - 4));
-                G = make_float4(grad_image[pix], grad_image[HW + pix], grad_image[2 * HW + pix], 0.f);
-                const float4 st = ck[r * 32 + lane];
-                T[r] = st.w;
-                rho[r] = G.x * (image[pix] - st.x) + G.y * (image[HW + pix] - st.y) + G.z * (image[2 * HW + pix] - st.z);
-            }
+        const int tx0 = (tile % cam.tiles_x) * kTile, ty0 = (tile / cam.tiles_x) * kTile;
+        if (lane < bsize) {
+            const int g = min(static_cast<int>(point_list[rg.x + bucket_start + lane]), n - 1);
+            s_id[warp][lane] = g;
+            s_mean[warp][lane] = mean2d[g];
+            const float4 co = conic_o[g];
+            s_con[warp][lane] = make_float4(-0.5f * kLog2e * co.x, -kLog2e * co.y, -0.5f * kLog2e * co.z, co.w);
+            const float4 cz = color_z[g];
+            s_col[warp][lane] = make_float4(fmaxf(cz.x, 0.f), fmaxf(cz.y, 0.f), fmaxf(cz.z, 0.f), 0.f);
+            s_rect[warp][lane] = rect[g];
         }
-        s_grad[warp][r * 32 + lane] = G;
-    }
-    __syncwarp();
 
-    for (int j = 0; j < bsize; ++j) {
-        const float2 mm = s_mean[warp][j];
-        const float4 co = s_con[warp][j];
-        const float4 c = s_col[warp][j];
-        const ushort4 rc = s_rect[warp][j];
-        // per-lane sums over its pixels: h = dL/dq2 moments (for mean2d and conic), opacity, colour
-        float s_x = 0.f, s_y = 0.f, s_xx = 0.f, s_xy = 0.f, s_yy = 0.f, g_o = 0.f, g_r = 0.f, g_g = 0.f, g_bl = 0.f;
-        bool used = false;
-        const bool col_hit = x >= rc.x && x <= rc.z;
+        const int x = tx0 + (lane & 15);
+        const int y0 = ty0 + (lane >> 4);
+        const float pxf = static_cast<float>(x) + 0.5f;
+        const size_t HW = static_cast<size_t>(cam.width) * cam.height;
+        const float4* ck = ckpt + b * kTilePixels;
+        float T[kPxPerLane], rho[kPxPerLane];
+        // per pixel, how many of this bucket's splats it used in the forward, clamped to [0, 32], 8 bits each
+        uint32_t lim_lo = 0u, lim_hi = 0u;
+        // Every load of the prologue is issued without waiting on another: addresses are clamped into the image
+        // (and the checkpoint block of this bucket), and pixels outside the image or already finished before
+        // this bucket get their values replaced by zeros afterwards.
 #pragma unroll
         for (int r = 0; r < kPxPerLane; ++r) {
-            const int yb = ty0 + 2 * r;  // rows yb, yb + 1 of this band
-            if (rc.y > yb + 1 || rc.w < yb) continue;  // warp-uniform
-            const uint32_t l = ((r < 4 ? lim_lo : lim_hi) >> (8 * (r & 3))) & 0xffu;
-            if (!col_hit || static_cast<uint32_t>(j) >= l) continue;
-            const float dx = mm.x - pxf, dy = mm.y - (static_cast<float>(y0 + 2 * r) + 0.5f);
-            const float G = hw_exp2(fminf(blend_q2(co.x, co.y, co.z, dx, dy), 0.f));
-            const float alpha = co.w * G;
-            if (alpha < kAlphaMin) continue;
-            used = true;
-            const float4 gp = s_grad[warp][r * 32 + lane];
-            const float w = alpha * T[r];
-            const float dot_c = gp.x * c.x + gp.y * c.y + gp.z * c.z;
-            g_r += w * gp.x;
-            g_g += w * gp.y;
-            g_bl += w * gp.z;
-            rho[r] -= w * dot_c;
-            const float one_minus = 1.f - alpha;
-            const float dL_dalpha = T[r] * dot_c - __fdividef(rho[r], fmaxf(one_minus, kOneMinusAlphaEps));
-            g_o += G * dL_dalpha;
-            const float h = alpha * dL_dalpha * kLn2;  // dL/dq2
-            const float hx = h * dx, hy = h * dy;
-            s_x += hx;
-            s_y += hy;
-            s_xx += hx * dx;
-            s_xy += hx * dy;
-            s_yy += hy * dy;
-            T[r] *= one_minus;
+            const int y = y0 + 2 * r;
+            const bool inside = x < cam.width && y < cam.height;
+            const int pix = inside ? y * cam.width + x : 0;
+            const long long used_here = static_cast<long long>(__ldg(n_contrib + pix)) - bucket_start;
+            const float4 st = ck[r * 32 + lane];
+            const float gx = __ldg(grad_image + pix), gy = __ldg(grad_image + HW + pix), gz = __ldg(grad_image + 2 * HW + pix);
+            const float ix = __ldg(image + pix), iy = __ldg(image + HW + pix), iz = __ldg(image + 2 * HW + pix);
+            const bool live = inside && used_here > 0;
+            const uint32_t l = live ? static_cast<uint32_t>(min(used_here, 32ll)) : 0u;
+            if (r < 4)
+                lim_lo |= l << (8 * r);
+            else
+                lim_hi |= l << (8 * (r - 4));
+            const float4 G = live ? make_float4(gx, gy, gz, 0.f) : make_float4(0.f, 0.f, 0.f, 0.f);
+            T[r] = live ? st.w : 0.f;
+            rho[r] = live ? G.x * (ix - st.x) + G.y * (iy - st.y) + G.z * (iz - st.z) : 0.f;
+            s_grad[warp][r * 32 + lane] = G;
         }
-        if (__ballot_sync(kFullMask, used) == 0u) continue;
+        __syncwarp();
+
+        for (int j = 0; j < bsize; ++j) {
+            const float2 mm = s_mean[warp][j];
+            const float4 co = s_con[warp][j];
+            const float4 c = s_col[warp][j];
+            const ushort4 rc = s_rect[warp][j];
+            // per-lane sums over its pixels: h = dL/dq2 moments (for mean2d and conic), opacity, colour
+            float s_x = 0.f, s_y = 0.f, s_xx = 0.f, s_xy = 0.f, s_yy = 0.f, g_o = 0.f, g_r = 0.f, g_g = 0.f, g_bl = 0.f;
+            float a_x = 0.f, a_y = 0.f;  // kAbs: sums of |per-pixel dL/dmean2d|
+            bool used = false;
+            const bool col_hit = x >= rc.x && x <= rc.z;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            s_x += __shfl_down_sync(kFullMask, s_x, o);
-            s_y += __shfl_down_sync(kFullMask, s_y, o);
-            s_xx += __shfl_down_sync(kFullMask, s_xx, o);
-            s_xy += __shfl_down_sync(kFullMask, s_xy, o);
-            s_yy += __shfl_down_sync(kFullMask, s_yy, o);
-            g_o += __shfl_down_sync(kFullMask, g_o, o);
-            g_r += __shfl_down_sync(kFullMask, g_r, o);
-            g_g += __shfl_down_sync(kFullMask, g_g, o);
-            g_bl += __shfl_down_sync(kFullMask, g_bl, o);
-        }
-        if (lane == 0) {
-            const int g = s_id[warp][j];
-            // q2 = a2 dx^2 + b2 dx dy + c2 dy^2: dq2/dmx = 2 a2 dx + b2 dy, dq2/dmy = b2 dx + 2 c2 dy; then back
-            // from the exp2-scaled conic (a2, b2, c2) = log2(e) (-0.5 A, -B, -0.5 C) to (A, B, C)
-            atomicAdd(acc.mean2d + g, make_float2(2.f * co.x * s_x + co.y * s_y, co.y * s_x + 2.f * co.z * s_y));
-            atomicAdd(acc.conic_o + g,
-                      make_float4(-0.5f * kLog2e * s_xx, -kLog2e * s_xy, -0.5f * kLog2e * s_yy, g_o));
-            atomicAdd(acc.color + g, make_float4(g_r, g_g, g_bl, 0.f));
+            for (int r = 0; r < kPxPerLane; ++r) {
+                const int yb = ty0 + 2 * r;  // rows yb, yb + 1 of this band
+                if (rc.y > yb + 1 || rc.w < yb) continue;  // warp-uniform
+                const uint32_t l = ((r < 4 ? lim_lo : lim_hi) >> (8 * (r & 3))) & 0xffu;
+                if (!col_hit || static_cast<uint32_t>(j) >= l) continue;
+                const float dx = mm.x - pxf, dy = mm.y - (static_cast<float>(y0 + 2 * r) + 0.5f);
+                const float G = hw_exp2(fminf(blend_q2(co.x, co.y, co.z, dx, dy), 0.f));
+                const float alpha = co.w * G;
+                if (alpha < kAlphaMin) continue;
+                used = true;
+                const float4 gp = s_grad[warp][r * 32 + lane];
+                const float w = alpha * T[r];
+                const float dot_c = gp.x * c.x + gp.y * c.y + gp.z * c.z;
+                g_r += w * gp.x;
+                g_g += w * gp.y;
+                g_bl += w * gp.z;
+                rho[r] -= w * dot_c;
+                const float one_minus = 1.f - alpha;
+                const float dL_dalpha = T[r] * dot_c - __fdividef(rho[r], fmaxf(one_minus, kOneMinusAlphaEps));
+                g_o += G * dL_dalpha;
+                const float h = alpha * dL_dalpha * kLn2;  // dL/dq2
+                const float hx = h * dx, hy = h * dy;
+                s_x += hx;
+                s_y += hy;
+                s_xx += hx * dx;
+                s_xy += hx * dy;
+                s_yy += hy * dy;
+                if (kAbs) {
+                    a_x += fabsf(2.f * co.x * hx + co.y * hy);
+                    a_y += fabsf(co.y * hx + 2.f * co.z * hy);
+                }
+                T[r] *= one_minus;
+            }
+            if (__ballot_sync(kFullMask, used) == 0u) continue;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                s_x += __shfl_down_sync(kFullMask, s_x, o);
+                s_y += __shfl_down_sync(kFullMask, s_y, o);
+                s_xx += __shfl_down_sync(kFullMask, s_xx, o);
+                s_xy += __shfl_down_sync(kFullMask, s_xy, o);
+                s_yy += __shfl_down_sync(kFullMask, s_yy, o);
+                g_o += __shfl_down_sync(kFullMask, g_o, o);
+                g_r += __shfl_down_sync(kFullMask, g_r, o);
+                g_g += __shfl_down_sync(kFullMask, g_g, o);
+                g_bl += __shfl_down_sync(kFullMask, g_bl, o);
+                if (kAbs) {
+                    a_x += __shfl_down_sync(kFullMask, a_x, o);
+                    a_y += __shfl_down_sync(kFullMask, a_y, o);
+                }
+            }
+            if (lane == 0) {
+                const int g = s_id[warp][j];
+                // q2 = a2 dx^2 + b2 dx dy + c2 dy^2: dq2/dmx = 2 a2 dx + b2 dy, dq2/dmy = b2 dx + 2 c2 dy; then back
+                // from the exp2-scaled conic (a2, b2, c2) = log2(e) (-0.5 A, -B, -0.5 C) to (A, B, C)
+                atomicAdd(acc.mean2d + g, make_float2(2.f * co.x * s_x + co.y * s_y, co.y * s_x + 2.f * co.z * s_y));
+                atomicAdd(acc.conic_o + g,
+                          make_float4(-0.5f * kLog2e * s_xx, -kLog2e * s_xy, -0.5f * kLog2e * s_yy, g_o));
+                atomicAdd(acc.color + g, make_float4(g_r, g_g, g_bl, 0.f));
+                if (kAbs) atomicAdd(acc.mean2d_abs + g, make_float2(a_x, a_y));
+            }
         }
     }
 }
@@ -249,8 +278,13 @@ __device__ __forceinline__ void sh_backward(float x, float y, float z, int bases
     }
 }
 
+struct Densification {
+    float* info;  // [rows, N], accumulated in place
+    int rows;     // 0, 2 or 3
+};
+
 __global__ void __launch_bounds__(kPbThreads) k_preprocess_backward(PParams P, Cam cam, PrimBuffers pb, GradAcc acc,
-                                                                    Grads out) {
+                                                                    Grads out, Densification dens) {
     extern __shared__ __align__(16) float s_sh[];  // [kPbWarps][32 * rest_bases * 3]
     const int i = blockIdx.x * kPbThreads + threadIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -436,6 +470,19 @@ __global__ void __launch_bounds__(kPbThreads) k_preprocess_backward(PParams P, C
         out.means[3 * i + 1] = gpy;
         out.means[3 * i + 2] = gpz;
 
+        // ---- densification statistics: visible count, |dL/dmean2d| in normalised device units (pixels scaled
+        // by half the image size), and with three rows the same norm of the summed per-pixel |dL/dmean2d|
+        if (dens.rows >= 2) {
+            const float hw = 0.5f * static_cast<float>(cam.width), hh = 0.5f * static_cast<float>(cam.height);
+            dens.info[i] += 1.f;
+            dens.info[static_cast<size_t>(P.n) + i] += sqrtf((gm.x * hw) * (gm.x * hw) + (gm.y * hh) * (gm.y * hh));
+            if (dens.rows == 3) {
+                const float2 ga2 = acc.mean2d_abs[i];
+                dens.info[2 * static_cast<size_t>(P.n) + i] +=
+                    sqrtf((ga2.x * hw) * (ga2.x * hw) + (ga2.y * hh) * (ga2.y * hh));
+            }
+        }
+
         // ---- Sc = Wr S3 Wr^T: dL/dS3 = Wr^T gSc Wr; S3 = M M^T: dL/dM = 2 dL/dS3 M
         float t1[3][3], gS3[3][3];
 #pragma unroll
@@ -524,7 +571,7 @@ int gs3d_backward_blend(const float* grad_image, const float* image, int n, long
                         const gs3d_settings* settings, void* prim_buf, size_t prim_bytes_, void* tile_buf,
                         size_t tile_bytes_, void* inst_buf, size_t inst_bytes_, void* bucket_buf,
                         size_t bucket_bytes_, long long bucket_capacity, void* workspace, size_t workspace_bytes,
-                        void* stream) {
+                        int densification_rows, void* stream) {
     Cam cam;
     SPLAT_TRY(fill_cam(settings, cam));
     const long long m = num_instances;
@@ -543,13 +590,22 @@ int gs3d_backward_blend(const float* grad_image, const float* image, int n, long
     TileBuffers tb = carve_tile(ct, cam.width, cam.height);
     InstBuffers ib = carve_inst(ci, m);
     BucketBuffers bb = carve_bucket(cb, bucket_capacity);
+    SPLAT_REQUIRE(densification_rows == 0 || densification_rows == 2 || densification_rows == 3,
+                  "gs3d_backward: densification_info must have 0, 2 or 3 rows (got %d)", densification_rows);
     GradAcc acc = carve_grad(cw, n);
-    SPLAT_CUDA(cudaMemsetAsync(workspace, 0, cw.used, st));
+    const bool abs_grad = densification_rows == 3;
+    // the |dL/dmean2d| sums come last in the workspace and are cleared only when they are accumulated
+    const size_t clear = abs_grad ? cw.used : static_cast<size_t>(reinterpret_cast<char*>(acc.mean2d_abs) -
+                                                                  static_cast<char*>(workspace));
+    SPLAT_CUDA(cudaMemsetAsync(workspace, 0, clear, st));
     if (m > 0) {
-        k_blend_backward<<<div_up(bucket_capacity, kBwdWarps), 32 * kBwdWarps, 0, st>>>(
-            cam, pb.counters, bb.tile, tb.ranges, tb.bstart, tb.max_contrib, ib.point_list, pb.mean2d, pb.conic_o,
-            pb.color_z, pb.rect, grad_image, image, tb.n_contrib, bb.ckpt, n, static_cast<int>(m), bucket_capacity,
-            acc);
+        const long long blocks = std::min<long long>(static_cast<long long>(sm_count()) * SPLAT_BWD_MIN_BLOCKS,
+                                                     div_up(bucket_capacity, kBwdWarps));
+        auto kernel = abs_grad ? k_blend_backward<true> : k_blend_backward<false>;
+        kernel<<<static_cast<unsigned>(blocks), 32 * kBwdWarps, 0, st>>>(
+            cam, pb.counters, bb.reached, acc.work, bb.tile, tb.ranges, tb.bstart, tb.max_contrib, ib.point_list,
+            pb.mean2d, pb.conic_o, pb.color_z, pb.rect, grad_image, image, tb.n_contrib, bb.ckpt, n,
+            static_cast<int>(m), bucket_capacity, acc);
         note_launch();
         SPLAT_TRY(check_launch("gs3d_blend_backward"));
     }
@@ -560,10 +616,14 @@ int gs3d_backward_preprocess(const float* means, const float* scales, const floa
                              const float* opacities, const float* sh_rest, int n, const gs3d_settings* settings,
                              void* prim_buf, size_t prim_bytes_, void* workspace, size_t workspace_bytes,
                              float* grad_means, float* grad_scales, float* grad_rotations, float* grad_opacities,
-                             float* grad_sh0, float* grad_sh_rest, void* stream) {
+                             float* grad_sh0, float* grad_sh_rest, float* densification_info,
+                             int densification_rows, void* stream) {
     Cam cam;
     SPLAT_TRY(fill_cam(settings, cam));
     SPLAT_REQUIRE(n >= 0, "gs3d_backward: bad size n=%d", n);
+    SPLAT_REQUIRE(densification_rows == 0 || ((densification_rows == 2 || densification_rows == 3) &&
+                                              densification_info != nullptr),
+                  "gs3d_backward: densification_info must have 0, 2 or 3 rows (got %d)", densification_rows);
     SPLAT_REQUIRE(prim_bytes_ >= prim_bytes(n) && workspace_bytes >= gs3d_backward_workspace_size(n),
                   "gs3d_backward: a buffer is smaller than its size query");
     if (n == 0) return SPLAT_OK;
@@ -573,7 +633,8 @@ int gs3d_backward_preprocess(const float* means, const float* scales, const floa
     PParams P{means, scales, rotations, opacities, sh_rest, settings->w2c, settings->cam_position, n};
     Grads g{grad_means, grad_scales, grad_rotations, grad_opacities, grad_sh0, grad_sh_rest};
     const size_t smem = static_cast<size_t>(kPbWarps) * 32 * cam.rest_bases * 3 * sizeof(float);
-    k_preprocess_backward<<<div_up(n, kPbThreads), kPbThreads, smem, as_stream(stream)>>>(P, cam, pb, acc, g);
+    const Densification dens{densification_info, densification_rows};
+    k_preprocess_backward<<<div_up(n, kPbThreads), kPbThreads, smem, as_stream(stream)>>>(P, cam, pb, acc, g, dens);
     note_launch();
     return check_launch("gs3d_preprocess_backward");
 }
@@ -584,13 +645,14 @@ int gs3d_backward(const float* grad_image, const float* image, const float* mean
                   size_t tile_bytes_, void* inst_buf, size_t inst_bytes_, void* bucket_buf, size_t bucket_bytes_,
                   long long bucket_capacity, void* workspace, size_t workspace_bytes, float* grad_means,
                   float* grad_scales, float* grad_rotations, float* grad_opacities, float* grad_sh0,
-                  float* grad_sh_rest, void* stream) {
+                  float* grad_sh_rest, float* densification_info, int densification_rows, void* stream) {
     SPLAT_TRY(gs3d_backward_blend(grad_image, image, n, num_instances, settings, prim_buf, prim_bytes_, tile_buf,
                                   tile_bytes_, inst_buf, inst_bytes_, bucket_buf, bucket_bytes_, bucket_capacity,
-                                  workspace, workspace_bytes, stream));
+                                  workspace, workspace_bytes, densification_rows, stream));
     return gs3d_backward_preprocess(means, scales, rotations, opacities, sh_rest, n, settings, prim_buf,
                                     prim_bytes_, workspace, workspace_bytes, grad_means, grad_scales, grad_rotations,
-                                    grad_opacities, grad_sh0, grad_sh_rest, stream);
+                                    grad_opacities, grad_sh0, grad_sh_rest, densification_info, densification_rows,
+                                    stream);
 }
 
 }  // extern "C"

@@ -77,7 +77,7 @@ struct PrimBuffers {
     uint32_t* depth_key_sorted;
     uint32_t* order;       // Gaussian ids in (depth, id) order: the depth passes of the 64-bit key sort
     uint32_t* offsets;     // exclusive prefix of n_touched, in that order
-    uint32_t* counters;    // [0] = instance count M, [1] = bucket count B
+    uint32_t* counters;    // [0] = instance count M, [1] = bucket count B, [2] = buckets the backward replays
     void* scan_ws;
     size_t scan_bytes;
     void* sort_ws;
@@ -109,8 +109,9 @@ struct InstBuffers {
 
 // Per-bucket buffer, sized by the bucket bound floor((M + 31 T) / 32) + 1
 struct BucketBuffers {
-    uint32_t* tile;  // [B] tile of each bucket
-    float4* ckpt;    // [B * 256] (C.r, C.g, C.b, T) at the bucket start, per tile pixel
+    uint32_t* tile;     // [B] tile of each bucket
+    uint32_t* reached;  // [B] the buckets before their tile's last contributor, in no set order (count: counters[2])
+    float4* ckpt;       // [B * 256] (C.r, C.g, C.b, T) at the bucket start, per tile pixel
 };
 
 inline long long bucket_bound(long long m, int T) { return (m + 31ll * T) / 32 + 1; }
@@ -169,6 +170,7 @@ inline InstBuffers carve_inst(Carver& c, long long m) {
 inline BucketBuffers carve_bucket(Carver& c, long long bcap) {
     BucketBuffers b;
     b.tile = c.take<uint32_t>(static_cast<size_t>(bcap < 1 ? 1 : bcap));
+    b.reached = c.take<uint32_t>(static_cast<size_t>(bcap < 1 ? 1 : bcap));
     b.ckpt = c.take<float4>(static_cast<size_t>(bcap < 1 ? 1 : bcap) * kTilePixels);
     return b;
 }

@@ -195,32 +195,123 @@ __global__ void k_gather_counts(const uint32_t* __restrict__ order, const uint32
     counts_sorted[r] = n_touched[min(order[r], static_cast<uint32_t>(n - 1))];
 }
 
+constexpr int kDupThreads = 256;
+constexpr int kDupStage = 4096;   // instances of a block staged in shared memory (32 KB)
+#ifndef SPLAT_DUP_WARP_MIN
+#define SPLAT_DUP_WARP_MIN 24
+#endif
+constexpr int kDupWarpMin = SPLAT_DUP_WARP_MIN;  // Gaussians listed in more tiles are enumerated by their warp
+
+// Instance `slot` of the block (counted from the block's first output slot `base`): staged in shared memory
+// when it fits, else written straight to global memory.
+__device__ __forceinline__ void put_instance(uint32_t* s_key, uint32_t* s_val, const InstBuffers& ib,
+                                             uint32_t base, uint32_t slot, uint32_t key, uint32_t id) {
+    if (slot < kDupStage) {
+        s_key[slot] = key;
+        s_val[slot] = id;
+    } else {
+        ib.keys[base + slot] = key;
+        ib.vals[base + slot] = id;
+    }
+}
+
 // One (tile, id) per listed tile, Gaussians taken in (depth, id) order so that the stable tile sort that
 // follows completes the LSD sort of the 64-bit (tile << 32 | depth) keys. Never more than the counted
 // n_touched per Gaussian (a shortfall, which the shared row test rules out, is padded past the last tile).
-__global__ void k_duplicate(int n, Cam cam, PrimBuffers pb, InstBuffers ib) {
-    const int r = blockIdx.x * blockDim.x + threadIdx.x;
-    if (r >= n) return;
-    const uint32_t i = pb.order[r];
-    if (i >= static_cast<uint32_t>(n)) return;
-    const uint32_t cnt = pb.n_touched[i];
-    if (cnt == 0) return;
-    const float2 m = pb.mean2d[i];
-    const float4 co = pb.conic_o[i];
-    const Ellipse e = make_ellipse(m.x, m.y, co.x, co.y, co.z, pb.thr[i]);
-    const uint32_t off = pb.offsets[r];
-    uint32_t k = 0;
-    const int2 rows = ellipse_rows(e, cam.height, cam.tiles_y);
-    for (int ty = rows.x; ty <= rows.y && k < cnt; ++ty) {
-        const int2 t = ellipse_row_tiles(e, ty, cam.width, cam.height, cam.tiles_x);
-        for (int tx = t.x; tx <= t.y && k < cnt; ++tx, ++k) {
-            ib.keys[off + k] = static_cast<uint32_t>(ty * cam.tiles_x + tx);
-            ib.vals[off + k] = i;
+// The 256 Gaussians of a block (consecutive in depth order) own one contiguous range of instance slots,
+// so their instances are assembled in shared memory and stored with coalesced writes. A Gaussian listed in
+// at most kDupWarpMin tiles is enumerated by its own thread; a larger one by its whole warp, lane per tile
+// row, then lane per instance - the same rows and tiles in the same order.
+__global__ void __launch_bounds__(kDupThreads) k_duplicate(int n, Cam cam, PrimBuffers pb, InstBuffers ib) {
+    __shared__ uint32_t s_key[kDupStage];
+    __shared__ uint32_t s_val[kDupStage];
+    const int lane = threadIdx.x & 31;
+    const int r0 = blockIdx.x * kDupThreads;  // < n: the grid covers n
+    const int r = r0 + threadIdx.x;
+    const uint32_t pad_key = static_cast<uint32_t>(cam.tiles_x * cam.tiles_y);
+    const uint32_t base = pb.offsets[r0];
+    const uint32_t end = r0 + kDupThreads < n ? pb.offsets[r0 + kDupThreads] : pb.counters[0];
+
+    uint32_t id = 0u, cnt = 0u, slot = 0u;
+    Ellipse e{};
+    if (r < n) {
+        id = pb.order[r];
+        if (id < static_cast<uint32_t>(n)) {
+            cnt = pb.n_touched[id];
+            slot = pb.offsets[r] - base;
+            if (cnt > 0u) {
+                const float2 m = pb.mean2d[id];
+                const float4 co = pb.conic_o[id];
+                e = make_ellipse(m.x, m.y, co.x, co.y, co.z, pb.thr[id]);
+            }
         }
     }
-    for (; k < cnt; ++k) {
-        ib.keys[off + k] = static_cast<uint32_t>(cam.tiles_x * cam.tiles_y);
-        ib.vals[off + k] = i;
+    if (cnt > 0u && cnt <= static_cast<uint32_t>(kDupWarpMin)) {
+        uint32_t k = 0u;
+        const int2 rows = ellipse_rows(e, cam.height, cam.tiles_y);
+        for (int ty = rows.x; ty <= rows.y && k < cnt; ++ty) {
+            const int2 t = ellipse_row_tiles(e, ty, cam.width, cam.height, cam.tiles_x);
+            for (int tx = t.x; tx <= t.y && k < cnt; ++tx, ++k)
+                put_instance(s_key, s_val, ib, base, slot + k, static_cast<uint32_t>(ty * cam.tiles_x + tx), id);
+        }
+        for (; k < cnt; ++k) put_instance(s_key, s_val, ib, base, slot + k, pad_key, id);
+    }
+    unsigned big = __ballot_sync(kFullMask, cnt > static_cast<uint32_t>(kDupWarpMin));
+    while (big) {
+        const int src = __ffs(big) - 1;
+        big &= big - 1u;
+        Ellipse g;
+        g.mx = __shfl_sync(kFullMask, e.mx, src);
+        g.my = __shfl_sync(kFullMask, e.my, src);
+        g.A = __shfl_sync(kFullMask, e.A, src);
+        g.B = __shfl_sync(kFullMask, e.B, src);
+        g.R = __shfl_sync(kFullMask, e.R, src);
+        g.D = __shfl_sync(kFullMask, e.D, src);
+        g.ey = __shfl_sync(kFullMask, e.ey, src);
+        g.s = __shfl_sync(kFullMask, e.s, src);
+        g.inv_a = __shfl_sync(kFullMask, e.inv_a, src);
+        const uint32_t gid = __shfl_sync(kFullMask, id, src);
+        const uint32_t gcnt = __shfl_sync(kFullMask, cnt, src);
+        const uint32_t gslot = __shfl_sync(kFullMask, slot, src);
+        const int2 rows = ellipse_rows(g, cam.height, cam.tiles_y);
+        uint32_t k = 0u;  // instances written so far (warp-uniform)
+        for (int ty0 = rows.x; ty0 <= rows.y && k < gcnt; ty0 += 32) {
+            const int ty = ty0 + lane;
+            int2 t = make_int2(1, 0);
+            if (ty <= rows.y) t = ellipse_row_tiles(g, ty, cam.width, cam.height, cam.tiles_x);
+            const uint32_t c = t.y >= t.x ? static_cast<uint32_t>(t.y - t.x + 1) : 0u;
+            uint32_t incl = c;  // inclusive prefix of the row counts over the lanes
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t v = __shfl_up_sync(kFullMask, incl, o);
+                if (lane >= o) incl += v;
+            }
+            const uint32_t chunk = __shfl_sync(kFullMask, incl, 31);
+            for (uint32_t j0 = 0u; j0 < chunk; j0 += 32u) {
+                const uint32_t j = j0 + lane;
+                int owner = 0;  // first lane whose inclusive count exceeds j
+#pragma unroll
+                for (int step = 16; step > 0; step >>= 1) {
+                    const uint32_t v = __shfl_sync(kFullMask, incl, owner + step - 1);
+                    if (v <= j) owner += step;
+                }
+                const uint32_t before = __shfl_sync(kFullMask, incl, owner > 0 ? owner - 1 : 0);
+                const int tx0 = __shfl_sync(kFullMask, t.x, owner);
+                if (j < chunk && k + j < gcnt) {
+                    const uint32_t row_start = owner > 0 ? before : 0u;
+                    const uint32_t key = static_cast<uint32_t>((ty0 + owner) * cam.tiles_x + tx0) + (j - row_start);
+                    put_instance(s_key, s_val, ib, base, gslot + k + j, key, gid);
+                }
+            }
+            k += min(chunk, gcnt - k);
+        }
+        for (uint32_t p = k + lane; p < gcnt; p += 32u) put_instance(s_key, s_val, ib, base, gslot + p, pad_key, gid);
+    }
+    __syncthreads();
+    const uint32_t staged = min(end - base, static_cast<uint32_t>(kDupStage));
+    for (uint32_t j = threadIdx.x; j < staged; j += kDupThreads) {
+        ib.keys[base + j] = s_key[j];
+        ib.vals[base + j] = s_val[j];
     }
 }
 
@@ -257,12 +348,14 @@ __global__ void __launch_bounds__(kTilePixels) k_blend(Cam cam, const uint2* __r
                                                        float* __restrict__ image, float* __restrict__ final_T,
                                                        uint32_t* __restrict__ n_contrib,
                                                        uint32_t* __restrict__ max_contrib, float4* __restrict__ ckpt,
+                                                       uint32_t* __restrict__ counters, uint32_t* __restrict__ reached,
                                                        int n, int m, long long bcap) {
     __shared__ float2 s_mean[kTilePixels];
     __shared__ float4 s_con[kTilePixels];
     __shared__ float4 s_col[kTilePixels];
     __shared__ ushort4 s_rect[kTilePixels];
     __shared__ uint32_t s_max[kTilePixels / 32];
+    __shared__ uint32_t s_reach[2];  // this tile's replayed buckets: first slot in `reached`, count
 
     const int tile = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -340,6 +433,15 @@ __global__ void __launch_bounds__(kTilePixels) k_blend(Cam cam, const uint2* __r
 #pragma unroll
         for (int w = 0; w < kTilePixels / 32; ++w) mxv = max(mxv, s_max[w]);
         max_contrib[tile] = mxv;
+        // the buckets up to the last contributor are the ones the backward replays: list them
+        const uint32_t nreach = (mxv + kBucket - 1) / kBucket;
+        s_reach[0] = nreach ? atomicAdd(counters + 2, nreach) : 0u;
+        s_reach[1] = nreach;
+    }
+    __syncthreads();
+    for (uint32_t i = tid; i < s_reach[1]; i += kTilePixels) {
+        const long long slot = static_cast<long long>(s_reach[0]) + i, b = b0 + i;
+        if (slot < bcap && b < bcap) reached[slot] = static_cast<uint32_t>(b);
     }
     if (inside) {
         const int pix = y * cam.width + x;
@@ -454,8 +556,9 @@ int gs3d_render(int n, long long num_instances, const gs3d_settings* settings, v
     InstBuffers ib = carve_inst(ci, m);
     BucketBuffers bb = carve_bucket(cb, bucket_capacity);
     SPLAT_CUDA(cudaMemsetAsync(tb.ranges, 0, sizeof(uint2) * T, st));
+    SPLAT_CUDA(cudaMemsetAsync(pb.counters + 2, 0, sizeof(uint32_t), st));  // k_blend counts the replayed buckets
     if (m > 0) {
-        k_duplicate<<<div_up(n, 256), 256, 0, st>>>(n, cam, pb, ib);
+        k_duplicate<<<div_up(n, kDupThreads), kDupThreads, 0, st>>>(n, cam, pb, ib);
         note_launch();
         SPLAT_TRY(check_launch("gs3d_duplicate"));
         // the tile-digit passes (the pad key T needs bit_width(T) bits)
@@ -475,7 +578,7 @@ int gs3d_render(int n, long long num_instances, const gs3d_settings* settings, v
     SPLAT_TRY(check_launch("gs3d_bucket_tiles"));
     k_blend<<<T, kTilePixels, 0, st>>>(cam, tb.ranges, tb.bstart, ib.point_list, pb.mean2d, pb.conic_o, pb.color_z,
                                        pb.rect, settings->bg, image, tb.final_T, tb.n_contrib, tb.max_contrib, bb.ckpt,
-                                       n < 1 ? 1 : n, static_cast<int>(m), bucket_capacity);
+                                       pb.counters, bb.reached, n < 1 ? 1 : n, static_cast<int>(m), bucket_capacity);
     note_launch();
     return check_launch("gs3d_blend");
 }

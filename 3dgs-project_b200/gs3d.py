@@ -121,7 +121,9 @@ def backward(densification_info, grad_image, image, means, scales, rotations, op
              focal_y, center_x, center_y, near_plane, far_plane, proper_antialiasing, n_instances, n_buckets,
              selector, *mode, out: tuple | None = None, stage_event: torch.cuda.Event | None = None):
     """Faster-GS `_C.backward` (the trailing blend-backward mode of the phase1 patch is accepted and ignored:
-    there is one blend backward here). Returns (means, scales, rotations, opacities[N,1], sh0[N,1,3], sh_rest).
+    there is one blend backward here). Returns (means, scales, rotations, opacities[N,1], sh0[N,1,3], sh_rest) and
+    accumulates densification_info ([0 | 2 | 3, N]) in place: visible count, |dL/dmean2d| in normalised device
+    units, and with three rows the norm of the summed per-pixel absolute mean2d gradients.
     ``out`` may supply the six contiguous float32 result tensors (e.g. views of one flat gradient buffer).
     It runs as its two launches (gs3d_backward_blend, gs3d_backward_preprocess); ``stage_event``, if given, is
     recorded on the stream between them."""
@@ -142,26 +144,47 @@ def backward(densification_info, grad_image, image, means, scales, rotations, op
     else:
         grads = (torch.empty(n, 3, device=dev), torch.empty(n, 3, device=dev), torch.empty(n, 4, device=dev),
                  torch.empty(n, 1, device=dev), torch.empty(n, 1, 3, device=dev), torch.empty(n, rest, 3, device=dev))
+    rows, dinfo = _densification(densification_info, n)
     stream = L.stream_of(means)
     L.call("gs3d_backward_blend", L.ptr(g_img), L.ptr(image), n, int(n_instances), ctypes.byref(s), L.ptr(prim_buf),
            prim_buf.numel(), L.ptr(tile_buf), tile_buf.numel(), L.ptr(inst_buf), inst_buf.numel(), L.ptr(bucket_buf),
-           bucket_buf.numel(), int(n_buckets), L.ptr(ws), ws.numel(), stream)
+           bucket_buf.numel(), int(n_buckets), L.ptr(ws), ws.numel(), rows, stream)
     if stage_event is not None:
         stage_event.record(torch.cuda.current_stream(dev))
     L.call("gs3d_backward_preprocess", L.ptr(means), L.ptr(scales), L.ptr(rotations), L.ptr(opacities),
            L.ptr(sh_rest), n, ctypes.byref(s), L.ptr(prim_buf), prim_buf.numel(), L.ptr(ws), ws.numel(),
-           *map(L.ptr, grads), stream)
+           *map(L.ptr, grads), L.ptr(dinfo), rows, stream)
     return grads
 
 
+def _densification(densification_info, n: int):
+    """(rows, tensor or None): the reference's densification_info argument, float32 [0 | 2 | 3, N] on the GPU,
+    accumulated in place (an empty tensor or None means no statistics)."""
+    if densification_info is None or densification_info.numel() == 0:
+        return 0, None
+    L.check_cuda("densification_info", densification_info, torch.float32)
+    if densification_info.dim() != 2 or densification_info.shape[0] not in (2, 3) or densification_info.shape[1] != n:
+        raise RuntimeError(f"densification_info must be [2 or 3, {n}], got {tuple(densification_info.shape)}")
+    return int(densification_info.shape[0]), densification_info
+
+
 class _Rasterize(torch.autograd.Function):
-    """The autograd function behind diff_rasterize (phase1/fastergs_macro.patch:565-594 shows its backward)."""
+    """The autograd function behind diff_rasterize (phase1/fastergs_macro.patch:565-594 shows its backward).
+
+    Visibility hand-off for the sparse optimizer (cluster/patches/fastergs_lean_adam.patch:213-220,328-345): while
+    track_visibility is set, each forward stores the per-primitive n_touched_tiles (int32 [N], > 0 = visible in
+    that view) in last_visibility."""
+
+    track_visibility: bool = False
+    last_visibility: torch.Tensor | None = None
 
     @staticmethod
     def forward(ctx: Any, means, scales, rotations, opacities, sh0, sh_rest, densification_info,
                 settings: RasterizerSettings):
         params = [t.contiguous() for t in (means, scales, rotations, opacities, sh0, sh_rest)]
         image, prim, tile, inst, bucket, m, nb, sel = forward(*params, *settings.as_tuple())
+        if _Rasterize.track_visibility:
+            _Rasterize.last_visibility = n_touched_tiles(prim, params[0].shape[0])
         ctx.settings = settings
         ctx.buffer_state = (m, nb, sel)
         ctx.densification_info = densification_info

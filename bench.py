@@ -45,9 +45,10 @@ METRIC = "fwd+bwd ms/iter (3M Gaussians, 1080p, SH3); train views/s at 1/2/4/8 B
 LRS = {"means": 1.6e-4, "scales": 5e-3, "rotations": 1e-3, "opacities": 5e-2, "sh0": 2.5e-3, "sh_rest": 2.5e-3}
 NAMES = ("means", "scales", "rotations", "opacities", "sh0", "sh_rest")
 WIDTHS = (3, 3, 4, 1, 3, 45)  # floats per Gaussian in each group: 59 in total
-# dram__bytes_read.sum + dram__bytes_write.sum of one k_blend_backward launch on the C3 workload, from one ncu
-# capture (profiles/); None until captured.
-BLEND_BWD_TRAFFIC = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch on the C3 workload, from one ncu capture each
+# (profiles/); None where not captured.
+BLEND_BWD_TRAFFIC = 225540096 + 5898240
+ADAM_TRAFFIC = 2832050688 + 2067712256
 
 
 class Clocks:
@@ -166,7 +167,7 @@ class Trainer:
         if timed:
             e[2].record()
             self.ev["blend_bwd"].append((e[1], e[5]))
-        self.last = (prim, m, cam)
+        self.last = (prim, tile, m, cam)
         if self.world > 1:
             torch.distributed.all_reduce(self.flat)
         if timed:
@@ -223,8 +224,7 @@ def run_ours(args) -> None:
         torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
     ms_max = float(ms_t.item())
     stage = {k: sum(a.elapsed_time(b) for a, b in v) / max(len(v), 1) for k, v in tr.ev.items()}
-    prim, m_last, cam_last = tr.last
-    buckets_last = int(gs3d.primitive_views(prim, tr.n)["counters"][1].item())
+    reach = blend_reach(tr, W, H)
 
     # end to end through the public API: pinned host upstream gradient in, loss out, every step
     e2e = run_e2e(sc, cams, dev, world, args, tr)
@@ -249,7 +249,7 @@ def run_ours(args) -> None:
             "e2e": e2e,
             "gpu_launches": launches,
         }
-        line.update(roofline(tr, stage, m_last, buckets_last, W * H))
+        line.update(roofline(tr, stage, reach, W * H))
         line["cpu_baseline"] = cpu_baseline(args, sc, cam) if not args.no_cpu_baseline else None
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -257,65 +257,117 @@ def run_ours(args) -> None:
 
 
 def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
+    """The training step through the public API (diff_rasterize + autograd + FusedAdam). Every step copies its
+    upstream gradient from pinned host memory (on a copy stream, into one of two device buffers, issued one step
+    ahead so that the copy overlaps the previous step's kernels) and copies its loss back into pinned host memory;
+    all of those copies sit inside the timed region."""
     leaves = [p.clone().requires_grad_(True) for p in tr.params]
     opt = gs_adam.FusedAdam([{"params": [p], "lr": LRS[nm]} for p, nm in zip(leaves, NAMES)], lr=0.0, eps=1e-15)
     cam = cams[0]
     H, W = cam["height"], cam["width"]
     host = (1e-3 * torch.randn(3, H, W, generator=torch.Generator().manual_seed(99))).pin_memory()
     settings = gs3d.RasterizerSettings(*scenes.settings_tuple(cam, tr.bases, dev))
-    flat_grads = None
+    compute = torch.cuda.current_stream(dev)
+    copier = torch.cuda.Stream(dev)
+    dbuf = [torch.empty_like(host, device=dev) for _ in range(2)]
+    copied = [torch.cuda.Event() for _ in range(2)]
+    used = [torch.cuda.Event() for _ in range(2)]
+    total = args.warmup + args.steps
+    losses = torch.empty(total, dtype=torch.float32).pin_memory()
 
-    def step():
-        dout = host.to(dev, non_blocking=True)
+    def issue_copy(k):
+        b = k % 2
+        with torch.cuda.stream(copier):
+            copier.wait_event(used[b])  # the step that last read this buffer is done with it
+            dbuf[b].copy_(host, non_blocking=True)
+            copied[b].record(copier)
+
+    def step(k):
+        b = k % 2
+        compute.wait_event(copied[b])
+        if k + 1 < total and k + 1 != args.warmup:  # the first timed step's copy is issued inside the timed region
+            issue_copy(k + 1)
+        dout = dbuf[b]
         img = gs3d.diff_rasterize(*leaves, torch.empty(0), settings)
         loss = (img * dout).sum()
         opt.zero_grad(set_to_none=True)
         loss.backward()
+        used[b].record(compute)
         if world > 1:
             for p in leaves:
                 torch.distributed.all_reduce(p.grad)
         opt.step()
-        return loss.detach().to("cpu", non_blocking=False)
+        losses[k:k + 1].copy_(loss.detach().view(1), non_blocking=True)
 
-    for _ in range(max(1, args.warmup)):
-        step()
+    for e in used:
+        e.record(compute)
+    issue_copy(0)
+    for k in range(args.warmup):
+        step(k)
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(args.steps):
-        step()
-    b.record()
+    a.record(compute)
+    copier.wait_stream(compute)  # the first timed copy starts after the timed region does
+    issue_copy(args.warmup)
+    for k in range(args.warmup, total):
+        step(k)
+    b.record(compute)
     torch.cuda.synchronize()
+    assert bool(torch.isfinite(losses).all())
     ms = torch.tensor([a.elapsed_time(b)], device=dev)
     if world > 1:
         torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
-    del flat_grads
     return {"value": round(world * args.steps / (float(ms.item()) / 1000.0), 3), "unit": "views/s",
-            "h2d_bytes_per_step": int(host.numel() * 4), "d2h_bytes_per_step": 4}
+            "h2d_bytes_per_step": int(host.numel() * 4), "d2h_bytes_per_step": 4,
+            "note": "upstream gradient copied from pinned host memory one step ahead on a copy stream; loss copied "
+                    "back to pinned host memory every step"}
 
 
-def roofline(tr: Trainer, stage: dict, m: int, buckets: int, pixels: int) -> dict:
-    """Roofline of the dominant kernel, the blend backward (k_blend_backward, with the clear of its
-    accumulators), timed live with CUDA events around its call in every timed step. Algorithmic bytes per
-    launch: checkpoints 16 B x 256 pixels x B buckets + 24 B per pixel (upstream gradient, image, final T /
-    contributor counts) + 40 B per instance (id, mean2d, conic + opacity, colour) + 36 B per Gaussian (the
-    accumulator clear). The bucket count B is read from the last step's counters."""
+def blend_reach(tr: Trainer, width: int, height: int) -> dict:
+    """What the last step's blend backward had to touch: per tile the list positions up to its last contributor
+    (min(max_contrib, range length)), the 32-splat buckets those make, and the bucket count of the whole view."""
+    prim, tile, m, _ = tr.last
+    tv = gs3d.tile_views(tile, width, height)
+    rg = tv["ranges"].long()
+    reach = torch.minimum(tv["max_contrib"].long(), (rg[:, 1] - rg[:, 0]).clamp(min=0))
+    return {"instances": m, "buckets": int(gs3d.primitive_views(prim, tr.n)["counters"][1].item()),
+            "reached_positions": int(reach.sum().item()), "reached_buckets": int(((reach + 31) // 32).sum().item())}
+
+
+def roofline(tr: Trainer, stage: dict, reach: dict, pixels: int) -> dict:
+    """Roofline of the kernel with the largest share of the step, each timed live with CUDA events around its call
+    in every timed step (k_blend_backward with the clear of its accumulators, or k_adam).
+      k_blend_backward: 16 B of checkpoint per pixel of every reached bucket + 28 B per pixel (upstream gradient,
+        image, contributor count) + 40 B per reached list position (id, mean2d, conic + opacity, colour) + 36 B per
+        Gaussian (accumulator clear). Its limiter is instruction issue (FP32, ex2, shuffles), not HBM: the HBM
+        fraction it reports is low by nature; profiles/ holds its issue and pipe utilisation.
+      k_adam: 59 floats x 4 B x 7 accesses (param, grad, m, v read; param, m, v written) = 1652 B per Gaussian."""
     peaks_path = ROOT / "MEASURED_PEAKS.json"
     hbm, src = 6650.0, "fallback"
     if peaks_path.exists():
         v = json.loads(peaks_path.read_text()).get("hbm_gbs")
         if v:
             hbm, src = float(v), "measured"
-    algo = 16.0 * 256 * buckets + 24.0 * pixels + 40.0 * m + 36.0 * tr.n
-    t_ms = stage["blend_bwd"]
-    ach = algo / (t_ms / 1000.0) / 1e9 if t_ms > 0 else 0.0
-    return {"roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(ach / hbm, 4), "traffic": BLEND_BWD_TRAFFIC,
-                         "kernel": "k_blend_backward (+ accumulator clear)", "kernel_ms": round(t_ms, 4),
-                         "algorithmic_bytes": int(algo), "buckets": buckets, "instances": m,
-                         "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src}}
+    blend = {"kernel": "k_blend_backward (+ accumulator clear)", "ms": stage["blend_bwd"],
+             "bytes": 16.0 * 256 * reach["reached_buckets"] + 28.0 * pixels + 40.0 * reach["reached_positions"]
+             + 36.0 * tr.n, "traffic": BLEND_BWD_TRAFFIC, "limiter": "issue (FP32 / ex2 / shuffles)"}
+    adam = {"kernel": "k_adam", "ms": stage["adam"], "bytes": 1652.0 * tr.n, "traffic": ADAM_TRAFFIC,
+            "limiter": "HBM"}
+    top, other = (blend, adam) if blend["ms"] >= adam["ms"] else (adam, blend)
+
+    def entry(k):
+        ach = k["bytes"] / (k["ms"] / 1000.0) / 1e9 if k["ms"] > 0 else 0.0
+        return {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s", "frac": round(ach / hbm, 4),
+                "traffic": k["traffic"], "kernel": k["kernel"], "kernel_ms": round(k["ms"], 4),
+                "algorithmic_bytes": int(k["bytes"]), "limiter": k["limiter"],
+                "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src}
+
+    out = entry(top)
+    out["next_kernel"] = entry(other)
+    out["blend_reach"] = reach
+    return {"roofline": out}
 
 
 def cpu_baseline(args, sc, cam):

@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define SPLAT_ABI_VERSION 1
+#define SPLAT_ABI_VERSION 2
 
 #define SPLAT_OK 0
 #define SPLAT_ERR_ARG 1      /* bad shape, size or pointer */
@@ -204,27 +204,34 @@ int gs3d_render(int n, long long num_instances, const gs3d_settings* settings, v
                 size_t bucket_bytes, long long bucket_capacity, float* image, void* stream);
 /* Backward: grad_image f32[3,H,W] -> grad_means f32[N,3], grad_scales f32[N,3], grad_rotations f32[N,4],
  * grad_opacities f32[N], grad_sh0 f32[N,3], grad_sh_rest f32[N,rest_bases,3] (zeros for Gaussians that
- * were not visible). The bucket count is read on the device, so no host sync happens. */
+ * were not visible). The bucket count is read on the device, so no host sync happens.
+ * densification_info f32[rows, N] (rows 0, 2 or 3; NULL when 0) is accumulated in place, as the reference's
+ * backward does with its first argument: row 0 += 1 for every visible Gaussian, row 1 += |dL/dmean2d| with the
+ * pixel gradient scaled by (W/2, H/2) to normalised device units, row 2 (three rows) += the same norm of the
+ * per-pixel absolute mean2d gradients summed over the view. */
 int gs3d_backward(const float* grad_image, const float* image, const float* means, const float* scales,
                   const float* rotations, const float* opacities, const float* sh_rest, int n, long long num_instances,
                   const gs3d_settings* settings, void* prim_buf, size_t prim_bytes, void* tile_buf,
                   size_t tile_bytes, void* inst_buf, size_t inst_bytes, void* bucket_buf, size_t bucket_bytes,
                   long long bucket_capacity, void* workspace, size_t workspace_bytes, float* grad_means,
                   float* grad_scales, float* grad_rotations, float* grad_opacities, float* grad_sh0,
-                  float* grad_sh_rest, void* stream);
+                  float* grad_sh_rest, float* densification_info, int densification_rows, void* stream);
 /* gs3d_backward in its two launches (the reference's _C.backward runs both back to back): the blend
- * backward accumulates the per-Gaussian 2D gradients (mean2d, conic, opacity, colour) into workspace,
- * which it clears first; the preprocess backward turns them into the parameter gradients. Called in this
- * order on one stream they give exactly gs3d_backward's results. */
+ * backward accumulates the per-Gaussian 2D gradients (mean2d, conic, opacity, colour, and with three
+ * densification rows the absolute mean2d gradients) into workspace, which it clears first; the preprocess
+ * backward turns them into the parameter gradients and the densification rows. Called in this order on one
+ * stream, with the same densification_rows, they give exactly gs3d_backward's results. */
 int gs3d_backward_blend(const float* grad_image, const float* image, int n, long long num_instances,
                         const gs3d_settings* settings, void* prim_buf, size_t prim_bytes, void* tile_buf,
                         size_t tile_bytes, void* inst_buf, size_t inst_bytes, void* bucket_buf, size_t bucket_bytes,
-                        long long bucket_capacity, void* workspace, size_t workspace_bytes, void* stream);
+                        long long bucket_capacity, void* workspace, size_t workspace_bytes, int densification_rows,
+                        void* stream);
 int gs3d_backward_preprocess(const float* means, const float* scales, const float* rotations,
                              const float* opacities, const float* sh_rest, int n, const gs3d_settings* settings,
                              void* prim_buf, size_t prim_bytes, void* workspace, size_t workspace_bytes,
                              float* grad_means, float* grad_scales, float* grad_rotations, float* grad_opacities,
-                             float* grad_sh0, float* grad_sh_rest, void* stream);
+                             float* grad_sh0, float* grad_sh_rest, float* densification_info,
+                             int densification_rows, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
  * Fused Adam (replaces the per-group `_C.adam_step` launches of Faster-GS's FusedAdam,
@@ -237,11 +244,36 @@ typedef struct adam_group {
     float* exp_avg;        /* device f32[n] first moment */
     float* exp_avg_sq;     /* device f32[n] second moment */
     long long n;
-    float lr;
+    double lr;
 } adam_group;
-/* One Adam step (step = t >= 1) over `count` groups (host array, at most SPLAT_ADAM_MAX_GROUPS). */
-int adam_step_multi(int count, const adam_group* groups, int step, float beta1, float beta2, float eps,
+/* One Adam step (step = t >= 1) over `count` groups (host array, at most SPLAT_ADAM_MAX_GROUPS). As in the
+ * reference's wrapper, lr and the betas arrive in double precision for the bias corrections (step size
+ * lr / (1 - beta1^t), 1 / sqrt(1 - beta2^t), computed in double and rounded once); the kernel uses their
+ * float32 values. */
+int adam_step_multi(int count, const adam_group* groups, int step, double beta1, double beta2, double eps,
                     void* stream);
+
+/* Lean Adam (replaces `_C.adam_step_sparse`, cluster/patches/fastergs_lean_adam.patch:84-182, again with one
+ * launch over every group). The per-element update of adam_step_multi, with two options:
+ *  - visibility (device int32[n_primitives], may be NULL = every primitive): element i of a group belongs to
+ *    primitive i / features; elements of primitives whose visibility is 0 keep their parameter and moments;
+ *  - lowp_moments (per group): exp_avg / exp_avg_sq are bfloat16, read exactly and written with stochastic
+ *    rounding - uniform noise in the 16 dropped bits, from the lowbias32 hash of ((uint32) i ^ seed) with
+ *    seed = 0x9E3779B9 * step + 0x85EBCA6B for the first moment and the hash of that for the second - then
+ *    truncated.
+ * With visibility NULL and fp32 moments it computes exactly what adam_step_multi computes. */
+typedef struct adam_lean_group {
+    float* param;          /* device f32[n], updated in place */
+    const float* grad;     /* device f32[n] */
+    void* exp_avg;         /* device f32[n], or bf16[n] when lowp_moments */
+    void* exp_avg_sq;      /* device f32[n], or bf16[n] when lowp_moments */
+    long long n;
+    double lr;
+    int features;          /* elements per primitive, n = features * n_primitives when visibility is given */
+    int lowp_moments;
+} adam_lean_group;
+int adam_step_multi_lean(int count, const adam_lean_group* groups, int step, double beta1, double beta2,
+                         double eps, const int32_t* visibility, long long n_primitives, void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -45,7 +45,7 @@ def load():
         lib.gs3o_backward_reset.argtypes = [_P]
         lib.gs3o_blend_backward.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int]
         lib.gs3o_preprocess_backward.argtypes = [_P] * 12
-        lib.gs3o_adam.argtypes = [_P] * 4 + [ctypes.c_longlong, ctypes.c_int] + [ctypes.c_float] * 4
+        lib.gs3o_adam.argtypes = [_P] * 4 + [ctypes.c_longlong, ctypes.c_int] + [ctypes.c_double] * 4
         for name in ("mean2d", "conic_o", "color_z", "thr", "n_touched", "point_list", "keys_sorted", "ranges",
                      "image", "final_T", "n_contrib"):
             getattr(lib, f"gs3o_{name}").restype = _P

@@ -629,10 +629,12 @@ void gs3o_preprocess_backward(gs3o_ctx* c, const float* means, const float* scal
     }
 }
 
-void gs3o_adam(float* param, const float* grad, float* m, float* v, long long n, int step, float lr, float b1,
-               float b2, float eps) {
-    const double bc1 = 1.0 - pow((double)b1, step), bc2 = 1.0 - pow((double)b2, step);
-    const float step_size = (float)(lr / bc1), bc2r = (float)(1.0 / sqrt(bc2));
+void gs3o_adam(float* param, const float* grad, float* m, float* v, long long n, int step, double lr_d, double b1_d,
+               double b2_d, double eps_d) {
+    // host arithmetic of the reference wrapper (fastergs_lean_adam.patch:162-164), kernel values in float
+    const float step_size = (float)(lr_d * (1.0 / (1.0 - pow(b1_d, step))));
+    const float bc2r = (float)(1.0 / sqrt(1.0 - pow(b2_d, step)));
+    const float b1 = (float)b1_d, b2 = (float)b2_d, eps = (float)eps_d;
     // squared tiny gradients are subnormal; x86 handles those in microcode, so flush them (each thread)
 #pragma omp parallel for schedule(static)
     for (long long e = 0; e < n; ++e) {

@@ -86,13 +86,20 @@ def preprocess(means, scales, rotations, opacities, sh0, sh_rest, w2c, cam_posit
     return mean2d, conic, o, color, z, det
 
 
-def render(means, scales, rotations, opacities, sh0, sh_rest, settings: tuple, tile_lists: list[torch.Tensor]):
-    """Image [3, H, W]. ``tile_lists[t]`` holds tile t's Gaussian ids in blend order."""
+def render(means, scales, rotations, opacities, sh0, sh_rest, settings: tuple, tile_lists: list[torch.Tensor],
+           mean2d_taps: list | None = None):
+    """Image [3, H, W]. ``tile_lists[t]`` holds tile t's Gaussian ids in blend order.
+    ``mean2d_taps`` (a list) receives the 2D means as a leaf that keeps its gradient, then for every (Gaussian,
+    tile) pair blended a (id, x copy, y copy) triple of per-pixel copies of that mean, whose gradients are the
+    per-pixel terms of dL/dmean2d (the densification statistics test sums their absolute values)."""
     (w2c, cam_position, bg, bases, width, height, fx, fy, cx, cy, _near, _far, aa) = settings
     dt = means.dtype
     w2c, cam_position, bg = w2c.to(dt), cam_position.to(dt), bg.to(dt)
     mean2d, conic, o, color, z, _ = preprocess(means, scales, rotations, opacities, sh0, sh_rest, w2c, cam_position,
                                                bases, width, height, fx, fy, cx, cy, aa)
+    if mean2d_taps is not None:
+        mean2d = mean2d.detach().requires_grad_(True)
+        mean2d_taps.append(mean2d)
     col = torch.clamp(color, min=0.0)
     tiles_x = (width + TILE - 1) // TILE
     out = torch.zeros(3, height, width, dtype=dt)
@@ -105,8 +112,17 @@ def render(means, scales, rotations, opacities, sh0, sh_rest, settings: tuple, t
         C = torch.zeros(3, h, w, dtype=dt)
         done = torch.zeros(h, w, dtype=torch.bool)
         for g in lst.tolist():
-            dx = mean2d[g, 0] - xs
-            dy = mean2d[g, 1] - ys
+            if mean2d_taps is not None:
+                mx = (mean2d[g, 0] + torch.zeros_like(xs)).detach().requires_grad_(True)
+                my = (mean2d[g, 1] + torch.zeros_like(ys)).detach().requires_grad_(True)
+                mean2d_taps.append((g, mx, my))
+                # the copies carry the per-pixel terms; the leaf gets their sum through the straight-through link
+                mx = mx + (mean2d[g, 0] - mean2d[g, 0].detach())
+                my = my + (mean2d[g, 1] - mean2d[g, 1].detach())
+            else:
+                mx, my = mean2d[g, 0], mean2d[g, 1]
+            dx = mx - xs
+            dy = my - ys
             power = -0.5 * (conic[g, 0] * dx * dx + 2 * conic[g, 1] * dx * dy + conic[g, 2] * dy * dy)
             alpha = o[g] * torch.exp(torch.clamp(power, max=0.0))
             with torch.no_grad():

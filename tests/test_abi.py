@@ -60,6 +60,8 @@ def _kind(decl: str):
         return ctypes.c_size_t
     if "long long" in decl:
         return ctypes.c_longlong
+    if re.search(r"\bdouble\b", decl):
+        return ctypes.c_double
     if re.search(r"\bfloat\b", decl):
         return ctypes.c_float
     if re.search(r"\bint\b", decl):

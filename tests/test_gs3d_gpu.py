@@ -133,18 +133,59 @@ def test_single_call_backward_matches_split(cuda):
     sc, cam, params, settings = _setup("partial_tiles", seed=5)
     image, prim, tile, inst, bucket, m, nb, sel = gs3d.forward(*params, *settings)
     dout = torch.randn_like(image)
-    split = gs3d.backward(None, dout, image, params[0], params[1], params[2], params[3], params[5], prim, tile, inst,
-                          bucket, *settings, m, nb, sel)
     n = params[0].shape[0]
+    d_split = torch.zeros(3, n, device=cuda)
+    split = gs3d.backward(d_split, dout, image, params[0], params[1], params[2], params[3], params[5], prim, tile, inst,
+                          bucket, *settings, m, nb, sel)
     rest = params[5].shape[1]
     keep: list = []
     s = gs3d._settings(params[0].device, *settings, rest, keep)
     ws = torch.empty(L.query("gs3d_backward_workspace_size", n), dtype=torch.uint8, device=cuda)
     single = tuple(torch.empty_like(g) for g in split)
+    d_single = torch.zeros(3, n, device=cuda)
     L.call("gs3d_backward", L.ptr(dout), L.ptr(image), *map(L.ptr, params[:4]), L.ptr(params[5]), n, m,
            ctypes.byref(s), L.ptr(prim), prim.numel(), L.ptr(tile), tile.numel(), L.ptr(inst), inst.numel(),
-           L.ptr(bucket), bucket.numel(), nb, L.ptr(ws), ws.numel(), *map(L.ptr, single), L.stream_of(image))
+           L.ptr(bucket), bucket.numel(), nb, L.ptr(ws), ws.numel(), *map(L.ptr, single), L.ptr(d_single), 3,
+           L.stream_of(image))
     assert max(rel(a, b) for a, b in zip(single, split)) < 1e-5  # float atomics: summation order differs
+    assert rel(d_single, d_split) < 1e-5
+
+
+@pytest.mark.parametrize("rows", [2, 3])
+def test_densification_rows_vs_float64_reference(rows, cuda):
+    """densification_info accumulated in place over two backward calls: row 0 counts the views a Gaussian was
+    visible in, row 1 sums |dL/dmean2d| scaled by (W/2, H/2), row 2 the same norm of the summed per-pixel absolute
+    mean2d gradients (per-pixel copies of mean2d in the reference give those)."""
+    sc, cam, params, settings = _setup("tiny", seed=8)
+    W, H = cam["width"], cam["height"]
+    n = params[0].shape[0]
+    image, prim, tile, inst, bucket, m, nb, sel = gs3d.forward(*params, *settings)
+    g = torch.Generator().manual_seed(9)
+    dout = torch.randn(image.shape, generator=g).to(cuda)
+    dinfo = torch.zeros(rows, n, device=cuda)
+    for _ in range(2):
+        gs3d.backward(dinfo, dout, image, params[0], params[1], params[2], params[3], params[5], prim, tile, inst,
+                      bucket, *settings, m, nb, sel)
+    vis = gs3d.primitive_views(prim, n)["n_touched"].cpu() > 0
+    tv = gs3d.tile_views(tile, W, H)
+    lists = R.tile_lists_from(tv["ranges"], gs3d.instance_views(inst, m)["point_list"])
+    ref_leaves = [p.detach().cpu().double() for p in params]
+    cpu_settings = tuple(s.cpu().double() if torch.is_tensor(s) else s for s in settings)
+    taps: list = []
+    ref = R.render(*ref_leaves, cpu_settings, lists, mean2d_taps=taps)
+    ref.backward(dout.cpu().double())
+    scale = torch.tensor([0.5 * W, 0.5 * H], dtype=torch.float64)
+    gm = taps[0].grad  # dL/dmean2d [N, 2]
+    want1 = 2 * (gm * scale).norm(dim=1)
+    got = dinfo.cpu().double()
+    assert torch.equal(got[0], 2 * vis.double())
+    assert rel(got[1], want1) < 1e-4
+    if rows == 3:
+        absg = torch.zeros(n, 2, dtype=torch.float64)
+        for gid, tx, ty in taps[1:]:
+            absg[gid, 0] += tx.grad.abs().sum()
+            absg[gid, 1] += ty.grad.abs().sum()
+        assert rel(got[2], 2 * (absg * scale).norm(dim=1)) < 1e-4
 
 
 def test_empty_scene(cuda):
