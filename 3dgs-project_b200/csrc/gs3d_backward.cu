@@ -283,7 +283,10 @@ struct Densification {
     int rows;     // 0, 2 or 3
 };
 
-__global__ void __launch_bounds__(kPbThreads) k_preprocess_backward(PParams P, Cam cam, PrimBuffers pb, GradAcc acc,
+#ifndef SPLAT_PB_MIN_BLOCKS
+#define SPLAT_PB_MIN_BLOCKS 8  // 64 registers, no spills: 32 warps per SM
+#endif
+__global__ void __launch_bounds__(kPbThreads, SPLAT_PB_MIN_BLOCKS) k_preprocess_backward(PParams P, Cam cam, PrimBuffers pb, GradAcc acc,
                                                                     Grads out, Densification dens) {
     extern __shared__ __align__(16) float s_sh[];  // [kPbWarps][32 * rest_bases * 3]
     const int i = blockIdx.x * kPbThreads + threadIdx.x;
@@ -299,17 +302,28 @@ __global__ void __launch_bounds__(kPbThreads) k_preprocess_backward(PParams P, C
     const bool vec = ((reinterpret_cast<uintptr_t>(P.sh_rest + static_cast<size_t>(first) * rest3) |
                        reinterpret_cast<uintptr_t>(out.sh_rest + static_cast<size_t>(first) * rest3)) & 15u) == 0;
     const unsigned any_vis = __ballot_sync(kFullMask, vis);
-    if (any_vis && cam.active_sh_bases > 1 && rest3 > 0) {
-        const float* src = P.sh_rest + static_cast<size_t>(first) * rest3;
-        int done = 0;
-        if (vec) {
-            const int n4 = nfl / 4;
-            for (int k = lane; k < n4; k += 32)
-                reinterpret_cast<float4*>(sh)[k] = __ldg(reinterpret_cast<const float4*>(src) + k);
-            done = n4 * 4;
-        }
-        for (int k = done + lane; k < nfl; k += 32) sh[k] = __ldg(src + k);
+    // The warp's SH rows stream into shared memory while every per-Gaussian input is loaded into registers.
+    const bool stage = any_vis && cam.active_sh_bases > 1 && rest3 > 0;
+    const float* sh_src = P.sh_rest + static_cast<size_t>(first) * rest3;
+    const int staged = stage ? stage_sh_begin(sh, sh_src, nfl, lane) : 0;
+    float px = 0.f, py = 0.f, pz = 0.f, ls0 = 0.f, ls1 = 0.f, ls2 = 0.f, op_logit = 0.f;
+    float2 gm = make_float2(0.f, 0.f);
+    float4 gco = make_float4(0.f, 0.f, 0.f, 0.f), gcl = gco, cz = gco, q = make_float4(1.f, 0.f, 0.f, 0.f);
+    if (vis) {
+        px = P.means[3 * i];
+        py = P.means[3 * i + 1];
+        pz = P.means[3 * i + 2];
+        gm = acc.mean2d[i];
+        gco = acc.conic_o[i];
+        gcl = acc.color[i];
+        cz = pb.color_z[i];
+        q = make_float4(P.rotations[4 * i], P.rotations[4 * i + 1], P.rotations[4 * i + 2], P.rotations[4 * i + 3]);
+        ls0 = P.scales[3 * i];
+        ls1 = P.scales[3 * i + 1];
+        ls2 = P.scales[3 * i + 2];
+        op_logit = P.opacities[i];
     }
+    if (stage) stage_sh_end(sh, sh_src, nfl, staged, lane);
     __syncwarp();
 
     float* my_sh = sh + lane * rest3;  // this Gaussian's coefficients, overwritten by their gradients
@@ -317,15 +331,10 @@ __global__ void __launch_bounds__(kPbThreads) k_preprocess_backward(PParams P, C
         float w2c[12];
 #pragma unroll
         for (int k = 0; k < 12; ++k) w2c[k] = __ldg(P.w2c + k);
-        const float px = P.means[3 * i], py = P.means[3 * i + 1], pz = P.means[3 * i + 2];
         const float xc = w2c[0] * px + w2c[1] * py + w2c[2] * pz + w2c[3];
         const float yc = w2c[4] * px + w2c[5] * py + w2c[6] * pz + w2c[7];
         const float zc = w2c[8] * px + w2c[9] * py + w2c[10] * pz + w2c[11];
 
-        const float2 gm = acc.mean2d[i];
-        const float4 gco = acc.conic_o[i];
-        const float4 gcl = acc.color[i];
-        const float4 cz = pb.color_z[i];
         const float gr = cz.x >= 0.f ? gcl.x : 0.f, gg = cz.y >= 0.f ? gcl.y : 0.f, gb = cz.z >= 0.f ? gcl.z : 0.f;
 
         // ---- SH: colour = sum_k basis_k(d) sh_k + 0.5, d = (p - cam) / |p - cam|
@@ -340,14 +349,17 @@ __global__ void __launch_bounds__(kPbThreads) k_preprocess_backward(PParams P, C
         float v[16];
         v[0] = 0.f;
         const int nb = min(cam.active_sh_bases, cam.rest_bases + 1);
-        for (int k = 1; k < nb; ++k) {
-            const float cr = my_sh[3 * (k - 1)], cg = my_sh[3 * (k - 1) + 1], cb = my_sh[3 * (k - 1) + 2];
-            v[k] = gr * cr + gg * cg + gb * cb;
-            my_sh[3 * (k - 1)] = bas[k] * gr;
-            my_sh[3 * (k - 1) + 1] = bas[k] * gg;
-            my_sh[3 * (k - 1) + 2] = bas[k] * gb;
+#pragma unroll
+        for (int k = 1; k < 16; ++k) {  // unrolled, so bas and v stay in registers
+            v[k] = 0.f;
+            if (k < nb) {
+                const float cr = my_sh[3 * (k - 1)], cg = my_sh[3 * (k - 1) + 1], cb = my_sh[3 * (k - 1) + 2];
+                v[k] = gr * cr + gg * cg + gb * cb;
+                my_sh[3 * (k - 1)] = bas[k] * gr;
+                my_sh[3 * (k - 1) + 1] = bas[k] * gg;
+                my_sh[3 * (k - 1) + 2] = bas[k] * gb;
+            }
         }
-        for (int k = nb; k < 16; ++k) v[k] = 0.f;
         for (int k = max(nb, 1); k <= cam.rest_bases; ++k) {
             my_sh[3 * (k - 1)] = 0.f;
             my_sh[3 * (k - 1) + 1] = 0.f;
@@ -359,11 +371,9 @@ __global__ void __launch_bounds__(kPbThreads) k_preprocess_backward(PParams P, C
         float gpx = (gdx - dx * dd) * inv_len, gpy = (gdy - dy * dd) * inv_len, gpz = (gdz - dz * dd) * inv_len;
 
         // ---- recompute the projection
-        const float4 q = make_float4(P.rotations[4 * i], P.rotations[4 * i + 1], P.rotations[4 * i + 2],
-                                     P.rotations[4 * i + 3]);
         float nsq;
         const Mat3 R = quat_to_rot(q, nsq);
-        const float s[3] = {expf(P.scales[3 * i]), expf(P.scales[3 * i + 1]), expf(P.scales[3 * i + 2])};
+        const float s[3] = {expf(ls0), expf(ls1), expf(ls2)};
         float M[3][3];
 #pragma unroll
         for (int r = 0; r < 3; ++r)
@@ -400,7 +410,7 @@ __global__ void __launch_bounds__(kPbThreads) k_preprocess_backward(PParams P, C
         const float det = ad * cd - b * b;
         const float inv_det = 1.f / det;
         const float A = cd * inv_det, B = -b * inv_det, C = ad * inv_det;
-        const float sig = 1.f / (1.f + expf(-P.opacities[i]));
+        const float sig = 1.f / (1.f + expf(-op_logit));
 
         // ---- opacity (and the antialiasing factor f = sqrt(det(Sigma2) / det(Sigma2 + 0.3 I)))
         float ga = 0.f, gb2 = 0.f, gc = 0.f;  // dL/d(a, b, c) of Sigma2 (b = the off-diagonal value)

@@ -260,6 +260,31 @@ __device__ __forceinline__ float hw_exp2(float x) {
     return y;
 }
 
+// ---- warp staging of a contiguous block of SH-rest rows in shared memory ----
+// The warp's rows [first, first + 32) are one contiguous block of nfl floats. stage_sh_begin starts 16-byte
+// asynchronous copies (cp.async, L1 bypassed) of its aligned part, so other loads and arithmetic overlap them;
+// stage_sh_end loads the unaligned remainder, waits for the copies and synchronises the warp. Both must be
+// called by all 32 lanes.
+__device__ __forceinline__ int stage_sh_begin(float* sh, const float* src, int nfl, int lane) {
+    int done = 0;
+    if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+        const int n4 = nfl / 4;
+        for (int k = lane; k < n4; k += 32) {
+            const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(sh + 4 * k));
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src + 4 * k) : "memory");
+        }
+        done = n4 * 4;
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+    return done;
+}
+
+__device__ __forceinline__ void stage_sh_end(float* sh, const float* src, int nfl, int done, int lane) {
+    for (int k = done + lane; k < nfl; k += 32) sh[k] = __ldg(src + k);
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    __syncwarp();
+}
+
 __device__ __forceinline__ float blend_q2(float a2, float b2, float c2, float dx, float dy) {
     return __fmaf_rn(dx, __fmaf_rn(a2, dx, __fmul_rn(b2, dy)), __fmul_rn(c2, __fmul_rn(dy, dy)));
 }

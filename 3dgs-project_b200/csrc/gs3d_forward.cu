@@ -59,15 +59,32 @@ __global__ void __launch_bounds__(kPreThreads) k_preprocess(Params P, Cam cam, P
     const float zc = w2c[8] * px + w2c[9] * py + w2c[10] * pz + w2c[11];
     bool vis = valid && zc >= cam.near_plane && zc <= cam.far_plane;
 
+    // The warp's SH rows (one contiguous block: its first Gaussian is a multiple of 32) start streaming into
+    // shared memory now, while the geometry below is computed; the per-Gaussian inputs are loaded up front too.
+    const unsigned any_near = __ballot_sync(kFullMask, vis);
+    float* sh = s_sh + warp * 32 * rest3;
+    const int first = i - lane;
+    const bool stage = any_near && cam.active_sh_bases > 1 && rest3 > 0;
+    const int nfl = stage ? min(32, P.n - first) * rest3 : 0;
+    const float* src = P.sh_rest + static_cast<size_t>(first) * rest3;
+    const int staged = stage ? stage_sh_begin(sh, src, nfl, lane) : 0;
+    float4 q = make_float4(1.f, 0.f, 0.f, 0.f);
+    float ls0 = 0.f, ls1 = 0.f, ls2 = 0.f, op_logit = 0.f;
+    if (vis) {
+        q = make_float4(P.rotations[4 * i], P.rotations[4 * i + 1], P.rotations[4 * i + 2], P.rotations[4 * i + 3]);
+        ls0 = P.scales[3 * i];
+        ls1 = P.scales[3 * i + 1];
+        ls2 = P.scales[3 * i + 2];
+        op_logit = P.opacities[i];
+    }
+
     float mx = 0.f, my = 0.f, A = 0.f, B = 0.f, C = 0.f, o = 0.f, thr = 0.f;
     int rx0 = 0, ry0 = 0, rx1 = -1, ry1 = -1;
     uint32_t touched = 0;
     if (vis) {
-        const float4 q = make_float4(P.rotations[4 * i], P.rotations[4 * i + 1], P.rotations[4 * i + 2],
-                                     P.rotations[4 * i + 3]);
         float nsq;
         const Mat3 R = quat_to_rot(q, nsq);
-        const float s[3] = {expf(P.scales[3 * i]), expf(P.scales[3 * i + 1]), expf(P.scales[3 * i + 2])};
+        const float s[3] = {expf(ls0), expf(ls1), expf(ls2)};
         float M[3][3];
 #pragma unroll
         for (int r = 0; r < 3; ++r)
@@ -101,7 +118,7 @@ __global__ void __launch_bounds__(kPreThreads) k_preprocess(Params P, Cam cam, P
         const float c = j11 * (j11 * Sc[1][1] + j12 * Sc[1][2]) + j12 * (j11 * Sc[2][1] + j12 * Sc[2][2]);
         const float ad = a + kDilation, cd = c + kDilation;
         const float det = ad * cd - b * b;
-        o = 1.f / (1.f + expf(-P.opacities[i]));
+        o = 1.f / (1.f + expf(-op_logit));
         if (cam.proper_aa) o *= sqrtf(fmaxf((a * c - b * b) / det, 0.f));
         mx = cam.fx * xc * inv_z + cam.cx;
         my = cam.fy * yc * inv_z + cam.cy;
@@ -133,26 +150,10 @@ __global__ void __launch_bounds__(kPreThreads) k_preprocess(Params P, Cam cam, P
         }
     }
 
-    // colour: the warp's SH rows are one contiguous block (its first Gaussian is a multiple of 32)
+    // colour from the staged SH rows
     float3 col = make_float3(0.f, 0.f, 0.f);
-    const unsigned any_vis = __ballot_sync(kFullMask, vis);
-    if (any_vis) {
-        float* sh = s_sh + warp * 32 * rest3;
-        const int first = i - lane;
-        const int cnt = min(32, P.n - first);
-        const int nfl = cnt * rest3;
-        const float* src = P.sh_rest + static_cast<size_t>(first) * rest3;
-        if (cam.active_sh_bases > 1 && rest3 > 0) {
-            int done = 0;
-            if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
-                const int n4 = nfl / 4;
-                for (int k = lane; k < n4; k += 32)
-                    reinterpret_cast<float4*>(sh)[k] = __ldg(reinterpret_cast<const float4*>(src) + k);
-                done = n4 * 4;
-            }
-            for (int k = done + lane; k < nfl; k += 32) sh[k] = __ldg(src + k);
-        }
-        __syncwarp();
+    if (any_near) {
+        if (stage) stage_sh_end(sh, src, nfl, staged, lane);
         if (vis) {
             float dx = px - __ldg(P.cam_pos), dy = py - __ldg(P.cam_pos + 1), dz = pz - __ldg(P.cam_pos + 2);
             const float inv_len = rsqrtf(dx * dx + dy * dy + dz * dz);
@@ -165,10 +166,13 @@ __global__ void __launch_bounds__(kPreThreads) k_preprocess(Params P, Cam cam, P
             col.y = bas[0] * P.sh0[3 * i + 1] + 0.5f;
             col.z = bas[0] * P.sh0[3 * i + 2] + 0.5f;
             const float* mine = sh + lane * rest3;
-            for (int k = 1; k < cam.active_sh_bases && k <= cam.rest_bases; ++k) {
-                col.x += bas[k] * mine[3 * (k - 1)];
-                col.y += bas[k] * mine[3 * (k - 1) + 1];
-                col.z += bas[k] * mine[3 * (k - 1) + 2];
+#pragma unroll
+            for (int k = 1; k < 16; ++k) {  // unrolled, so bas stays in registers
+                if (k < cam.active_sh_bases && k <= cam.rest_bases) {
+                    col.x += bas[k] * mine[3 * (k - 1)];
+                    col.y += bas[k] * mine[3 * (k - 1) + 1];
+                    col.z += bas[k] * mine[3 * (k - 1) + 2];
+                }
             }
         }
     }
