@@ -1,7 +1,9 @@
 // gs3d_backward.cu - 3DGS backward: per-Gaussian warp-bucketed blend backward, then the preprocess
 // backward to the six parameter gradients.
 //
-// k_blend_backward: one warp per (tile, 32-splat bucket). Lane l owns the 8 pixels r*32 + l of the
+// k_blend_backward: persistent warps (a grid sized to the SMs) take, from an atomic work counter, the
+// buckets the forward listed as reached (those before their tile's last contributor); one warp per
+// (tile, 32-splat bucket) at a time. Lane l owns the 8 pixels r*32 + l of the
 // 16x16 tile (column l % 16, rows 2r + l / 16). From the bucket's (C, T) checkpoint each pixel keeps
 // T and rho = G . (image - C) (image with background), so that
 //     dL/dalpha_j = T_j (G . c_j) - rho_after_j / max(1 - alpha_j, 1e-6),  rho_after_j = rho_j - T_j alpha_j (G . c_j)
@@ -9,7 +11,8 @@
 // front-to-back order up to the pixel's last contributor. Row bands whose culling rectangle misses
 // the splat are skipped by the whole warp. Per splat the lanes' nine sums (mean2d 2, conic 3,
 // opacity, colour 3) are reduced with shuffles and lane 0 issues three vector atomics (float2,
-// float4, float4) instead of nine scalar ones. Buckets past the tile's last contributor exit at once.
+// float4, float4) instead of nine scalar ones. With three densification rows it also sums the per-pixel
+// absolute mean2d gradients (two more values and one more float2 atomic per splat).
 //
 // k_preprocess_backward: one thread per Gaussian recomputes the projection and chains
 // (dL/dmean2d, dL/dconic, dL/dopacity, dL/dcolour) to means, scales, rotations, opacity logits,

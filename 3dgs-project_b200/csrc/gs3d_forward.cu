@@ -200,7 +200,10 @@ __global__ void k_gather_counts(const uint32_t* __restrict__ order, const uint32
 }
 
 constexpr int kDupThreads = 256;
-constexpr int kDupStage = 4096;   // instances of a block staged in shared memory (32 KB)
+#ifndef SPLAT_DUP_STAGE
+#define SPLAT_DUP_STAGE 2048
+#endif
+constexpr int kDupStage = SPLAT_DUP_STAGE;  // instances of a block staged in shared memory (8 B each)
 #ifndef SPLAT_DUP_WARP_MIN
 #define SPLAT_DUP_WARP_MIN 24
 #endif
@@ -227,8 +230,8 @@ __device__ __forceinline__ void put_instance(uint32_t* s_key, uint32_t* s_val, c
 // at most kDupWarpMin tiles is enumerated by its own thread; a larger one by its whole warp, lane per tile
 // row, then lane per instance - the same rows and tiles in the same order.
 __global__ void __launch_bounds__(kDupThreads) k_duplicate(int n, Cam cam, PrimBuffers pb, InstBuffers ib) {
-    __shared__ uint32_t s_key[kDupStage];
-    __shared__ uint32_t s_val[kDupStage];
+    __shared__ uint32_t s_key[kDupStage > 0 ? kDupStage : 1];
+    __shared__ uint32_t s_val[kDupStage > 0 ? kDupStage : 1];
     const int lane = threadIdx.x & 31;
     const int r0 = blockIdx.x * kDupThreads;  // < n: the grid covers n
     const int r = r0 + threadIdx.x;

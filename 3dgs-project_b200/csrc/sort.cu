@@ -484,6 +484,12 @@ int radix_sort_pairs(const K* keys_in, const uint32_t* vals_in, K* keys_out, uin
     return SPLAT_OK;
 }
 
+// Moves the wait counter into *dst (device memory) in stream order and clears it.
+__global__ void k_take_wait_timeouts(uint32_t* dst) {
+    *dst = g_wait_timeouts;
+    g_wait_timeouts = 0u;
+}
+
 int take_wait_timeouts(unsigned int* count) {
     unsigned int h = 0u;
     SPLAT_CUDA(cudaMemcpyFromSymbol(&h, g_wait_timeouts, sizeof(h)));
@@ -578,6 +584,13 @@ int splat_scan_exclusive_u32_noalloc(const uint32_t* in, uint32_t* out, long lon
 size_t splat_sort_workspace_size(long long n, int key_bytes) {
     return key_bytes == 8 ? splat::sort_workspace_bytes<unsigned long long>(n)
                           : splat::sort_workspace_bytes<uint32_t>(n);
+}
+
+int splat_take_device_waits_async(uint32_t* dst, void* stream) {
+    SPLAT_REQUIRE(dst != nullptr, "splat_take_device_waits_async: dst is NULL");
+    splat::k_take_wait_timeouts<<<1, 1, 0, splat::as_stream(stream)>>>(dst);
+    splat::note_launch();
+    return splat::check_launch("splat_take_device_waits_async");
 }
 
 int splat_check_device_waits(void) {

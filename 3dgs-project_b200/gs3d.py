@@ -101,11 +101,14 @@ def forward(means, scales, rotations, opacities, sh0, sh_rest, w2c, cam_position
     stream = L.stream_of(means)
     prim = torch.empty(L.query("gs3d_primitive_buffer_size", n), dtype=torch.uint8, device=dev)
     tile = torch.empty(L.query("gs3d_tile_buffer_size", width, height), dtype=torch.uint8, device=dev)
-    count = torch.zeros(1, dtype=torch.int32, device=dev)
+    count = torch.zeros(2, dtype=torch.int32, device=dev)
     L.call("gs3d_preprocess", L.ptr(means), L.ptr(scales), L.ptr(rotations), L.ptr(opacities), L.ptr(sh0),
            L.ptr(sh_rest), n, ctypes.byref(s), L.ptr(prim), prim.numel(), L.ptr(count), stream)
-    m = int(count.item())  # the one host read of a forward
-    L.check_device_waits(dev)  # covers this depth sort and the previous forward's tile sort
+    # the device's count of look-back waits that gave up (this depth sort, the previous forward's tile sort)
+    L.call("splat_take_device_waits_async", L.ptr(count[1:]), stream)
+    m, waits = count.tolist()  # the one host read of a forward
+    if waits:
+        raise RuntimeError(f"{waits} bounded device-side wait(s) in the radix sort gave up; results are unreliable")
     bcap = int(L.load().gs3d_bucket_bound(m, width, height))
     inst = torch.empty(L.query("gs3d_instance_buffer_size", m), dtype=torch.uint8, device=dev)
     bucket = torch.empty(L.query("gs3d_bucket_buffer_size", bcap), dtype=torch.uint8, device=dev)

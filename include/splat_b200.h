@@ -74,6 +74,10 @@ int splat_radix_sort_pairs(const void* keys_in, const uint32_t* vals_in, void* k
  * (results produced since then are unreliable), else SPLAT_OK. Synchronises the device; clears the count.
  * No counterpart in the reference (CUB's single-sweep sort waits without a bound). */
 int splat_check_device_waits(void);
+/* The same count without a synchronisation: enqueues on `stream` a copy of it into dst (device uint32) and
+ * clears it, so a caller that reads dst at a point where it waits anyway learns of a wait that gave up in
+ * the work enqueued before. No counterpart in the reference. */
+int splat_take_device_waits_async(uint32_t* dst, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
  * gs2d: toy2d 2D Gaussian rasterizer (replaces toy2d/csrc/rasterize.cu:366-454 and the device
