@@ -31,6 +31,9 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "splat_sort_workspace_size": (_SZ, [_LL, _I]),
     "splat_radix_sort_pairs": (_I, [_P, _P, _P, _P, _LL, _I, _I, _I, _P, _SZ, _P]),
     "splat_check_device_waits": (_I, []),
+    "splat_l1_ssim_workspace_size": (_SZ, [_I, _I, _I, _I]),
+    "splat_l1_ssim_forward": (_I, [_P, _P, _I, _I, _I, _I, ctypes.c_float, _I, _P, _P, _P, _SZ, _P]),
+    "splat_l1_ssim_backward": (_I, [_P, _P, _I, _I, _I, _I, ctypes.c_float, _I, _P, _P, _P, _SZ, _P]),
     "splat_take_device_waits_async": (_I, [_P, _P]),
     "gs2d_bin_count_workspace_size": (_SZ, [_I]),
     "gs2d_bin_fill_workspace_size": (_SZ, [_LL, _I, _I]),

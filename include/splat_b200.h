@@ -279,6 +279,23 @@ typedef struct adam_lean_group {
 int adam_step_multi_lean(int count, const adam_lean_group* groups, int step, double beta1, double beta2,
                          double eps, const int32_t* visibility, long long n_primitives, void* stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * Fused L1 + SSIM loss (the training loss around the rasterizer; replaces the external fused-ssim call of the
+ * reference's trainer, whose share of the step results/phase1/README.md:46-47 reports, and the L1 term beside it).
+ * img, gt: device f32[B, C, H, W]. loss = (1 - lambda) mean|img - gt| + lambda (1 - mean SSIM), SSIM with the
+ * 11x11 Gaussian window (sigma 1.5), C1 = 0.01^2, C2 = 0.03^2, zero padding; padding_valid = 1 averages the
+ * SSIM map only where the window lies inside the image. The forward writes loss and mean SSIM (device f32[1]
+ * each, either may be NULL) and keeps in the workspace what the backward needs; the backward writes
+ * grad_img = dloss/dimg times *grad_loss (device f32[1], NULL = 1). Deterministic (fixed-order sums).
+ * ------------------------------------------------------------------------------------------- */
+size_t splat_l1_ssim_workspace_size(int B, int C, int H, int W);
+int splat_l1_ssim_forward(const float* img, const float* gt, int B, int C, int H, int W, float lambda,
+                          int padding_valid, float* loss, float* ssim_mean, void* workspace, size_t workspace_bytes,
+                          void* stream);
+int splat_l1_ssim_backward(const float* img, const float* gt, int B, int C, int H, int W, float lambda,
+                           int padding_valid, const float* grad_loss, float* grad_img, const void* workspace,
+                           size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif
