@@ -32,6 +32,12 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "splat_radix_sort_pairs": (_I, [_P, _P, _P, _P, _LL, _I, _I, _I, _P, _SZ, _P]),
     "splat_check_device_waits": (_I, []),
     "splat_l1_ssim_workspace_size": (_SZ, [_I, _I, _I, _I]),
+    "splat_peer_alloc": (_I, [_SZ, _P, _P]),
+    "splat_peer_open": (_I, [_P, _P]),
+    "splat_peer_close": (_I, [_P]),
+    "splat_peer_free": (_I, [_P]),
+    "adam_step_dp_fused": (_I, [_I, _I, _P, _P, _LL, _LL, _P, _P, _I, _P, _I, ctypes.c_double, ctypes.c_double,
+                                ctypes.c_double, _P]),
     "splat_l1_ssim_forward": (_I, [_P, _P, _I, _I, _I, _I, ctypes.c_float, _I, _P, _P, _P, _SZ, _P]),
     "splat_l1_ssim_backward": (_I, [_P, _P, _I, _I, _I, _I, ctypes.c_float, _I, _P, _P, _P, _SZ, _P]),
     "splat_take_device_waits_async": (_I, [_P, _P]),

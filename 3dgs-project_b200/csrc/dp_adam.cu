@@ -1,0 +1,191 @@
+// dp_adam.cu - data-parallel Adam as one kernel over peer memory (the exchange step of multi-view training).
+//
+// With G ranks (one per GPU, NVLink / NVSwitch between them), rank r owns the slice [lo, hi) of the flat
+// parameter vector. Its kernel reads the gradients of that slice from every rank's memory (peer loads), sums
+// them in rank order, applies Adam with the moments kept for the slice only, and stores the updated parameters
+// of the slice into every rank's parameter vector (peer stores). This replaces an all-reduce of the whole
+// gradient followed by G identical Adam steps: the same bytes cross NVLink once in each direction (the slice's
+// gradients in, its parameters out) and each rank does 1/G of the optimizer work. The kernel waits on nothing;
+// the caller orders it between two device-side barriers (see the header).
+#include <algorithm>
+#include <cstring>
+
+#include "common.cuh"
+
+namespace splat {
+namespace dp {
+
+constexpr int kThreads = 256;
+
+struct Segment {
+    long long begin, end;
+    float step_size;
+};
+
+struct Args {
+    const float* grads[SPLAT_DP_MAX_RANKS];
+    float* params[SPLAT_DP_MAX_RANKS];
+    float* exp_avg;
+    float* exp_avg_sq;
+    long long lo, hi;
+    Segment seg[SPLAT_DP_MAX_SEGMENTS];
+    int nseg;
+    int world, rank;
+    float beta1, beta2, eps, bc2_sqrt_rcp;
+};
+
+__device__ __forceinline__ float step_size_of(const Args& a, long long i) {
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < SPLAT_DP_MAX_SEGMENTS; ++k)
+        if (k < a.nseg && i >= a.seg[k].begin && i < a.seg[k].end) s = a.seg[k].step_size;
+    return s;
+}
+
+__device__ __forceinline__ float adam(float p, float g, float& m, float& v, float step_size, const Args& a) {
+    const float g2 = g * g;
+    m = fmaf(a.beta1, m - g, g);
+    v = fmaf(a.beta2, v - g2, g2);
+    const float denom = sqrtf(v) * a.bc2_sqrt_rcp + a.eps;
+    return p - step_size * m / denom;
+}
+
+__global__ void __launch_bounds__(kThreads) k_dp_adam(Args a) {
+    const long long n = a.hi - a.lo;
+    const long long n4 = n / 4;  // lo is a multiple of 4 and the buffers 16-byte aligned
+    const long long stride = static_cast<long long>(gridDim.x) * kThreads;
+    for (long long q = static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x; q < n4; q += stride) {
+        const long long e = a.lo + 4 * q;
+        float4 gv[SPLAT_DP_MAX_RANKS];
+#pragma unroll
+        for (int k = 0; k < SPLAT_DP_MAX_RANKS; ++k)  // every rank's load in flight before the sum
+            if (k < a.world) gv[k] = *reinterpret_cast<const float4*>(a.grads[k] + e);
+        float4 g = gv[0];
+#pragma unroll
+        for (int k = 1; k < SPLAT_DP_MAX_RANKS; ++k)
+            if (k < a.world) {
+                g.x += gv[k].x;
+                g.y += gv[k].y;
+                g.z += gv[k].z;
+                g.w += gv[k].w;
+            }
+        float4 p = *reinterpret_cast<const float4*>(a.params[a.rank] + e);  // this rank's own copy
+        float4 m = *reinterpret_cast<const float4*>(a.exp_avg + 4 * q);
+        float4 v = *reinterpret_cast<const float4*>(a.exp_avg_sq + 4 * q);
+        p.x = adam(p.x, g.x, m.x, v.x, step_size_of(a, e), a);
+        p.y = adam(p.y, g.y, m.y, v.y, step_size_of(a, e + 1), a);
+        p.z = adam(p.z, g.z, m.z, v.z, step_size_of(a, e + 2), a);
+        p.w = adam(p.w, g.w, m.w, v.w, step_size_of(a, e + 3), a);
+        *reinterpret_cast<float4*>(a.exp_avg + 4 * q) = m;
+        *reinterpret_cast<float4*>(a.exp_avg_sq + 4 * q) = v;
+#pragma unroll
+        for (int k = 0; k < SPLAT_DP_MAX_RANKS; ++k)
+            if (k < a.world) *reinterpret_cast<float4*>(a.params[k] + e) = p;
+    }
+    // the last n % 4 elements, one thread
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        for (long long i = a.lo + 4 * n4; i < a.hi; ++i) {
+            float g = 0.f;
+            for (int k = 0; k < a.world; ++k) g += a.grads[k][i];
+            const long long j = i - a.lo;
+            float mm = a.exp_avg[j], vv = a.exp_avg_sq[j];
+            const float p = adam(a.params[a.rank][i], g, mm, vv, step_size_of(a, i), a);
+            a.exp_avg[j] = mm;
+            a.exp_avg_sq[j] = vv;
+            for (int k = 0; k < a.world; ++k) a.params[k][i] = p;
+        }
+    }
+    __threadfence_system();  // the peer stores are visible to every GPU before the caller's barrier completes
+}
+
+}  // namespace dp
+}  // namespace splat
+
+using namespace splat;
+
+extern "C" {
+
+int splat_peer_alloc(size_t bytes, void** ptr, unsigned char* ipc_handle) {
+    SPLAT_REQUIRE(ptr && ipc_handle && bytes > 0, "splat_peer_alloc: bad arguments");
+    void* p = nullptr;
+    SPLAT_CUDA(cudaMalloc(&p, bytes));
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        set_error("cudaIpcGetMemHandle failed: %s", cudaGetErrorString(e));
+        return SPLAT_ERR_CUDA;
+    }
+    SPLAT_CUDA(cudaMemset(p, 0, bytes));
+    memcpy(ipc_handle, &h, sizeof(h));
+    *ptr = p;
+    return SPLAT_OK;
+}
+
+int splat_peer_open(const unsigned char* ipc_handle, void** ptr) {
+    SPLAT_REQUIRE(ptr && ipc_handle, "splat_peer_open: bad arguments");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handle, sizeof(h));
+    SPLAT_CUDA(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+    return SPLAT_OK;
+}
+
+int splat_peer_close(void* ptr) {
+    SPLAT_CUDA(cudaIpcCloseMemHandle(ptr));
+    return SPLAT_OK;
+}
+
+int splat_peer_free(void* ptr) {
+    SPLAT_CUDA(cudaFree(ptr));
+    return SPLAT_OK;
+}
+
+int adam_step_dp_fused(int world, int rank, const float* const* grads, float* const* params, long long lo,
+                       long long hi, float* exp_avg, float* exp_avg_sq, int segment_count,
+                       const dp_adam_segment* segments, int step, double beta1, double beta2, double eps,
+                       void* stream) {
+    SPLAT_REQUIRE(world >= 1 && world <= SPLAT_DP_MAX_RANKS && rank >= 0 && rank < world,
+                  "adam_step_dp_fused: rank %d of %d (at most %d ranks)", rank, world, SPLAT_DP_MAX_RANKS);
+    SPLAT_REQUIRE(step >= 1, "adam_step_dp_fused: step must be >= 1");
+    SPLAT_REQUIRE(segment_count >= 1 && segment_count <= SPLAT_DP_MAX_SEGMENTS,
+                  "adam_step_dp_fused: %d segments (1 to %d)", segment_count, SPLAT_DP_MAX_SEGMENTS);
+    SPLAT_REQUIRE(0 <= lo && lo <= hi, "adam_step_dp_fused: slice [%lld, %lld)", lo, hi);
+    if (hi == lo) return SPLAT_OK;
+    SPLAT_REQUIRE(lo % 4 == 0, "adam_step_dp_fused: slice [%lld, %lld) must start at a multiple of 4", lo, hi);
+    SPLAT_REQUIRE(exp_avg && exp_avg_sq, "adam_step_dp_fused: null moments");
+    dp::Args a{};
+    uintptr_t align = reinterpret_cast<uintptr_t>(exp_avg) | reinterpret_cast<uintptr_t>(exp_avg_sq);
+    for (int k = 0; k < world; ++k) {
+        SPLAT_REQUIRE(grads[k] && params[k], "adam_step_dp_fused: null buffer of rank %d", k);
+        a.grads[k] = grads[k];
+        a.params[k] = params[k];
+        align |= reinterpret_cast<uintptr_t>(grads[k]) | reinterpret_cast<uintptr_t>(params[k]);
+    }
+    SPLAT_REQUIRE((align & 15u) == 0, "adam_step_dp_fused: buffers must be 16-byte aligned");
+    a.exp_avg = exp_avg;
+    a.exp_avg_sq = exp_avg_sq;
+    a.lo = lo;
+    a.hi = hi;
+    a.world = world;
+    a.rank = rank;
+    a.nseg = segment_count;
+    // the reference wrapper's host arithmetic (fastergs_lean_adam.patch:162-164), per segment
+    const double bc1_rcp = 1.0 / (1.0 - pow(beta1, step));
+    for (int k = 0; k < segment_count; ++k) {
+        SPLAT_REQUIRE(segments[k].begin <= segments[k].end, "adam_step_dp_fused: segment %d is reversed", k);
+        a.seg[k].begin = segments[k].begin;
+        a.seg[k].end = segments[k].end;
+        a.seg[k].step_size = static_cast<float>(segments[k].lr * bc1_rcp);
+    }
+    a.beta1 = static_cast<float>(beta1);
+    a.beta2 = static_cast<float>(beta2);
+    a.eps = static_cast<float>(eps);
+    a.bc2_sqrt_rcp = static_cast<float>(1.0 / sqrt(1.0 - pow(beta2, step)));
+    const long long n4 = (hi - lo) / 4;
+    const long long blocks = std::max<long long>(1, std::min<long long>(div_up(n4, dp::kThreads), 8ll * sm_count()));
+    dp::k_dp_adam<<<static_cast<unsigned>(blocks), dp::kThreads, 0, as_stream(stream)>>>(a);
+    note_launch();
+    return check_launch("adam_step_dp_fused");
+}
+
+}  // extern "C"

@@ -7,9 +7,13 @@
     ... the same fused Adam step on every rank ...
 
 The reference has no multi-GPU path (every job is single-GPU); this is the sharding the benchmark spec asks
-for: independent views plus one exchange step, no peer-memory or multicast loads.
+for: independent views plus one exchange step. PeerAdam below fuses that exchange with the optimizer: one kernel
+per rank reads its slice of every rank's gradients over NVLink, applies Adam, and writes the slice of parameters
+back to every rank (plain peer loads and stores; no multicast loads).
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -53,3 +57,143 @@ class FlatGradients:
         """Sum over ranks (no-op without an initialised process group of more than one rank)."""
         if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
             dist.all_reduce(self.flat, op=dist.ReduceOp.SUM, group=group)
+
+
+# ---------------------------------------------------------------------------------------------
+# Fused data-parallel Adam over peer memory (csrc/dp_adam.cu)
+# ---------------------------------------------------------------------------------------------
+
+def owned_slice(total: int, rank: int, world: int) -> tuple[int, int]:
+    """The elements [lo, hi) of a flat vector of `total` elements that rank `rank` of `world` updates: equal
+    chunks rounded up to a multiple of 4 elements (16-byte aligned starts), the last ones possibly short or empty."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of {world}")
+    chunk = ((total + world - 1) // world + 3) // 4 * 4
+    lo = min(rank * chunk, total)
+    return lo, min(lo + chunk, total)
+
+
+class _CudaArray:
+    """A device address range exposed through the CUDA array interface, so torch can view it without a copy."""
+
+    def __init__(self, ptr: int, numel: int):
+        self.__cuda_array_interface__ = {"shape": (numel,), "typestr": "<f4", "data": (ptr, False), "version": 2}
+
+
+class PeerFlat:
+    """A flat float32 vector in device memory that every rank of the group can address: this rank's buffer
+    as a tensor, and the device addresses of every rank's buffer as this GPU sees them (its own and peer
+    mappings opened from the handles the ranks exchange)."""
+
+    def __init__(self, numel: int, group=None, device=None):
+        from . import _lib as L
+
+        self._L = L
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.numel = numel
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * 64)()
+        L.call("splat_peer_alloc", max(4 * numel, 16), ctypes.byref(ptr), handle)
+        self._own = ptr.value
+        handles: list = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.ptrs, self._opened = [], []
+        for k, h in enumerate(handles):
+            if k == self.rank:
+                self.ptrs.append(self._own)
+                continue
+            p = ctypes.c_void_p()
+            L.call("splat_peer_open", (ctypes.c_ubyte * 64).from_buffer_copy(h), ctypes.byref(p))
+            self.ptrs.append(p.value)
+            self._opened.append(p.value)
+        self.tensor = torch.as_tensor(_CudaArray(self._own, numel), device=device)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers, wait for every rank to do the same, then free this rank's buffer."""
+        if self._own is None:
+            return
+        self.tensor = None
+        for p in self._opened:
+            self._L.call("splat_peer_close", p)
+        self._opened = []
+        dist.barrier(group=self.group)
+        self._L.call("splat_peer_free", self._own)
+        self._own = None
+
+
+class PeerAdam:
+    """Data-parallel Adam for replicated parameters, one fused kernel per step instead of an all-reduce of the
+    gradients followed by the same Adam step on every rank.
+
+    Parameters and gradients live in peer-addressable flat buffers (`params`, `grads`: per-group views). Each rank
+    updates the slice `owned_slice(total, rank, world)` of the flat vector: its kernel sums that slice's gradients
+    over the ranks (peer loads), applies Adam with the slice's moments, and writes the updated slice into every
+    rank's parameters (peer stores). Two stream-ordered barriers (one-element all-reduces) bracket the kernel.
+    Bias corrections and the per-element update are those of FusedAdam; the gradient sum is taken in rank order.
+    """
+
+    def __init__(self, tensors, lrs, group=None, betas=(0.9, 0.999), eps: float = 1e-15):
+        from . import _lib as L
+
+        self._L = L
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise RuntimeError("PeerAdam supports at most 8 ranks")
+        dev = tensors[0].device
+        self.shapes = [tuple(t.shape) for t in tensors]
+        sizes = [t.numel() for t in tensors]
+        self.total = sum(sizes)
+        self.param_buf = PeerFlat(self.total, group, dev)
+        self.grad_buf = PeerFlat(self.total, group, dev)
+        self.params, self.grads, self.segments, off = [], [], [], 0
+        for t, n, lr in zip(tensors, sizes, lrs):
+            pv = self.param_buf.tensor[off:off + n].view(t.shape)
+            pv.copy_(t.detach())
+            self.params.append(pv)
+            self.grads.append(self.grad_buf.tensor[off:off + n].view(t.shape))
+            self.segments.append((off, off + n, float(lr)))
+            off += n
+        self.lo, self.hi = owned_slice(self.total, self.rank, self.world)
+        self.exp_avg = torch.zeros(max(self.hi - self.lo, 1), dtype=torch.float32, device=dev)
+        self.exp_avg_sq = torch.zeros_like(self.exp_avg)
+        self.betas, self.eps, self.t = betas, eps, 0
+        self._tiny = torch.zeros(1, dtype=torch.float32, device=dev)
+        self._seg = (_Segment * len(self.segments))(*[_Segment(a, b, lr) for a, b, lr in self.segments])
+        self._gptr = (ctypes.c_void_p * 8)(*self.grad_buf.ptrs)
+        self._pptr = (ctypes.c_void_p * 8)(*self.param_buf.ptrs)
+        dist.barrier(group=group)  # every rank's initial parameters are in place
+
+    def _barrier(self) -> None:
+        dist.all_reduce(self._tiny, group=self.group)
+
+    @torch.no_grad()
+    def step(self, grads=None) -> None:
+        """One step. `grads` (a list of per-group tensors, e.g. the leaves' .grad) is first copied into this rank's
+        gradient buffer; leave it None when the backward wrote into `grads` directly."""
+        if grads is not None:
+            for v, g in zip(self.grads, grads):
+                v.copy_(g.reshape(v.shape))
+        self.t += 1
+        self._barrier()
+        self._L.call("adam_step_dp_fused", self.world, self.rank, ctypes.addressof(self._gptr),
+                     ctypes.addressof(self._pptr), self.lo, self.hi, self._L.ptr(self.exp_avg),
+                     self._L.ptr(self.exp_avg_sq), len(self.segments), ctypes.addressof(self._seg), self.t,
+                     float(self.betas[0]), float(self.betas[1]), float(self.eps),
+                     torch.cuda.current_stream(self.exp_avg.device).cuda_stream)
+        self._barrier()
+
+    def close(self) -> None:
+        torch.cuda.synchronize()
+        self.params = self.grads = []
+        self.param_buf.close()
+        self.grad_buf.close()
+
+
+class _Segment(ctypes.Structure):
+    """Mirror of dp_adam_segment in include/splat_b200.h."""
+
+    _fields_ = [("begin", ctypes.c_longlong), ("end", ctypes.c_longlong), ("lr", ctypes.c_double)]

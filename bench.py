@@ -39,6 +39,7 @@ from __graft_entry__ import load_package  # noqa: E402
 load_package()
 from gs_b200 import _lib as L  # noqa: E402
 from gs_b200 import adam as gs_adam  # noqa: E402
+from gs_b200 import dist as gs_dist  # noqa: E402
 from gs_b200 import gs3d, scenes  # noqa: E402
 
 METRIC = "fwd+bwd ms/iter (3M Gaussians, 1080p, SH3); train views/s at 1/2/4/8 B200"
@@ -138,17 +139,22 @@ class Trainer:
     def __init__(self, sc: dict, dev, world: int):
         self.dev = dev
         self.world = world
-        self.params = [sc[k].to(dev).contiguous() for k in NAMES]
         self.bases = sc["active_sh_bases"]
-        n = self.params[0].shape[0]
-        self.n = n
-        self.flat = torch.zeros(59 * n, device=dev)
-        self.grads, off = [], 0
-        for p, w in zip(self.params, WIDTHS):
-            self.grads.append(self.flat[off:off + w * n].view(p.shape))
-            off += w * n
-        self.m = [torch.zeros_like(p) for p in self.params]
-        self.v = [torch.zeros_like(p) for p in self.params]
+        self.peer = None
+        if world > 1:  # parameters and gradients in peer-addressable buffers, one fused exchange + Adam kernel
+            self.peer = gs_dist.PeerAdam([sc[k].to(dev).contiguous() for k in NAMES], [LRS[k] for k in NAMES],
+                                         eps=1e-15)
+            self.params, self.grads = self.peer.params, self.peer.grads
+        else:
+            self.params = [sc[k].to(dev).contiguous() for k in NAMES]
+            self.flat = torch.zeros(59 * self.params[0].shape[0], device=dev)
+            self.grads, off = [], 0
+            for p, w in zip(self.params, WIDTHS):
+                self.grads.append(self.flat[off:off + w * p.shape[0]].view(p.shape))
+                off += w * p.shape[0]
+            self.m = [torch.zeros_like(p) for p in self.params]
+            self.v = [torch.zeros_like(p) for p in self.params]
+        self.n = self.params[0].shape[0]
         self.t = 0
         self.ev = {k: [] for k in ("fwd", "bwd", "comm", "adam", "blend_bwd")}
         self.last = None
@@ -168,13 +174,16 @@ class Trainer:
             e[2].record()
             self.ev["blend_bwd"].append((e[1], e[5]))
         self.last = (prim, tile, m, cam)
-        if self.world > 1:
-            torch.distributed.all_reduce(self.flat)
-        if timed:
-            e[3].record()
         self.t += 1
-        gs_adam.adam_step([(p, g, mm, vv, LRS[nm]) for p, g, mm, vv, nm in
-                           zip(self.params, self.grads, self.m, self.v, NAMES)], self.t, eps=1e-15)
+        if self.peer is not None:  # exchange and Adam in one kernel per rank (timed as "comm")
+            self.peer.step()
+            if timed:
+                e[3].record()
+        else:
+            if timed:
+                e[3].record()
+            gs_adam.adam_step([(p, g, mm, vv, LRS[nm]) for p, g, mm, vv, nm in
+                               zip(self.params, self.grads, self.m, self.v, NAMES)], self.t, eps=1e-15)
         if timed:
             e[4].record()
             for k, (a, b) in zip(("fwd", "bwd", "comm", "adam"), zip(e[:-1], e[1:])):
@@ -238,7 +247,8 @@ def run_ours(args) -> None:
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config-shaped)",
             "config": {"workload": f"{args.workload}: 3DGS training step of one {W}x{H} view per GPU per step, "
-                                   f"{n} Gaussians, SH3; fwd + bwd + grad all-reduce (N>1) + fused Adam",
+                                   f"{n} Gaussians, SH3; fwd + bwd + fused Adam (N>1: gradient exchange and Adam "
+                                   f"in one peer-memory kernel per rank)",
                        "gaussians": n, "width": W, "height": H, "views_per_gpu_per_step": views_per_step,
                        "instances_per_view": round(m_avg), "l2": "state (2.8 GB) larger than L2; no flush",
                        "parallelism": f"dp{world} (views)"},
@@ -250,19 +260,29 @@ def run_ours(args) -> None:
             "gpu_launches": launches,
         }
         line.update(roofline(tr, stage, reach, W * H))
+        if tr.peer is not None:
+            line["exchange"] = exchange_figures(tr, stage)
         line["cpu_baseline"] = cpu_baseline(args, sc, cam) if not args.no_cpu_baseline else None
         print(json.dumps(line), flush=True)
     if world > 1:
+        tr.params = tr.grads = []
+        tr.peer.close()
         torch.distributed.destroy_process_group()
 
 
 def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
-    """The training step through the public API (diff_rasterize + autograd + FusedAdam). Every step copies its
-    upstream gradient from pinned host memory (on a copy stream, into one of two device buffers, issued one step
-    ahead so that the copy overlaps the previous step's kernels) and copies its loss back into pinned host memory;
-    all of those copies sit inside the timed region."""
-    leaves = [p.clone().requires_grad_(True) for p in tr.params]
-    opt = gs_adam.FusedAdam([{"params": [p], "lr": LRS[nm]} for p, nm in zip(leaves, NAMES)], lr=0.0, eps=1e-15)
+    """The training step through the public API (diff_rasterize + autograd + FusedAdam at N = 1, PeerAdam over
+    the ranks at N > 1). Every step copies its upstream gradient from pinned host memory (on a copy stream, into
+    one of two device buffers, issued one step ahead so that the copy overlaps the previous step's kernels) and
+    copies its loss back into pinned host memory; all of those copies sit inside the timed region."""
+    peer = None
+    if world > 1:  # the leaves are views of PeerAdam's parameter buffer; step() takes their .grad
+        peer = gs_dist.PeerAdam([p.detach() for p in tr.params], [LRS[nm] for nm in NAMES], eps=1e-15)
+        leaves = [p.requires_grad_(True) for p in peer.params]
+    else:
+        leaves = [p.clone().requires_grad_(True) for p in tr.params]
+        opt = gs_adam.FusedAdam([{"params": [p], "lr": LRS[nm]} for p, nm in zip(leaves, NAMES)], lr=0.0,
+                                eps=1e-15)
     cam = cams[0]
     H, W = cam["height"], cam["width"]
     host = (1e-3 * torch.randn(3, H, W, generator=torch.Generator().manual_seed(99))).pin_memory()
@@ -290,13 +310,14 @@ def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
         dout = dbuf[b]
         img = gs3d.diff_rasterize(*leaves, torch.empty(0), settings)
         loss = (img * dout).sum()
-        opt.zero_grad(set_to_none=True)
+        for p in leaves:
+            p.grad = None
         loss.backward()
         used[b].record(compute)
-        if world > 1:
-            for p in leaves:
-                torch.distributed.all_reduce(p.grad)
-        opt.step()
+        if peer is not None:
+            peer.step(grads=[p.grad for p in leaves])
+        else:
+            opt.step()
         losses[k:k + 1].copy_(loss.detach().view(1), non_blocking=True)
 
     for e in used:
@@ -319,6 +340,11 @@ def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
     ms = torch.tensor([a.elapsed_time(b)], device=dev)
     if world > 1:
         torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+    if peer is not None:
+        for p in leaves:
+            p.grad = None
+        del leaves
+        peer.close()
     return {"value": round(world * args.steps / (float(ms.item()) / 1000.0), 3), "unit": "views/s",
             "h2d_bytes_per_step": int(host.numel() * 4), "d2h_bytes_per_step": 4,
             "note": "upstream gradient copied from pinned host memory one step ahead on a copy stream; loss copied "
@@ -355,7 +381,7 @@ def roofline(tr: Trainer, stage: dict, reach: dict, pixels: int) -> dict:
              + 36.0 * tr.n, "traffic": BLEND_BWD_TRAFFIC, "limiter": "issue (FP32 / ex2 / shuffles)"}
     adam = {"kernel": "k_adam", "ms": stage["adam"], "bytes": 1652.0 * tr.n, "traffic": ADAM_TRAFFIC,
             "limiter": "HBM"}
-    top, other = (blend, adam) if blend["ms"] >= adam["ms"] else (adam, blend)
+    top, other = (blend, adam) if blend["ms"] >= adam["ms"] or tr.peer is not None else (adam, blend)
 
     def entry(k):
         ach = k["bytes"] / (k["ms"] / 1000.0) / 1e9 if k["ms"] > 0 else 0.0
@@ -365,9 +391,25 @@ def roofline(tr: Trainer, stage: dict, reach: dict, pixels: int) -> dict:
                 "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src}
 
     out = entry(top)
-    out["next_kernel"] = entry(other)
+    if tr.peer is None:  # with N > 1 Adam runs inside the fused exchange kernel instead (see "exchange")
+        out["next_kernel"] = entry(other)
     out["blend_reach"] = reach
     return {"roofline": out}
+
+
+def exchange_figures(tr: Trainer, stage: dict) -> dict:
+    """N > 1: the fused exchange + Adam (adam_step_dp_fused between two barriers), against NVLink. Each rank
+    reads its slice's gradients from the other G - 1 ranks while they read theirs from it, and writes its updated
+    slice to them while they write theirs to it: 2 (G - 1) slices cross its links in each direction, at the
+    measured 770 GB/s peer-copy bandwidth per direction."""
+    g = tr.world
+    slice_bytes = 4.0 * (tr.peer.hi - tr.peer.lo)
+    cross = 2 * (g - 1) * slice_bytes
+    t = stage["comm"]
+    ach = cross / (t / 1000.0) / 1e9 if t > 0 else 0.0
+    return {"kernel": "adam_step_dp_fused (+ 2 barriers)", "ms": round(t, 4), "bytes_each_direction": int(cross),
+            "achieved": round(ach, 1), "peak": 770.0, "unit": "GB/s", "frac": round(ach / 770.0, 4),
+            "peak_source": "measured peer copy, per direction"}
 
 
 def cpu_baseline(args, sc, cam):

@@ -280,6 +280,35 @@ int adam_step_multi_lean(int count, const adam_lean_group* groups, int step, dou
                          double eps, const int32_t* visibility, long long n_primitives, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
+ * Data-parallel Adam over peer memory (multi-view training on one node; the reference has no multi-GPU
+ * path, so none of these has a counterpart in it). Buffers that other GPUs address directly: allocated
+ * with splat_peer_alloc (zeroed; ipc_handle receives 64 bytes to send to the other ranks), mapped on
+ * another rank with splat_peer_open, unmapped with splat_peer_close, freed by the owner with splat_peer_free.
+ * ------------------------------------------------------------------------------------------- */
+int splat_peer_alloc(size_t bytes, void** ptr, unsigned char* ipc_handle);
+int splat_peer_open(const unsigned char* ipc_handle, void** ptr);
+int splat_peer_close(void* ptr);
+int splat_peer_free(void* ptr);
+
+#define SPLAT_DP_MAX_RANKS 8
+#define SPLAT_DP_MAX_SEGMENTS 8
+typedef struct dp_adam_segment {
+    long long begin, end; /* element range of one parameter group in the flat vector */
+    double lr;
+} dp_adam_segment;
+/* Rank `rank` of `world` (<= SPLAT_DP_MAX_RANKS) owns elements [lo, hi) (lo a multiple of 4 unless empty) of the flat
+ * parameter vector. grads[k] / params[k] are rank k's flat gradient / parameter vectors as this GPU addresses
+ * them (its own and peer mappings; 16-byte aligned). The kernel sums the slice's gradients over the ranks in
+ * rank order, applies Adam (exp_avg / exp_avg_sq hold the slice's hi - lo moments; each element takes the lr
+ * of its segment; bias corrections as in adam_step_multi) and stores the updated slice into every rank's
+ * params. It waits on nothing: enqueue it after a device-side barrier that follows every rank's backward, and
+ * enqueue a second barrier after it before any rank reads its parameters or writes its gradients again. */
+int adam_step_dp_fused(int world, int rank, const float* const* grads, float* const* params, long long lo,
+                       long long hi, float* exp_avg, float* exp_avg_sq, int segment_count,
+                       const dp_adam_segment* segments, int step, double beta1, double beta2, double eps,
+                       void* stream);
+
+/* ---------------------------------------------------------------------------------------------
  * Fused L1 + SSIM loss (the training loss around the rasterizer; replaces the external fused-ssim call of the
  * reference's trainer, whose share of the step results/phase1/README.md:46-47 reports, and the L1 term beside it).
  * img, gt: device f32[B, C, H, W]. loss = (1 - lambda) mean|img - gt| + lambda (1 - mean SSIM), SSIM with the

@@ -113,3 +113,15 @@ def test_shard_views_rejects_bad_ranks():
     with pytest.raises(ValueError):
         gdist.shard_views([1, 2], 2, 2)
     assert gdist.shard_views(list(range(8)), 3, 8) == [3]
+
+
+def test_owned_slices_tile_the_vector():
+    for total in (0, 1, 5, 17, 4096, 177_000_001):
+        for world in (1, 2, 3, 4, 7, 8):
+            spans = [gdist.owned_slice(total, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == total
+            for (a, b), (c, d) in zip(spans, spans[1:]):
+                assert b == c
+            assert all(lo <= hi and (lo % 4 == 0 or lo == hi) for lo, hi in spans)
+    with pytest.raises(ValueError):
+        gdist.owned_slice(10, 2, 2)
