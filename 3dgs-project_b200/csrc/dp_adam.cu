@@ -50,25 +50,26 @@ __device__ __forceinline__ float adam(float p, float g, float& m, float& v, floa
     return p - step_size * m / denom;
 }
 
+// kWorld: the number of ranks, a template argument so that the per-rank loads live in exactly that many registers.
+template <int kWorld>
 __global__ void __launch_bounds__(kThreads) k_dp_adam(Args a) {
     const long long n = a.hi - a.lo;
     const long long n4 = n / 4;  // lo is a multiple of 4 and the buffers 16-byte aligned
     const long long stride = static_cast<long long>(gridDim.x) * kThreads;
     for (long long q = static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x; q < n4; q += stride) {
         const long long e = a.lo + 4 * q;
-        float4 gv[SPLAT_DP_MAX_RANKS];
+        float4 gv[kWorld];
 #pragma unroll
-        for (int k = 0; k < SPLAT_DP_MAX_RANKS; ++k)  // every rank's load in flight before the sum
-            if (k < a.world) gv[k] = *reinterpret_cast<const float4*>(a.grads[k] + e);
+        for (int k = 0; k < kWorld; ++k)  // every rank's load in flight before the sum
+            gv[k] = *reinterpret_cast<const float4*>(a.grads[k] + e);
         float4 g = gv[0];
 #pragma unroll
-        for (int k = 1; k < SPLAT_DP_MAX_RANKS; ++k)
-            if (k < a.world) {
-                g.x += gv[k].x;
-                g.y += gv[k].y;
-                g.z += gv[k].z;
-                g.w += gv[k].w;
-            }
+        for (int k = 1; k < kWorld; ++k) {
+            g.x += gv[k].x;
+            g.y += gv[k].y;
+            g.z += gv[k].z;
+            g.w += gv[k].w;
+        }
         float4 p = *reinterpret_cast<const float4*>(a.params[a.rank] + e);  // this rank's own copy
         float4 m = *reinterpret_cast<const float4*>(a.exp_avg + 4 * q);
         float4 v = *reinterpret_cast<const float4*>(a.exp_avg_sq + 4 * q);
@@ -79,8 +80,7 @@ __global__ void __launch_bounds__(kThreads) k_dp_adam(Args a) {
         *reinterpret_cast<float4*>(a.exp_avg + 4 * q) = m;
         *reinterpret_cast<float4*>(a.exp_avg_sq + 4 * q) = v;
 #pragma unroll
-        for (int k = 0; k < SPLAT_DP_MAX_RANKS; ++k)
-            if (k < a.world) *reinterpret_cast<float4*>(a.params[k] + e) = p;
+        for (int k = 0; k < kWorld; ++k) *reinterpret_cast<float4*>(a.params[k] + e) = p;
     }
     // the last n % 4 elements, one thread
     if (blockIdx.x == 0 && threadIdx.x == 0) {
@@ -183,7 +183,18 @@ int adam_step_dp_fused(int world, int rank, const float* const* grads, float* co
     a.bc2_sqrt_rcp = static_cast<float>(1.0 / sqrt(1.0 - pow(beta2, step)));
     const long long n4 = (hi - lo) / 4;
     const long long blocks = std::max<long long>(1, std::min<long long>(div_up(n4, dp::kThreads), 8ll * sm_count()));
-    dp::k_dp_adam<<<static_cast<unsigned>(blocks), dp::kThreads, 0, as_stream(stream)>>>(a);
+    cudaStream_t st = as_stream(stream);
+    const unsigned nb = static_cast<unsigned>(blocks);
+    switch (world) {
+        case 1: dp::k_dp_adam<1><<<nb, dp::kThreads, 0, st>>>(a); break;
+        case 2: dp::k_dp_adam<2><<<nb, dp::kThreads, 0, st>>>(a); break;
+        case 3: dp::k_dp_adam<3><<<nb, dp::kThreads, 0, st>>>(a); break;
+        case 4: dp::k_dp_adam<4><<<nb, dp::kThreads, 0, st>>>(a); break;
+        case 5: dp::k_dp_adam<5><<<nb, dp::kThreads, 0, st>>>(a); break;
+        case 6: dp::k_dp_adam<6><<<nb, dp::kThreads, 0, st>>>(a); break;
+        case 7: dp::k_dp_adam<7><<<nb, dp::kThreads, 0, st>>>(a); break;
+        default: dp::k_dp_adam<8><<<nb, dp::kThreads, 0, st>>>(a); break;
+    }
     note_launch();
     return check_launch("adam_step_dp_fused");
 }

@@ -345,6 +345,9 @@ __global__ void k_bucket_tiles(const uint32_t* __restrict__ nb, const uint32_t* 
     for (uint32_t k = 0; k < nb[t] && s + k < bcap; ++k) bucket_tile[s + k] = t;
 }
 
+// kTrain = false is the render-only variant: no checkpoints, per-pixel counts, final T, tile maxima or replay
+// list are written (and bstart / ckpt / counters / reached may be null).
+template <bool kTrain>
 __global__ void __launch_bounds__(kTilePixels) k_blend(Cam cam, const uint2* __restrict__ ranges,
                                                        const uint32_t* __restrict__ bstart,
                                                        const uint32_t* __restrict__ point_list,
@@ -377,7 +380,7 @@ __global__ void __launch_bounds__(kTilePixels) k_blend(Cam cam, const uint2* __r
     rg.y = min(rg.y, static_cast<uint32_t>(m));
     rg.x = min(rg.x, rg.y);
     const int count = static_cast<int>(rg.y - rg.x);
-    const long long b0 = bstart[tile];
+    const long long b0 = kTrain ? bstart[tile] : 0;
 
     float Cr = 0.f, Cg = 0.f, Cb = 0.f, T = 1.f;
     uint32_t last = 0;
@@ -398,7 +401,7 @@ __global__ void __launch_bounds__(kTilePixels) k_blend(Cam cam, const uint2* __r
         const int in_batch = min(kTilePixels, count - base);
         for (int j0 = 0; j0 < in_batch; j0 += kBucket) {
             const long long bucket = b0 + ((base + j0) >> 5);
-            if (bucket < bcap) ckpt[bucket * kTilePixels + local] = make_float4(Cr, Cg, Cb, T);
+            if (kTrain && bucket < bcap) ckpt[bucket * kTilePixels + local] = make_float4(Cr, Cg, Cb, T);
             if (__all_sync(kFullMask, done)) continue;
             const int cnt = min(kBucket, in_batch - j0);
             bool hit = false;
@@ -432,23 +435,25 @@ __global__ void __launch_bounds__(kTilePixels) k_blend(Cam cam, const uint2* __r
         }
         __syncthreads();
     }
-    const uint32_t wmax = __reduce_max_sync(kFullMask, last);
-    if (lane == 0) s_max[warp] = wmax;
-    __syncthreads();
-    if (tid == 0) {
-        uint32_t mxv = 0;
+    if (kTrain) {
+        const uint32_t wmax = __reduce_max_sync(kFullMask, last);
+        if (lane == 0) s_max[warp] = wmax;
+        __syncthreads();
+        if (tid == 0) {
+            uint32_t mxv = 0;
 #pragma unroll
-        for (int w = 0; w < kTilePixels / 32; ++w) mxv = max(mxv, s_max[w]);
-        max_contrib[tile] = mxv;
-        // the buckets up to the last contributor are the ones the backward replays: list them
-        const uint32_t nreach = (mxv + kBucket - 1) / kBucket;
-        s_reach[0] = nreach ? atomicAdd(counters + 2, nreach) : 0u;
-        s_reach[1] = nreach;
-    }
-    __syncthreads();
-    for (uint32_t i = tid; i < s_reach[1]; i += kTilePixels) {
-        const long long slot = static_cast<long long>(s_reach[0]) + i, b = b0 + i;
-        if (slot < bcap && b < bcap) reached[slot] = static_cast<uint32_t>(b);
+            for (int w = 0; w < kTilePixels / 32; ++w) mxv = max(mxv, s_max[w]);
+            max_contrib[tile] = mxv;
+            // the buckets up to the last contributor are the ones the backward replays: list them
+            const uint32_t nreach = (mxv + kBucket - 1) / kBucket;
+            s_reach[0] = nreach ? atomicAdd(counters + 2, nreach) : 0u;
+            s_reach[1] = nreach;
+        }
+        __syncthreads();
+        for (uint32_t i = tid; i < s_reach[1]; i += kTilePixels) {
+            const long long slot = static_cast<long long>(s_reach[0]) + i, b = b0 + i;
+            if (slot < bcap && b < bcap) reached[slot] = static_cast<uint32_t>(b);
+        }
     }
     if (inside) {
         const int pix = y * cam.width + x;
@@ -456,8 +461,10 @@ __global__ void __launch_bounds__(kTilePixels) k_blend(Cam cam, const uint2* __r
         image[pix] = Cr + T * __ldg(bg);
         image[HW + pix] = Cg + T * __ldg(bg + 1);
         image[2 * HW + pix] = Cb + T * __ldg(bg + 2);
-        final_T[pix] = T;
-        n_contrib[pix] = last;
+        if (kTrain) {
+            final_T[pix] = T;
+            n_contrib[pix] = last;
+        }
     }
 }
 
@@ -484,6 +491,26 @@ int fill_cam(const gs3d_settings* s, Cam& cam) {
     cam.active_sh_bases = s->active_sh_bases;
     cam.rest_bases = s->rest_bases;
     cam.proper_aa = s->proper_antialiasing;
+    return SPLAT_OK;
+}
+
+// Duplication, the tile-digit sort passes and the tile ranges (shared by the training and the render-only path).
+int bin_instances(int n, long long m, const Cam& cam, const PrimBuffers& pb, const TileBuffers& tb,
+                  const InstBuffers& ib, cudaStream_t st) {
+    const int T = cam.tiles_x * cam.tiles_y;
+    SPLAT_CUDA(cudaMemsetAsync(tb.ranges, 0, sizeof(uint2) * T, st));
+    if (m > 0) {
+        k_duplicate<<<div_up(n, kDupThreads), kDupThreads, 0, st>>>(n, cam, pb, ib);
+        note_launch();
+        SPLAT_TRY(check_launch("gs3d_duplicate"));
+        // the tile-digit passes (the pad key T needs bit_width(T) bits)
+        const int tile_bits = bit_width(static_cast<unsigned long long>(T));
+        SPLAT_TRY(radix_sort_pairs<uint32_t>(ib.keys, ib.vals, ib.keys_sorted, ib.point_list, m, 0, tile_bits,
+                                             ib.sort_ws, ib.sort_bytes, st));
+        k_ranges<<<div_up(m, 256), 256, 0, st>>>(ib.keys_sorted, static_cast<int>(m), T, tb.ranges);
+        note_launch();
+        SPLAT_TRY(check_launch("gs3d_ranges"));
+    }
     return SPLAT_OK;
 }
 
@@ -562,20 +589,8 @@ int gs3d_render(int n, long long num_instances, const gs3d_settings* settings, v
     TileBuffers tb = carve_tile(ct, cam.width, cam.height);
     InstBuffers ib = carve_inst(ci, m);
     BucketBuffers bb = carve_bucket(cb, bucket_capacity);
-    SPLAT_CUDA(cudaMemsetAsync(tb.ranges, 0, sizeof(uint2) * T, st));
     SPLAT_CUDA(cudaMemsetAsync(pb.counters + 2, 0, sizeof(uint32_t), st));  // k_blend counts the replayed buckets
-    if (m > 0) {
-        k_duplicate<<<div_up(n, kDupThreads), kDupThreads, 0, st>>>(n, cam, pb, ib);
-        note_launch();
-        SPLAT_TRY(check_launch("gs3d_duplicate"));
-        // the tile-digit passes (the pad key T needs bit_width(T) bits)
-        const int tile_bits = bit_width(static_cast<unsigned long long>(T));
-        SPLAT_TRY(radix_sort_pairs<uint32_t>(ib.keys, ib.vals, ib.keys_sorted, ib.point_list, m, 0, tile_bits,
-                                             ib.sort_ws, ib.sort_bytes, st));
-        k_ranges<<<div_up(m, 256), 256, 0, st>>>(ib.keys_sorted, static_cast<int>(m), T, tb.ranges);
-        note_launch();
-        SPLAT_TRY(check_launch("gs3d_ranges"));
-    }
+    SPLAT_TRY(bin_instances(n, m, cam, pb, tb, ib, st));
     k_bucket_counts<<<div_up(T + 1, 256), 256, 0, st>>>(tb.ranges, T, tb.nb);
     note_launch();
     SPLAT_TRY(check_launch("gs3d_bucket_counts"));
@@ -583,11 +598,37 @@ int gs3d_render(int n, long long num_instances, const gs3d_settings* settings, v
     k_bucket_tiles<<<div_up(T, 256), 256, 0, st>>>(tb.nb, tb.bstart, T, bucket_capacity, bb.tile);
     note_launch();
     SPLAT_TRY(check_launch("gs3d_bucket_tiles"));
-    k_blend<<<T, kTilePixels, 0, st>>>(cam, tb.ranges, tb.bstart, ib.point_list, pb.mean2d, pb.conic_o, pb.color_z,
-                                       pb.rect, settings->bg, image, tb.final_T, tb.n_contrib, tb.max_contrib, bb.ckpt,
-                                       pb.counters, bb.reached, n < 1 ? 1 : n, static_cast<int>(m), bucket_capacity);
+    k_blend<true><<<T, kTilePixels, 0, st>>>(cam, tb.ranges, tb.bstart, ib.point_list, pb.mean2d, pb.conic_o,
+                                             pb.color_z, pb.rect, settings->bg, image, tb.final_T, tb.n_contrib,
+                                             tb.max_contrib, bb.ckpt, pb.counters, bb.reached, n < 1 ? 1 : n,
+                                             static_cast<int>(m), bucket_capacity);
     note_launch();
     return check_launch("gs3d_blend");
+}
+
+int gs3d_render_inference(int n, long long num_instances, const gs3d_settings* settings, void* prim_buf,
+                          size_t prim_bytes_, void* tile_buf, size_t tile_bytes_, void* inst_buf, size_t inst_bytes_,
+                          float* image, void* stream) {
+    Cam cam;
+    SPLAT_TRY(fill_cam(settings, cam));
+    const long long m = num_instances;
+    const int T = cam.tiles_x * cam.tiles_y;
+    SPLAT_REQUIRE(n >= 0 && m >= 0 && m < (1ll << 31), "gs3d_render_inference: bad sizes n=%d M=%lld", n, m);
+    SPLAT_REQUIRE(n > 0 || m == 0, "gs3d_render_inference: instances without Gaussians");
+    SPLAT_REQUIRE(prim_bytes_ >= prim_bytes(n) && tile_bytes_ >= tile_bytes(cam.width, cam.height) &&
+                      inst_bytes_ >= inst_bytes(m),
+                  "gs3d_render_inference: a buffer is smaller than its size query");
+    cudaStream_t st = as_stream(stream);
+    Carver cp(prim_buf, prim_bytes_), ct(tile_buf, tile_bytes_), ci(inst_buf, inst_bytes_);
+    PrimBuffers pb = carve_prim(cp, n);
+    TileBuffers tb = carve_tile(ct, cam.width, cam.height);
+    InstBuffers ib = carve_inst(ci, m);
+    SPLAT_TRY(bin_instances(n, m, cam, pb, tb, ib, st));
+    k_blend<false><<<T, kTilePixels, 0, st>>>(cam, tb.ranges, nullptr, ib.point_list, pb.mean2d, pb.conic_o,
+                                              pb.color_z, pb.rect, settings->bg, image, nullptr, nullptr, nullptr,
+                                              nullptr, nullptr, nullptr, n < 1 ? 1 : n, static_cast<int>(m), 0);
+    note_launch();
+    return check_launch("gs3d_blend_inference");
 }
 
 }  // extern "C"

@@ -89,16 +89,13 @@ def _check_params(means, scales, rotations, opacities, sh0, sh_rest):
     return n, (sh_rest.numel() // (3 * n) if n else 0)
 
 
-@torch.no_grad()
-def forward(means, scales, rotations, opacities, sh0, sh_rest, w2c, cam_position, bg_color, active_sh_bases, width,
-            height, focal_x, focal_y, center_x, center_y, near_plane, far_plane, proper_antialiasing):
-    """Faster-GS `_C.forward`: (image[3,H,W], prim_buf, tile_buf, inst_buf, bucket_buf, n_instances, n_buckets, 0)."""
+def _preprocess(means, scales, rotations, opacities, sh0, sh_rest, settings_args):
     n, rest = _check_params(means, scales, rotations, opacities, sh0, sh_rest)
     dev = means.device
     keep: list = []
-    s = _settings(dev, w2c, cam_position, bg_color, active_sh_bases, width, height, focal_x, focal_y, center_x,
-                  center_y, near_plane, far_plane, proper_antialiasing, rest, keep)
+    s = _settings(dev, *settings_args, rest, keep)
     stream = L.stream_of(means)
+    width, height = settings_args[4], settings_args[5]
     prim = torch.empty(L.query("gs3d_primitive_buffer_size", n), dtype=torch.uint8, device=dev)
     tile = torch.empty(L.query("gs3d_tile_buffer_size", width, height), dtype=torch.uint8, device=dev)
     count = torch.zeros(2, dtype=torch.int32, device=dev)
@@ -109,6 +106,32 @@ def forward(means, scales, rotations, opacities, sh0, sh_rest, w2c, cam_position
     m, waits = count.tolist()  # the one host read of a forward
     if waits:
         raise RuntimeError(f"{waits} bounded device-side wait(s) in the radix sort gave up; results are unreliable")
+    return n, dev, s, keep, stream, prim, tile, m
+
+
+@torch.no_grad()
+def inference(means, scales, rotations, opacities, sh0, sh_rest, w2c, cam_position, bg_color, active_sh_bases,
+              width, height, focal_x, focal_y, center_x, center_y, near_plane, far_plane, proper_antialiasing):
+    """Faster-GS `_C.inference`: the image [3, H, W] alone (render-only path: no buffers for a backward)."""
+    n, dev, s, keep, stream, prim, tile, m = _preprocess(
+        means, scales, rotations, opacities, sh0, sh_rest,
+        (w2c, cam_position, bg_color, active_sh_bases, width, height, focal_x, focal_y, center_x, center_y,
+         near_plane, far_plane, proper_antialiasing))
+    inst = torch.empty(L.query("gs3d_instance_buffer_size", m), dtype=torch.uint8, device=dev)
+    image = torch.empty(3, height, width, dtype=torch.float32, device=dev)
+    L.call("gs3d_render_inference", n, m, ctypes.byref(s), L.ptr(prim), prim.numel(), L.ptr(tile), tile.numel(),
+           L.ptr(inst), inst.numel(), L.ptr(image), stream)
+    return image
+
+
+@torch.no_grad()
+def forward(means, scales, rotations, opacities, sh0, sh_rest, w2c, cam_position, bg_color, active_sh_bases, width,
+            height, focal_x, focal_y, center_x, center_y, near_plane, far_plane, proper_antialiasing):
+    """Faster-GS `_C.forward`: (image[3,H,W], prim_buf, tile_buf, inst_buf, bucket_buf, n_instances, n_buckets, 0)."""
+    n, dev, s, keep, stream, prim, tile, m = _preprocess(
+        means, scales, rotations, opacities, sh0, sh_rest,
+        (w2c, cam_position, bg_color, active_sh_bases, width, height, focal_x, focal_y, center_x, center_y,
+         near_plane, far_plane, proper_antialiasing))
     bcap = int(L.load().gs3d_bucket_bound(m, width, height))
     inst = torch.empty(L.query("gs3d_instance_buffer_size", m), dtype=torch.uint8, device=dev)
     bucket = torch.empty(L.query("gs3d_bucket_buffer_size", bcap), dtype=torch.uint8, device=dev)

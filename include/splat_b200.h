@@ -206,6 +206,12 @@ int gs3d_preprocess(const float* means, const float* scales, const float* rotati
 int gs3d_render(int n, long long num_instances, const gs3d_settings* settings, void* prim_buf, size_t prim_bytes,
                 void* tile_buf, size_t tile_bytes, void* inst_buf, size_t inst_bytes, void* bucket_buf,
                 size_t bucket_bytes, long long bucket_capacity, float* image, void* stream);
+/* Render only (replaces Faster-GS's `_C.inference`, whose blend loop upstream/upstream_main_kernels.patch:131-165
+ * shows): gs3d_preprocess, then this in place of gs3d_render. The same image as gs3d_render, without the
+ * checkpoints, per-pixel counts and bucket tables a backward needs (no bucket buffer). */
+int gs3d_render_inference(int n, long long num_instances, const gs3d_settings* settings, void* prim_buf,
+                          size_t prim_bytes, void* tile_buf, size_t tile_bytes, void* inst_buf, size_t inst_bytes,
+                          float* image, void* stream);
 /* Backward: grad_image f32[3,H,W] -> grad_means f32[N,3], grad_scales f32[N,3], grad_rotations f32[N,4],
  * grad_opacities f32[N], grad_sh0 f32[N,3], grad_sh_rest f32[N,rest_bases,3] (zeros for Gaussians that
  * were not visible). The bucket count is read on the device, so no host sync happens.

@@ -188,6 +188,27 @@ def test_densification_rows_vs_float64_reference(rows, cuda):
         assert rel(got[2], 2 * (absg * scale).norm(dim=1)) < 1e-4
 
 
+@pytest.mark.parametrize("name", ["micro", "tiny", "garden_res", "heavy_overlap", "empty"])
+def test_render_only_path_matches_training_forward(name, cuda):
+    """gs3d.inference (Faster-GS `_C.inference`) gives the training forward's image bit for bit."""
+    sc, cam, params, settings = _setup(name, seed=11)
+    img = gs3d.forward(*params, *settings)[0]
+    inf = gs3d.inference(*params, *settings)
+    assert torch.equal(img, inf)
+
+
+def test_render_only_c5_scale(cuda):
+    """Config C5 (6M Gaussians, 3840x2160): the render-only image equals the training forward's, one frame."""
+    sc = scenes.gs3d_config("c5", seed=0)
+    params = [sc[k].to(cuda).contiguous() for k in ("means", "scales", "rotations", "opacities", "sh0", "sh_rest")]
+    cam = sc["cameras"][0]
+    settings = scenes.settings_tuple(cam, sc["active_sh_bases"], cuda)
+    inf = gs3d.inference(*params, *settings)
+    img = gs3d.forward(*params, *settings)[0]
+    assert torch.equal(img, inf)
+    assert bool(torch.isfinite(inf).all()) and float(inf.std()) > 0
+
+
 def test_empty_scene(cuda):
     """All Gaussians behind the camera: no instances, zero gradients, no launch error (test_parity.py:143-153)."""
     sc, cam, params, settings = _setup("empty", seed=3)
