@@ -11,8 +11,10 @@
 // front-to-back order up to the pixel's last contributor. Row bands whose culling rectangle misses
 // the splat are skipped by the whole warp. Per splat the lanes' nine sums (mean2d 2, conic 3,
 // opacity, colour 3) are reduced with shuffles and lane 0 issues three vector atomics (float2,
-// float4, float4) instead of nine scalar ones. With three densification rows it also sums the per-pixel
-// absolute mean2d gradients (two more values and one more float2 atomic per splat).
+// float4, float4) instead of nine scalar ones; the reduction halves the nine sums across the lanes (9 -> 5 ->
+// 3 -> 2 -> 1 per lane, 12 shuffles) and lane 0 collects the totals (8 shuffles) instead of 45 butterfly
+// shuffles. With three densification rows it also sums the per-pixel absolute mean2d gradients (two more
+// values and one more float2 atomic per splat).
 //
 // k_preprocess_backward: one thread per Gaussian recomputes the projection and chains
 // (dL/dmean2d, dL/dconic, dL/dopacity, dL/dcolour) to means, scales, rotations, opacity logits,
@@ -52,6 +54,19 @@ inline GradAcc carve_grad(Carver& c, int n) {
     g.color = c.take<float4>(nn);
     g.mean2d_abs = c.take<float2>(nn);
     return g;
+}
+
+// One halving step of a warp sum of N values per lane: lanes with the `off` bit clear keep the first ceil(N/2)
+// partial sums, the others the rest, each adding its partner's copy of the half it keeps.
+template <int N>
+__device__ __forceinline__ void fold_half(const float (&v)[N], float (&out)[(N + 1) / 2], int off, bool upper) {
+    constexpr int H = (N + 1) / 2;
+#pragma unroll
+    for (int i = 0; i < H; ++i) {
+        const float hi = i + H < N ? v[i + H] : 0.f;
+        const float recv = __shfl_xor_sync(kFullMask, upper ? v[i] : hi, off);
+        out[i] = (upper ? hi : v[i]) + recv;
+    }
 }
 
 // kAbs: also accumulate the per-pixel absolute values of the mean2d gradient (the third densification row).
@@ -184,25 +199,37 @@ __global__ void __launch_bounds__(32 * kBwdWarps, SPLAT_BWD_MIN_BLOCKS) k_blend_
                 }
                 T[r] *= one_minus;
             }
-            if (__ballot_sync(kFullMask, used) == 0u) continue;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                s_x += __shfl_down_sync(kFullMask, s_x, o);
-                s_y += __shfl_down_sync(kFullMask, s_y, o);
-                s_xx += __shfl_down_sync(kFullMask, s_xx, o);
-                s_xy += __shfl_down_sync(kFullMask, s_xy, o);
-                s_yy += __shfl_down_sync(kFullMask, s_yy, o);
-                g_o += __shfl_down_sync(kFullMask, g_o, o);
-                g_r += __shfl_down_sync(kFullMask, g_r, o);
-                g_g += __shfl_down_sync(kFullMask, g_g, o);
-                g_bl += __shfl_down_sync(kFullMask, g_bl, o);
+            const unsigned used_mask = __ballot_sync(kFullMask, used);
+            if (used_mask == 0u) continue;
+            const int g = s_id[warp][j];
+            {
+                // halving exchanges: 9 -> 5 -> 3 -> 2 -> 1 partial sums per lane (11 shuffles), a last exchange,
+                // then lane 0 collects the nine totals from the lanes that hold them (8 shuffles)
+                const float v9[9] = {s_x, s_y, s_xx, s_xy, s_yy, g_o, g_r, g_g, g_bl};
+                float f5[5], f3[3], f2[2], f1[1];
+                fold_half<9>(v9, f5, 16, lane & 16);
+                fold_half<5>(f5, f3, 8, lane & 8);
+                fold_half<3>(f3, f2, 4, lane & 4);
+                fold_half<2>(f2, f1, 2, lane & 2);
+                const float t = f1[0] + __shfl_xor_sync(kFullMask, f1[0], 1);
+                s_x = t;
+                s_y = __shfl_sync(kFullMask, t, 2);
+                s_xx = __shfl_sync(kFullMask, t, 4);
+                s_xy = __shfl_sync(kFullMask, t, 8);
+                s_yy = __shfl_sync(kFullMask, t, 10);
+                g_o = __shfl_sync(kFullMask, t, 16);
+                g_r = __shfl_sync(kFullMask, t, 18);
+                g_g = __shfl_sync(kFullMask, t, 20);
+                g_bl = __shfl_sync(kFullMask, t, 24);
                 if (kAbs) {
-                    a_x += __shfl_down_sync(kFullMask, a_x, o);
-                    a_y += __shfl_down_sync(kFullMask, a_y, o);
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        a_x += __shfl_down_sync(kFullMask, a_x, o);
+                        a_y += __shfl_down_sync(kFullMask, a_y, o);
+                    }
                 }
             }
             if (lane == 0) {
-                const int g = s_id[warp][j];
                 // q2 = a2 dx^2 + b2 dx dy + c2 dy^2: dq2/dmx = 2 a2 dx + b2 dy, dq2/dmy = b2 dx + 2 c2 dy; then back
                 // from the exp2-scaled conic (a2, b2, c2) = log2(e) (-0.5 A, -B, -0.5 C) to (A, B, C)
                 atomicAdd(acc.mean2d + g, make_float2(2.f * co.x * s_x + co.y * s_y, co.y * s_x + 2.f * co.z * s_y));
