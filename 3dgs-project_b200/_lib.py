@@ -36,6 +36,8 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "splat_peer_open": (_I, [_P, _P]),
     "splat_peer_close": (_I, [_P]),
     "splat_peer_free": (_I, [_P]),
+    "adam_step_dp_nvls": (_I, [_LL, _LL, _P, _P, _P, _P, _P, _I, _P, _I, ctypes.c_double, ctypes.c_double,
+                               ctypes.c_double, _P]),
     "adam_step_dp_fused": (_I, [_I, _I, _P, _P, _LL, _LL, _P, _P, _I, _P, _I, ctypes.c_double, ctypes.c_double,
                                 ctypes.c_double, _P]),
     "splat_l1_ssim_forward": (_I, [_P, _P, _I, _I, _I, _I, ctypes.c_float, _I, _P, _P, _P, _SZ, _P]),

@@ -98,6 +98,65 @@ __global__ void __launch_bounds__(kThreads) k_dp_adam(Args a) {
     __threadfence_system();  // the peer stores are visible to every GPU before the caller's barrier completes
 }
 
+// The same step through NVLink SHARP (multicast memory): each 16-byte group of the slice's gradients is summed
+// over the ranks by the switch (multimem.ld_reduce) and the updated parameters are written to every rank with one
+// multicast store (multimem.st), so each rank's links carry the slice once in and once out per direction instead
+// of G - 1 times. grads_mc / params_mc are multicast addresses of the flat vectors; params_local this rank's copy.
+struct NvlsArgs {
+    const float* grads_mc;
+    float* params_mc;
+    const float* params_local;
+    float* exp_avg;
+    float* exp_avg_sq;
+    long long lo, hi;
+    Segment seg[SPLAT_DP_MAX_SEGMENTS];
+    int nseg;
+    float beta1, beta2, eps, bc2_sqrt_rcp;
+};
+
+__device__ __forceinline__ float step_size_nvls(const NvlsArgs& a, long long i) {
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < SPLAT_DP_MAX_SEGMENTS; ++k)
+        if (k < a.nseg && i >= a.seg[k].begin && i < a.seg[k].end) s = a.seg[k].step_size;
+    return s;
+}
+
+__device__ __forceinline__ float adam_nvls(float p, float g, float& m, float& v, float step_size, const NvlsArgs& a) {
+    const float g2 = g * g;
+    m = fmaf(a.beta1, m - g, g);
+    v = fmaf(a.beta2, v - g2, g2);
+    const float denom = sqrtf(v) * a.bc2_sqrt_rcp + a.eps;
+    return p - step_size * m / denom;
+}
+
+__global__ void __launch_bounds__(kThreads) k_dp_adam_nvls(NvlsArgs a) {
+    const long long n4 = (a.hi - a.lo) / 4;  // lo and hi are multiples of 4
+    const long long stride = static_cast<long long>(gridDim.x) * kThreads;
+    for (long long q = static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x; q < n4; q += stride) {
+        const long long e = a.lo + 4 * q;
+        float4 g;
+        asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(g.x), "=f"(g.y), "=f"(g.z), "=f"(g.w)
+                     : "l"(a.grads_mc + e)
+                     : "memory");
+        float4 p = *reinterpret_cast<const float4*>(a.params_local + e);
+        float4 m = *reinterpret_cast<const float4*>(a.exp_avg + 4 * q);
+        float4 v = *reinterpret_cast<const float4*>(a.exp_avg_sq + 4 * q);
+        p.x = adam_nvls(p.x, g.x, m.x, v.x, step_size_nvls(a, e), a);
+        p.y = adam_nvls(p.y, g.y, m.y, v.y, step_size_nvls(a, e + 1), a);
+        p.z = adam_nvls(p.z, g.z, m.z, v.z, step_size_nvls(a, e + 2), a);
+        p.w = adam_nvls(p.w, g.w, m.w, v.w, step_size_nvls(a, e + 3), a);
+        *reinterpret_cast<float4*>(a.exp_avg + 4 * q) = m;
+        *reinterpret_cast<float4*>(a.exp_avg_sq + 4 * q) = v;
+        asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};"
+                     :
+                     : "l"(a.params_mc + e), "f"(p.x), "f"(p.y), "f"(p.z), "f"(p.w)
+                     : "memory");
+    }
+    __threadfence_system();
+}
+
 }  // namespace dp
 }  // namespace splat
 
@@ -197,6 +256,47 @@ int adam_step_dp_fused(int world, int rank, const float* const* grads, float* co
     }
     note_launch();
     return check_launch("adam_step_dp_fused");
+}
+
+int adam_step_dp_nvls(long long lo, long long hi, const float* grads_mc, float* params_mc, const float* params_local,
+                      float* exp_avg, float* exp_avg_sq, int segment_count, const dp_adam_segment* segments, int step,
+                      double beta1, double beta2, double eps, void* stream) {
+    SPLAT_REQUIRE(step >= 1, "adam_step_dp_nvls: step must be >= 1");
+    SPLAT_REQUIRE(segment_count >= 1 && segment_count <= SPLAT_DP_MAX_SEGMENTS,
+                  "adam_step_dp_nvls: %d segments (1 to %d)", segment_count, SPLAT_DP_MAX_SEGMENTS);
+    SPLAT_REQUIRE(0 <= lo && lo <= hi && lo % 4 == 0 && hi % 4 == 0,
+                  "adam_step_dp_nvls: slice [%lld, %lld) must start and end at multiples of 4", lo, hi);
+    if (hi == lo) return SPLAT_OK;
+    SPLAT_REQUIRE(grads_mc && params_mc && params_local && exp_avg && exp_avg_sq, "adam_step_dp_nvls: null buffer");
+    SPLAT_REQUIRE(((reinterpret_cast<uintptr_t>(grads_mc) | reinterpret_cast<uintptr_t>(params_mc) |
+                    reinterpret_cast<uintptr_t>(params_local) | reinterpret_cast<uintptr_t>(exp_avg) |
+                    reinterpret_cast<uintptr_t>(exp_avg_sq)) & 15u) == 0,
+                  "adam_step_dp_nvls: buffers must be 16-byte aligned");
+    dp::NvlsArgs a{};
+    a.grads_mc = grads_mc;
+    a.params_mc = params_mc;
+    a.params_local = params_local;
+    a.exp_avg = exp_avg;
+    a.exp_avg_sq = exp_avg_sq;
+    a.lo = lo;
+    a.hi = hi;
+    a.nseg = segment_count;
+    const double bc1_rcp = 1.0 / (1.0 - pow(beta1, step));
+    for (int k = 0; k < segment_count; ++k) {
+        SPLAT_REQUIRE(segments[k].begin <= segments[k].end, "adam_step_dp_nvls: segment %d is reversed", k);
+        a.seg[k].begin = segments[k].begin;
+        a.seg[k].end = segments[k].end;
+        a.seg[k].step_size = static_cast<float>(segments[k].lr * bc1_rcp);
+    }
+    a.beta1 = static_cast<float>(beta1);
+    a.beta2 = static_cast<float>(beta2);
+    a.eps = static_cast<float>(eps);
+    a.bc2_sqrt_rcp = static_cast<float>(1.0 / sqrt(1.0 - pow(beta2, step)));
+    const long long n4 = (hi - lo) / 4;
+    const long long blocks = std::max<long long>(1, std::min<long long>(div_up(n4, dp::kThreads), 8ll * sm_count()));
+    dp::k_dp_adam_nvls<<<static_cast<unsigned>(blocks), dp::kThreads, 0, as_stream(stream)>>>(a);
+    note_launch();
+    return check_launch("adam_step_dp_nvls");
 }
 
 }  // extern "C"

@@ -123,6 +123,30 @@ class PeerFlat:
         self._own = None
 
 
+class MulticastFlat:
+    """A flat float32 vector allocated as PyTorch symmetric memory: this rank's buffer as a tensor, every rank's
+    buffer address (`ptrs`) and the NVLink multicast address bound to all of them (`mc`, 0 when the node has no
+    NVLS)."""
+
+    def __init__(self, numel: int, group=None, device=None):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.group = group
+        self.numel = numel
+        self.tensor = symm_mem.empty(max(numel, 4), dtype=torch.float32, device=device)
+        self.tensor.zero_()
+        self._handle = symm_mem.rendezvous(self.tensor, group if group is not None else dist.group.WORLD)
+        self.ptrs = list(self._handle.buffer_ptrs)
+        self.mc = int(self._handle.multicast_ptr)
+
+    def close(self) -> None:
+        if self.tensor is None:
+            return
+        dist.barrier(group=self.group)  # nobody addresses this buffer any more
+        self.tensor = None
+        self._handle = None
+
+
 class PeerAdam:
     """Data-parallel Adam for replicated parameters, one fused kernel per step instead of an all-reduce of the
     gradients followed by the same Adam step on every rank.
@@ -132,9 +156,13 @@ class PeerAdam:
     over the ranks (peer loads), applies Adam with the slice's moments, and writes the updated slice into every
     rank's parameters (peer stores). Two stream-ordered barriers (one-element all-reduces) bracket the kernel.
     Bias corrections and the per-element update are those of FusedAdam; the gradient sum is taken in rank order.
+
+    nvls: use NVLink SHARP when the node has it (the buffers come from PyTorch's symmetric memory and the kernel
+    sums through multimem.ld_reduce and writes through multimem.st, halving the bytes per link at G = 8);
+    None = the SPLAT_NVLS environment variable (on unless "0"). Without NVLS the peer-load / peer-store kernel runs.
     """
 
-    def __init__(self, tensors, lrs, group=None, betas=(0.9, 0.999), eps: float = 1e-15):
+    def __init__(self, tensors, lrs, group=None, betas=(0.9, 0.999), eps: float = 1e-15, nvls: bool | None = None):
         from . import _lib as L
 
         self._L = L
@@ -147,8 +175,27 @@ class PeerAdam:
         self.shapes = [tuple(t.shape) for t in tensors]
         sizes = [t.numel() for t in tensors]
         self.total = sum(sizes)
-        self.param_buf = PeerFlat(self.total, group, dev)
-        self.grad_buf = PeerFlat(self.total, group, dev)
+        if nvls is None:
+            import os
+
+            nvls = os.environ.get("SPLAT_NVLS", "1") != "0"
+        self.nvls = False
+        if nvls and self.world > 1:
+            padded = (self.total + 3) // 4 * 4  # the multicast kernel moves whole 16-byte groups
+            try:
+                pb, gb = MulticastFlat(padded, group, dev), MulticastFlat(padded, group, dev)
+                ok = torch.tensor([int(pb.mc != 0 and gb.mc != 0)], device=dev)
+                dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)  # every rank takes the same path
+                if int(ok.item()):
+                    self.param_buf, self.grad_buf, self.nvls = pb, gb, True
+                else:
+                    pb.close()
+                    gb.close()
+            except (RuntimeError, ImportError, AttributeError):
+                self.nvls = False
+        if not self.nvls:
+            self.param_buf = PeerFlat(self.total, group, dev)
+            self.grad_buf = PeerFlat(self.total, group, dev)
         self.params, self.grads, self.segments, off = [], [], [], 0
         for t, n, lr in zip(tensors, sizes, lrs):
             pv = self.param_buf.tensor[off:off + n].view(t.shape)
@@ -157,7 +204,7 @@ class PeerAdam:
             self.grads.append(self.grad_buf.tensor[off:off + n].view(t.shape))
             self.segments.append((off, off + n, float(lr)))
             off += n
-        self.lo, self.hi = owned_slice(self.total, self.rank, self.world)
+        self.lo, self.hi = owned_slice(self.param_buf.numel if self.nvls else self.total, self.rank, self.world)
         self.exp_avg = torch.zeros(max(self.hi - self.lo, 1), dtype=torch.float32, device=dev)
         self.exp_avg_sq = torch.zeros_like(self.exp_avg)
         self.betas, self.eps, self.t = betas, eps, 0
@@ -178,12 +225,18 @@ class PeerAdam:
             for v, g in zip(self.grads, grads):
                 v.copy_(g.reshape(v.shape))
         self.t += 1
+        stream = torch.cuda.current_stream(self.exp_avg.device).cuda_stream
         self._barrier()
-        self._L.call("adam_step_dp_fused", self.world, self.rank, ctypes.addressof(self._gptr),
-                     ctypes.addressof(self._pptr), self.lo, self.hi, self._L.ptr(self.exp_avg),
-                     self._L.ptr(self.exp_avg_sq), len(self.segments), ctypes.addressof(self._seg), self.t,
-                     float(self.betas[0]), float(self.betas[1]), float(self.eps),
-                     torch.cuda.current_stream(self.exp_avg.device).cuda_stream)
+        if self.nvls:
+            self._L.call("adam_step_dp_nvls", self.lo, self.hi, self.grad_buf.mc, self.param_buf.mc,
+                         self._L.ptr(self.param_buf.tensor), self._L.ptr(self.exp_avg), self._L.ptr(self.exp_avg_sq),
+                         len(self.segments), ctypes.addressof(self._seg), self.t, float(self.betas[0]),
+                         float(self.betas[1]), float(self.eps), stream)
+        else:
+            self._L.call("adam_step_dp_fused", self.world, self.rank, ctypes.addressof(self._gptr),
+                         ctypes.addressof(self._pptr), self.lo, self.hi, self._L.ptr(self.exp_avg),
+                         self._L.ptr(self.exp_avg_sq), len(self.segments), ctypes.addressof(self._seg), self.t,
+                         float(self.betas[0]), float(self.betas[1]), float(self.eps), stream)
         self._barrier()
 
     def close(self) -> None:

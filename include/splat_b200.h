@@ -314,6 +314,14 @@ int adam_step_dp_fused(int world, int rank, const float* const* grads, float* co
                        const dp_adam_segment* segments, int step, double beta1, double beta2, double eps,
                        void* stream);
 
+/* The same step over NVLink multicast memory (NVLS): grads_mc / params_mc are multicast addresses of the
+ * flat gradient / parameter vectors (bound to every rank's buffer), params_local this rank's copy. The switch
+ * sums the slice's gradients (multimem.ld_reduce) and one multicast store writes the updated slice to every
+ * rank (multimem.st); lo and hi multiples of 4. Same ordering requirements as adam_step_dp_fused. */
+int adam_step_dp_nvls(long long lo, long long hi, const float* grads_mc, float* params_mc, const float* params_local,
+                      float* exp_avg, float* exp_avg_sq, int segment_count, const dp_adam_segment* segments, int step,
+                      double beta1, double beta2, double eps, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Fused L1 + SSIM loss (the training loss around the rasterizer; replaces the external fused-ssim call of the
  * reference's trainer, whose share of the step results/phase1/README.md:46-47 reports, and the L1 term beside it).

@@ -212,3 +212,38 @@ def time_training_step(sc: dict, cam: dict, budget_s: float = 20.0) -> dict:
                         "blend_fwd_bwd_full_view_est": round(full_blend, 3),
                         "preprocess_backward": round(t4 - t3, 3), "adam": round(t5 - t4, 3)},
             "threads": os.cpu_count()}
+
+
+def time_render_frame(sc: dict, cam: dict, budget_s: float = 20.0) -> dict:
+    """One render-only frame on the CPU: preprocess, binning, and the blend over a band of tile rows (grown until
+    about ``budget_s`` of work), extrapolated to the whole frame."""
+    import torch
+
+    params = [sc[k].numpy() if torch.is_tensor(sc[k]) else sc[k]
+              for k in ("means", "scales", "rotations", "opacities", "sh0", "sh_rest")]
+    o = Oracle(params, {k: (v.numpy() if torch.is_tensor(v) else v) for k, v in cam.items()}, sc["active_sh_bases"])
+    threads = o.lib.gs3o_threads()
+    t0 = time.perf_counter()
+    o.preprocess()
+    t1 = time.perf_counter()
+    o.bin()
+    t2 = time.perf_counter()
+    mid = o.tiles_y // 2
+    rows, blend_s, band = 0, 0.0, 1
+    while True:
+        r0 = max(mid - band // 2, 0)
+        r1 = min(r0 + band, o.tiles_y)
+        ta = time.perf_counter()
+        o.blend(r0, r1)
+        tb = time.perf_counter()
+        rows, blend_s = r1 - r0, tb - ta
+        if tb - t0 > budget_s * 0.6 or r1 - r0 >= o.tiles_y:
+            break
+        band = min(band * 2, o.tiles_y)
+    full = blend_s * o.tiles_y / max(rows, 1)
+    frame_s = (t1 - t0) + (t2 - t1) + full
+    return {"value": round(1.0 / frame_s, 5), "unit": "frames/s", "cores": threads, "kind": "port",
+            "sample": f"one {o.W}x{o.H} frame of {o.n} Gaussians: preprocess and binning ({o.m} instances) in full, "
+                      f"blend on {rows} of {o.tiles_y} tile rows ({blend_s:.2f} s), scaled to the whole frame",
+            "seconds": {"preprocess": round(t1 - t0, 3), "binning": round(t2 - t1, 3),
+                        "blend_full_frame_est": round(full, 3)}}

@@ -1,6 +1,7 @@
-"""PeerAdam (csrc/dp_adam.cu) on 2 GPUs against an NCCL all-reduce of the gradients followed by adam_step_multi on
-every rank. With two ranks the gradient sum g0 + g1 is the same single addition in both, so parameters and the
-owned moments must agree bit for bit. Skipped with fewer than two GPUs."""
+"""PeerAdam (csrc/dp_adam.cu) on 2 GPUs, with peer loads / stores and with NVLink multicast, against an NCCL
+all-reduce of the gradients followed by adam_step_multi on every rank. With two ranks the gradient sum g0 + g1 is
+the same single addition in all of them, so parameters and the owned moments must agree bit for bit. Skipped with
+fewer than two GPUs."""
 from __future__ import annotations
 
 import datetime
@@ -14,7 +15,7 @@ import torch.multiprocessing as mp
 pytestmark = pytest.mark.gpu
 
 
-def _worker(rank: int, world: int, port: int, q) -> None:
+def _worker(rank: int, world: int, port: int, q, nvls: bool) -> None:
     try:
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
@@ -34,7 +35,7 @@ def _worker(rank: int, world: int, port: int, q) -> None:
         init = [torch.randn(n, 3, device=dev, generator=g0), torch.randn(n, 4, device=dev, generator=g0),
                 torch.randn(n, 1, device=dev, generator=g0), torch.randn(n, 15, 3, device=dev, generator=g0)]
         lrs = [1e-3, 2e-3, 5e-2, 2.5e-3]
-        opt = D.PeerAdam(init, lrs)
+        opt = D.PeerAdam(init, lrs, nvls=nvls)
         ref = [t.clone() for t in init]
         m = [torch.zeros_like(t) for t in init]
         v = [torch.zeros_like(t) for t in init]
@@ -50,28 +51,34 @@ def _worker(rank: int, world: int, port: int, q) -> None:
             A.adam_step([(p, s, mm, vv, lr) for p, s, mm, vv, lr in zip(ref, summed, m, v, lrs)], step)
         torch.cuda.synchronize()
         ok_p = all(torch.equal(a, b) for a, b in zip(opt.params, ref))
-        flat_m = torch.cat([x.flatten() for x in m])[opt.lo:opt.hi]
-        ok_m = torch.equal(opt.exp_avg[:opt.hi - opt.lo], flat_m)
+        flat_m = torch.cat([x.flatten() for x in m])[opt.lo:opt.hi]  # the multicast path pads the vector to 4
+        ok_m = torch.equal(opt.exp_avg[:flat_m.numel()], flat_m)
         # the copied-in path: step(grads=...) gives the same as writing into opt.grads
+        used_nvls = opt.nvls
         opt.close()
-        q.put((rank, ok_p, ok_m, None))
+        q.put((rank, ok_p, ok_m, None if used_nvls or not nvls else "no NVLS"))
         dist.destroy_process_group()
     except Exception as exc:  # report instead of hanging the parent
         q.put((rank, False, False, repr(exc)))
 
 
-def test_peer_adam_matches_allreduce_adam():
+@pytest.mark.parametrize("nvls", [False, True], ids=["peer_loads", "multicast"])
+def test_peer_adam_matches_allreduce_adam(nvls):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29600 + os.getpid() % 300
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    port = 29600 + os.getpid() % 300 + (7 if nvls else 0)
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, nvls)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]
     for p in procs:
         p.join(timeout=60)
+        if p.is_alive():  # never leave a rank behind
+            p.kill()
     for rank, ok_p, ok_m, err in res:
+        if err == "no NVLS":
+            pytest.skip("this node has no NVLink multicast")
         assert err is None, f"rank {rank}: {err}"
         assert ok_p and ok_m, f"rank {rank}: params equal {ok_p}, moments equal {ok_m}"
