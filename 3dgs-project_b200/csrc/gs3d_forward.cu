@@ -11,9 +11,9 @@
 //   gs3d_render       k_duplicate in depth order, stable radix sort on the tile digits (completing
 //                     the LSD sort of the 64-bit keys: same order, ties by Gaussian id), k_ranges,
 //                     k_bucket_counts + scan, k_bucket_tiles, k_blend
-// k_blend: one 256-thread block per 16x16 tile; each warp owns an 8x4 subtile and walks the
-// tile list in 32-splat buckets staged in shared memory, skipping (by ballot) the splats whose
-// culling rectangle misses its subtile - a rectangle that holds every pixel with alpha >= 1/255,
+// k_blend: one 128-thread block per 16x16 tile, two pixels per thread; each warp owns an 8x8 subtile
+// and walks the tile list in 32-splat buckets staged in shared memory, skipping (by ballot) the splats
+// whose culling rectangle misses its subtile - a rectangle that holds every pixel with alpha >= 1/255,
 // so the skip changes no result. The (C, T) state of every pixel is saved at each bucket start for
 // the backward; a block stops once every pixel has stopped.
 #include "gs3d_common.cuh"
@@ -345,36 +345,39 @@ __global__ void k_bucket_tiles(const uint32_t* __restrict__ nb, const uint32_t* 
     for (uint32_t k = 0; k < nb[t] && s + k < bcap; ++k) bucket_tile[s + k] = t;
 }
 
-// kTrain = false is the render-only variant: no checkpoints, per-pixel counts, final T, tile maxima or replay
-// list are written (and bstart / ckpt / counters / reached may be null).
+// One 128-thread block per 16x16 tile, two pixels per thread: each warp owns an 8x8 subtile, lane (column
+// lane % 8, rows lane / 8 and lane / 8 + 4); a splat's parameters are read from shared memory once for both pixels,
+// whose evaluations are independent. kTrain = false is the render-only variant: no checkpoints, per-pixel counts,
+// final T, tile maxima or replay list are written (and bstart / ckpt / counters / reached may be null).
 template <bool kTrain>
-__global__ void __launch_bounds__(kTilePixels) k_blend(Cam cam, const uint2* __restrict__ ranges,
-                                                       const uint32_t* __restrict__ bstart,
-                                                       const uint32_t* __restrict__ point_list,
-                                                       const float2* __restrict__ mean2d,
-                                                       const float4* __restrict__ conic_o,
-                                                       const float4* __restrict__ color_z,
-                                                       const ushort4* __restrict__ rect, const float* __restrict__ bg,
-                                                       float* __restrict__ image, float* __restrict__ final_T,
-                                                       uint32_t* __restrict__ n_contrib,
-                                                       uint32_t* __restrict__ max_contrib, float4* __restrict__ ckpt,
-                                                       uint32_t* __restrict__ counters, uint32_t* __restrict__ reached,
-                                                       int n, int m, long long bcap) {
+__global__ void __launch_bounds__(kTilePixels / 2) k_blend(Cam cam, const uint2* __restrict__ ranges,
+                                                          const uint32_t* __restrict__ bstart,
+                                                          const uint32_t* __restrict__ point_list,
+                                                          const float2* __restrict__ mean2d,
+                                                          const float4* __restrict__ conic_o,
+                                                          const float4* __restrict__ color_z,
+                                                          const ushort4* __restrict__ rect,
+                                                          const float* __restrict__ bg, float* __restrict__ image,
+                                                          float* __restrict__ final_T, uint32_t* __restrict__ n_contrib,
+                                                          uint32_t* __restrict__ max_contrib,
+                                                          float4* __restrict__ ckpt, uint32_t* __restrict__ counters,
+                                                          uint32_t* __restrict__ reached, int n, int m, long long bcap) {
+    constexpr int kThreads = kTilePixels / 2;
     __shared__ float2 s_mean[kTilePixels];
     __shared__ float4 s_con[kTilePixels];
     __shared__ float4 s_col[kTilePixels];
     __shared__ ushort4 s_rect[kTilePixels];
-    __shared__ uint32_t s_max[kTilePixels / 32];
-    __shared__ uint32_t s_reach[2];  // this tile's replayed buckets: first slot in `reached`, count
+    __shared__ uint32_t s_max[kThreads / 32];
+    __shared__ uint32_t s_reach[2];
 
     const int tile = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int tx0 = (tile % cam.tiles_x) * kTile, ty0 = (tile / cam.tiles_x) * kTile;
-    const int sx0 = tx0 + (warp & 1) * 8, sy0 = ty0 + (warp >> 1) * 4;  // this warp's 8x4 subtile
-    const int x = sx0 + (lane & 7), y = sy0 + (lane >> 3);
-    const int local = (y - ty0) * kTile + (x - tx0);
-    const bool inside = x < cam.width && y < cam.height;
-    const float pxf = static_cast<float>(x) + 0.5f, pyf = static_cast<float>(y) + 0.5f;
+    const int sx0 = tx0 + (warp & 1) * 8, sy0 = ty0 + (warp >> 1) * 8;  // this warp's 8x8 subtile
+    const int x = sx0 + (lane & 7), ya = sy0 + (lane >> 3), yb = ya + 4;
+    const int local_a = (ya - ty0) * kTile + (x - tx0), local_b = local_a + 4 * kTile;
+    const bool in_a = x < cam.width && ya < cam.height, in_b = x < cam.width && yb < cam.height;
+    const float pxf = static_cast<float>(x) + 0.5f, pya = static_cast<float>(ya) + 0.5f, pyb = pya + 4.f;
 
     uint2 rg = ranges[tile];
     rg.y = min(rg.y, static_cast<uint32_t>(m));
@@ -382,53 +385,69 @@ __global__ void __launch_bounds__(kTilePixels) k_blend(Cam cam, const uint2* __r
     const int count = static_cast<int>(rg.y - rg.x);
     const long long b0 = kTrain ? bstart[tile] : 0;
 
-    float Cr = 0.f, Cg = 0.f, Cb = 0.f, T = 1.f;
-    uint32_t last = 0;
-    bool done = !inside;
+    float Ra = 0.f, Ga = 0.f, Ba = 0.f, Ta = 1.f, Rb = 0.f, Gb = 0.f, Bb = 0.f, Tb = 1.f;
+    uint32_t last_a = 0, last_b = 0;
+    bool done_a = !in_a, done_b = !in_b;
     for (int base = 0; base < count; base += kTilePixels) {
-        if (__syncthreads_count(!done) == 0) break;
-        const int k = static_cast<int>(rg.x) + base + tid;
-        if (k < static_cast<int>(rg.y)) {
-            const int g = min(static_cast<int>(point_list[k]), n - 1);
-            s_mean[tid] = mean2d[g];
-            const float4 co = conic_o[g];
-            s_con[tid] = make_float4(-0.5f * kLog2e * co.x, -kLog2e * co.y, -0.5f * kLog2e * co.z, co.w);
-            const float4 cz = color_z[g];
-            s_col[tid] = make_float4(fmaxf(cz.x, 0.f), fmaxf(cz.y, 0.f), fmaxf(cz.z, 0.f), 0.f);
-            s_rect[tid] = rect[g];
+        if (__syncthreads_count(!(done_a && done_b)) == 0) break;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int slot = tid + h * kThreads;
+            const int k = static_cast<int>(rg.x) + base + slot;
+            if (k < static_cast<int>(rg.y)) {
+                const int g = min(static_cast<int>(point_list[k]), n - 1);
+                s_mean[slot] = mean2d[g];
+                const float4 co = conic_o[g];
+                s_con[slot] = make_float4(-0.5f * kLog2e * co.x, -kLog2e * co.y, -0.5f * kLog2e * co.z, co.w);
+                const float4 cz = color_z[g];
+                s_col[slot] = make_float4(fmaxf(cz.x, 0.f), fmaxf(cz.y, 0.f), fmaxf(cz.z, 0.f), 0.f);
+                s_rect[slot] = rect[g];
+            }
         }
         __syncthreads();
         const int in_batch = min(kTilePixels, count - base);
         for (int j0 = 0; j0 < in_batch; j0 += kBucket) {
             const long long bucket = b0 + ((base + j0) >> 5);
-            if (kTrain && bucket < bcap) ckpt[bucket * kTilePixels + local] = make_float4(Cr, Cg, Cb, T);
-            if (__all_sync(kFullMask, done)) continue;
+            if (kTrain && bucket < bcap) {
+                ckpt[bucket * kTilePixels + local_a] = make_float4(Ra, Ga, Ba, Ta);
+                ckpt[bucket * kTilePixels + local_b] = make_float4(Rb, Gb, Bb, Tb);
+            }
+            if (__all_sync(kFullMask, done_a && done_b)) continue;
             const int cnt = min(kBucket, in_batch - j0);
             bool hit = false;
             if (lane < cnt) {
                 const ushort4 r = s_rect[j0 + lane];
-                hit = r.x <= sx0 + 7 && r.z >= sx0 && r.y <= sy0 + 3 && r.w >= sy0;
+                hit = r.x <= sx0 + 7 && r.z >= sx0 && r.y <= sy0 + 7 && r.w >= sy0;
             }
             unsigned pending = __ballot_sync(kFullMask, hit);
-            if (!done) {
-                while (pending) {
-                    const int j = j0 + __ffs(pending) - 1;
-                    pending &= pending - 1;
-                    const float2 mm = s_mean[j];
-                    const float4 co = s_con[j];
-                    const float alpha = co.w * hw_exp2(fminf(blend_q2(co.x, co.y, co.z, mm.x - pxf, mm.y - pyf), 0.f));
-                    if (alpha >= kAlphaMin) {
-                        const float4 c = s_col[j];
-                        const float w = alpha * T;
-                        Cr += w * c.x;
-                        Cg += w * c.y;
-                        Cb += w * c.z;
-                        T *= 1.f - alpha;
-                        last = static_cast<uint32_t>(base + j + 1);
-                        if (T < kTMin) {
-                            done = true;
-                            break;
-                        }
+            while (pending && !(done_a && done_b)) {
+                const int j = j0 + __ffs(pending) - 1;
+                pending &= pending - 1;
+                const float2 mm = s_mean[j];
+                const float4 co = s_con[j];
+                const float dx = mm.x - pxf;
+                const float aa = co.w * hw_exp2(fminf(blend_q2(co.x, co.y, co.z, dx, mm.y - pya), 0.f));
+                const float ab = co.w * hw_exp2(fminf(blend_q2(co.x, co.y, co.z, dx, mm.y - pyb), 0.f));
+                const bool ua = !done_a && aa >= kAlphaMin, ub = !done_b && ab >= kAlphaMin;
+                if (ua || ub) {
+                    const float4 c = s_col[j];
+                    if (ua) {
+                        const float w = aa * Ta;
+                        Ra += w * c.x;
+                        Ga += w * c.y;
+                        Ba += w * c.z;
+                        Ta *= 1.f - aa;
+                        last_a = static_cast<uint32_t>(base + j + 1);
+                        done_a = Ta < kTMin;
+                    }
+                    if (ub) {
+                        const float w = ab * Tb;
+                        Rb += w * c.x;
+                        Gb += w * c.y;
+                        Bb += w * c.z;
+                        Tb *= 1.f - ab;
+                        last_b = static_cast<uint32_t>(base + j + 1);
+                        done_b = Tb < kTMin;
                     }
                 }
             }
@@ -436,34 +455,43 @@ __global__ void __launch_bounds__(kTilePixels) k_blend(Cam cam, const uint2* __r
         __syncthreads();
     }
     if (kTrain) {
-        const uint32_t wmax = __reduce_max_sync(kFullMask, last);
+        const uint32_t wmax = __reduce_max_sync(kFullMask, max(last_a, last_b));
         if (lane == 0) s_max[warp] = wmax;
         __syncthreads();
         if (tid == 0) {
             uint32_t mxv = 0;
 #pragma unroll
-            for (int w = 0; w < kTilePixels / 32; ++w) mxv = max(mxv, s_max[w]);
+            for (int w = 0; w < kThreads / 32; ++w) mxv = max(mxv, s_max[w]);
             max_contrib[tile] = mxv;
-            // the buckets up to the last contributor are the ones the backward replays: list them
             const uint32_t nreach = (mxv + kBucket - 1) / kBucket;
             s_reach[0] = nreach ? atomicAdd(counters + 2, nreach) : 0u;
             s_reach[1] = nreach;
         }
         __syncthreads();
-        for (uint32_t i = tid; i < s_reach[1]; i += kTilePixels) {
+        for (uint32_t i = tid; i < s_reach[1]; i += kThreads) {
             const long long slot = static_cast<long long>(s_reach[0]) + i, b = b0 + i;
             if (slot < bcap && b < bcap) reached[slot] = static_cast<uint32_t>(b);
         }
     }
-    if (inside) {
-        const int pix = y * cam.width + x;
-        const size_t HW = static_cast<size_t>(cam.width) * cam.height;
-        image[pix] = Cr + T * __ldg(bg);
-        image[HW + pix] = Cg + T * __ldg(bg + 1);
-        image[2 * HW + pix] = Cb + T * __ldg(bg + 2);
+    const size_t HW = static_cast<size_t>(cam.width) * cam.height;
+    if (in_a) {
+        const int pix = ya * cam.width + x;
+        image[pix] = Ra + Ta * __ldg(bg);
+        image[HW + pix] = Ga + Ta * __ldg(bg + 1);
+        image[2 * HW + pix] = Ba + Ta * __ldg(bg + 2);
         if (kTrain) {
-            final_T[pix] = T;
-            n_contrib[pix] = last;
+            final_T[pix] = Ta;
+            n_contrib[pix] = last_a;
+        }
+    }
+    if (in_b) {
+        const int pix = yb * cam.width + x;
+        image[pix] = Rb + Tb * __ldg(bg);
+        image[HW + pix] = Gb + Tb * __ldg(bg + 1);
+        image[2 * HW + pix] = Bb + Tb * __ldg(bg + 2);
+        if (kTrain) {
+            final_T[pix] = Tb;
+            n_contrib[pix] = last_b;
         }
     }
 }
@@ -598,10 +626,10 @@ int gs3d_render(int n, long long num_instances, const gs3d_settings* settings, v
     k_bucket_tiles<<<div_up(T, 256), 256, 0, st>>>(tb.nb, tb.bstart, T, bucket_capacity, bb.tile);
     note_launch();
     SPLAT_TRY(check_launch("gs3d_bucket_tiles"));
-    k_blend<true><<<T, kTilePixels, 0, st>>>(cam, tb.ranges, tb.bstart, ib.point_list, pb.mean2d, pb.conic_o,
-                                             pb.color_z, pb.rect, settings->bg, image, tb.final_T, tb.n_contrib,
-                                             tb.max_contrib, bb.ckpt, pb.counters, bb.reached, n < 1 ? 1 : n,
-                                             static_cast<int>(m), bucket_capacity);
+    k_blend<true><<<T, kTilePixels / 2, 0, st>>>(cam, tb.ranges, tb.bstart, ib.point_list, pb.mean2d, pb.conic_o,
+                                                 pb.color_z, pb.rect, settings->bg, image, tb.final_T, tb.n_contrib,
+                                                 tb.max_contrib, bb.ckpt, pb.counters, bb.reached, n < 1 ? 1 : n,
+                                                 static_cast<int>(m), bucket_capacity);
     note_launch();
     return check_launch("gs3d_blend");
 }
@@ -624,9 +652,9 @@ int gs3d_render_inference(int n, long long num_instances, const gs3d_settings* s
     TileBuffers tb = carve_tile(ct, cam.width, cam.height);
     InstBuffers ib = carve_inst(ci, m);
     SPLAT_TRY(bin_instances(n, m, cam, pb, tb, ib, st));
-    k_blend<false><<<T, kTilePixels, 0, st>>>(cam, tb.ranges, nullptr, ib.point_list, pb.mean2d, pb.conic_o,
-                                              pb.color_z, pb.rect, settings->bg, image, nullptr, nullptr, nullptr,
-                                              nullptr, nullptr, nullptr, n < 1 ? 1 : n, static_cast<int>(m), 0);
+    k_blend<false><<<T, kTilePixels / 2, 0, st>>>(cam, tb.ranges, nullptr, ib.point_list, pb.mean2d, pb.conic_o,
+                                                  pb.color_z, pb.rect, settings->bg, image, nullptr, nullptr, nullptr,
+                                                  nullptr, nullptr, nullptr, n < 1 ? 1 : n, static_cast<int>(m), 0);
     note_launch();
     return check_launch("gs3d_blend_inference");
 }

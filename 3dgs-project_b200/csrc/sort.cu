@@ -12,10 +12,6 @@
 
 #include "sort.cuh"
 
-#ifndef SPLAT_SORT_MATCH
-#define SPLAT_SORT_MATCH 0
-#endif
-
 namespace splat {
 namespace {
 
@@ -148,11 +144,6 @@ __device__ __forceinline__ uint32_t digit_of(K key, int shift, uint32_t mask) {
 
 // Lanes of the warp whose digit equals this lane's (among the lanes in `valid`): one ballot per digit bit.
 __device__ __forceinline__ unsigned digit_peers(uint32_t d, int bits, unsigned valid) {
-#if SPLAT_SORT_MATCH
-    (void)bits;
-    const bool mine = (valid >> (threadIdx.x & 31)) & 1u;
-    return __match_any_sync(kFullMask, mine ? d : 0xFFFFFFFFu) & valid;
-#endif
     unsigned peers = valid;
 #pragma unroll
     for (int b = 0; b < kRadixBits; ++b) {
