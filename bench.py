@@ -1,18 +1,20 @@
 """Benchmark of the 3DGS training step on B200, one process per GPU.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c3|c4|c2]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c3|c4|c2|c1|c5]
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \
         bench.py --gpus N --steps K --warmup W
 
 Workload (default c3): the scene of config C3 - 3M Gaussians from 64 isotropic clusters, SH degree 3, seeded
 synthetic parameters (no dataset is available) - rendered at 1920x1080 / 60 deg. One step on each rank is the
-training step of one view: forward, backward with dL/dimage ~ N(0, 1e-3), (N > 1: one NCCL all-reduce of the flat
-59-float-per-Gaussian gradient), fused Adam over the six parameter groups. Each rank renders its own view (a
-seeded camera at radius 12), so the work per GPU is fixed as N grows (weak scaling) and
+training step of one view: forward, backward with dL/dimage ~ N(0, 1e-3), then Adam over the six parameter groups
+(N = 1: one fused Adam launch; N > 1: the gradient exchange and Adam as one peer-memory kernel per rank,
+dist.PeerAdam). Each rank renders its own view (a seeded camera at radius 12), so the work per GPU is fixed as N
+grows (weak scaling) and
     value = N * K / (max over ranks of the device time of K steps)  [views/s],  ms_per_step = that time / K.
 The Gaussian state (2.8 GB with moments) is far larger than the 126 MB L2, so no flush is needed between steps.
-``e2e`` runs the same step through the public API (diff_rasterize + autograd + FusedAdam) with the upstream
-gradient copied from pinned host memory every step and the loss read back.
+``e2e`` runs the same step through the public API (diff_rasterize + autograd + FusedAdam, PeerAdam for N > 1)
+with the upstream gradient copied from pinned host memory every step and the loss read back. --workload c1 / c5
+measure the toy2d fit step and the render-only orbit instead (their own metric lines).
 
 --impl reference times the CPU restatement of the same step (oracle/liboracle.so, OpenMP over all host cores)
 on rank 0 only, over a bounded sample (a horizontal band of the image), and reports the same metric.
@@ -53,50 +55,76 @@ ADAM_TRAFFIC = 2832050688 + 2067712256
 
 
 class Clocks:
-    """nvidia-smi sampled every 200 ms during the timed region."""
+    """nvidia-smi sampled every 50 ms; only the samples stamped inside the timed region (mark_start / mark_end) are
+    summarised."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.5)  # nvidia-smi takes a moment to start sampling
         except OSError:
             self.proc = None
         return self
+
+    def mark_start(self) -> None:
+        import datetime
+
+        self.t0 = datetime.datetime.now()
+
+    def mark_end(self) -> None:
+        import datetime
+
+        self.t1 = datetime.datetime.now()
 
     def __exit__(self, *exc):
         self.rows = []
         if self.proc is None:
             return False
+        time.sleep(0.1)
         self.proc.terminate()
         out, _ = self.proc.communicate(timeout=10)
+        import datetime
+
         for line in out.splitlines():
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                self.rows.append(parts)
+            if len(parts) < 10:
+                continue
+            try:
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f")
+            except ValueError:
+                continue
+            self.rows.append((ts, parts[1:]))
         return False
 
     def summary(self) -> dict:
         rows = getattr(self, "rows", [])
-        if not rows:
+        inside = [r for ts, r in rows if self.t0 is not None and self.t1 is not None and self.t0 <= ts <= self.t1]
+        note = "samples inside the timed region"
+        if not inside and rows and self.t0 is not None:  # a region shorter than the sampling period: the nearest
+            inside = [min(rows, key=lambda tr: abs((tr[0] - self.t0).total_seconds()))[1]]
+            note = "no sample fell inside the timed region; the nearest one"
+        if not inside:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        sm = [float(r[1]) for r in inside if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in inside if r[2].replace(".", "").isdigit()]
         reasons = set()
-        for r in rows:
+        for r in inside:
             for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), r[5:9]):
                 if v.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(rows)}
+                "reasons": sorted(reasons), "samples": len(inside), "note": note}
 
 
 def setup_dist(n_gpus: int):
@@ -217,12 +245,14 @@ def run_ours(args) -> None:
     with Clocks(local) as clk:
         t0 = time.perf_counter()
         launches0 = L.query("splat_launch_count")
+        clk.mark_start()
         start.record()
         insts = []
         for _ in range(args.steps):
             insts += one_step(True)
         end.record()
         torch.cuda.synchronize()
+        clk.mark_end()
         launches = L.query("splat_launch_count") - launches0
         wall = time.perf_counter() - t0
     if world > 1:
@@ -598,7 +628,7 @@ def run_c5(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["c3", "c4", "c2", "c1", "c5"], default="c3")
