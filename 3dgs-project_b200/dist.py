@@ -157,11 +157,12 @@ class PeerAdam:
     rank's parameters (peer stores). Two stream-ordered barriers (one-element all-reduces) bracket the kernel.
     Bias corrections and the per-element update are those of FusedAdam; the gradient sum is taken in rank order.
 
-    nvls: use NVLink SHARP when the node has it (the buffers come from PyTorch's symmetric memory and the kernel
-    sums through multimem.ld_reduce and writes through multimem.st: each link carries the slice once per
-    direction instead of 2 (G - 1) / G times); None = the SPLAT_NVLS environment variable (off unless "1").
-    Measured at G = 2 on B200, where both move the same bytes, the multicast kernel took 1.84 ms against 1.17 ms
-    for the peer-load / peer-store kernel, so the latter is the default.
+    nvls: use NVLink SHARP when the node has it (the buffers come from PyTorch's symmetric memory, the kernel sums
+    through multimem.ld_reduce and writes through multimem.st). Per rank and direction its links then carry
+    (G + 1) / G slices-worth of the vector against 2 (G - 1) / G for peer loads and stores: more at G = 2 (1.5 vs
+    1), fewer from G = 4 on (1.25 vs 1.5; 1.125 vs 1.75 at G = 8). Measured at G = 2 both kernels move their bytes
+    at about 580-600 GB/s per direction (1.84 ms multicast, 1.17 ms peer), so the default is the multicast form
+    from 4 ranks on and peer loads / stores below; the SPLAT_NVLS environment variable ("0" / "1") overrides it.
     """
 
     def __init__(self, tensors, lrs, group=None, betas=(0.9, 0.999), eps: float = 1e-15, nvls: bool | None = None):
@@ -180,7 +181,8 @@ class PeerAdam:
         if nvls is None:
             import os
 
-            nvls = os.environ.get("SPLAT_NVLS", "0") == "1"
+            env = os.environ.get("SPLAT_NVLS")
+            nvls = (env == "1") if env in ("0", "1") else self.world >= 4
         self.nvls = False
         if nvls and self.world > 1:
             padded = (self.total + 3) // 4 * 4  # the multicast kernel moves whole 16-byte groups
