@@ -50,7 +50,7 @@ NAMES = ("means", "scales", "rotations", "opacities", "sh0", "sh_rest")
 WIDTHS = (3, 3, 4, 1, 3, 45)  # floats per Gaussian in each group: 59 in total
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch on the C3 workload, from one ncu capture each
 # (profiles/); None where not captured.
-BLEND_BWD_TRAFFIC = 225540096 + 5898240
+BLEND_BWD_TRAFFIC = 240830464 + 5681408
 ADAM_TRAFFIC = 2832050688 + 2067712256
 
 
