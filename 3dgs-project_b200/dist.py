@@ -160,9 +160,10 @@ class PeerAdam:
     nvls: use NVLink SHARP when the node has it (the buffers come from PyTorch's symmetric memory, the kernel sums
     through multimem.ld_reduce and writes through multimem.st). Per rank and direction its links then carry
     (G + 1) / G slices-worth of the vector against 2 (G - 1) / G for peer loads and stores: more at G = 2 (1.5 vs
-    1), fewer from G = 4 on (1.25 vs 1.5; 1.125 vs 1.75 at G = 8). Measured at G = 2 both kernels move their bytes
-    at about 580-600 GB/s per direction (1.84 ms multicast, 1.17 ms peer), so the default is the multicast form
-    from 4 ranks on and peer loads / stores below; the SPLAT_NVLS environment variable ("0" / "1") overrides it.
+    1), fewer from G = 4 on (1.25 vs 1.5; 1.125 vs 1.75 at G = 8). Measured on the 3M-Gaussian C3 scene: at G = 2
+    1.84 ms multicast against 1.17 ms peer; at G = 4 1.73 ms multicast (513 GB/s per direction) against 1.84 ms
+    peer (577 GB/s). The default is therefore the multicast form from 4 ranks on and peer loads / stores below;
+    the SPLAT_NVLS environment variable ("0" / "1") overrides it.
     """
 
     def __init__(self, tensors, lrs, group=None, betas=(0.9, 0.999), eps: float = 1e-15, nvls: bool | None = None):

@@ -428,16 +428,22 @@ def roofline(tr: Trainer, stage: dict, reach: dict, pixels: int) -> dict:
 
 
 def exchange_figures(tr: Trainer, stage: dict) -> dict:
-    """N > 1: the fused exchange + Adam (adam_step_dp_fused between two barriers), against NVLink. Each rank
-    reads its slice's gradients from the other G - 1 ranks while they read theirs from it, and writes its updated
-    slice to them while they write theirs to it: 2 (G - 1) slices cross its links in each direction, at the
-    measured 770 GB/s peer-copy bandwidth per direction."""
+    """N > 1: the fused exchange + Adam between two barriers, against NVLink (measured 770 GB/s per direction).
+
+    Peer form (adam_step_dp_fused): each rank reads its slice's gradients from the other G - 1 ranks while they
+    read theirs from it, and writes its updated slice to them while they write theirs to it: 2 (G - 1) slices
+    cross its links in each direction.
+    Multicast form (adam_step_dp_nvls): the switch reduces, so a rank sends its whole gradient buffer (G slices)
+    out and takes its reduced slice in; its multicast store sends one slice out and the switch delivers all G
+    slices in: G + 1 slices in each direction."""
     g = tr.world
     slice_bytes = 4.0 * (tr.peer.hi - tr.peer.lo)
-    cross = 2 * (g - 1) * slice_bytes
+    nvls = bool(getattr(tr.peer, "nvls", False))
+    cross = (g + 1) * slice_bytes if nvls else 2 * (g - 1) * slice_bytes
+    kernel = "adam_step_dp_nvls" if nvls else "adam_step_dp_fused"
     t = stage["comm"]
     ach = cross / (t / 1000.0) / 1e9 if t > 0 else 0.0
-    return {"kernel": "adam_step_dp_fused (+ 2 barriers)", "ms": round(t, 4), "bytes_each_direction": int(cross),
+    return {"kernel": kernel + " (+ 2 barriers)", "ms": round(t, 4), "bytes_each_direction": int(cross),
             "achieved": round(ach, 1), "peak": 770.0, "unit": "GB/s", "frac": round(ach / 770.0, 4),
             "peak_source": "measured peer copy, per direction"}
 
