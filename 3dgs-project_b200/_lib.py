@@ -71,6 +71,8 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gs3d_backward": (_I, [_P] * 7 + [_I, _LL, _P] + [_P, _SZ] * 4 + [_LL, _P, _SZ] + [_P] * 7 + [_I, _P]),
     "gs3d_backward_blend": (_I, [_P, _P, _I, _LL, _P] + [_P, _SZ] * 4 + [_LL, _P, _SZ, _I, _P]),
     "gs3d_backward_preprocess": (_I, [_P] * 5 + [_I, _P, _P, _SZ, _P, _SZ] + [_P] * 7 + [_I, _P]),
+    "gs3d_backward_densification": (_I, [_I, _P, _P, _SZ, _P, _SZ, _P, _I, _P]),
+    "gs3d_backward_preprocess_adam": (_I, [_P] * 6 + [_I, _P, _P, _SZ, _P, _SZ, _P, _P]),
     "adam_step_multi": (_I, [_I, _P, _I, ctypes.c_double, ctypes.c_double, ctypes.c_double, _P]),
     "adam_step_multi_lean": (_I, [_I, _P, _I, ctypes.c_double, ctypes.c_double, ctypes.c_double, _P, _LL, _P]),
 }

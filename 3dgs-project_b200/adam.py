@@ -42,23 +42,101 @@ class FusedAdam(torch.optim.Adam):
                           and moments for that step
       lowp_moment_groups  names of parameter groups whose exp_avg / exp_avg_sq are kept in bfloat16 (stochastic
                           rounding on write)
+    and one of this build (off by default; with the dense update only):
+      fuse_backward       when the six 3DGS tensors of a diff_rasterize call (means, scales, rotations, opacities,
+                          sh0, sh_rest) are parameters of this optimizer, each alone in its group, the rasterizer's
+                          backward leaves their preprocess backward to step(), which runs it fused with their Adam
+                          update (gs3d_backward_preprocess_adam): their gradients are never written, so .grad stays
+                          None for them after backward() unless other loss terms contributed (those gradients are
+                          added inside the fused step). The parameters, moments and densification statistics are
+                          bit-identical to the unfused path for one rendered view per step; with several views per
+                          step all but the last are materialised into .grad when the next one arrives.
     """
 
     def __init__(self, params, lr, eps, betas=(0.9, 0.999), sparse: bool = False,
-                 lowp_moment_groups: tuple = ()) -> None:
+                 lowp_moment_groups: tuple = (), fuse_backward: bool = False) -> None:
         super().__init__(params=params, lr=lr, eps=eps, betas=betas)
         self.sparse = bool(sparse)
         self.lowp_moment_groups = set(lowp_moment_groups)
         self.lean = self.sparse or bool(self.lowp_moment_groups)
         self.n_dense_fallbacks = 0
+        self.fuse_backward = bool(fuse_backward)
+        self._pending = None  # (PendingBackward, the six parameter tensors)
+        if self.fuse_backward and self.lean:
+            raise RuntimeError("fuse_backward takes the dense update (no sparse / lowp_moment_groups)")
         from . import gs3d
 
         gs3d._Rasterize.track_visibility = self.sparse
+        if self.fuse_backward:
+            gs3d._Rasterize.fused_optimizer = self
+
+    # ---- fused preprocess backward + Adam ----
+
+    def _group_of(self, t: torch.Tensor):
+        for group in self.param_groups:
+            if len(group["params"]) == 1 and group["params"][0].data_ptr() == t.data_ptr() \
+                    and group["params"][0].shape == t.shape:
+                return group
+        return None
+
+    def _owns(self, six) -> bool:
+        """True when the six rasterizer tensors are this optimizer's parameters (one per group, float32 CUDA,
+        contiguous), so their preprocess backward can be deferred to step()."""
+        if not self.fuse_backward:
+            return False
+        for t in six:
+            if not (t.is_cuda and t.dtype == torch.float32 and t.is_contiguous()) or self._group_of(t) is None:
+                return False
+        return True
+
+    def _defer(self, pending, six) -> None:
+        if self._pending is not None:  # an earlier view of this step: its gradients go to .grad now
+            earlier, tensors = self._pending
+            grads = earlier.preprocess()
+            for p, g in zip(self._params_of(tensors), grads):
+                g = g.view(p.shape)
+                p.grad = g if p.grad is None else p.grad + g
+        self._pending = (pending, six)
+
+    def _params_of(self, tensors):
+        return [self._group_of(t)["params"][0] for t in tensors]
+
+    def zero_grad(self, set_to_none: bool = True) -> None:  # noqa: D102
+        self._pending = None
+        super().zero_grad(set_to_none=set_to_none)
+
+    @torch.no_grad()
+    def _fused_step(self) -> set:
+        pending, tensors = self._pending
+        self._pending = None
+        params = self._params_of(tensors)
+        groups = [self._group_of(t) for t in tensors]
+        exp_avg, exp_avg_sq, steps, lrs, grad_in = [], [], [], [], []
+        for p, group in zip(params, groups):
+            state = self.state[p]
+            if len(state) == 0:
+                state["step"] = torch.tensor(0.0)
+                state["exp_avg"] = torch.zeros_like(p)
+                state["exp_avg_sq"] = torch.zeros_like(p)
+            state["step"] += 1
+            exp_avg.append(state["exp_avg"])
+            exp_avg_sq.append(state["exp_avg_sq"])
+            steps.append(int(state["step"].item()))
+            lrs.append(float(group["lr"]))
+            grad_in.append(p.grad)
+        b1, b2 = groups[0]["betas"]
+        eps = groups[0]["eps"]
+        for group in groups[1:]:
+            if tuple(group["betas"]) != (b1, b2) or group["eps"] != eps:
+                raise RuntimeError("fuse_backward needs the same betas and eps in the six groups")
+        pending.preprocess_adam(params, exp_avg, exp_avg_sq, lrs, steps, (b1, b2), eps, grad_in)
+        return {id(p) for p in params}
 
     @torch.no_grad()
     def step(self, closure=None) -> None:  # noqa: D102
         if closure is not None:
             raise RuntimeError("FusedAdam does not take a closure")
+        done = self._fused_step() if self._pending is not None else set()
         visibility = None
         if self.sparse:
             from . import gs3d
@@ -70,7 +148,7 @@ class FusedAdam(torch.optim.Adam):
             if len(group["params"]) != 1:
                 raise RuntimeError("more than one tensor in group")
             param = group["params"][0]
-            if param.grad is None or param.numel() == 0:
+            if id(param) in done or param.grad is None or param.numel() == 0:
                 continue
             L.check_cuda("param", param, torch.float32)
             lowp = group.get("name") in self.lowp_moment_groups

@@ -9,6 +9,7 @@
 // the group's buffers allow, so a step reads 4 and writes 3 floats per element and nothing else.
 // k_adam_lean adds the two options of the reference's lean Adam (adam_step_sparse_cu<LOWP>, same patch):
 // a per-primitive visibility mask and bfloat16 moments written with stochastic rounding.
+#include "adam_math.cuh"
 #include "common.cuh"
 
 namespace splat {
@@ -37,11 +38,7 @@ struct Table {
 };
 
 __device__ __forceinline__ float upd(float& p, float g, float& m, float& v, const Group& G, const Table& t) {
-    const float g2 = g * g;
-    m = fmaf(t.beta1, m - g, g);
-    v = fmaf(t.beta2, v - g2, g2);
-    const float denom = sqrtf(v) * G.bc2_sqrt_rcp + t.eps;
-    p -= G.step_size * m / denom;
+    adam_element(p, g, m, v, G.step_size, G.bc2_sqrt_rcp, t.beta1, t.beta2, t.eps);
     return p;
 }
 
@@ -130,11 +127,7 @@ __device__ __forceinline__ void lean_one(const LeanGroup& G, const LeanTable& t,
         m = static_cast<const float*>(G.exp_avg)[i];
         v = static_cast<const float*>(G.exp_avg_sq)[i];
     }
-    const float g2 = g * g;
-    m = fmaf(t.beta1, m - g, g);
-    v = fmaf(t.beta2, v - g2, g2);
-    const float denom = sqrtf(v) * G.bc2_sqrt_rcp + t.eps;
-    G.param[i] -= G.step_size * m / denom;
+    adam_element(G.param[i], g, m, v, G.step_size, G.bc2_sqrt_rcp, t.beta1, t.beta2, t.eps);
     if (kLowp) {
         const uint32_t r1 = lowbias32(static_cast<uint32_t>(i) ^ t.seed);
         const uint32_t r2 = lowbias32(r1);
@@ -181,13 +174,8 @@ __device__ __forceinline__ void lean_four(const LeanGroup& G, const LeanTable& t
 #pragma unroll
     for (int k = 0; k < kVec; ++k) {
         if (!on[k]) continue;
-        const float g = gv[k], g2 = g * g;
-        const float m = fmaf(t.beta1, mv[k] - g, g);
-        const float v = fmaf(t.beta2, vv[k] - g2, g2);
-        const float denom = sqrtf(v) * G.bc2_sqrt_rcp + t.eps;
-        pv[k] -= G.step_size * m / denom;
-        mv[k] = m;
-        vv[k] = v;
+        adam_element(pv[k], gv[k], mv[k], vv[k], G.step_size, G.bc2_sqrt_rcp, t.beta1, t.beta2, t.eps);
+        const float m = mv[k], v = vv[k];
         if (kLowp) {
             const uint32_t r1 = lowbias32(static_cast<uint32_t>(e + k) ^ t.seed);
             const uint32_t r2 = lowbias32(r1);
@@ -244,9 +232,7 @@ namespace {
 
 // The reference wrapper's host arithmetic (fastergs_lean_adam.patch:162-164): in double, rounded once to float.
 void bias_corrections(double lr, double beta1, double beta2, int step, float& step_size, float& bc2_sqrt_rcp) {
-    const double bc1_rcp = 1.0 / (1.0 - pow(beta1, step));
-    step_size = static_cast<float>(lr * bc1_rcp);
-    bc2_sqrt_rcp = static_cast<float>(1.0 / sqrt(1.0 - pow(beta2, step)));
+    adam_bias_corrections(lr, beta1, beta2, step, step_size, bc2_sqrt_rcp);
 }
 
 }  // namespace

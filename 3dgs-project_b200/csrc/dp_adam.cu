@@ -10,6 +10,7 @@
 #include <algorithm>
 #include <cstring>
 
+#include "adam_math.cuh"
 #include "common.cuh"
 
 namespace splat {
@@ -43,11 +44,8 @@ __device__ __forceinline__ float step_size_of(const Args& a, long long i) {
 }
 
 __device__ __forceinline__ float adam(float p, float g, float& m, float& v, float step_size, const Args& a) {
-    const float g2 = g * g;
-    m = fmaf(a.beta1, m - g, g);
-    v = fmaf(a.beta2, v - g2, g2);
-    const float denom = sqrtf(v) * a.bc2_sqrt_rcp + a.eps;
-    return p - step_size * m / denom;
+    adam_element(p, g, m, v, step_size, a.bc2_sqrt_rcp, a.beta1, a.beta2, a.eps);
+    return p;
 }
 
 // kWorld: the number of ranks, a template argument so that the per-rank loads live in exactly that many registers.
@@ -123,11 +121,8 @@ __device__ __forceinline__ float step_size_nvls(const NvlsArgs& a, long long i) 
 }
 
 __device__ __forceinline__ float adam_nvls(float p, float g, float& m, float& v, float step_size, const NvlsArgs& a) {
-    const float g2 = g * g;
-    m = fmaf(a.beta1, m - g, g);
-    v = fmaf(a.beta2, v - g2, g2);
-    const float denom = sqrtf(v) * a.bc2_sqrt_rcp + a.eps;
-    return p - step_size * m / denom;
+    adam_element(p, g, m, v, step_size, a.bc2_sqrt_rcp, a.beta1, a.beta2, a.eps);
+    return p;
 }
 
 __global__ void __launch_bounds__(kThreads) k_dp_adam_nvls(NvlsArgs a) {

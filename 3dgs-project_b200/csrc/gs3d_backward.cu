@@ -23,6 +23,7 @@
 // that were not visible get zero gradients.
 #include <algorithm>
 
+#include "adam_math.cuh"
 #include "gs3d_common.cuh"
 
 namespace splat {
@@ -253,13 +254,10 @@ struct PParams {
     int n;
 };
 
+// The six gradient outputs (means, scales, rotations, opacities, sh0, sh_rest) of the unfused preprocess backward.
 struct Grads {
-    float* means;
-    float* scales;
-    float* rotations;
-    float* opacities;
-    float* sh0;
-    float* sh_rest;
+    float* ptr[6];
+    int vec;  // the SH-rest output 16-byte aligned
 };
 
 __device__ __forceinline__ void sh_backward(float x, float y, float z, int bases, const float* v, float& gx, float& gy,
@@ -313,24 +311,175 @@ struct Densification {
     int rows;     // 0, 2 or 3
 };
 
+// Densification statistics of visible Gaussian i: visible count, |dL/dmean2d| in normalised device units (pixels
+// scaled by half the image size), and with three rows the same norm of the summed per-pixel |dL/dmean2d|.
+__device__ __forceinline__ void accumulate_densification(const Densification& dens, const GradAcc& acc, const Cam& cam,
+                                                         int n, int i, float2 gm) {
+    // each operation rounded on its own: the rows do not depend on how the calling kernel was compiled
+    const float hw = 0.5f * static_cast<float>(cam.width), hh = 0.5f * static_cast<float>(cam.height);
+    auto norm = [&](float2 g) {
+        const float a = __fmul_rn(g.x, hw), b = __fmul_rn(g.y, hh);
+        return __fsqrt_rn(__fadd_rn(__fmul_rn(a, a), __fmul_rn(b, b)));
+    };
+    dens.info[i] = __fadd_rn(dens.info[i], 1.f);
+    float* row1 = dens.info + static_cast<size_t>(n) + i;
+    *row1 = __fadd_rn(*row1, norm(gm));
+    if (dens.rows == 3) {
+        float* row2 = dens.info + 2 * static_cast<size_t>(n) + i;
+        *row2 = __fadd_rn(*row2, norm(acc.mean2d_abs[i]));
+    }
+}
+
+// The densification rows alone (when the preprocess backward is deferred to a fused Adam step).
+__global__ void k_densification(int n, Cam cam, PrimBuffers pb, GradAcc acc, Densification dens) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n || pb.n_touched[i] == 0) return;
+    accumulate_densification(dens, acc, cam, n, i, acc.mean2d[i]);
+}
+
+// The Adam step fused into the preprocess backward (when `fused`): groups in the order means, scales, rotations,
+// opacities, sh0, sh_rest. Each gradient element is added to grad_in (the gradient other terms of the loss left,
+// when given: autograd's accumulation, existing + new) and applied to its parameter and moments in place; the
+// gradient itself is never stored.
+struct AdamArgs {
+    float* param[6];
+    float* exp_avg[6];
+    float* exp_avg_sq[6];
+    const float* grad_in[6];
+    float step_size[6];
+    float bc2_sqrt_rcp[6];
+    float beta1, beta2, eps;
+    int vec;    // every buffer of every group 16-byte aligned
+    int fused;  // 0: the gradients are stored (Grads) instead
+};
+
+__device__ __forceinline__ void fused_adam(const AdamArgs& A, int gi, size_t e, float g) {
+    if (A.grad_in[gi]) g = __fadd_rn(A.grad_in[gi][e], g);  // rounded on its own: no contraction with g's product
+    float p = A.param[gi][e], m = A.exp_avg[gi][e], v = A.exp_avg_sq[gi][e];
+    adam_element(p, g, m, v, A.step_size[gi], A.bc2_sqrt_rcp[gi], A.beta1, A.beta2, A.eps);
+    A.param[gi][e] = p;
+    A.exp_avg[gi][e] = m;
+    A.exp_avg_sq[gi][e] = v;
+}
+
+// Shared-memory staging of one warp's gradients for the fused step: the five small groups of its 32 Gaussians in
+// Gaussian-major order (means 96, scales 96, rotations 128, opacities 32, sh0 96 floats), after its SH-rest block.
+constexpr int kSmallFloats = 448;
+__host__ __device__ constexpr int small_offset(int gi) {
+    return gi == 0 ? 0 : gi == 1 ? 96 : gi == 2 ? 192 : gi == 3 ? 320 : 352;
+}
+__host__ __device__ constexpr int group_width(int gi, int rest3) {
+    return gi == 0 || gi == 1 || gi == 4 ? 3 : gi == 2 ? 4 : gi == 3 ? 1 : rest3;
+}
+template <int GI>
+__device__ __forceinline__ void adam4_load(const AdamArgs& A, size_t e, float4& p, float4& m, float4& v, float4& h) {
+    p = *reinterpret_cast<const float4*>(A.param[GI] + e);
+    m = *reinterpret_cast<const float4*>(A.exp_avg[GI] + e);
+    v = *reinterpret_cast<const float4*>(A.exp_avg_sq[GI] + e);
+    h = A.grad_in[GI] ? *reinterpret_cast<const float4*>(A.grad_in[GI] + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+template <int GI>
+__device__ __forceinline__ void adam4_apply(const AdamArgs& A, size_t e, float4 p, float4 m, float4 v, float4 h,
+                                            float4 g) {
+    if (A.grad_in[GI])
+        g = make_float4(__fadd_rn(h.x, g.x), __fadd_rn(h.y, g.y), __fadd_rn(h.z, g.z), __fadd_rn(h.w, g.w));
+    const float ss = A.step_size[GI], bc = A.bc2_sqrt_rcp[GI];
+    adam_element(p.x, g.x, m.x, v.x, ss, bc, A.beta1, A.beta2, A.eps);
+    adam_element(p.y, g.y, m.y, v.y, ss, bc, A.beta1, A.beta2, A.eps);
+    adam_element(p.z, g.z, m.z, v.z, ss, bc, A.beta1, A.beta2, A.eps);
+    adam_element(p.w, g.w, m.w, v.w, ss, bc, A.beta1, A.beta2, A.eps);
+    *reinterpret_cast<float4*>(A.param[GI] + e) = p;
+    *reinterpret_cast<float4*>(A.exp_avg[GI] + e) = m;
+    *reinterpret_cast<float4*>(A.exp_avg_sq[GI] + e) = v;
+}
+
+// The Adam phase of one warp whose 32 Gaussians' gradients are staged (sh: SH rest, zeros when !sh_staged; sg: the
+// small groups): the warp's contiguous block of every group is streamed with 16-byte accesses, the small groups in
+// two passes, then the SH-rest block two float4 per lane at a time; each pass loads all its parameters, moments and
+// grad_in before it stores any. A partial warp, or buffers that are not 16-byte aligned, take element-wise accesses.
+__device__ __forceinline__ void warp_adam(const AdamArgs& A, int first, int cnt, int rest3, const float* sh,
+                                          bool sh_staged, const float* sg, int lane) {
+    if (cnt == 32 && A.vec) {
+        const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+        {
+            float4 p0 = z, m0 = z, v0 = z, h0 = z, p1 = z, m1 = z, v1 = z, h1 = z, p3 = z, m3 = z, v3 = z, h3 = z;
+            const size_t e3w = 3 * static_cast<size_t>(first) + 4 * lane, e1w = static_cast<size_t>(first) + 4 * lane;
+            if (lane < 24) {
+                adam4_load<0>(A, e3w, p0, m0, v0, h0);
+                adam4_load<1>(A, e3w, p1, m1, v1, h1);
+            }
+            if (lane < 8) adam4_load<3>(A, e1w, p3, m3, v3, h3);
+            if (lane < 24) {
+                adam4_apply<0>(A, e3w, p0, m0, v0, h0, *reinterpret_cast<const float4*>(sg + small_offset(0) + 4 * lane));
+                adam4_apply<1>(A, e3w, p1, m1, v1, h1, *reinterpret_cast<const float4*>(sg + small_offset(1) + 4 * lane));
+            }
+            if (lane < 8)
+                adam4_apply<3>(A, e1w, p3, m3, v3, h3, *reinterpret_cast<const float4*>(sg + small_offset(3) + 4 * lane));
+        }
+        {
+            float4 p2 = z, m2 = z, v2 = z, h2 = z, p4 = z, m4 = z, v4 = z, h4 = z;
+            const size_t e4w = 4 * static_cast<size_t>(first) + 4 * lane, e3w = 3 * static_cast<size_t>(first) + 4 * lane;
+            adam4_load<2>(A, e4w, p2, m2, v2, h2);
+            if (lane < 24) adam4_load<4>(A, e3w, p4, m4, v4, h4);
+            adam4_apply<2>(A, e4w, p2, m2, v2, h2, *reinterpret_cast<const float4*>(sg + small_offset(2) + 4 * lane));
+            if (lane < 24)
+                adam4_apply<4>(A, e3w, p4, m4, v4, h4, *reinterpret_cast<const float4*>(sg + small_offset(4) + 4 * lane));
+        }
+        const int n4 = 8 * rest3;
+        const size_t e0 = static_cast<size_t>(rest3) * first;
+        for (int k0 = lane; k0 < n4; k0 += 64) {
+            const int k1 = k0 + 32;
+            float4 pa, ma, va, ha, pb = z, mb = z, vb = z, hb = z;
+            adam4_load<5>(A, e0 + 4 * k0, pa, ma, va, ha);
+            if (k1 < n4) adam4_load<5>(A, e0 + 4 * k1, pb, mb, vb, hb);
+            adam4_apply<5>(A, e0 + 4 * k0, pa, ma, va, ha, sh_staged ? *reinterpret_cast<const float4*>(sh + 4 * k0) : z);
+            if (k1 < n4)
+                adam4_apply<5>(A, e0 + 4 * k1, pb, mb, vb, hb,
+                               sh_staged ? *reinterpret_cast<const float4*>(sh + 4 * k1) : z);
+        }
+        return;
+    }
+#pragma unroll 1
+    for (int gi = 0; gi < 6; ++gi) {
+        const int w = group_width(gi, rest3);
+        const size_t e0 = static_cast<size_t>(w) * first;
+        for (int k = lane; k < cnt * w; k += 32) {
+            const float g = gi < 5 ? sg[small_offset(gi) + k] : (sh_staged ? sh[k] : 0.f);
+            fused_adam(A, gi, e0 + k, g);
+        }
+    }
+}
+
 #ifndef SPLAT_PB_MIN_BLOCKS
 #define SPLAT_PB_MIN_BLOCKS 8  // 64 registers, no spills: 32 warps per SM
 #endif
-__global__ void __launch_bounds__(kPbThreads, SPLAT_PB_MIN_BLOCKS) k_preprocess_backward(PParams P, Cam cam, PrimBuffers pb, GradAcc acc,
-                                                                    Grads out, Densification dens) {
-    extern __shared__ __align__(16) float s_sh[];  // [kPbWarps][32 * rest_bases * 3]
+// One kernel for both modes, so that the gradient arithmetic is the same machine code. Unfused, each gradient is
+// stored as it is found (SH rest through shared memory, per warp). Fused (A.fused), every gradient of the warp is
+// staged in shared memory and the warp then streams its blocks through the Adam step.
+__global__ void __launch_bounds__(kPbThreads, SPLAT_PB_MIN_BLOCKS) k_preprocess_backward(
+    PParams P, Cam cam, PrimBuffers pb, GradAcc acc, const __grid_constant__ Grads out, Densification dens,
+    const __grid_constant__ AdamArgs A) {
+    // [kPbWarps][32 * rest_bases * 3 (+ kSmallFloats when fused)]
+    extern __shared__ __align__(16) float s_sh[];
     const int i = blockIdx.x * kPbThreads + threadIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (i - lane >= P.n) return;  // whole warp past the end
     const bool valid = i < P.n;
     const bool vis = valid && pb.n_touched[i] > 0;
     const int rest3 = cam.rest_bases * 3;
-    float* sh = s_sh + warp * 32 * rest3;
+    float* sh = s_sh + warp * (32 * rest3 + (A.fused ? kSmallFloats : 0));
+    float* sg = sh + 32 * rest3;  // fused: the small groups' gradients
     const int first = i - lane;
     const int cnt = min(32, P.n - first);
     const int nfl = cnt * rest3;
-    const bool vec = ((reinterpret_cast<uintptr_t>(P.sh_rest + static_cast<size_t>(first) * rest3) |
-                       reinterpret_cast<uintptr_t>(out.sh_rest + static_cast<size_t>(first) * rest3)) & 15u) == 0;
+    // one gradient element of group gi: stored, or staged for the warp's Adam phase
+    auto emit = [&](int gi, size_t e, float g) {
+        if (A.fused)
+            sg[small_offset(gi) + static_cast<int>(e - static_cast<size_t>(group_width(gi, rest3)) * first)] = g;
+        else
+            out.ptr[gi][e] = g;
+    };
     const unsigned any_vis = __ballot_sync(kFullMask, vis);
     // The warp's SH rows stream into shared memory while every per-Gaussian input is loaded into registers.
     const bool stage = any_vis && cam.active_sh_bases > 1 && rest3 > 0;
@@ -373,9 +522,9 @@ __global__ void __launch_bounds__(kPbThreads, SPLAT_PB_MIN_BLOCKS) k_preprocess_
         const float dx = ux * inv_len, dy = uy * inv_len, dz = uz * inv_len;
         float bas[16];
         sh_basis(dx, dy, dz, cam.active_sh_bases, bas);
-        out.sh0[3 * i] = bas[0] * gr;
-        out.sh0[3 * i + 1] = bas[0] * gg;
-        out.sh0[3 * i + 2] = bas[0] * gb;
+        emit(4, 3 * i, bas[0] * gr);
+        emit(4, 3 * i + 1, bas[0] * gg);
+        emit(4, 3 * i + 2, bas[0] * gb);
         float v[16];
         v[0] = 0.f;
         const int nb = min(cam.active_sh_bases, cam.rest_bases + 1);
@@ -459,7 +608,7 @@ __global__ void __launch_bounds__(kPbThreads, SPLAT_PB_MIN_BLOCKS) k_preprocess_
                 f = 0.f;
             }
         }
-        out.opacities[i] = gco.w * f * sig * (1.f - sig);
+        emit(3, i, gco.w * f * sig * (1.f - sig));
 
         // ---- conic = inverse of [[ad, b], [b, cd]]: dL/dS = -K G K with G = [[gA, gB/2], [gB/2, gC]]
         {
@@ -506,22 +655,13 @@ __global__ void __launch_bounds__(kPbThreads, SPLAT_PB_MIN_BLOCKS) k_preprocess_
         gpx += w2c[0] * gxc + w2c[4] * gyc + w2c[8] * gzc;
         gpy += w2c[1] * gxc + w2c[5] * gyc + w2c[9] * gzc;
         gpz += w2c[2] * gxc + w2c[6] * gyc + w2c[10] * gzc;
-        out.means[3 * i] = gpx;
-        out.means[3 * i + 1] = gpy;
-        out.means[3 * i + 2] = gpz;
+        emit(0, 3 * i, gpx);
+        emit(0, 3 * i + 1, gpy);
+        emit(0, 3 * i + 2, gpz);
 
         // ---- densification statistics: visible count, |dL/dmean2d| in normalised device units (pixels scaled
         // by half the image size), and with three rows the same norm of the summed per-pixel |dL/dmean2d|
-        if (dens.rows >= 2) {
-            const float hw = 0.5f * static_cast<float>(cam.width), hh = 0.5f * static_cast<float>(cam.height);
-            dens.info[i] += 1.f;
-            dens.info[static_cast<size_t>(P.n) + i] += sqrtf((gm.x * hw) * (gm.x * hw) + (gm.y * hh) * (gm.y * hh));
-            if (dens.rows == 3) {
-                const float2 ga2 = acc.mean2d_abs[i];
-                dens.info[2 * static_cast<size_t>(P.n) + i] +=
-                    sqrtf((ga2.x * hw) * (ga2.x * hw) + (ga2.y * hh) * (ga2.y * hh));
-            }
-        }
+        if (dens.rows >= 2) accumulate_densification(dens, acc, cam, P.n, i, gm);
 
         // ---- Sc = Wr S3 Wr^T: dL/dS3 = Wr^T gSc Wr; S3 = M M^T: dL/dM = 2 dL/dS3 M
         float t1[3][3], gS3[3][3];
@@ -543,7 +683,7 @@ __global__ void __launch_bounds__(kPbThreads, SPLAT_PB_MIN_BLOCKS) k_preprocess_
 #pragma unroll
         for (int k = 0; k < 3; ++k) {
             const float gs = gM[0][k] * R.m[0][k] + gM[1][k] * R.m[1][k] + gM[2][k] * R.m[2][k];
-            out.scales[3 * i + k] = gs * s[k];
+            emit(1, 3 * i + k, gs * s[k]);
 #pragma unroll
             for (int r = 0; r < 3; ++r) gR[r][k] = gM[r][k] * s[k];
         }
@@ -559,37 +699,41 @@ __global__ void __launch_bounds__(kPbThreads, SPLAT_PB_MIN_BLOCKS) k_preprocess_
         const float gz = 2.f * (-2.f * qz * gR[0][0] - w * gR[0][1] + qx * gR[0][2] + w * gR[1][0] -
                                 2.f * qz * gR[1][1] + qy * gR[1][2] + qx * gR[2][0] + qy * gR[2][1]);
         const float qd = gw * w + gx * qx + gy * qy + gz * qz;
-        out.rotations[4 * i] = (gw - w * qd) * inv_n;
-        out.rotations[4 * i + 1] = (gx - qx * qd) * inv_n;
-        out.rotations[4 * i + 2] = (gy - qy * qd) * inv_n;
-        out.rotations[4 * i + 3] = (gz - qz * qd) * inv_n;
+        emit(2, 4 * i, (gw - w * qd) * inv_n);
+        emit(2, 4 * i + 1, (gx - qx * qd) * inv_n);
+        emit(2, 4 * i + 2, (gy - qy * qd) * inv_n);
+        emit(2, 4 * i + 3, (gz - qz * qd) * inv_n);
     } else if (valid) {
 #pragma unroll
         for (int k = 0; k < 3; ++k) {
-            out.means[3 * i + k] = 0.f;
-            out.scales[3 * i + k] = 0.f;
-            out.sh0[3 * i + k] = 0.f;
+            emit(0, 3 * i + k, 0.f);
+            emit(1, 3 * i + k, 0.f);
+            emit(4, 3 * i + k, 0.f);
         }
 #pragma unroll
-        for (int k = 0; k < 4; ++k) out.rotations[4 * i + k] = 0.f;
-        out.opacities[i] = 0.f;
+        for (int k = 0; k < 4; ++k) emit(2, 4 * i + k, 0.f);
+        emit(3, i, 0.f);
         if (rest3 > 0 && any_vis && cam.active_sh_bases > 1)
             for (int k = 0; k < rest3; ++k) my_sh[k] = 0.f;
     }
     __syncwarp();
-    // write the warp's SH-rest gradients as one contiguous block
+    const bool sh_staged = any_vis && cam.active_sh_bases > 1;
+    if (A.fused) {  // every gradient of the warp is staged: one streaming Adam phase over its blocks
+        warp_adam(A, first, cnt, rest3, sh, sh_staged, sg, lane);
+        return;
+    }
+    // the warp's SH-rest gradients as one contiguous block
     if (rest3 > 0) {
-        float* dst = out.sh_rest + static_cast<size_t>(first) * rest3;
-        const bool staged = any_vis && cam.active_sh_bases > 1;
+        float* dst = out.ptr[5] + static_cast<size_t>(first) * rest3;
         int done = 0;
-        if (vec) {
+        if (out.vec) {
             const int n4 = nfl / 4;
             for (int k = lane; k < n4; k += 32)
-                reinterpret_cast<float4*>(dst)[k] = staged ? reinterpret_cast<const float4*>(sh)[k]
-                                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+                reinterpret_cast<float4*>(dst)[k] = sh_staged ? reinterpret_cast<const float4*>(sh)[k]
+                                                              : make_float4(0.f, 0.f, 0.f, 0.f);
             done = n4 * 4;
         }
-        for (int k = done + lane; k < nfl; k += 32) dst[k] = staged ? sh[k] : 0.f;
+        for (int k = done + lane; k < nfl; k += 32) dst[k] = sh_staged ? sh[k] : 0.f;
     }
 }
 
@@ -671,12 +815,84 @@ int gs3d_backward_preprocess(const float* means, const float* scales, const floa
     PrimBuffers pb = carve_prim(cp, n);
     GradAcc acc = carve_grad(cw, n);
     PParams P{means, scales, rotations, opacities, sh_rest, settings->w2c, settings->cam_position, n};
-    Grads g{grad_means, grad_scales, grad_rotations, grad_opacities, grad_sh0, grad_sh_rest};
+    Grads g{{grad_means, grad_scales, grad_rotations, grad_opacities, grad_sh0, grad_sh_rest}, 0};
+    for (int gi = 0; gi < 6; ++gi)
+        SPLAT_REQUIRE(g.ptr[gi] || (gi == 5 && cam.rest_bases == 0), "gs3d_backward: gradient output %d is null", gi);
+    g.vec = (reinterpret_cast<uintptr_t>(grad_sh_rest) & 15u) == 0;
     const size_t smem = static_cast<size_t>(kPbWarps) * 32 * cam.rest_bases * 3 * sizeof(float);
     const Densification dens{densification_info, densification_rows};
-    k_preprocess_backward<<<div_up(n, kPbThreads), kPbThreads, smem, as_stream(stream)>>>(P, cam, pb, acc, g, dens);
+    k_preprocess_backward<<<div_up(n, kPbThreads), kPbThreads, smem, as_stream(stream)>>>(P, cam, pb, acc, g, dens,
+                                                                                           AdamArgs{});
     note_launch();
     return check_launch("gs3d_preprocess_backward");
+}
+
+int gs3d_backward_densification(int n, const gs3d_settings* settings, void* prim_buf, size_t prim_bytes_,
+                                void* workspace, size_t workspace_bytes, float* densification_info,
+                                int densification_rows, void* stream) {
+    Cam cam;
+    SPLAT_TRY(fill_cam(settings, cam));
+    SPLAT_REQUIRE(n >= 0, "gs3d_backward_densification: bad size n=%d", n);
+    SPLAT_REQUIRE(densification_rows == 0 || ((densification_rows == 2 || densification_rows == 3) &&
+                                              densification_info != nullptr),
+                  "gs3d_backward_densification: densification_info must have 0, 2 or 3 rows (got %d)",
+                  densification_rows);
+    SPLAT_REQUIRE(prim_bytes_ >= prim_bytes(n) && workspace_bytes >= gs3d_backward_workspace_size(n),
+                  "gs3d_backward_densification: a buffer is smaller than its size query");
+    if (n == 0 || densification_rows == 0) return SPLAT_OK;
+    Carver cp(prim_buf, prim_bytes_), cw(workspace, workspace_bytes);
+    PrimBuffers pb = carve_prim(cp, n);
+    GradAcc acc = carve_grad(cw, n);
+    k_densification<<<div_up(n, 256), 256, 0, as_stream(stream)>>>(n, cam, pb, acc,
+                                                                   Densification{densification_info,
+                                                                                 densification_rows});
+    note_launch();
+    return check_launch("gs3d_backward_densification");
+}
+
+int gs3d_backward_preprocess_adam(float* means, float* scales, float* rotations, float* opacities, float* sh0,
+                                  float* sh_rest, int n, const gs3d_settings* settings, void* prim_buf,
+                                  size_t prim_bytes_, void* workspace, size_t workspace_bytes,
+                                  const gs3d_adam_state* adam, void* stream) {
+    Cam cam;
+    SPLAT_TRY(fill_cam(settings, cam));
+    SPLAT_REQUIRE(n >= 0, "gs3d_backward_preprocess_adam: bad size n=%d", n);
+    SPLAT_REQUIRE(adam != nullptr, "gs3d_backward_preprocess_adam: no Adam state");
+    SPLAT_REQUIRE(prim_bytes_ >= prim_bytes(n) && workspace_bytes >= gs3d_backward_workspace_size(n),
+                  "gs3d_backward_preprocess_adam: a buffer is smaller than its size query");
+    if (n == 0) return SPLAT_OK;
+    float* params[6] = {means, scales, rotations, opacities, sh0, sh_rest};
+    AdamArgs A{};
+    for (int gi = 0; gi < 6; ++gi) {
+        const bool empty = gi == 5 && cam.rest_bases == 0;  // no SH-rest coefficients: nothing to update
+        SPLAT_REQUIRE(empty || (params[gi] && adam->exp_avg[gi] && adam->exp_avg_sq[gi]),
+                      "gs3d_backward_preprocess_adam: group %d has a null buffer", gi);
+        SPLAT_REQUIRE(adam->step[gi] >= 1, "gs3d_backward_preprocess_adam: group %d step must be >= 1", gi);
+        A.param[gi] = params[gi];
+        A.exp_avg[gi] = adam->exp_avg[gi];
+        A.exp_avg_sq[gi] = adam->exp_avg_sq[gi];
+        A.grad_in[gi] = adam->grad_in[gi];
+        adam_bias_corrections(adam->lr[gi], adam->beta1, adam->beta2, adam->step[gi], A.step_size[gi],
+                              A.bc2_sqrt_rcp[gi]);
+    }
+    A.beta1 = static_cast<float>(adam->beta1);
+    A.beta2 = static_cast<float>(adam->beta2);
+    A.eps = static_cast<float>(adam->eps);
+    uintptr_t align = 0;
+    for (int gi = 0; gi < 6; ++gi)
+        align |= reinterpret_cast<uintptr_t>(A.param[gi]) | reinterpret_cast<uintptr_t>(A.exp_avg[gi]) |
+                 reinterpret_cast<uintptr_t>(A.exp_avg_sq[gi]) | reinterpret_cast<uintptr_t>(A.grad_in[gi]);
+    A.vec = (align & 15u) == 0;
+    A.fused = 1;
+    Carver cp(prim_buf, prim_bytes_), cw(workspace, workspace_bytes);
+    PrimBuffers pb = carve_prim(cp, n);
+    GradAcc acc = carve_grad(cw, n);
+    PParams P{means, scales, rotations, opacities, sh_rest, settings->w2c, settings->cam_position, n};
+    const size_t smem = static_cast<size_t>(kPbWarps) * (32 * cam.rest_bases * 3 + kSmallFloats) * sizeof(float);
+    k_preprocess_backward<<<div_up(n, kPbThreads), kPbThreads, smem, as_stream(stream)>>>(
+        P, cam, pb, acc, Grads{}, Densification{nullptr, 0}, A);
+    note_launch();
+    return check_launch("gs3d_backward_preprocess_adam");
 }
 
 int gs3d_backward(const float* grad_image, const float* image, const float* means, const float* scales,

@@ -92,8 +92,7 @@ struct TileBuffers {
     uint32_t* max_contrib;  // [T] max over the tile's pixels of n_contrib
     float* final_T;         // [H * W]
     uint32_t* n_contrib;    // [H * W] list position of the last contributor + 1
-    void* scan_ws;
-    size_t scan_bytes;
+    uint32_t* lb;           // [T + 1] first sorted-list position whose tile key is >= t (scratch)
 };
 
 // Per-instance buffer, sized by M. Instances are written in depth order, so a stable sort on the tile
@@ -150,8 +149,7 @@ inline TileBuffers carve_tile(Carver& c, int W, int H) {
     b.max_contrib = c.take<uint32_t>(T);
     b.final_T = c.take<float>(static_cast<size_t>(W) * H);
     b.n_contrib = c.take<uint32_t>(static_cast<size_t>(W) * H);
-    b.scan_bytes = scan_workspace_bytes(T + 1);
-    b.scan_ws = c.take<unsigned char>(b.scan_bytes);
+    b.lb = c.take<uint32_t>(T + 1);
     return b;
 }
 

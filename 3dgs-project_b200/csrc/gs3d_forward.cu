@@ -9,8 +9,9 @@
 //                     instances), tile counts gathered in that order and scanned -> M on the device
 //   (host reads M once to size the instance buffer; the bucket buffer is sized by a bound)
 //   gs3d_render       k_duplicate in depth order, stable radix sort on the tile digits (completing
-//                     the LSD sort of the 64-bit keys: same order, ties by Gaussian id), k_ranges,
-//                     k_bucket_counts + scan, k_bucket_tiles, k_blend
+//                     the LSD sort of the 64-bit keys: same order, ties by Gaussian id),
+//                     k_tile_bounds (32-ary search of each tile's first list position), k_tile_tables
+//                     (ranges, buckets per tile and their scan, bucket -> tile), k_blend
 // k_blend: one 128-thread block per 16x16 tile, two pixels per thread; each warp owns an 8x8 subtile
 // and walks the tile list in 32-splat buckets staged in shared memory, skipping (by ballot) the splats
 // whose culling rectangle misses its subtile - a rectangle that holds every pixel with alpha >= 1/255,
@@ -242,15 +243,17 @@ __global__ void __launch_bounds__(kDupThreads) k_duplicate(int n, Cam cam, PrimB
     uint32_t id = 0u, cnt = 0u, slot = 0u;
     Ellipse e{};
     if (r < n) {
-        id = pb.order[r];
-        if (id < static_cast<uint32_t>(n)) {
-            cnt = pb.n_touched[id];
-            slot = pb.offsets[r] - base;
-            if (cnt > 0u) {
-                const float2 m = pb.mean2d[id];
-                const float4 co = pb.conic_o[id];
-                e = make_ellipse(m.x, m.y, co.x, co.y, co.z, pb.thr[id]);
-            }
+        // the tile count is the step of the scanned offsets (no gather of n_touched), and the listing threshold
+        // is recomputed from the opacity exactly as k_preprocess computed it, so the only gathers by id are the
+        // two that the ellipse needs
+        id = min(pb.order[r], static_cast<uint32_t>(n - 1));
+        const uint32_t off = pb.offsets[r];
+        cnt = (r + 1 < n ? pb.offsets[r + 1] : pb.counters[0]) - off;
+        slot = off - base;
+        if (cnt > 0u) {
+            const float2 m = pb.mean2d[id];
+            const float4 co = pb.conic_o[id];
+            e = make_ellipse(m.x, m.y, co.x, co.y, co.z, logf(255.f * co.w));
         }
     }
     if (cnt > 0u && cnt <= static_cast<uint32_t>(kDupWarpMin)) {
@@ -322,27 +325,128 @@ __global__ void __launch_bounds__(kDupThreads) k_duplicate(int n, Cam cam, PrimB
     }
 }
 
-__global__ void k_ranges(const uint32_t* __restrict__ keys, int m, int T, uint2* __restrict__ ranges) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= m) return;
-    const uint32_t t = keys[i];
-    if (t >= static_cast<uint32_t>(T)) return;
-    if (i == 0 || keys[i - 1] != t) ranges[t].x = i;
-    if (i == m - 1 || keys[i + 1] != t) ranges[t].y = i + 1;
+// Tile ranges from the sorted tile keys without reading every key: warp t finds lb[t], the first list position
+// whose key is >= t (t in [0, T]; keys lie in [0, T], T being the pad key), by a 32-ary search. Each round its
+// lanes probe 32 cut points of the interval that holds the answer; the keys are sorted, so the probes below t
+// form a prefix of the lanes and one ballot leaves the stretch between the last of them and the first probe at
+// or above t (six rounds at 12M instances).
+constexpr int kBoundsThreads = 256;
+
+__global__ void __launch_bounds__(kBoundsThreads) k_tile_bounds(const uint32_t* __restrict__ keys, int m, int T,
+                                                                uint32_t* __restrict__ lb) {
+    const int t = (blockIdx.x * kBoundsThreads + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (t > T) return;  // whole warps
+    int lo = 0, hi = m;  // lb[t] lies in [lo, hi]
+    while (hi > lo) {
+        const long long len = hi - lo;
+        const int p = lo + static_cast<int>(len * (lane + 1) / 33);  // in [lo, hi), non-decreasing in lane
+        const unsigned below = __ballot_sync(kFullMask, keys[p] < static_cast<uint32_t>(t));
+        const int c = __popc(below);
+        const int p_last = __shfl_sync(kFullMask, p, c > 0 ? c - 1 : 0);
+        const int p_next = __shfl_sync(kFullMask, p, c < 32 ? c : 31);
+        if (c > 0) lo = p_last + 1;
+        if (c < 32) hi = p_next;
+    }
+    if (lane == 0) lb[t] = static_cast<uint32_t>(lo);
 }
 
-__global__ void k_bucket_counts(const uint2* __restrict__ ranges, int T, uint32_t* __restrict__ nb) {
-    const int t = blockIdx.x * blockDim.x + threadIdx.x;
-    if (t > T) return;
-    nb[t] = t < T ? (ranges[t].y - ranges[t].x + kBucket - 1) / kBucket : 0u;
+constexpr int kTableThreads = 1024;
+constexpr int kTableItems = 8;                             // tiles per thread in one scan chunk
+constexpr int kTableChunk = kTableThreads * kTableItems;  // tiles per scan chunk
+constexpr int kTableTiles = 256;                           // tiles whose tables one block writes
+
+__device__ __forceinline__ uint32_t table_block_scan(uint32_t v, uint32_t* s_warp, uint32_t& total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t u = __shfl_up_sync(kFullMask, inc, o);
+        if (lane >= o) inc += u;
+    }
+    if (lane == 31) s_warp[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        const uint32_t w = s_warp[lane];  // kTableThreads / 32 == 32 warps
+        uint32_t wi = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t u = __shfl_up_sync(kFullMask, wi, o);
+            if (lane >= o) wi += u;
+        }
+        s_warp[lane] = wi - w;
+        if (lane == 31) s_warp[32] = wi;
+    }
+    __syncthreads();
+    const uint32_t res = inc - v + s_warp[warp];
+    total = s_warp[32];
+    __syncthreads();
+    return res;
 }
 
-__global__ void k_bucket_tiles(const uint32_t* __restrict__ nb, const uint32_t* __restrict__ bstart, int T,
-                               long long bcap, uint32_t* __restrict__ bucket_tile) {
-    const int t = blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= T) return;
-    const uint32_t s = bstart[t];
-    for (uint32_t k = 0; k < nb[t] && s + k < bcap; ++k) bucket_tile[s + k] = t;
+// Per-tile tables from lb: ranges (empty tiles get (0, 0)), buckets per tile, first bucket of each tile (the
+// exclusive prefix, whose total goes to *total_buckets), and the bucket -> tile table. Block b writes the tables
+// of tiles [256 b, 256 b + 256): it scans the bucket counts of every tile before the end of its share (8192 tiles
+// per chunk, one chunk for a 1080p view), then its warps write the bucket -> tile entries of its tiles, one tile
+// per warp with the lanes on consecutive buckets. The bucket outputs may be null (render-only path).
+__global__ void __launch_bounds__(kTableThreads) k_tile_tables(const uint32_t* __restrict__ lb, int T, long long bcap,
+                                                               uint2* __restrict__ ranges, uint32_t* __restrict__ nb,
+                                                               uint32_t* __restrict__ bstart,
+                                                               uint32_t* __restrict__ bucket_tile,
+                                                               uint32_t* __restrict__ total_buckets) {
+    static_assert(kTableThreads == 32 * 32, "table_block_scan takes 32 warps");
+    __shared__ uint32_t s_warp[33];
+    __shared__ uint32_t s_first[kTableTiles];
+    __shared__ uint32_t s_count[kTableTiles];
+    const int t0 = blockIdx.x * kTableTiles;
+    const int t1 = min(t0 + kTableTiles, T);
+    uint32_t carry = 0u;
+    for (int c0 = 0; c0 < t1; c0 += kTableChunk) {
+        const int tb = c0 + threadIdx.x * kTableItems;
+        uint32_t b[kTableItems + 1];
+#pragma unroll
+        for (int k = 0; k <= kTableItems; ++k) b[k] = tb + k <= T ? lb[tb + k] : 0u;
+        uint32_t nbk[kTableItems];
+        uint32_t sum = 0u;
+#pragma unroll
+        for (int k = 0; k < kTableItems; ++k) {
+            const uint32_t cnt = tb + k < T ? b[k + 1] - b[k] : 0u;
+            nbk[k] = (cnt + kBucket - 1) / kBucket;
+            sum += nbk[k];
+        }
+        uint32_t total;
+        uint32_t run = table_block_scan(sum, s_warp, total) + carry;
+#pragma unroll
+        for (int k = 0; k < kTableItems; ++k) {
+            const int t = tb + k;
+            if (t >= t0 && t < t1) {
+                ranges[t] = b[k + 1] > b[k] ? make_uint2(b[k], b[k + 1]) : make_uint2(0u, 0u);
+                if (nb) {
+                    nb[t] = nbk[k];
+                    bstart[t] = run;
+                }
+                s_first[t - t0] = run;
+                s_count[t - t0] = nbk[k];
+            }
+            run += nbk[k];
+        }
+        carry += total;
+    }
+    if (t1 == T && threadIdx.x == 0) {  // the last block has scanned every tile
+        if (nb) {
+            nb[T] = 0u;
+            bstart[T] = carry;
+        }
+        if (total_buckets) *total_buckets = carry;
+    }
+    if (!bucket_tile) return;  // block-uniform
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int j = warp; j < t1 - t0; j += kTableThreads / 32) {
+        const uint32_t first = s_first[j], count = s_count[j];
+        for (uint32_t k = lane; k < count; k += 32u)
+            if (first + k < bcap) bucket_tile[first + k] = static_cast<uint32_t>(t0 + j);
+    }
 }
 
 // One 128-thread block per 16x16 tile, two pixels per thread: each warp owns an 8x8 subtile, lane (column
@@ -522,11 +626,12 @@ int fill_cam(const gs3d_settings* s, Cam& cam) {
     return SPLAT_OK;
 }
 
-// Duplication, the tile-digit sort passes and the tile ranges (shared by the training and the render-only path).
+// Duplication, the tile-digit sort passes and the per-tile tables (shared by the training and the render-only
+// path; the render-only path passes no bucket outputs).
 int bin_instances(int n, long long m, const Cam& cam, const PrimBuffers& pb, const TileBuffers& tb,
-                  const InstBuffers& ib, cudaStream_t st) {
+                  const InstBuffers& ib, long long bcap, uint32_t* bucket_tile, uint32_t* total_buckets,
+                  cudaStream_t st) {
     const int T = cam.tiles_x * cam.tiles_y;
-    SPLAT_CUDA(cudaMemsetAsync(tb.ranges, 0, sizeof(uint2) * T, st));
     if (m > 0) {
         k_duplicate<<<div_up(n, kDupThreads), kDupThreads, 0, st>>>(n, cam, pb, ib);
         note_launch();
@@ -535,11 +640,17 @@ int bin_instances(int n, long long m, const Cam& cam, const PrimBuffers& pb, con
         const int tile_bits = bit_width(static_cast<unsigned long long>(T));
         SPLAT_TRY(radix_sort_pairs<uint32_t>(ib.keys, ib.vals, ib.keys_sorted, ib.point_list, m, 0, tile_bits,
                                              ib.sort_ws, ib.sort_bytes, st));
-        k_ranges<<<div_up(m, 256), 256, 0, st>>>(ib.keys_sorted, static_cast<int>(m), T, tb.ranges);
-        note_launch();
-        SPLAT_TRY(check_launch("gs3d_ranges"));
     }
-    return SPLAT_OK;
+    k_tile_bounds<<<div_up(32ll * (T + 1), kBoundsThreads), kBoundsThreads, 0, st>>>(
+        ib.keys_sorted, static_cast<int>(m), T, tb.lb);
+    note_launch();
+    SPLAT_TRY(check_launch("gs3d_tile_bounds"));
+    k_tile_tables<<<div_up(T, kTableTiles), kTableThreads, 0, st>>>(tb.lb, T, bcap, tb.ranges,
+                                                                     bucket_tile ? tb.nb : nullptr,
+                                                                     bucket_tile ? tb.bstart : nullptr, bucket_tile,
+                                                                     total_buckets);
+    note_launch();
+    return check_launch("gs3d_tile_tables");
 }
 
 }  // namespace gs3d
@@ -618,14 +729,7 @@ int gs3d_render(int n, long long num_instances, const gs3d_settings* settings, v
     InstBuffers ib = carve_inst(ci, m);
     BucketBuffers bb = carve_bucket(cb, bucket_capacity);
     SPLAT_CUDA(cudaMemsetAsync(pb.counters + 2, 0, sizeof(uint32_t), st));  // k_blend counts the replayed buckets
-    SPLAT_TRY(bin_instances(n, m, cam, pb, tb, ib, st));
-    k_bucket_counts<<<div_up(T + 1, 256), 256, 0, st>>>(tb.ranges, T, tb.nb);
-    note_launch();
-    SPLAT_TRY(check_launch("gs3d_bucket_counts"));
-    SPLAT_TRY(scan_exclusive_u32(tb.nb, tb.bstart, T + 1, pb.counters + 1, tb.scan_ws, tb.scan_bytes, st));
-    k_bucket_tiles<<<div_up(T, 256), 256, 0, st>>>(tb.nb, tb.bstart, T, bucket_capacity, bb.tile);
-    note_launch();
-    SPLAT_TRY(check_launch("gs3d_bucket_tiles"));
+    SPLAT_TRY(bin_instances(n, m, cam, pb, tb, ib, bucket_capacity, bb.tile, pb.counters + 1, st));
     k_blend<true><<<T, kTilePixels / 2, 0, st>>>(cam, tb.ranges, tb.bstart, ib.point_list, pb.mean2d, pb.conic_o,
                                                  pb.color_z, pb.rect, settings->bg, image, tb.final_T, tb.n_contrib,
                                                  tb.max_contrib, bb.ckpt, pb.counters, bb.reached, n < 1 ? 1 : n,
@@ -651,7 +755,7 @@ int gs3d_render_inference(int n, long long num_instances, const gs3d_settings* s
     PrimBuffers pb = carve_prim(cp, n);
     TileBuffers tb = carve_tile(ct, cam.width, cam.height);
     InstBuffers ib = carve_inst(ci, m);
-    SPLAT_TRY(bin_instances(n, m, cam, pb, tb, ib, st));
+    SPLAT_TRY(bin_instances(n, m, cam, pb, tb, ib, 0, nullptr, nullptr, st));
     k_blend<false><<<T, kTilePixels / 2, 0, st>>>(cam, tb.ranges, nullptr, ib.point_list, pb.mean2d, pb.conic_o,
                                                   pb.color_z, pb.rect, settings->bg, image, nullptr, nullptr, nullptr,
                                                   nullptr, nullptr, nullptr, n < 1 ? 1 : n, static_cast<int>(m), 0);

@@ -37,6 +37,14 @@ class _Settings(ctypes.Structure):
                 ("proper_antialiasing", ctypes.c_int)]
 
 
+class _AdamState(ctypes.Structure):
+    """Mirror of gs3d_adam_state in include/splat_b200.h."""
+
+    _fields_ = [("exp_avg", ctypes.c_void_p * 6), ("exp_avg_sq", ctypes.c_void_p * 6),
+                ("grad_in", ctypes.c_void_p * 6), ("lr", ctypes.c_double * 6), ("step", ctypes.c_int * 6),
+                ("beta1", ctypes.c_double), ("beta2", ctypes.c_double), ("eps", ctypes.c_double)]
+
+
 class RasterizerSettings(NamedTuple):
     """Faster-GS's RasterizerSettings (field names as used in cluster/tests/test_lean_adam.py:119-121)."""
 
@@ -153,6 +161,93 @@ def backward(densification_info, grad_image, image, means, scales, rotations, op
     ``out`` may supply the six contiguous float32 result tensors (e.g. views of one flat gradient buffer).
     It runs as its two launches (gs3d_backward_blend, gs3d_backward_preprocess); ``stage_event``, if given, is
     recorded on the stream between them."""
+    pending = backward_blend(densification_info, grad_image, image, means, scales, rotations, opacities, sh_rest,
+                             prim_buf, tile_buf, inst_buf, bucket_buf, w2c, cam_position, bg_color, active_sh_bases,
+                             width, height, focal_x, focal_y, center_x, center_y, near_plane, far_plane,
+                             proper_antialiasing, n_instances, n_buckets, selector, defer_densification=True)
+    if stage_event is not None:
+        stage_event.record(torch.cuda.current_stream(means.device))
+    return pending.preprocess(out=out)
+
+
+class PendingBackward:
+    """One view's backward after its blend backward: the per-Gaussian 2D gradients sit in the workspace and the
+    preprocess backward is still to run, either on its own (preprocess: the six parameter gradients) or fused with
+    the Adam step of the six parameter tensors (preprocess_adam: the gradients are never stored)."""
+
+    def __init__(self, ws, s, keep, prim_buf, tensors, n, rest, rows, dinfo, stream):
+        self.ws, self.s, self.keep, self.prim = ws, s, keep, prim_buf
+        self.means, self.scales, self.rotations, self.opacities, self.sh_rest = tensors
+        self.n, self.rest, self.rows, self.dinfo, self.stream = n, rest, rows, dinfo, stream
+
+    def preprocess(self, out: tuple | None = None) -> tuple:
+        """The six parameter gradients (gs3d_backward_preprocess), with the densification rows when they were
+        deferred to this call."""
+        n, rest, dev = self.n, self.rest, self.means.device
+        if out is not None:
+            grads = tuple(out)
+            for t, numel in zip(grads, (3 * n, 3 * n, 4 * n, n, 3 * n, 3 * rest * n)):
+                L.check_cuda("out", t, torch.float32)
+                if t.numel() != numel:
+                    raise RuntimeError("out tensors must match the parameter shapes")
+        else:
+            grads = (torch.empty(n, 3, device=dev), torch.empty(n, 3, device=dev), torch.empty(n, 4, device=dev),
+                     torch.empty(n, 1, device=dev), torch.empty(n, 1, 3, device=dev),
+                     torch.empty(n, rest, 3, device=dev))
+        L.call("gs3d_backward_preprocess", L.ptr(self.means), L.ptr(self.scales), L.ptr(self.rotations),
+               L.ptr(self.opacities), L.ptr(self.sh_rest), n, ctypes.byref(self.s), L.ptr(self.prim),
+               self.prim.numel(), L.ptr(self.ws), self.ws.numel(), *map(L.ptr, grads), L.ptr(self.dinfo), self.rows,
+               self.stream)
+        self.rows, self.dinfo = 0, None
+        return grads
+
+    def preprocess_adam(self, params, exp_avg, exp_avg_sq, lrs, steps, betas=(0.9, 0.999), eps: float = 1e-15,
+                        grad_in=None) -> None:
+        """The preprocess backward fused with one Adam step of the six parameter tensors (means, scales, rotations,
+        opacities, sh0, sh_rest; updated in place with their moments): gs3d_backward_preprocess_adam. grad_in: per
+        tensor, the gradient other loss terms already left (added first), or None. Bit-identical to preprocess()
+        followed by FusedAdam's step over the same six tensors."""
+        if self.rows:
+            raise RuntimeError("densification rows were deferred to the preprocess backward; take them first")
+        params = list(params)
+        if len(params) != 6 or len(exp_avg) != 6 or len(exp_avg_sq) != 6 or len(lrs) != 6 or len(steps) != 6:
+            raise RuntimeError("six parameter tensors (means, scales, rotations, opacities, sh0, sh_rest) expected")
+        for got, want in zip((params[0], params[1], params[2], params[3], params[5]),
+                             (self.means, self.scales, self.rotations, self.opacities, self.sh_rest)):
+            if got.data_ptr() != want.data_ptr():
+                raise RuntimeError("preprocess_adam updates the tensors the forward read; got another tensor")
+        grad_in = list(grad_in) if grad_in is not None else [None] * 6
+        st = _AdamState()
+        keep = []
+        for k in range(6):
+            p, m, v, g = params[k], exp_avg[k], exp_avg_sq[k], grad_in[k]
+            for name, t in (("param", p), ("exp_avg", m), ("exp_avg_sq", v)):
+                L.check_cuda(name, t, torch.float32)
+                if t.numel() != p.numel():
+                    raise RuntimeError(f"{name} of group {k} does not match its parameter")
+            if g is not None:
+                g = g.detach().to(torch.float32).contiguous()
+                if g.numel() != p.numel():
+                    raise RuntimeError(f"grad_in of group {k} does not match its parameter")
+                keep.append(g)
+            st.exp_avg[k] = m.data_ptr()
+            st.exp_avg_sq[k] = v.data_ptr()
+            st.grad_in[k] = g.data_ptr() if g is not None else None
+            st.lr[k] = float(lrs[k])
+            st.step[k] = int(steps[k])
+        st.beta1, st.beta2, st.eps = float(betas[0]), float(betas[1]), float(eps)
+        L.call("gs3d_backward_preprocess_adam", *map(L.ptr, params), self.n, ctypes.byref(self.s), L.ptr(self.prim),
+               self.prim.numel(), L.ptr(self.ws), self.ws.numel(), ctypes.byref(st), self.stream)
+
+
+@torch.no_grad()
+def backward_blend(densification_info, grad_image, image, means, scales, rotations, opacities, sh_rest, prim_buf,
+                   tile_buf, inst_buf, bucket_buf, w2c, cam_position, bg_color, active_sh_bases, width, height,
+                   focal_x, focal_y, center_x, center_y, near_plane, far_plane, proper_antialiasing, n_instances,
+                   n_buckets, selector, *mode, defer_densification: bool = False) -> PendingBackward:
+    """The blend backward of `_C.backward` alone (gs3d_backward_blend): returns the PendingBackward whose
+    preprocess()/preprocess_adam() finishes it. The densification rows are accumulated now
+    (gs3d_backward_densification) unless defer_densification leaves them to preprocess()."""
     n = means.shape[0]
     rest = sh_rest.shape[1] if sh_rest.dim() == 3 else 0
     dev = means.device
@@ -161,26 +256,17 @@ def backward(densification_info, grad_image, image, means, scales, rotations, op
                   center_y, near_plane, far_plane, proper_antialiasing, rest, keep)
     g_img = grad_image.detach().to(torch.float32).contiguous()
     ws = torch.empty(L.query("gs3d_backward_workspace_size", n), dtype=torch.uint8, device=dev)
-    if out is not None:
-        grads = tuple(out)
-        for t, numel in zip(grads, (3 * n, 3 * n, 4 * n, n, 3 * n, 3 * rest * n)):
-            L.check_cuda("out", t, torch.float32)
-            if t.numel() != numel:
-                raise RuntimeError("out tensors must match the parameter shapes")
-    else:
-        grads = (torch.empty(n, 3, device=dev), torch.empty(n, 3, device=dev), torch.empty(n, 4, device=dev),
-                 torch.empty(n, 1, device=dev), torch.empty(n, 1, 3, device=dev), torch.empty(n, rest, 3, device=dev))
     rows, dinfo = _densification(densification_info, n)
     stream = L.stream_of(means)
     L.call("gs3d_backward_blend", L.ptr(g_img), L.ptr(image), n, int(n_instances), ctypes.byref(s), L.ptr(prim_buf),
            prim_buf.numel(), L.ptr(tile_buf), tile_buf.numel(), L.ptr(inst_buf), inst_buf.numel(), L.ptr(bucket_buf),
            bucket_buf.numel(), int(n_buckets), L.ptr(ws), ws.numel(), rows, stream)
-    if stage_event is not None:
-        stage_event.record(torch.cuda.current_stream(dev))
-    L.call("gs3d_backward_preprocess", L.ptr(means), L.ptr(scales), L.ptr(rotations), L.ptr(opacities),
-           L.ptr(sh_rest), n, ctypes.byref(s), L.ptr(prim_buf), prim_buf.numel(), L.ptr(ws), ws.numel(),
-           *map(L.ptr, grads), L.ptr(dinfo), rows, stream)
-    return grads
+    if rows and not defer_densification:
+        L.call("gs3d_backward_densification", n, ctypes.byref(s), L.ptr(prim_buf), prim_buf.numel(), L.ptr(ws),
+               ws.numel(), L.ptr(dinfo), rows, stream)
+        rows, dinfo = 0, None
+    return PendingBackward(ws, s, keep, prim_buf, (means, scales, rotations, opacities, sh_rest), n, rest, rows,
+                           dinfo, stream)
 
 
 def _densification(densification_info, n: int):
@@ -203,6 +289,10 @@ class _Rasterize(torch.autograd.Function):
 
     track_visibility: bool = False
     last_visibility: torch.Tensor | None = None
+    # A FusedAdam(fuse_backward=True) that owns the six parameter tensors takes the preprocess backward into its
+    # step: backward then runs the blend backward (and the densification rows) only and returns no parameter
+    # gradients; the optimizer's next step() applies the gradients inside the fused kernel.
+    fused_optimizer: Any = None
 
     @staticmethod
     def forward(ctx: Any, means, scales, rotations, opacities, sh0, sh_rest, densification_info,
@@ -215,12 +305,20 @@ class _Rasterize(torch.autograd.Function):
         ctx.buffer_state = (m, nb, sel)
         ctx.densification_info = densification_info
         ctx.shapes = (opacities.shape, sh0.shape, sh_rest.shape)
-        ctx.save_for_backward(image, params[0], params[1], params[2], params[3], params[5], prim, tile, inst, bucket)
+        ctx.save_for_backward(image, params[0], params[1], params[2], params[3], params[5], prim, tile, inst, bucket,
+                              params[4])
         return image
 
     @staticmethod
     def backward(ctx: Any, grad_image):
-        image, means, scales, rotations, opacities, sh_rest, prim, tile, inst, bucket = ctx.saved_tensors
+        image, means, scales, rotations, opacities, sh_rest, prim, tile, inst, bucket, sh0 = ctx.saved_tensors
+        opt = _Rasterize.fused_optimizer
+        six = (means, scales, rotations, opacities, sh0, sh_rest)
+        if opt is not None and opt._owns(six):
+            pending = backward_blend(ctx.densification_info, grad_image, image, means, scales, rotations, opacities,
+                                     sh_rest, prim, tile, inst, bucket, *ctx.settings.as_tuple(), *ctx.buffer_state)
+            opt._defer(pending, six)
+            return (None,) * 8
         g = backward(ctx.densification_info, grad_image, image, means, scales, rotations, opacities, sh_rest, prim,
                      tile, inst, bucket, *ctx.settings.as_tuple(), *ctx.buffer_state)
         op_shape, sh0_shape, rest_shape = ctx.shapes

@@ -52,6 +52,7 @@ WIDTHS = (3, 3, 4, 1, 3, 45)  # floats per Gaussian in each group: 59 in total
 # (profiles/); None where not captured.
 BLEND_BWD_TRAFFIC = 240830464 + 5681408
 ADAM_TRAFFIC = 2832050688 + 2067712256
+FUSED_TRAFFIC = None  # not captured yet
 
 
 class Clocks:
@@ -164,9 +165,10 @@ def scene_for(workload: str, rank: int, world: int):
 class Trainer:
     """Replicated Gaussians, flat gradient buffer, Adam state; one training step per call."""
 
-    def __init__(self, sc: dict, dev, world: int):
+    def __init__(self, sc: dict, dev, world: int, fuse: bool = False):
         self.dev = dev
         self.world = world
+        self.fuse = fuse and world == 1  # preprocess backward + Adam in one kernel (N > 1: the exchange kernel)
         self.bases = sc["active_sh_bases"]
         self.peer = None
         if world > 1:  # parameters and gradients in peer-addressable buffers, one fused exchange + Adam kernel
@@ -195,14 +197,28 @@ class Trainer:
         image, prim, tile, inst, bucket, m, nb, sel = gs3d.forward(*self.params, *s)
         if timed:
             e[1].record()
+        self.last = (prim, tile, m, cam)
+        self.t += 1
+        if self.fuse:  # blend backward, then the preprocess backward fused with Adam (timed as "adam")
+            pend = gs3d.backward_blend(None, dout, image, self.params[0], self.params[1], self.params[2],
+                                       self.params[3], self.params[5], prim, tile, inst, bucket, *s, m, nb, sel)
+            if timed:
+                for k in (5, 2, 3):
+                    e[k].record()
+                self.ev["blend_bwd"].append((e[1], e[5]))
+            pend.preprocess_adam(self.params, self.m, self.v, [LRS[nm] for nm in NAMES], [self.t] * 6,
+                                 (0.9, 0.999), 1e-15)
+            if timed:
+                e[4].record()
+                for k, (a, b) in zip(("fwd", "bwd", "comm", "adam"), zip(e[:-1], e[1:])):
+                    self.ev[k].append((a, b))
+            return m
         gs3d.backward(None, dout, image, self.params[0], self.params[1], self.params[2], self.params[3],
                       self.params[5], prim, tile, inst, bucket, *s, m, nb, sel, out=self.grads,
                       stage_event=e[5] if timed else None)
         if timed:
             e[2].record()
             self.ev["blend_bwd"].append((e[1], e[5]))
-        self.last = (prim, tile, m, cam)
-        self.t += 1
         if self.peer is not None:  # exchange and Adam in one kernel per rank (timed as "comm")
             self.peer.step()
             if timed:
@@ -224,7 +240,7 @@ def run_ours(args) -> None:
     dev = torch.device("cuda", local)
     sc, cams = scene_for(args.workload, rank, world)
     cam = cams[0]
-    tr = Trainer(sc, dev, world)
+    tr = Trainer(sc, dev, world, fuse=args.fuse)
     g = torch.Generator().manual_seed(77 + rank)
     H, W = cam["height"], cam["width"]
     dout = (1e-3 * torch.randn(3, H, W, generator=g)).to(dev)
@@ -281,7 +297,8 @@ def run_ours(args) -> None:
                                    f"in one peer-memory kernel per rank)",
                        "gaussians": n, "width": W, "height": H, "views_per_gpu_per_step": views_per_step,
                        "instances_per_view": round(m_avg), "l2": "state (2.8 GB) larger than L2; no flush",
-                       "parallelism": f"dp{world} (views)"},
+                       "parallelism": f"dp{world} (views)",
+                       "fused_preprocess_backward_adam": tr.fuse},
             "stage_ms": {k: round(v, 4) for k, v in stage.items()},
             "fwd_bwd_ms": round(stage["fwd"] + stage["bwd"], 4),
             "wall_s": round(wall, 3),
@@ -309,10 +326,10 @@ def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
     if world > 1:  # the leaves are views of PeerAdam's parameter buffer; step() takes their .grad
         peer = gs_dist.PeerAdam([p.detach() for p in tr.params], [LRS[nm] for nm in NAMES], eps=1e-15)
         leaves = [p.requires_grad_(True) for p in peer.params]
-    else:
+    else:  # with fuse_backward the rasterizer's preprocess backward runs inside the optimizer's fused step
         leaves = [p.clone().requires_grad_(True) for p in tr.params]
         opt = gs_adam.FusedAdam([{"params": [p], "lr": LRS[nm]} for p, nm in zip(leaves, NAMES)], lr=0.0,
-                                eps=1e-15)
+                                eps=1e-15, fuse_backward=tr.fuse)
     cam = cams[0]
     H, W = cam["height"], cam["width"]
     host = (1e-3 * torch.randn(3, H, W, generator=torch.Generator().manual_seed(99))).pin_memory()
@@ -375,6 +392,7 @@ def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
             p.grad = None
         del leaves
         peer.close()
+    gs3d._Rasterize.fused_optimizer = None
     return {"value": round(world * args.steps / (float(ms.item()) / 1000.0), 3), "unit": "views/s",
             "h2d_bytes_per_step": int(host.numel() * 4), "d2h_bytes_per_step": 4,
             "note": "upstream gradient copied from pinned host memory one step ahead on a copy stream; loss copied "
@@ -399,7 +417,10 @@ def roofline(tr: Trainer, stage: dict, reach: dict, pixels: int) -> dict:
         image, contributor count) + 40 B per reached list position (id, mean2d, conic + opacity, colour) + 36 B per
         Gaussian (accumulator clear). Its limiter is instruction issue (FP32, ex2, shuffles), not HBM: the HBM
         fraction it reports is low by nature; profiles/ holds its issue and pipe utilisation.
-      k_adam: 59 floats x 4 B x 7 accesses (param, grad, m, v read; param, m, v written) = 1652 B per Gaussian."""
+      k_adam: 59 floats x 4 B x 7 accesses (param, grad, m, v read; param, m, v written) = 1652 B per Gaussian.
+      k_preprocess_backward fused with Adam (--fuse): 59 floats x 4 B x 6 accesses (param, m, v read and written)
+        + 4 B (n_touched) per Gaussian, + 56 B per visible Gaussian (the blend backward's mean2d, conic + opacity
+        and colour sums, colour + depth): 1420 N + 56 V."""
     peaks_path = ROOT / "MEASURED_PEAKS.json"
     hbm, src = 6650.0, "fallback"
     if peaks_path.exists():
@@ -411,14 +432,22 @@ def roofline(tr: Trainer, stage: dict, reach: dict, pixels: int) -> dict:
              + 36.0 * tr.n, "traffic": BLEND_BWD_TRAFFIC, "limiter": "issue (FP32 / ex2 / shuffles)"}
     adam = {"kernel": "k_adam", "ms": stage["adam"], "bytes": 1652.0 * tr.n, "traffic": ADAM_TRAFFIC,
             "limiter": "HBM"}
+    if tr.fuse:
+        visible = int((gs3d.primitive_views(tr.last[0], tr.n)["n_touched"] > 0).sum().item())
+        adam = {"kernel": "k_preprocess_backward (fused with Adam)", "ms": stage["adam"],
+                "bytes": 1420.0 * tr.n + 56.0 * visible, "traffic": FUSED_TRAFFIC, "limiter": "HBM",
+                "visible": visible}
     top, other = (blend, adam) if blend["ms"] >= adam["ms"] or tr.peer is not None else (adam, blend)
 
     def entry(k):
         ach = k["bytes"] / (k["ms"] / 1000.0) / 1e9 if k["ms"] > 0 else 0.0
-        return {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s", "frac": round(ach / hbm, 4),
-                "traffic": k["traffic"], "kernel": k["kernel"], "kernel_ms": round(k["ms"], 4),
-                "algorithmic_bytes": int(k["bytes"]), "limiter": k["limiter"],
-                "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src}
+        out = {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s", "frac": round(ach / hbm, 4),
+               "traffic": k["traffic"], "kernel": k["kernel"], "kernel_ms": round(k["ms"], 4),
+               "algorithmic_bytes": int(k["bytes"]), "limiter": k["limiter"],
+               "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src}
+        if "visible" in k:
+            out["visible_gaussians"] = k["visible"]
+        return out
 
     out = entry(top)
     if tr.peer is None:  # with N > 1 Adam runs inside the fused exchange kernel instead (see "exchange")
@@ -640,6 +669,9 @@ def main() -> None:
     ap.add_argument("--workload", choices=["c3", "c4", "c2", "c1", "c5"], default="c3")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for the baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--fuse", action="store_true",
+                    help="N = 1: the preprocess backward fused with Adam (FusedAdam(fuse_backward=True)) instead of "
+                         "separate launches; measured slower on C3 (1.01 ms against 0.24 + 0.74 ms)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

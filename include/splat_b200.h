@@ -242,6 +242,32 @@ int gs3d_backward_preprocess(const float* means, const float* scales, const floa
                              float* grad_means, float* grad_scales, float* grad_rotations, float* grad_opacities,
                              float* grad_sh0, float* grad_sh_rest, float* densification_info,
                              int densification_rows, void* stream);
+/* The densification rows of gs3d_backward_preprocess alone, from the blend backward's workspace (the same
+ * arithmetic, so the rows equal those gs3d_backward_preprocess accumulates). For callers that defer the
+ * preprocess backward to gs3d_backward_preprocess_adam but read the statistics before the optimizer step. */
+int gs3d_backward_densification(int n, const gs3d_settings* settings, void* prim_buf, size_t prim_bytes,
+                                void* workspace, size_t workspace_bytes, float* densification_info,
+                                int densification_rows, void* stream);
+/* The preprocess backward fused with the Adam step of the six parameter tensors (no counterpart in the
+ * reference, which runs `_C.backward`'s preprocess backward and then FusedAdam's `_C.adam_step` per group,
+ * cluster/patches/fastergs_lean_adam.patch:251-307): each parameter gradient element is added to grad_in[g]
+ * when given (the gradient other loss terms left, autograd's existing + new) and applied in place to the
+ * parameter and its moments with FusedAdam's arithmetic; the gradient is never written to memory. Groups in
+ * the order means, scales, rotations, opacities, sh0, sh_rest (sh_rest may be NULL when rest_bases is 0).
+ * Bit-identical to gs3d_backward_preprocess followed by adam_step_multi over the six groups. No densification
+ * rows (see gs3d_backward_densification). */
+typedef struct gs3d_adam_state {
+    float* exp_avg[6];
+    float* exp_avg_sq[6];
+    const float* grad_in[6]; /* may be NULL */
+    double lr[6];
+    int step[6]; /* t >= 1 of this update, per group */
+    double beta1, beta2, eps;
+} gs3d_adam_state;
+int gs3d_backward_preprocess_adam(float* means, float* scales, float* rotations, float* opacities, float* sh0,
+                                  float* sh_rest, int n, const gs3d_settings* settings, void* prim_buf,
+                                  size_t prim_bytes, void* workspace, size_t workspace_bytes,
+                                  const gs3d_adam_state* adam, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
  * Fused Adam (replaces the per-group `_C.adam_step` launches of Faster-GS's FusedAdam,

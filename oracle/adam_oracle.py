@@ -5,7 +5,7 @@ Follows `adam_step_sparse_cu<LOWP>` of cluster/patches/fastergs_lean_adam.patch:
   bf16 read (:77-79)     bits << 16
   SR write (:83-86)      (bits(f) + (rnd & 0xFFFF)) >> 16, rnd = hash((uint32) i ^ seed) for exp_avg and
                          hash of that for exp_avg_sq (:122-123), seed = 0x9E3779B9 * step + 0x85EBCA6B (:165)
-  update (:116-120)      m = fma(b1, m - g, g); v = fma(b2, v - g^2, g^2); p -= step_size * m / (sqrt(v) bc2 + eps)
+  update (:116-120)      m = fma(b1, m - g, g); v = fma(b2, v - g^2, g^2); p -= step_size * m / fma(sqrt(v), bc2, eps)
   mask (:106)            element i is skipped when visibility[i // features] == 0
 numpy uint32 arithmetic wraps like the device's. The update below uses float64 for the fused multiply-adds, which
 is exact for the products and can differ from a float32 fma in the last bit of the sum, so parity tests compare the
@@ -60,7 +60,7 @@ def adam_lean(param, grad, m, v, step: int, lr: float, beta1=0.9, beta2=0.999, e
     g2 = (g * g).astype(np.float32)
     m1 = (np.float64(np.float32(beta1)) * (mf - g).astype(np.float64) + g).astype(np.float32)
     m2 = (np.float64(np.float32(beta2)) * (vf - g2).astype(np.float64) + g2).astype(np.float32)
-    denom = (np.sqrt(m2) * bc2_sqrt_rcp + np.float32(eps)).astype(np.float32)
+    denom = (np.sqrt(m2).astype(np.float64) * np.float64(bc2_sqrt_rcp) + np.float64(np.float32(eps))).astype(np.float32)
     upd = (p - step_size * m1 / denom).astype(np.float32)
     on = np.ones(p.shape, bool) if visibility is None else (np.asarray(visibility)[np.arange(p.size) // features] != 0)
     p = np.where(on, upd, p)

@@ -642,7 +642,7 @@ void gs3o_adam(float* param, const float* grad, float* m, float* v, long long n,
         const float g = grad[e], g2 = g * g;
         m[e] = fmaf(b1, m[e] - g, g);
         v[e] = fmaf(b2, v[e] - g2, g2);
-        param[e] -= step_size * m[e] / (sqrtf(v[e]) * bc2r + eps);
+        param[e] -= step_size * m[e] / fmaf(sqrtf(v[e]), bc2r, eps);  // the device's denominator
     }
 }
 
