@@ -49,36 +49,51 @@ __device__ __forceinline__ float adam(float p, float g, float& m, float& v, floa
 }
 
 // kWorld: the number of ranks, a template argument so that the per-rank loads live in exactly that many registers.
+// Each thread takes kUnroll float4 groups per round (8 / kWorld of them, at least one), so that every peer load of
+// the round is in flight before the first sum.
 template <int kWorld>
 __global__ void __launch_bounds__(kThreads) k_dp_adam(Args a) {
+    constexpr int kUnroll = kWorld >= 8 ? 1 : 8 / kWorld;
     const long long n = a.hi - a.lo;
     const long long n4 = n / 4;  // lo is a multiple of 4 and the buffers 16-byte aligned
     const long long stride = static_cast<long long>(gridDim.x) * kThreads;
-    for (long long q = static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x; q < n4; q += stride) {
-        const long long e = a.lo + 4 * q;
-        float4 gv[kWorld];
+    for (long long q0 = static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x; q0 < n4; q0 += stride * kUnroll) {
+        float4 gv[kUnroll][kWorld], p[kUnroll], m[kUnroll], v[kUnroll];
 #pragma unroll
-        for (int k = 0; k < kWorld; ++k)  // every rank's load in flight before the sum
-            gv[k] = *reinterpret_cast<const float4*>(a.grads[k] + e);
-        float4 g = gv[0];
+        for (int u = 0; u < kUnroll; ++u) {
+            const long long q = q0 + u * stride;
+            if (q < n4) {
+                const long long e = a.lo + 4 * q;
 #pragma unroll
-        for (int k = 1; k < kWorld; ++k) {
-            g.x += gv[k].x;
-            g.y += gv[k].y;
-            g.z += gv[k].z;
-            g.w += gv[k].w;
+                for (int k = 0; k < kWorld; ++k) gv[u][k] = *reinterpret_cast<const float4*>(a.grads[k] + e);
+                p[u] = *reinterpret_cast<const float4*>(a.params[a.rank] + e);  // this rank's own copy
+                m[u] = *reinterpret_cast<const float4*>(a.exp_avg + 4 * q);
+                v[u] = *reinterpret_cast<const float4*>(a.exp_avg_sq + 4 * q);
+            }
         }
-        float4 p = *reinterpret_cast<const float4*>(a.params[a.rank] + e);  // this rank's own copy
-        float4 m = *reinterpret_cast<const float4*>(a.exp_avg + 4 * q);
-        float4 v = *reinterpret_cast<const float4*>(a.exp_avg_sq + 4 * q);
-        p.x = adam(p.x, g.x, m.x, v.x, step_size_of(a, e), a);
-        p.y = adam(p.y, g.y, m.y, v.y, step_size_of(a, e + 1), a);
-        p.z = adam(p.z, g.z, m.z, v.z, step_size_of(a, e + 2), a);
-        p.w = adam(p.w, g.w, m.w, v.w, step_size_of(a, e + 3), a);
-        *reinterpret_cast<float4*>(a.exp_avg + 4 * q) = m;
-        *reinterpret_cast<float4*>(a.exp_avg_sq + 4 * q) = v;
 #pragma unroll
-        for (int k = 0; k < kWorld; ++k) *reinterpret_cast<float4*>(a.params[k] + e) = p;
+        for (int u = 0; u < kUnroll; ++u) {
+            const long long q = q0 + u * stride;
+            if (q < n4) {
+                const long long e = a.lo + 4 * q;
+                float4 g = gv[u][0];
+#pragma unroll
+                for (int k = 1; k < kWorld; ++k) {  // in rank order
+                    g.x += gv[u][k].x;
+                    g.y += gv[u][k].y;
+                    g.z += gv[u][k].z;
+                    g.w += gv[u][k].w;
+                }
+                p[u].x = adam(p[u].x, g.x, m[u].x, v[u].x, step_size_of(a, e), a);
+                p[u].y = adam(p[u].y, g.y, m[u].y, v[u].y, step_size_of(a, e + 1), a);
+                p[u].z = adam(p[u].z, g.z, m[u].z, v[u].z, step_size_of(a, e + 2), a);
+                p[u].w = adam(p[u].w, g.w, m[u].w, v[u].w, step_size_of(a, e + 3), a);
+                *reinterpret_cast<float4*>(a.exp_avg + 4 * q) = m[u];
+                *reinterpret_cast<float4*>(a.exp_avg_sq + 4 * q) = v[u];
+#pragma unroll
+                for (int k = 0; k < kWorld; ++k) *reinterpret_cast<float4*>(a.params[k] + e) = p[u];
+            }
+        }
     }
     // the last n % 4 elements, one thread
     if (blockIdx.x == 0 && threadIdx.x == 0) {
@@ -125,29 +140,46 @@ __device__ __forceinline__ float adam_nvls(float p, float g, float& m, float& v,
     return p;
 }
 
+// Four float4 groups per thread per round: their four multimem loads are in flight together.
+constexpr int kNvlsUnroll = 4;
+
 __global__ void __launch_bounds__(kThreads) k_dp_adam_nvls(NvlsArgs a) {
     const long long n4 = (a.hi - a.lo) / 4;  // lo and hi are multiples of 4
     const long long stride = static_cast<long long>(gridDim.x) * kThreads;
-    for (long long q = static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x; q < n4; q += stride) {
-        const long long e = a.lo + 4 * q;
-        float4 g;
-        asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
-                     : "=f"(g.x), "=f"(g.y), "=f"(g.z), "=f"(g.w)
-                     : "l"(a.grads_mc + e)
-                     : "memory");
-        float4 p = *reinterpret_cast<const float4*>(a.params_local + e);
-        float4 m = *reinterpret_cast<const float4*>(a.exp_avg + 4 * q);
-        float4 v = *reinterpret_cast<const float4*>(a.exp_avg_sq + 4 * q);
-        p.x = adam_nvls(p.x, g.x, m.x, v.x, step_size_nvls(a, e), a);
-        p.y = adam_nvls(p.y, g.y, m.y, v.y, step_size_nvls(a, e + 1), a);
-        p.z = adam_nvls(p.z, g.z, m.z, v.z, step_size_nvls(a, e + 2), a);
-        p.w = adam_nvls(p.w, g.w, m.w, v.w, step_size_nvls(a, e + 3), a);
-        *reinterpret_cast<float4*>(a.exp_avg + 4 * q) = m;
-        *reinterpret_cast<float4*>(a.exp_avg_sq + 4 * q) = v;
-        asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};"
-                     :
-                     : "l"(a.params_mc + e), "f"(p.x), "f"(p.y), "f"(p.z), "f"(p.w)
-                     : "memory");
+    for (long long q0 = static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x; q0 < n4;
+         q0 += stride * kNvlsUnroll) {
+        float4 g[kNvlsUnroll], p[kNvlsUnroll], m[kNvlsUnroll], v[kNvlsUnroll];
+#pragma unroll
+        for (int u = 0; u < kNvlsUnroll; ++u) {
+            const long long q = q0 + u * stride;
+            if (q < n4) {
+                const long long e = a.lo + 4 * q;
+                asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+                             : "=f"(g[u].x), "=f"(g[u].y), "=f"(g[u].z), "=f"(g[u].w)
+                             : "l"(a.grads_mc + e)
+                             : "memory");
+                p[u] = *reinterpret_cast<const float4*>(a.params_local + e);
+                m[u] = *reinterpret_cast<const float4*>(a.exp_avg + 4 * q);
+                v[u] = *reinterpret_cast<const float4*>(a.exp_avg_sq + 4 * q);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kNvlsUnroll; ++u) {
+            const long long q = q0 + u * stride;
+            if (q < n4) {
+                const long long e = a.lo + 4 * q;
+                p[u].x = adam_nvls(p[u].x, g[u].x, m[u].x, v[u].x, step_size_nvls(a, e), a);
+                p[u].y = adam_nvls(p[u].y, g[u].y, m[u].y, v[u].y, step_size_nvls(a, e + 1), a);
+                p[u].z = adam_nvls(p[u].z, g[u].z, m[u].z, v[u].z, step_size_nvls(a, e + 2), a);
+                p[u].w = adam_nvls(p[u].w, g[u].w, m[u].w, v[u].w, step_size_nvls(a, e + 3), a);
+                *reinterpret_cast<float4*>(a.exp_avg + 4 * q) = m[u];
+                *reinterpret_cast<float4*>(a.exp_avg_sq + 4 * q) = v[u];
+                asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};"
+                             :
+                             : "l"(a.params_mc + e), "f"(p[u].x), "f"(p[u].y), "f"(p[u].z), "f"(p[u].w)
+                             : "memory");
+            }
+        }
     }
     __threadfence_system();
 }

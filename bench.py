@@ -472,9 +472,14 @@ def exchange_figures(tr: Trainer, stage: dict) -> dict:
     kernel = "adam_step_dp_nvls" if nvls else "adam_step_dp_fused"
     t = stage["comm"]
     ach = cross / (t / 1000.0) / 1e9 if t > 0 else 0.0
+    # the same exchange measured as an all-reduce: bus bandwidth 2 (G - 1) / G x vector bytes / time, against the
+    # measured 8-rank NCCL all-reduce bus bandwidth of this pool (725 GB/s at 1 GiB), which also carries no Adam step
+    vector = 4.0 * tr.peer.total
+    bus = 2.0 * (g - 1) / g * vector / (t / 1000.0) / 1e9 if t > 0 else 0.0
     return {"kernel": kernel + " (+ 2 barriers)", "ms": round(t, 4), "bytes_each_direction": int(cross),
             "achieved": round(ach, 1), "peak": 770.0, "unit": "GB/s", "frac": round(ach / 770.0, 4),
-            "peak_source": "measured peer copy, per direction"}
+            "peak_source": "measured peer copy, per direction",
+            "allreduce_bus_gbs": round(bus, 1), "allreduce_bus_frac_of_nccl": round(bus / 725.0, 4)}
 
 
 def cpu_baseline(args, sc, cam):
