@@ -3,11 +3,13 @@
 //
 // Launch sequence of one forward (all on the caller's stream):
 //   gs3d_preprocess   k_preprocess (1 thread per Gaussian; SH rows loaded per warp with 16-byte
-//                     loads through shared memory; listed tiles counted row by row in closed form),
-//                     radix sort of the Gaussians by depth bits (the four depth-digit passes of the
-//                     64-bit (tile << 32 | depth) key sort, done on N Gaussians instead of M
-//                     instances), tile counts gathered in that order and scanned -> M on the device
-//   (host reads M once to size the instance buffer; the bucket buffer is sized by a bound)
+//                     loads through shared memory; listed tiles counted row by row in closed form;
+//                     M summed on the device), then (gs3d_preprocess_order) radix sort of the
+//                     Gaussians by depth bits (the four depth-digit passes of the 64-bit
+//                     (tile << 32 | depth) key sort, done on N Gaussians instead of M instances),
+//                     tile counts gathered in that order and scanned
+//   (host reads M once to size the instance buffer, while the depth sort runs; the bucket buffer
+//   is sized by a bound)
 //   gs3d_render       k_duplicate in depth order, stable radix sort on the tile digits (completing
 //                     the LSD sort of the 64-bit keys: same order, ties by Gaussian id),
 //                     k_tile_bounds (32-ary search of each tile's first list position), k_tile_tables
@@ -177,6 +179,9 @@ __global__ void __launch_bounds__(kPreThreads) k_preprocess(Params P, Cam cam, P
             }
         }
     }
+    // the instance count M, summed per warp (every lane of the block reaches this point)
+    const uint32_t warp_touched = __reduce_add_sync(kFullMask, touched);
+    if (lane == 0 && warp_touched) atomicAdd(pb.counters + 3, warp_touched);
     if (!valid) return;
     pb.n_touched[i] = touched;
     pb.ids[i] = static_cast<uint32_t>(i);
@@ -670,9 +675,9 @@ long long gs3d_bucket_bound(long long num_instances, int width, int height) {
 }
 size_t gs3d_bucket_buffer_size(long long bucket_capacity) { return bucket_bytes(bucket_capacity); }
 
-int gs3d_preprocess(const float* means, const float* scales, const float* rotations, const float* opacities,
-                    const float* sh0, const float* sh_rest, int n, const gs3d_settings* settings, void* prim_buf,
-                    size_t prim_bytes_, uint32_t* num_instances, void* stream) {
+int gs3d_preprocess_count(const float* means, const float* scales, const float* rotations, const float* opacities,
+                          const float* sh0, const float* sh_rest, int n, const gs3d_settings* settings, void* prim_buf,
+                          size_t prim_bytes_, uint32_t* num_instances, void* stream) {
     Cam cam;
     SPLAT_TRY(fill_cam(settings, cam));
     SPLAT_REQUIRE(n >= 0 && n < (1 << 30), "gs3d_preprocess: n=%d out of range", n);
@@ -680,32 +685,47 @@ int gs3d_preprocess(const float* means, const float* scales, const float* rotati
     cudaStream_t st = as_stream(stream);
     Carver c(prim_buf, prim_bytes_);
     PrimBuffers pb = carve_prim(c, n);
-    if (n == 0) {
-        SPLAT_CUDA(cudaMemsetAsync(pb.counters, 0, 4 * sizeof(uint32_t), st));
-        if (num_instances) SPLAT_CUDA(cudaMemsetAsync(num_instances, 0, sizeof(uint32_t), st));
-        return SPLAT_OK;
+    SPLAT_CUDA(cudaMemsetAsync(pb.counters, 0, 4 * sizeof(uint32_t), st));
+    if (n > 0) {
+        Params P{means, scales, rotations, opacities, sh0, sh_rest, settings->w2c, settings->cam_position, n};
+        const size_t smem = static_cast<size_t>(kPreWarps) * 32 * cam.rest_bases * 3 * sizeof(float);
+        static bool configured = false;
+        if (!configured) {
+            SPLAT_CUDA(cudaFuncSetAttribute(k_preprocess, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            kPreWarps * 32 * kMaxRestBases * 3 * static_cast<int>(sizeof(float))));
+            configured = true;
+        }
+        k_preprocess<<<div_up(n, kPreThreads), kPreThreads, smem, st>>>(P, cam, pb);
+        note_launch();
+        SPLAT_TRY(check_launch("gs3d_preprocess"));
     }
-    Params P{means, scales, rotations, opacities, sh0, sh_rest, settings->w2c, settings->cam_position, n};
-    const size_t smem = static_cast<size_t>(kPreWarps) * 32 * cam.rest_bases * 3 * sizeof(float);
-    static bool configured = false;
-    if (!configured) {
-        SPLAT_CUDA(cudaFuncSetAttribute(k_preprocess, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        kPreWarps * 32 * kMaxRestBases * 3 * static_cast<int>(sizeof(float))));
-        configured = true;
-    }
-    k_preprocess<<<div_up(n, kPreThreads), kPreThreads, smem, st>>>(P, cam, pb);
-    note_launch();
-    SPLAT_TRY(check_launch("gs3d_preprocess"));
+    if (num_instances)
+        SPLAT_CUDA(cudaMemcpyAsync(num_instances, pb.counters + 3, sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
+    return SPLAT_OK;
+}
+
+int gs3d_preprocess_order(int n, void* prim_buf, size_t prim_bytes_, void* stream) {
+    SPLAT_REQUIRE(n >= 0 && n < (1 << 30), "gs3d_preprocess_order: n=%d out of range", n);
+    SPLAT_REQUIRE(prim_bytes_ >= prim_bytes(n), "gs3d_preprocess_order: primitive buffer too small");
+    if (n == 0) return SPLAT_OK;
+    cudaStream_t st = as_stream(stream);
+    Carver c(prim_buf, prim_bytes_);
+    PrimBuffers pb = carve_prim(c, n);
     // the depth-digit passes of the (tile << 32 | depth) key sort, on the Gaussians before duplication
     SPLAT_TRY(radix_sort_pairs<uint32_t>(pb.depth_key, pb.ids, pb.depth_key_sorted, pb.order, n, 0, 32, pb.sort_ws,
                                          pb.sort_bytes, st));
     k_gather_counts<<<div_up(n, 256), 256, 0, st>>>(pb.order, pb.n_touched, n, pb.offsets);
     note_launch();
     SPLAT_TRY(check_launch("gs3d_gather_counts"));
-    SPLAT_TRY(scan_exclusive_u32(pb.offsets, pb.offsets, n, pb.counters, pb.scan_ws, pb.scan_bytes, st));
-    if (num_instances)
-        SPLAT_CUDA(cudaMemcpyAsync(num_instances, pb.counters, sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
-    return SPLAT_OK;
+    return scan_exclusive_u32(pb.offsets, pb.offsets, n, pb.counters, pb.scan_ws, pb.scan_bytes, st);
+}
+
+int gs3d_preprocess(const float* means, const float* scales, const float* rotations, const float* opacities,
+                    const float* sh0, const float* sh_rest, int n, const gs3d_settings* settings, void* prim_buf,
+                    size_t prim_bytes_, uint32_t* num_instances, void* stream) {
+    SPLAT_TRY(gs3d_preprocess_count(means, scales, rotations, opacities, sh0, sh_rest, n, settings, prim_buf,
+                                    prim_bytes_, num_instances, stream));
+    return gs3d_preprocess_order(n, prim_buf, prim_bytes_, stream);
 }
 
 int gs3d_render(int n, long long num_instances, const gs3d_settings* settings, void* prim_buf, size_t prim_bytes_,

@@ -11,13 +11,15 @@ graphdeco-style (requested by the benchmark spec): rasterize_gaussians(means3D, 
 
 The rasterization rules are Faster-GS's (alpha = opacity * G with no 0.99 clamp, a pixel stops after the splat that
 drops T below 1e-4, (1 - alpha) floored at 1e-6 in the backward); they are listed in csrc/gs3d_common.cuh.
-One host read per forward (the instance count, to size the instance buffer); the bucket buffer is sized by a bound
-and ``n_buckets`` returns that bound, as phase2/tests/test_readback_equiv.py:100-104 allows.
+One host read per forward (the instance count, to size the instance buffer), taken while the device sorts the Gaussians
+by depth, so the device does not wait for it; the bucket buffer is sized by a bound and ``n_buckets`` returns that
+bound, as phase2/tests/test_readback_equiv.py:100-104 allows.
 """
 from __future__ import annotations
 
 import ctypes
 import math
+import threading
 from typing import Any, NamedTuple
 
 import torch
@@ -97,6 +99,21 @@ def _check_params(means, scales, rotations, opacities, sh0, sh_rest):
     return n, (sh_rest.numel() // (3 * n) if n else 0)
 
 
+_readback = threading.local()
+
+
+def _readback_slot(dev):
+    """(pinned int32[2], event) of this host thread and device: a forward waits on its read before it returns, so
+    one slot per thread and device is never in use twice at a time."""
+    slots = getattr(_readback, "slots", None)
+    if slots is None:
+        slots = _readback.slots = {}
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    if key not in slots:
+        slots[key] = (torch.empty(2, dtype=torch.int32, pin_memory=True), torch.cuda.Event())
+    return slots[key]
+
+
 def _preprocess(means, scales, rotations, opacities, sh0, sh_rest, settings_args):
     n, rest = _check_params(means, scales, rotations, opacities, sh0, sh_rest)
     dev = means.device
@@ -106,12 +123,18 @@ def _preprocess(means, scales, rotations, opacities, sh0, sh_rest, settings_args
     width, height = settings_args[4], settings_args[5]
     prim = torch.empty(L.query("gs3d_primitive_buffer_size", n), dtype=torch.uint8, device=dev)
     tile = torch.empty(L.query("gs3d_tile_buffer_size", width, height), dtype=torch.uint8, device=dev)
-    count = torch.zeros(2, dtype=torch.int32, device=dev)
-    L.call("gs3d_preprocess", L.ptr(means), L.ptr(scales), L.ptr(rotations), L.ptr(opacities), L.ptr(sh0),
+    count = torch.empty(2, dtype=torch.int32, device=dev)
+    L.call("gs3d_preprocess_count", L.ptr(means), L.ptr(scales), L.ptr(rotations), L.ptr(opacities), L.ptr(sh0),
            L.ptr(sh_rest), n, ctypes.byref(s), L.ptr(prim), prim.numel(), L.ptr(count), stream)
-    # the device's count of look-back waits that gave up (this depth sort, the previous forward's tile sort)
+    # the device's count of look-back waits that gave up (the sorts of the forwards before this one)
     L.call("splat_take_device_waits_async", L.ptr(count[1:]), stream)
-    m, waits = count.tolist()  # the one host read of a forward
+    host, counted = _readback_slot(dev)
+    host.copy_(count, non_blocking=True)
+    counted.record(torch.cuda.current_stream(dev))
+    # the depth order runs on the device while the host waits for M (the one host read of a forward)
+    L.call("gs3d_preprocess_order", n, L.ptr(prim), prim.numel(), stream)
+    counted.synchronize()
+    m, waits = host.tolist()
     if waits:
         raise RuntimeError(f"{waits} bounded device-side wait(s) in the radix sort gave up; results are unreliable")
     return n, dev, s, keep, stream, prim, tile, m

@@ -186,11 +186,15 @@ class Trainer:
             self.v = [torch.zeros_like(p) for p in self.params]
         self.n = self.params[0].shape[0]
         self.t = 0
+        self.settings = {}
         self.ev = {k: [] for k in ("fwd", "bwd", "comm", "adam", "blend_bwd")}
         self.last = None
 
     def step(self, cam: dict, dout: torch.Tensor, timed: bool):
-        s = scenes.settings_tuple(cam, self.bases, self.dev)
+        key = id(cam)  # the camera's settings are staged on the device once, as a training loop keeps them
+        if key not in self.settings:
+            self.settings[key] = scenes.settings_tuple(cam, self.bases, self.dev)
+        s = self.settings[key]
         e = [torch.cuda.Event(enable_timing=True) for _ in range(6)] if timed else None
         if timed:
             e[0].record()

@@ -197,10 +197,19 @@ long long gs3d_bucket_bound(long long num_instances, int width, int height);
 size_t gs3d_bucket_buffer_size(long long bucket_capacity);
 size_t gs3d_backward_workspace_size(int n);
 /* Forward, phase 1: projection, SH colour, conic, culling rectangle, exact listed-tile count and depth
- * per Gaussian, and the instance count M (device u32 *num_instances, may be NULL). */
+ * per Gaussian, and the instance count M (device u32 *num_instances, may be NULL). It is
+ * gs3d_preprocess_count followed by gs3d_preprocess_order. */
 int gs3d_preprocess(const float* means, const float* scales, const float* rotations, const float* opacities,
                     const float* sh0, const float* sh_rest, int n, const gs3d_settings* settings, void* prim_buf,
                     size_t prim_bytes, uint32_t* num_instances, void* stream);
+/* The two halves of gs3d_preprocess, so that the host can read M (written by the first) while the device
+ * runs the second: the per-Gaussian preprocess and M; then the depth order of the Gaussians and the
+ * instance offsets in that order (the reference's preprocess_cu + its depth sort, read back in one
+ * round trip in phase2/fastergs_readback.patch:48-56). */
+int gs3d_preprocess_count(const float* means, const float* scales, const float* rotations, const float* opacities,
+                          const float* sh0, const float* sh_rest, int n, const gs3d_settings* settings, void* prim_buf,
+                          size_t prim_bytes, uint32_t* num_instances, void* stream);
+int gs3d_preprocess_order(int n, void* prim_buf, size_t prim_bytes, void* stream);
 /* Forward, phase 2 (M read back by the host): duplication, 64-bit (tile | depth) key sort, tile ranges,
  * buckets, blend. image f32[3,H,W]; per-pixel final T and contributor counts stay in tile_buf. */
 int gs3d_render(int n, long long num_instances, const gs3d_settings* settings, void* prim_buf, size_t prim_bytes,
