@@ -65,6 +65,8 @@ struct Cam {
 // ---------------------------------------------------------------------------------------------
 // Per-Gaussian ("primitive") buffer, sized by N
 // ---------------------------------------------------------------------------------------------
+constexpr int kCounters = 8;  // the primitive buffer's device counters
+
 struct PrimBuffers {
     float2* mean2d;        // pixel units
     float4* conic_o;       // (A, B, C, opacity); power = -0.5 (A dx^2 + 2B dx dy + C dy^2)
@@ -77,7 +79,8 @@ struct PrimBuffers {
     uint32_t* depth_key_sorted;
     uint32_t* order;       // Gaussian ids in (depth, id) order: the depth passes of the 64-bit key sort
     uint32_t* offsets;     // exclusive prefix of n_touched, in that order
-    uint32_t* counters;    // [0] = instance count M, [1] = bucket count B, [2] = buckets the backward replays
+    uint32_t* counters;    // [0] = instance count M (offsets scan), [1] = bucket count B, [2] = buckets the
+                           // backward replays, [3] = M (k_count_instances, read by the host)
     void* scan_ws;
     size_t scan_bytes;
     void* sort_ws;
@@ -132,7 +135,7 @@ inline PrimBuffers carve_prim(Carver& c, int n) {
     b.depth_key_sorted = c.take<uint32_t>(nn);
     b.order = c.take<uint32_t>(nn);
     b.offsets = c.take<uint32_t>(nn);
-    b.counters = c.take<uint32_t>(4);
+    b.counters = c.take<uint32_t>(kCounters);
     b.scan_bytes = scan_workspace_bytes(static_cast<long long>(nn));
     b.scan_ws = c.take<unsigned char>(b.scan_bytes);
     b.sort_bytes = sort_workspace_bytes<uint32_t>(static_cast<long long>(nn));

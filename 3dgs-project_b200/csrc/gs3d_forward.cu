@@ -3,8 +3,8 @@
 //
 // Launch sequence of one forward (all on the caller's stream):
 //   gs3d_preprocess   k_preprocess (1 thread per Gaussian; SH rows loaded per warp with 16-byte
-//                     loads through shared memory; listed tiles counted row by row in closed form;
-//                     M summed on the device), then (gs3d_preprocess_order) radix sort of the
+//                     loads through shared memory; listed tiles counted row by row in closed form),
+//                     k_count_instances (M), then (gs3d_preprocess_order) radix sort of the
 //                     Gaussians by depth bits (the four depth-digit passes of the 64-bit
 //                     (tile << 32 | depth) key sort, done on N Gaussians instead of M instances),
 //                     tile counts gathered in that order and scanned
@@ -179,9 +179,6 @@ __global__ void __launch_bounds__(kPreThreads) k_preprocess(Params P, Cam cam, P
             }
         }
     }
-    // the instance count M, summed per warp (every lane of the block reaches this point)
-    const uint32_t warp_touched = __reduce_add_sync(kFullMask, touched);
-    if (lane == 0 && warp_touched) atomicAdd(pb.counters + 3, warp_touched);
     if (!valid) return;
     pb.n_touched[i] = touched;
     pb.ids[i] = static_cast<uint32_t>(i);
@@ -203,6 +200,30 @@ __global__ void k_gather_counts(const uint32_t* __restrict__ order, const uint32
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= n) return;
     counts_sorted[r] = n_touched[min(order[r], static_cast<uint32_t>(n - 1))];
+}
+
+// M = the sum of the listed-tile counts, one atomic per block (its own counter word, counters[3]).
+constexpr int kCountThreads = 256;
+constexpr int kCountItems = 16;
+__global__ void __launch_bounds__(kCountThreads) k_count_instances(const uint32_t* __restrict__ n_touched, int n,
+                                                                   uint32_t* __restrict__ total) {
+    __shared__ uint32_t s_warp[kCountThreads / 32];
+    const long long base = static_cast<long long>(blockIdx.x) * kCountThreads * kCountItems;
+    uint32_t sum = 0u;
+#pragma unroll
+    for (int k = 0; k < kCountItems; ++k) {
+        const long long i = base + k * kCountThreads + threadIdx.x;
+        if (i < n) sum += n_touched[i];
+    }
+    sum = __reduce_add_sync(kFullMask, sum);
+    if ((threadIdx.x & 31) == 0) s_warp[threadIdx.x >> 5] = sum;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t t = 0u;
+#pragma unroll
+        for (int w = 0; w < kCountThreads / 32; ++w) t += s_warp[w];
+        if (t) atomicAdd(total, t);
+    }
 }
 
 constexpr int kDupThreads = 256;
@@ -685,7 +706,7 @@ int gs3d_preprocess_count(const float* means, const float* scales, const float* 
     cudaStream_t st = as_stream(stream);
     Carver c(prim_buf, prim_bytes_);
     PrimBuffers pb = carve_prim(c, n);
-    SPLAT_CUDA(cudaMemsetAsync(pb.counters, 0, 4 * sizeof(uint32_t), st));
+    SPLAT_CUDA(cudaMemsetAsync(pb.counters, 0, kCounters * sizeof(uint32_t), st));
     if (n > 0) {
         Params P{means, scales, rotations, opacities, sh0, sh_rest, settings->w2c, settings->cam_position, n};
         const size_t smem = static_cast<size_t>(kPreWarps) * 32 * cam.rest_bases * 3 * sizeof(float);
@@ -698,6 +719,10 @@ int gs3d_preprocess_count(const float* means, const float* scales, const float* 
         k_preprocess<<<div_up(n, kPreThreads), kPreThreads, smem, st>>>(P, cam, pb);
         note_launch();
         SPLAT_TRY(check_launch("gs3d_preprocess"));
+        k_count_instances<<<div_up(n, kCountThreads * kCountItems), kCountThreads, 0, st>>>(pb.n_touched, n,
+                                                                                           pb.counters + 3);
+        note_launch();
+        SPLAT_TRY(check_launch("gs3d_count_instances"));
     }
     if (num_instances)
         SPLAT_CUDA(cudaMemcpyAsync(num_instances, pb.counters + 3, sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));

@@ -406,8 +406,8 @@ def primitive_views(prim_buf: torch.Tensor, n: int) -> dict[str, torch.Tensor]:
     """Typed views into a primitive buffer (the layout of carve_prim in csrc/gs3d_common.cuh):
     mean2d [N,2], conic_o [N,4] (A, B, C, opacity), color_z [N,4] (r, g, b, depth), rect [N,4] (int16 pixels),
     thr [N], n_touched [N] (int32), depth_key / ids / depth_key_sorted [N], order [N] (ids in depth order),
-    offsets [N] (instance offsets in that order), counters [4] (int32: instance count M, bucket count B). Per-Gaussian
-    values are valid where n_touched > 0."""
+    offsets [N] (instance offsets in that order), counters [8] (int32: instance count M, bucket count B, replayed
+    buckets, M again). Per-Gaussian values are valid where n_touched > 0."""
     nn = max(n, 1)
     off = 0
     out = {}
@@ -422,7 +422,7 @@ def primitive_views(prim_buf: torch.Tensor, n: int) -> dict[str, torch.Tensor]:
         out[name] = t.view(nn, width)[:n] if width > 1 else t[:n]
         off += elem * nn
     off = _align(off)
-    out["counters"] = prim_buf[off:off + 16].view(torch.int32)
+    out["counters"] = prim_buf[off:off + 32].view(torch.int32)
     out["rect"] = out["rect"].to(torch.int32) & 0xFFFF
     return out
 
