@@ -6,8 +6,8 @@
 //                     loads through shared memory; listed tiles counted row by row in closed form),
 //                     k_count_instances (M), then (gs3d_preprocess_order) radix sort of the
 //                     Gaussians by depth bits (the four depth-digit passes of the 64-bit
-//                     (tile << 32 | depth) key sort, done on N Gaussians instead of M instances),
-//                     tile counts gathered in that order and scanned
+//                     (tile << 32 | depth) key sort, done on N Gaussians instead of M instances; its
+//                     last pass gathers the tile counts into that order), the counts scanned
 //   (host reads M once to size the instance buffer, while the depth sort runs; the bucket buffer
 //   is sized by a bound)
 //   gs3d_render       k_duplicate in depth order, stable radix sort on the tile digits (completing
@@ -192,14 +192,6 @@ __global__ void __launch_bounds__(kPreThreads) k_preprocess(Params P, Cam cam, P
     pb.rect[i] = make_ushort4(static_cast<unsigned short>(rx0), static_cast<unsigned short>(ry0),
                               static_cast<unsigned short>(rx1), static_cast<unsigned short>(ry1));
     pb.thr[i] = thr;
-}
-
-// Tile counts in depth order (the input of the offsets scan).
-__global__ void k_gather_counts(const uint32_t* __restrict__ order, const uint32_t* __restrict__ n_touched, int n,
-                                uint32_t* __restrict__ counts_sorted) {
-    const int r = blockIdx.x * blockDim.x + threadIdx.x;
-    if (r >= n) return;
-    counts_sorted[r] = n_touched[min(order[r], static_cast<uint32_t>(n - 1))];
 }
 
 // M = the sum of the listed-tile counts, one atomic per block (its own counter word, counters[3]).
@@ -736,12 +728,10 @@ int gs3d_preprocess_order(int n, void* prim_buf, size_t prim_bytes_, void* strea
     cudaStream_t st = as_stream(stream);
     Carver c(prim_buf, prim_bytes_);
     PrimBuffers pb = carve_prim(c, n);
-    // the depth-digit passes of the (tile << 32 | depth) key sort, on the Gaussians before duplication
+    // the depth-digit passes of the (tile << 32 | depth) key sort, on the Gaussians before duplication; the last
+    // pass also gathers each Gaussian's tile count into depth order (the input of the offsets scan)
     SPLAT_TRY(radix_sort_pairs<uint32_t>(pb.depth_key, pb.ids, pb.depth_key_sorted, pb.order, n, 0, 32, pb.sort_ws,
-                                         pb.sort_bytes, st));
-    k_gather_counts<<<div_up(n, 256), 256, 0, st>>>(pb.order, pb.n_touched, n, pb.offsets);
-    note_launch();
-    SPLAT_TRY(check_launch("gs3d_gather_counts"));
+                                         pb.sort_bytes, st, pb.n_touched, pb.offsets));
     return scan_exclusive_u32(pb.offsets, pb.offsets, n, pb.counters, pb.scan_ws, pb.scan_bytes, st);
 }
 

@@ -280,7 +280,8 @@ __device__ __forceinline__ uint32_t look_back(const uint32_t* status, long long 
 // only waits on tiles that took their ticket earlier, which are running; every wait is bounded, and on
 // timeout the wait counter is raised and the pass completes (with wrong offsets) instead of hanging.
 // Pairs are then placed in digit order in shared memory and written out digit run by digit run.
-template <typename K>
+// kGather: the last pass also writes gather_out[i] = gather_table[value] for every output slot i.
+template <typename K, bool kGather>
 __global__ void __launch_bounds__(kSortThreads, kSortMinBlocks) k_sort_scatter(const K* __restrict__ keys_in,
                                                                const uint32_t* __restrict__ vals_in,
                                                                K* __restrict__ keys_out,
@@ -288,7 +289,9 @@ __global__ void __launch_bounds__(kSortThreads, kSortMinBlocks) k_sort_scatter(c
                                                                int shift, uint32_t mask,
                                                                const uint32_t* __restrict__ digit_base,
                                                                uint32_t* __restrict__ status,
-                                                               uint32_t* __restrict__ ticket) {
+                                                               uint32_t* __restrict__ ticket,
+                                                               const uint32_t* __restrict__ gather_table,
+                                                               uint32_t* __restrict__ gather_out) {
     static_assert(kRadix == kSortThreads, "one thread per digit");
     constexpr int kWarps = kSortThreads / 32;
     constexpr int kWarpItems = 32 * kSortRounds;
@@ -372,7 +375,9 @@ __global__ void __launch_bounds__(kSortThreads, kSortMinBlocks) k_sort_scatter(c
         const uint32_t d = digit_of(k, shift, mask);
         const long long g = static_cast<long long>(s_goff[d]) + (li - static_cast<int>(s_start[d]));
         keys_out[g] = k;
-        vals_out[g] = s_vals[li];
+        const uint32_t v = s_vals[li];
+        vals_out[g] = v;
+        if (kGather) gather_out[g] = gather_table[v];
     }
 }
 
@@ -380,7 +385,9 @@ template <typename K>
 int configure_scatter() {
     static bool done = false;  // one attribute call per instantiation and process
     if (!done) {
-        SPLAT_CUDA(cudaFuncSetAttribute(k_sort_scatter<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        SPLAT_CUDA(cudaFuncSetAttribute(k_sort_scatter<K, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(scatter_smem_bytes<K>())));
+        SPLAT_CUDA(cudaFuncSetAttribute(k_sort_scatter<K, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(scatter_smem_bytes<K>())));
         SPLAT_CUDA(cudaFuncSetAttribute(k_sort_global_hist<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(global_hist_smem_bytes(kMaxPasses))));
@@ -431,7 +438,8 @@ size_t sort_workspace_bytes(long long n) {
 
 template <typename K>
 int radix_sort_pairs(const K* keys_in, const uint32_t* vals_in, K* keys_out, uint32_t* vals_out, long long n,
-                     int begin_bit, int end_bit, void* ws, size_t ws_bytes, cudaStream_t stream) {
+                     int begin_bit, int end_bit, void* ws, size_t ws_bytes, cudaStream_t stream,
+                     const uint32_t* gather_table, uint32_t* gather_out) {
     constexpr int kKeyBits = static_cast<int>(sizeof(K) * 8);
     SPLAT_REQUIRE(0 <= begin_bit && begin_bit <= end_bit && end_bit <= kKeyBits, "bad bit range [%d, %d)",
                   begin_bit, end_bit);
@@ -439,6 +447,7 @@ int radix_sort_pairs(const K* keys_in, const uint32_t* vals_in, K* keys_out, uin
                   kCountMask);
     if (n == 0) return SPLAT_OK;
     const int passes = (end_bit - begin_bit + kRadixBits - 1) / kRadixBits;
+    SPLAT_REQUIRE(!gather_out || (gather_table && passes > 0), "radix_sort_pairs: a gather needs a table and a pass");
     if (passes == 0) {
         SPLAT_CUDA(cudaMemcpyAsync(keys_out, keys_in, n * sizeof(K), cudaMemcpyDeviceToDevice, stream));
         SPLAT_CUDA(cudaMemcpyAsync(vals_out, vals_in, n * sizeof(uint32_t), cudaMemcpyDeviceToDevice, stream));
@@ -473,9 +482,11 @@ int radix_sort_pairs(const K* keys_in, const uint32_t* vals_in, K* keys_out, uin
         const bool to_out = ((passes - 1 - p) % 2) == 0;
         K* dst_k = to_out ? keys_out : alt_keys;
         uint32_t* dst_v = to_out ? vals_out : alt_vals;
-        k_sort_scatter<K><<<static_cast<unsigned>(nb), kSortThreads, scatter_smem_bytes<K>(), stream>>>(
+        const bool gather = gather_out && p == passes - 1;
+        auto kernel = gather ? k_sort_scatter<K, true> : k_sort_scatter<K, false>;
+        kernel<<<static_cast<unsigned>(nb), kSortThreads, scatter_smem_bytes<K>(), stream>>>(
             src_k, src_v, dst_k, dst_v, n, shift, mask, hist + p * kRadix,
-            status + static_cast<size_t>(p) * nb * kRadix, tickets + p);
+            status + static_cast<size_t>(p) * nb * kRadix, tickets + p, gather_table, gather_out);
         note_launch();
         SPLAT_TRY(check_launch("radix_sort_pairs"));
         src_k = dst_k;
@@ -559,9 +570,10 @@ int scan_exclusive_u32_noalloc(const uint32_t* in, uint32_t* out, long long n, u
 template size_t sort_workspace_bytes<uint32_t>(long long);
 template size_t sort_workspace_bytes<unsigned long long>(long long);
 template int radix_sort_pairs<uint32_t>(const uint32_t*, const uint32_t*, uint32_t*, uint32_t*, long long, int,
-                                        int, void*, size_t, cudaStream_t);
+                                        int, void*, size_t, cudaStream_t, const uint32_t*, uint32_t*);
 template int radix_sort_pairs<unsigned long long>(const unsigned long long*, const uint32_t*, unsigned long long*,
-                                                  uint32_t*, long long, int, int, void*, size_t, cudaStream_t);
+                                                  uint32_t*, long long, int, int, void*, size_t, cudaStream_t,
+                                                  const uint32_t*, uint32_t*);
 
 }  // namespace splat
 

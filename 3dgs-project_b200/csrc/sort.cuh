@@ -46,11 +46,13 @@ template <typename K>
 size_t sort_workspace_bytes(long long n);
 
 // Stable sort of (key, value) pairs by key bits [begin_bit, end_bit). keys_in/vals_in are not
-// modified; results land in keys_out/vals_out (which must not alias the inputs).
+// modified; results land in keys_out/vals_out (which must not alias the inputs). With gather_out
+// (device, n entries), the last pass also writes gather_out[i] = gather_table[vals_out[i]].
 template <typename K>
 int radix_sort_pairs(const K* keys_in, const uint32_t* vals_in, K* keys_out, uint32_t* vals_out,
                      long long n, int begin_bit, int end_bit, void* ws, size_t ws_bytes,
-                     cudaStream_t stream);
+                     cudaStream_t stream, const uint32_t* gather_table = nullptr,
+                     uint32_t* gather_out = nullptr);
 
 // Number of significant bits needed to represent v (0 for v == 0).
 inline int bit_width(unsigned long long v) {
