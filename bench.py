@@ -324,8 +324,9 @@ def run_ours(args) -> None:
 def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
     """The training step through the public API (diff_rasterize + autograd + FusedAdam at N = 1, PeerAdam over
     the ranks at N > 1). Every step copies its upstream gradient from pinned host memory (on a copy stream, into
-    one of two device buffers, issued one step ahead so that the copy overlaps the previous step's kernels) and
-    copies its loss back into pinned host memory; all of those copies sit inside the timed region."""
+    one of two device buffers, issued one step ahead, after the forward's read of its instance count, so that the
+    copy overlaps the step's kernels) and copies its loss back into pinned host memory; all of those copies sit
+    inside the timed region."""
     peer = None
     if world > 1:  # the leaves are views of PeerAdam's parameter buffer; step() takes their .grad
         peer = gs_dist.PeerAdam([p.detach() for p in tr.params], [LRS[nm] for nm in NAMES], eps=1e-15)
@@ -356,10 +357,12 @@ def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
     def step(k):
         b = k % 2
         compute.wait_event(copied[b])
-        if k + 1 < total and k + 1 != args.warmup:  # the first timed step's copy is issued inside the timed region
-            issue_copy(k + 1)
         dout = dbuf[b]
         img = gs3d.diff_rasterize(*leaves, torch.empty(0), settings)
+        # the next step's copy goes out once this forward has read its instance count back, so that the 25 MB
+        # host-to-device copy never sits in front of that small device-to-host read
+        if k + 1 < total and k + 1 != args.warmup:  # the first timed step's copy is issued inside the timed region
+            issue_copy(k + 1)
         loss = (img * dout).sum()
         for p in leaves:
             p.grad = None
