@@ -30,9 +30,6 @@ namespace splat {
 namespace gs3d {
 
 constexpr int kBwdWarps = 4;
-#ifndef SPLAT_BWD_PY
-#define SPLAT_BWD_PY 0
-#endif
 #ifndef SPLAT_BWD_MIN_BLOCKS
 #define SPLAT_BWD_MIN_BLOCKS 7  // 72 registers (4 bytes spilled): 28 warps per SM instead of 20
 #endif
@@ -159,11 +156,6 @@ __global__ void __launch_bounds__(32 * kBwdWarps, SPLAT_BWD_MIN_BLOCKS) k_blend_
         }
         __syncwarp();
 
-#if SPLAT_BWD_PY
-        float pyr[kPxPerLane];  // the centres of this lane's pixel rows
-#pragma unroll
-        for (int r = 0; r < kPxPerLane; ++r) pyr[r] = static_cast<float>(y0 + 2 * r) + 0.5f;
-#endif
         for (int j = 0; j < bsize; ++j) {
             const float2 mm = s_mean[warp][j];
             const float4 co = s_con[warp][j];
@@ -180,11 +172,7 @@ __global__ void __launch_bounds__(32 * kBwdWarps, SPLAT_BWD_MIN_BLOCKS) k_blend_
                 if (rc.y > yb + 1 || rc.w < yb) continue;  // warp-uniform
                 const uint32_t l = ((r < 4 ? lim_lo : lim_hi) >> (8 * (r & 3))) & 0xffu;
                 if (!col_hit || static_cast<uint32_t>(j) >= l) continue;
-#if SPLAT_BWD_PY
-                const float dx = mm.x - pxf, dy = mm.y - pyr[r];
-#else
                 const float dx = mm.x - pxf, dy = mm.y - (static_cast<float>(y0 + 2 * r) + 0.5f);
-#endif
                 const float G = hw_exp2(fminf(blend_q2(co.x, co.y, co.z, dx, dy), 0.f));
                 const float alpha = co.w * G;
                 if (alpha < kAlphaMin) continue;
