@@ -31,7 +31,7 @@ namespace gs3d {
 
 constexpr int kBwdWarps = 4;
 #ifndef SPLAT_BWD_MIN_BLOCKS
-#define SPLAT_BWD_MIN_BLOCKS 7  // 72 registers (4 bytes spilled): 28 warps per SM instead of 20
+#define SPLAT_BWD_MIN_BLOCKS 7  // 72 registers, no spills: 28 warps per SM instead of 20
 #endif
 constexpr int kPxPerLane = kTilePixels / 32;  // 8
 constexpr int kPbThreads = 128;

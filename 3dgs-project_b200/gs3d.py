@@ -103,14 +103,17 @@ _readback = threading.local()
 
 
 def _readback_slot(dev):
-    """(pinned int32[2], event) of this host thread and device: a forward waits on its read before it returns, so
-    one slot per thread and device is never in use twice at a time."""
+    """(pinned int32[2], stream, event, event) of this host thread and device for the forward's one read: the copy
+    runs on its own stream, so the compute stream goes on with the depth order instead of waiting for the copy
+    engine. A forward waits on its read before it returns, so one slot per thread and device is never in use twice
+    at a time."""
     slots = getattr(_readback, "slots", None)
     if slots is None:
         slots = _readback.slots = {}
     key = dev.index if dev.index is not None else torch.cuda.current_device()
     if key not in slots:
-        slots[key] = (torch.empty(2, dtype=torch.int32, pin_memory=True), torch.cuda.Event())
+        slots[key] = (torch.empty(2, dtype=torch.int32, pin_memory=True), torch.cuda.Stream(key), torch.cuda.Event(),
+                      torch.cuda.Event())
     return slots[key]
 
 
@@ -128,9 +131,12 @@ def _preprocess(means, scales, rotations, opacities, sh0, sh_rest, settings_args
            L.ptr(sh_rest), n, ctypes.byref(s), L.ptr(prim), prim.numel(), L.ptr(count), stream)
     # the device's count of look-back waits that gave up (the sorts of the forwards before this one)
     L.call("splat_take_device_waits_async", L.ptr(count[1:]), stream)
-    host, counted = _readback_slot(dev)
-    host.copy_(count, non_blocking=True)
-    counted.record(torch.cuda.current_stream(dev))
+    host, side, ready, counted = _readback_slot(dev)
+    ready.record(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        side.wait_event(ready)
+        host.copy_(count, non_blocking=True)
+        counted.record(side)
     # the depth order runs on the device while the host waits for M (the one host read of a forward)
     L.call("gs3d_preprocess_order", n, L.ptr(prim), prim.numel(), stream)
     counted.synchronize()

@@ -119,13 +119,15 @@ class Clocks:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         sm = [float(r[1]) for r in inside if r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in inside if r[2].replace(".", "").isdigit()]
+        pw = [float(r[3]) for r in inside if r[3].replace(".", "").isdigit()]
         reasons = set()
         for r in inside:
             for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), r[5:9]):
                 if v.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(inside), "note": note}
+                "reasons": sorted(reasons), "samples": len(inside), "power_w": statistics.median(pw) if pw else None,
+                "note": note}
 
 
 def setup_dist(n_gpus: int):
@@ -245,15 +247,20 @@ def run_ours(args) -> None:
     sc, cams = scene_for(args.workload, rank, world)
     cam = cams[0]
     tr = Trainer(sc, dev, world, fuse=args.fuse)
-    g = torch.Generator().manual_seed(77 + rank)
     H, W = cam["height"], cam["width"]
-    dout = (1e-3 * torch.randn(3, H, W, generator=g)).to(dev)
+    # The upstream gradient is the config's fixed random image with its sign alternating step to step: under Adam a
+    # fixed gradient would move every parameter by about lr per step in one direction, and after a few hundred
+    # steps the scene (visible Gaussians, instances, blend depth) would no longer be the configured one. Alternating
+    # signs keep it there, so every timed step (and the end-to-end run, which restarts from the same parameters)
+    # renders the configured scene; the work of a step does not depend on the sign.
+    dout_host = upstream_gradient(rank, H, W)
+    douts = (dout_host.to(dev), (-dout_host).to(dev))
     views_per_step = len(cams)
 
     def one_step(timed):
         insts = []
         for c in cams:
-            insts.append(tr.step(c, dout, timed))
+            insts.append(tr.step(c, douts[tr.t % 2], timed))
         return insts
 
     for _ in range(args.warmup):
@@ -321,6 +328,11 @@ def run_ours(args) -> None:
         torch.distributed.destroy_process_group()
 
 
+def upstream_gradient(rank: int, H: int, W: int) -> torch.Tensor:
+    """The config's upstream gradient dL/dimage ~ N(0, 1e-3), seeded per rank (host, float32 [3, H, W])."""
+    return 1e-3 * torch.randn(3, H, W, generator=torch.Generator().manual_seed(77 + rank))
+
+
 def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
     """The training step through the public API (diff_rasterize + autograd + FusedAdam at N = 1, PeerAdam over
     the ranks at N > 1). Every step copies its upstream gradient from pinned host memory (on a copy stream, into
@@ -328,22 +340,25 @@ def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
     copy overlaps the step's kernels) and copies its loss back into pinned host memory; all of those copies sit
     inside the timed region."""
     peer = None
+    start = [sc[k].to(dev).contiguous() for k in NAMES]  # the configured scene, as the device-timed run started
     if world > 1:  # the leaves are views of PeerAdam's parameter buffer; step() takes their .grad
-        peer = gs_dist.PeerAdam([p.detach() for p in tr.params], [LRS[nm] for nm in NAMES], eps=1e-15)
+        peer = gs_dist.PeerAdam(start, [LRS[nm] for nm in NAMES], eps=1e-15)
         leaves = [p.requires_grad_(True) for p in peer.params]
     else:  # with fuse_backward the rasterizer's preprocess backward runs inside the optimizer's fused step
-        leaves = [p.clone().requires_grad_(True) for p in tr.params]
+        leaves = [p.requires_grad_(True) for p in start]
         opt = gs_adam.FusedAdam([{"params": [p], "lr": LRS[nm]} for p, nm in zip(leaves, NAMES)], lr=0.0,
                                 eps=1e-15, fuse_backward=tr.fuse)
     cam = cams[0]
     H, W = cam["height"], cam["width"]
-    host = (1e-3 * torch.randn(3, H, W, generator=torch.Generator().manual_seed(99))).pin_memory()
+    rank = torch.distributed.get_rank() if world > 1 else 0
+    host = upstream_gradient(rank, H, W).pin_memory()  # as in the device-timed run, its sign alternating
     settings = gs3d.RasterizerSettings(*scenes.settings_tuple(cam, tr.bases, dev))
     compute = torch.cuda.current_stream(dev)
     copier = torch.cuda.Stream(dev)
     dbuf = [torch.empty_like(host, device=dev) for _ in range(2)]
     copied = [torch.cuda.Event() for _ in range(2)]
     used = [torch.cuda.Event() for _ in range(2)]
+    done = [torch.cuda.Event() for _ in range(2)]
     total = args.warmup + args.steps
     losses = torch.empty(total, dtype=torch.float32).pin_memory()
 
@@ -363,7 +378,7 @@ def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
         # host-to-device copy never sits in front of that small device-to-host read
         if k + 1 < total and k + 1 != args.warmup:  # the first timed step's copy is issued inside the timed region
             issue_copy(k + 1)
-        loss = (img * dout).sum()
+        loss = (img * dout).sum() if k % 2 == 0 else -(img * dout).sum()
         for p in leaves:
             p.grad = None
         loss.backward()
@@ -372,7 +387,12 @@ def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
             peer.step(grads=[p.grad for p in leaves])
         else:
             opt.step()
-        losses[k:k + 1].copy_(loss.detach().view(1), non_blocking=True)
+        # the loss goes back to the host on the copy stream, so the compute stream does not wait for the copy
+        done[b].record(compute)
+        with torch.cuda.stream(copier):
+            copier.wait_event(done[b])
+            losses[k:k + 1].copy_(loss.detach().view(1), non_blocking=True)
+            loss.record_stream(copier)
 
     for e in used:
         e.record(compute)
@@ -383,13 +403,17 @@ def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
     if world > 1:
         torch.distributed.barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(compute)
-    copier.wait_stream(compute)  # the first timed copy starts after the timed region does
-    issue_copy(args.warmup)
-    for k in range(args.warmup, total):
-        step(k)
-    b.record(compute)
-    torch.cuda.synchronize()
+    with Clocks(dev.index) as clk:
+        clk.mark_start()
+        a.record(compute)
+        copier.wait_stream(compute)  # the first timed copy starts after the timed region does
+        issue_copy(args.warmup)
+        for k in range(args.warmup, total):
+            step(k)
+        compute.wait_stream(copier)  # the last step's loss has reached the host when the region ends
+        b.record(compute)
+        torch.cuda.synchronize()
+        clk.mark_end()
     assert bool(torch.isfinite(losses).all())
     ms = torch.tensor([a.elapsed_time(b)], device=dev)
     if world > 1:
@@ -401,9 +425,10 @@ def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
         peer.close()
     gs3d._Rasterize.fused_optimizer = None
     return {"value": round(world * args.steps / (float(ms.item()) / 1000.0), 3), "unit": "views/s",
-            "h2d_bytes_per_step": int(host.numel() * 4), "d2h_bytes_per_step": 4,
-            "note": "upstream gradient copied from pinned host memory one step ahead on a copy stream; loss copied "
-                    "back to pinned host memory every step"}
+            "h2d_bytes_per_step": int(host.numel() * 4), "d2h_bytes_per_step": 4, "clocks": clk.summary(),
+            "note": "from the configured scene, as the device-timed run; upstream gradient (sign alternating step to "
+                    "step) copied from pinned host memory one step ahead on a copy stream; loss copied back to pinned "
+                    "host memory every step, on the copy stream"}
 
 
 def blend_reach(tr: Trainer, width: int, height: int) -> dict:
