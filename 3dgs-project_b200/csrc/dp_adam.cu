@@ -8,6 +8,7 @@
 // gradients in, its parameters out) and each rank does 1/G of the optimizer work. The kernel waits on nothing;
 // the caller orders it between two device-side barriers (see the header).
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 
 #include "adam_math.cuh"
@@ -189,6 +190,16 @@ __global__ void __launch_bounds__(kThreads) k_dp_adam_nvls(NvlsArgs a) {
 
 using namespace splat;
 
+namespace {
+// Resident blocks per SM the exchange kernels are launched with (SPLAT_DP_BLOCKS_PER_SM, 1 to 32, default 8),
+// read on every call so that one process can compare settings.
+long long dp_blocks_per_sm() {
+    const char* v = getenv("SPLAT_DP_BLOCKS_PER_SM");
+    const long long k = v ? atoll(v) : 8;
+    return k < 1 ? 1 : (k > 32 ? 32 : k);
+}
+}  // namespace
+
 extern "C" {
 
 int splat_peer_alloc(size_t bytes, void** ptr, unsigned char* ipc_handle) {
@@ -268,7 +279,7 @@ int adam_step_dp_fused(int world, int rank, const float* const* grads, float* co
     a.eps = static_cast<float>(eps);
     a.bc2_sqrt_rcp = static_cast<float>(1.0 / sqrt(1.0 - pow(beta2, step)));
     const long long n4 = (hi - lo) / 4;
-    const long long blocks = std::max<long long>(1, std::min<long long>(div_up(n4, dp::kThreads), 8ll * sm_count()));
+    const long long blocks = std::max<long long>(1, std::min<long long>(div_up(n4, dp::kThreads), dp_blocks_per_sm() * sm_count()));
     cudaStream_t st = as_stream(stream);
     const unsigned nb = static_cast<unsigned>(blocks);
     switch (world) {
@@ -320,7 +331,7 @@ int adam_step_dp_nvls(long long lo, long long hi, const float* grads_mc, float* 
     a.eps = static_cast<float>(eps);
     a.bc2_sqrt_rcp = static_cast<float>(1.0 / sqrt(1.0 - pow(beta2, step)));
     const long long n4 = (hi - lo) / 4;
-    const long long blocks = std::max<long long>(1, std::min<long long>(div_up(n4, dp::kThreads), 8ll * sm_count()));
+    const long long blocks = std::max<long long>(1, std::min<long long>(div_up(n4, dp::kThreads), dp_blocks_per_sm() * sm_count()));
     dp::k_dp_adam_nvls<<<static_cast<unsigned>(blocks), dp::kThreads, 0, as_stream(stream)>>>(a);
     note_launch();
     return check_launch("adam_step_dp_nvls");
