@@ -697,13 +697,82 @@ def run_c5(args) -> None:
         torch.distributed.destroy_process_group()
 
 
+# The reference's toy2d kernel timings on an H100 (toy2d/results/bench-cfda5b4-4473561.json): (size, n) ->
+# (forward, forward saving buckets, backward pixel, backward splat) in ms, CUDA-event medians.
+GS2D_H100_MS = {
+    (512, 10000): (0.0760, 0.0814, 0.3039, 0.1671), (512, 50000): (0.0895, 0.0956, 0.2410, 0.2572),
+    (512, 200000): (0.1912, 0.2227, 0.2844, 0.4969), (1024, 10000): (0.0866, 0.1007, 1.1088, 0.3631),
+    (1024, 50000): (0.1259, 0.1463, 0.8664, 0.4918), (1024, 200000): (0.2252, 0.2700, 0.7995, 0.8257),
+}
+
+
+def run_gs2d(args) -> None:
+    """The reference's toy2d kernel benchmark (toy2d/bench.py:43-70) through this library's gs2d ext(): the same
+    seeded Gaussians2D scenes (bit-exact binning, so the same pairs and buckets), the same four kernels, CUDA-event
+    medians; the reference's H100 figures beside them where it published the configuration."""
+    from gs_b200 import gs2d
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    e = gs2d.ext()
+    rows = []
+    launches0 = L.query("splat_launch_count")
+
+    def timed(fn, warmup, iters):
+        for _ in range(warmup):
+            fn()
+        times = []
+        for _ in range(iters):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(b))
+        return statistics.median(times)
+
+    for size in (512, 1024):
+        for n in (10_000, 50_000, 200_000):
+            H = W = size
+            g = gs2d.Gaussians2D(n, H, W, seed=0).to(dev)
+            with torch.no_grad():
+                means, conic, color, opacity, cov = (t.contiguous() for t in g.activated())
+                bins = gs2d.bin_gaussians(means, gs2d.radii_from_cov(cov), g.depth, H, W)
+            bg = torch.zeros(3, device=dev)
+            dout = torch.randn(3, H, W, generator=torch.Generator(device=dev).manual_seed(1), device=dev)
+            common = (means, conic, color, opacity, bg, bins.ranges, bins.point_list)
+
+            def fwd(save):
+                return e.forward(*common, bins.bucket_offsets, bins.num_buckets, H, W, save)
+
+            out, final_T, n_contrib, _ = fwd(False)
+            out_s, final_T_s, n_contrib_s, bstate = fwd(True)
+            w, it = max(args.warmup, 5), max(args.steps, 20)
+            r = {"size": size, "n": n, "pairs": int(bins.point_list.numel()), "buckets": int(bins.num_buckets),
+                 "forward_ms": timed(lambda: fwd(False), w, it),
+                 "forward_save_buckets_ms": timed(lambda: fwd(True), w, it),
+                 "backward_pixel_ms": timed(lambda: e.backward_pixel(*common, final_T, n_contrib, dout), w, it),
+                 "backward_splat_ms": timed(lambda: e.backward_splat(*common, bins.bucket_offsets, bins.bucket_to_tile,
+                                                                     out_s, final_T_s, n_contrib_s, bstate, dout),
+                                            w, it)}
+            ref = GS2D_H100_MS.get((size, n))
+            if ref:
+                r["reference_h100_ms"] = dict(zip(("forward", "forward_save_buckets", "backward_pixel",
+                                                   "backward_splat"), ref))
+            rows.append({k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()})
+    print(json.dumps({"metric": "toy2d kernel ms (the reference's toy2d/bench.py sweep)", "unit": "ms",
+                      "higher_is_better": False, "n_gpus": 1, "data": "synthetic (the reference's seeded scenes)",
+                      "dtype": "f32", "results": rows,
+                      "gpu_launches": L.query("splat_launch_count") - launches0}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c3", "c4", "c2", "c1", "c5"], default="c3")
+    ap.add_argument("--workload", choices=["c3", "c4", "c2", "c1", "c5", "gs2d"], default="c3")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for the baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--fuse", action="store_true",
@@ -718,6 +787,8 @@ def main() -> None:
         run_c1(args)
     elif args.workload == "c5":
         run_c5(args)
+    elif args.workload == "gs2d":
+        run_gs2d(args)
     else:
         run_ours(args)
 

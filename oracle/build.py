@@ -8,6 +8,11 @@
                              splat2d_cpu.cpp, compiled in place from the reference tree with g++)
                              behind oracle/splat2d_ref_capi.cpp; built only where the reference
                              tree exists (REFERENCE_ROOT or --reference)
+  oracle/_ref/gs2d_cuda_ref/gs2d_cuda_ref.so   the reference's own toy2d CUDA rasterizer
+                             (toy2d/csrc/rasterize.cu, the extension toy2d/gs2d/raster.py:13-26 JIT-builds),
+                             compiled from the reference tree for sm_100a by torch's extension builder into
+                             that folder - a GPU comparator for the gs2d parity tests, loaded there as a
+                             module from the built file (the reference tree is not on the GPU box)
 
 Built files are git-ignored; they travel to the GPU box with the working tree.
 """
@@ -58,11 +63,32 @@ def build(reference: str | None = None) -> None:
         _compile(HERE / "liboracle.so", mine, FLAGS + ["-fopenmp"], list(HERE.glob("*.h")))
     ref = reference_root(reference)
     if ref is not None:
+        build_toy2d_cuda_ref(ref)
         mt = ref / "phase0" / "csrc" / "macrotile"
         if (mt / "splat2d_cpu.cpp").exists():
             REF_OUT.mkdir(exist_ok=True)
             _compile(REF_OUT / "libsplat2d_ref.so", [HERE / "splat2d_ref_capi.cpp", mt / "splat2d_cpu.cpp"],
                      FLAGS + [f"-I{mt}"], [mt / "splat2d_common.h"])
+
+
+TOY2D_REF_NAME = "gs2d_cuda_ref"
+
+
+def build_toy2d_cuda_ref(ref: Path) -> Path | None:
+    """The reference's toy2d CUDA extension, built for sm_100a into oracle/_ref/gs2d_cuda_ref (ninja keeps it
+    current). Returns the built module file, or None when the reference's source is absent."""
+    src = ref / "toy2d" / "csrc" / "rasterize.cu"
+    if not src.exists():
+        return None
+    out_dir = REF_OUT / TOY2D_REF_NAME
+    out_dir.mkdir(parents=True, exist_ok=True)
+    os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0")
+    from torch.utils.cpp_extension import load
+
+    load(name=TOY2D_REF_NAME, sources=[str(src)], build_directory=str(out_dir),
+         extra_cuda_cflags=["-O3", "-gencode", "arch=compute_100a,code=sm_100a"], verbose=False)
+    built = out_dir / f"{TOY2D_REF_NAME}.so"
+    return built if built.exists() else None
 
 
 def main() -> int:
