@@ -281,6 +281,9 @@ static FillScratch carve_fill(Carver& c, long long m, int T) {
 // ---------------------------------------------------------------------------------------------
 // Forward: one 256-thread block per 16x16 tile, one pixel per thread (rasterize.cu:106-177)
 // ---------------------------------------------------------------------------------------------
+// kSave: the (T, C) state of every pixel is written at the start of each 32-splat bucket (bucket_state non-null).
+// The splats of a staged batch are walked bucket by bucket, so the save is decided once per bucket.
+template <bool kSave>
 __global__ void __launch_bounds__(kBlock) k_forward(const int2* __restrict__ ranges,
                                                     const int32_t* __restrict__ point_list,
                                                     const float* __restrict__ means, const float* __restrict__ conic,
@@ -314,27 +317,31 @@ __global__ void __launch_bounds__(kBlock) k_forward(const int2* __restrict__ ran
         if (k < range.y) s_splat[tid] = load_splat(clamp_id(point_list[k], N), means, conic, color, opacity);
         __syncthreads();
         const int n = min(kBlock, todo - r * kBlock);
-        for (int j = 0; j < n; ++j) {
-            const int idx = r * kBlock + j;
-            const int bkt = bbase + idx / kBucket;
-            if (bucket_state && (idx % kBucket) == 0 && bkt >= 0 && bkt < num_buckets)
-                bucket_state[static_cast<size_t>(bkt) * kBlock + tid] = make_float4(T, Cr, Cg, Cb);
-            if (done) continue;
-            const Splat& s = s_splat[j];
-            float dx, dy, G, alpha;
-            bool clamped;
-            if (!eval_splat(s, fpx, fpy, dx, dy, G, alpha, clamped)) continue;
-            const float test_T = T * (1.0f - alpha);
-            if (test_T < kTMin) {
-                done = true;
-                continue;
+        for (int j0 = 0; j0 < n; j0 += kBucket) {  // kBlock is a whole number of buckets
+            if (kSave) {
+                const int bkt = bbase + (r * kBlock + j0) / kBucket;
+                if (bkt >= 0 && bkt < num_buckets)
+                    bucket_state[static_cast<size_t>(bkt) * kBlock + tid] = make_float4(T, Cr, Cg, Cb);
             }
-            const float w = alpha * T;
-            Cr += s.r * w;
-            Cg += s.g * w;
-            Cb += s.b * w;
-            T = test_T;
-            last = idx + 1;
+            if (done) continue;
+            const int j1 = min(j0 + kBucket, n);
+            for (int j = j0; j < j1; ++j) {
+                const Splat& s = s_splat[j];
+                float dx, dy, G, alpha;
+                bool clamped;
+                if (!eval_splat(s, fpx, fpy, dx, dy, G, alpha, clamped)) continue;
+                const float test_T = T * (1.0f - alpha);
+                if (test_T < kTMin) {
+                    done = true;
+                    break;
+                }
+                const float w = alpha * T;
+                Cr += s.r * w;
+                Cg += s.g * w;
+                Cb += s.b * w;
+                T = test_T;
+                last = r * kBlock + j + 1;
+            }
         }
     }
     if (inside) {
@@ -660,10 +667,12 @@ int gs2d_forward(const float* means, const float* conic, const float* color, con
     SPLAT_REQUIRE(!save_buckets || num_buckets == 0 || bucket_state, "gs2d_forward: bucket_state missing");
     const int tiles_x = (W + kTile - 1) / kTile, tiles_y = (H + kTile - 1) / kTile;
     const dim3 grid(tiles_x, tiles_y), block(kBlock);
-    k_forward<<<grid, block, 0, as_stream(stream)>>>(
+    const bool save = save_buckets && num_buckets > 0;
+    auto kernel = save ? k_forward<true> : k_forward<false>;
+    kernel<<<grid, block, 0, as_stream(stream)>>>(
         reinterpret_cast<const int2*>(ranges), point_list, means, conic, color, opacity, bg, N,
         static_cast<int>(num_instances), num_buckets, W, H, tiles_x, out, final_T, n_contrib, bucket_offsets,
-        (save_buckets && num_buckets > 0) ? reinterpret_cast<float4*>(bucket_state) : nullptr);
+        save ? reinterpret_cast<float4*>(bucket_state) : nullptr);
     note_launch();
     return check_launch("gs2d_forward");
 }
