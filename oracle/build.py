@@ -13,6 +13,10 @@
                              compiled from the reference tree for sm_100a by torch's extension builder into
                              that folder - a GPU comparator for the gs2d parity tests, loaded there as a
                              module from the built file (the reference tree is not on the GPU box)
+  oracle/_ref/splat2d_cuda_ref/splat2d_cuda_ref.so   the reference's own splat2d extension with its CUDA
+                             kernels (phase0/csrc/macrotile: bindings.cpp, splat2d_cpu.cpp, splat2d_fwd.cu,
+                             splat2d_bwd_pixel.cu, splat2d_bwd_splat.cu, the sources and -DWITH_CUDA build of
+                             phase0/splat2d/ops.py:33-45 with an sm_100a target), built the same way
 
 Built files are git-ignored; they travel to the GPU box with the working tree.
 """
@@ -64,6 +68,7 @@ def build(reference: str | None = None) -> None:
     ref = reference_root(reference)
     if ref is not None:
         build_toy2d_cuda_ref(ref)
+        build_splat2d_cuda_ref(ref)
         mt = ref / "phase0" / "csrc" / "macrotile"
         if (mt / "splat2d_cpu.cpp").exists():
             REF_OUT.mkdir(exist_ok=True)
@@ -88,6 +93,28 @@ def build_toy2d_cuda_ref(ref: Path) -> Path | None:
     load(name=TOY2D_REF_NAME, sources=[str(src)], build_directory=str(out_dir),
          extra_cuda_cflags=["-O3", "-gencode", "arch=compute_100a,code=sm_100a"], verbose=False)
     built = out_dir / f"{TOY2D_REF_NAME}.so"
+    return built if built.exists() else None
+
+
+SPLAT2D_REF_NAME = "splat2d_cuda_ref"
+
+
+def build_splat2d_cuda_ref(ref: Path) -> Path | None:
+    """The reference's splat2d extension with CUDA, built for sm_100a into oracle/_ref/splat2d_cuda_ref."""
+    mt = ref / "phase0" / "csrc" / "macrotile"
+    names = ("splat2d_cpu.cpp", "bindings.cpp", "splat2d_fwd.cu", "splat2d_bwd_pixel.cu", "splat2d_bwd_splat.cu")
+    if not all((mt / nm).exists() for nm in names):
+        return None
+    out_dir = REF_OUT / SPLAT2D_REF_NAME
+    out_dir.mkdir(parents=True, exist_ok=True)
+    os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0")
+    from torch.utils.cpp_extension import load
+
+    load(name=SPLAT2D_REF_NAME, sources=[str(mt / nm) for nm in names], build_directory=str(out_dir),
+         extra_cflags=["-O2", "-DWITH_CUDA"],
+         extra_cuda_cflags=["-O2", "-std=c++17", "-DWITH_CUDA", "-gencode", "arch=compute_100a,code=sm_100a"],
+         extra_include_paths=[str(mt)], with_cuda=True, verbose=False)
+    built = out_dir / f"{SPLAT2D_REF_NAME}.so"
     return built if built.exists() else None
 
 
