@@ -24,7 +24,10 @@
 namespace splat {
 namespace gs3d {
 
-constexpr int kPreThreads = 128;
+#ifndef SPLAT_PRE_THREADS
+#define SPLAT_PRE_THREADS 128
+#endif
+constexpr int kPreThreads = SPLAT_PRE_THREADS;
 constexpr int kPreWarps = kPreThreads / 32;
 constexpr int kMaxRestBases = 15;
 
@@ -218,7 +221,10 @@ __global__ void __launch_bounds__(kCountThreads) k_count_instances(const uint32_
     }
 }
 
-constexpr int kDupThreads = 256;
+#ifndef SPLAT_DUP_THREADS
+#define SPLAT_DUP_THREADS 256
+#endif
+constexpr int kDupThreads = SPLAT_DUP_THREADS;
 #ifndef SPLAT_DUP_STAGE
 #define SPLAT_DUP_STAGE 2048
 #endif
