@@ -96,10 +96,11 @@ class _CudaExtension:
                                             (tile_offsets, tile_ids, bucket_offsets, bucket_tile), height, width)
         H, W = int(height), int(width)
         opts = dict(dtype=m.dtype, device=m.device)
-        image = torch.zeros(H, W, 3, **opts)
-        t_final = torch.ones(H, W, **opts)
-        n_contrib = torch.zeros(H, W, dtype=torch.int32, device=m.device)
-        last_contrib = torch.zeros(H, W, dtype=torch.int32, device=m.device)
+        # the kernel writes every pixel of these four (one thread per pixel of every tile), so no fill is needed
+        image = torch.empty(H, W, 3, **opts)
+        t_final = torch.empty(H, W, **opts)
+        n_contrib = torch.empty(H, W, dtype=torch.int32, device=m.device)
+        last_contrib = torch.empty(H, W, dtype=torch.int32, device=m.device)
         B = int(tabs[3].numel())
         ckpt = torch.empty(B, TILE_PIXELS, CKPT_STRIDE, **opts)
         L.call("splat2d_forward", int(m.dtype == torch.float64), L.ptr(m), L.ptr(c), L.ptr(z), L.ptr(col),
