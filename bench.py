@@ -1,20 +1,22 @@
 """Benchmark of the 3DGS training step on B200, one process per GPU.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c3|c4|c2|c1|c5]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c3|c4|c2|c1|c5|gs2d]
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \
         bench.py --gpus N --steps K --warmup W
 
 Workload (default c3): the scene of config C3 - 3M Gaussians from 64 isotropic clusters, SH degree 3, seeded
 synthetic parameters (no dataset is available) - rendered at 1920x1080 / 60 deg. One step on each rank is the
-training step of one view: forward, backward with dL/dimage ~ N(0, 1e-3), then Adam over the six parameter groups
+training step of one view: forward, backward with dL/dimage ~ N(0, 1e-3) (one fixed seeded image whose sign
+alternates step to step, so that Adam keeps the scene at its configured state), then Adam over the six parameter groups
 (N = 1: one fused Adam launch; N > 1: the gradient exchange and Adam as one peer-memory kernel per rank,
 dist.PeerAdam). Each rank renders its own view (a seeded camera at radius 12), so the work per GPU is fixed as N
 grows (weak scaling) and
     value = N * K / (max over ranks of the device time of K steps)  [views/s],  ms_per_step = that time / K.
 The Gaussian state (2.8 GB with moments) is far larger than the 126 MB L2, so no flush is needed between steps.
 ``e2e`` runs the same step through the public API (diff_rasterize + autograd + FusedAdam, PeerAdam for N > 1)
-with the upstream gradient copied from pinned host memory every step and the loss read back. --workload c1 / c5
-measure the toy2d fit step and the render-only orbit instead (their own metric lines).
+with the upstream gradient copied from pinned host memory every step and the loss read back, starting from the same
+configured parameters. --workload c1 / c5 measure the toy2d fit step and the render-only orbit instead, and
+--workload gs2d the reference's toy2d kernel sweep (their own metric lines).
 
 --impl reference times the CPU restatement of the same step (oracle/liboracle.so, OpenMP over all host cores)
 on rank 0 only, over a bounded sample (a horizontal band of the image), and reports the same metric.
