@@ -139,12 +139,33 @@ class MulticastFlat:
         self.ptrs = list(self._handle.buffer_ptrs)
         self.mc = int(self._handle.multicast_ptr)
 
-    def close(self) -> None:
+    def close(self, barrier: bool = True) -> None:
         if self.tensor is None:
             return
-        dist.barrier(group=self.group)  # nobody addresses this buffer any more
+        if barrier:
+            dist.barrier(group=self.group)  # nobody addresses this buffer any more
         self.tensor = None
         self._handle = None
+
+
+def agree_on_buffers(make, count: int, group=None, device=None):
+    """Make `count` multicast buffers with `make()` on every rank and return them where every rank made them all
+    with a multicast address; otherwise close this rank's (no rank has addressed them, so without a barrier) and
+    return None. Every rank gets the same answer, also when the buffers failed on some ranks only."""
+    made = []
+    try:
+        for _ in range(count):
+            made.append(make())
+        usable = int(all(b.mc != 0 for b in made))
+    except (RuntimeError, ImportError, AttributeError):
+        usable = 0
+    ok = torch.tensor([usable], device=device)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+    if int(ok.item()):
+        return made
+    for b in made:
+        b.close(barrier=False)
+    return None
 
 
 class PeerAdam:
@@ -187,17 +208,9 @@ class PeerAdam:
         self.nvls = False
         if nvls and self.world > 1:
             padded = (self.total + 3) // 4 * 4  # the multicast kernel moves whole 16-byte groups
-            try:
-                pb, gb = MulticastFlat(padded, group, dev), MulticastFlat(padded, group, dev)
-                ok = torch.tensor([int(pb.mc != 0 and gb.mc != 0)], device=dev)
-                dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)  # every rank takes the same path
-                if int(ok.item()):
-                    self.param_buf, self.grad_buf, self.nvls = pb, gb, True
-                else:
-                    pb.close()
-                    gb.close()
-            except (RuntimeError, ImportError, AttributeError):
-                self.nvls = False
+            bufs = agree_on_buffers(lambda: MulticastFlat(padded, group, dev), 2, group, dev)
+            if bufs is not None:
+                self.param_buf, self.grad_buf, self.nvls = bufs[0], bufs[1], True
         if not self.nvls:
             self.param_buf = PeerFlat(self.total, group, dev)
             self.grad_buf = PeerFlat(self.total, group, dev)

@@ -125,3 +125,61 @@ def test_owned_slices_tile_the_vector():
             assert all(lo <= hi and (lo % 4 == 0 or lo == hi) for lo, hi in spans)
     with pytest.raises(ValueError):
         gdist.owned_slice(10, 2, 2)
+
+
+class _FakeMulticast:
+    """Stands in for MulticastFlat on the host: a multicast address, or none, and a record of how it was closed."""
+
+    closed: list = []
+
+    def __init__(self, mc: int):
+        self.mc = mc
+
+    def close(self, barrier: bool = True) -> None:
+        _FakeMulticast.closed.append(barrier)
+
+
+def _agree_worker(rank, world, port, q, case):
+    try:
+        _init(rank, world, port, timeout_s=30)
+        made = [0]
+
+        def make():
+            made[0] += 1
+            if case == "raises" and rank == 1 and made[0] == 2:  # the second buffer fails on one rank only
+                raise RuntimeError("no multicast object")
+            return _FakeMulticast(0 if case == "no_mc" and rank == 0 else 0x1000 * made[0])
+
+        got = gdist.agree_on_buffers(make, 2)
+        # the ranks then take the same next collective step whichever way they went
+        t = torch.tensor([1.0])
+        dist.all_reduce(t)
+        q.put((rank, None if got is None else len(got), list(_FakeMulticast.closed), float(t.item())))
+        dist.destroy_process_group()
+    except Exception as exc:  # report instead of hanging the parent
+        q.put((rank, "error", repr(exc), 0.0))
+
+
+@pytest.mark.parametrize("case", ["ok", "raises", "no_mc"])
+def test_ranks_agree_on_the_multicast_buffers(case):
+    """PeerAdam's choice of the multicast form: the same answer on every rank, also when the buffers fail or lack a
+    multicast address on one rank only; what was made is closed without a barrier (a failure injected on the
+    host, in the buffer factory)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_agree_worker, args=(r, 2, port, q, case)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for rank, got, closed, total in res:
+        assert got != "error", closed
+        assert total == 2.0
+        if case == "ok":
+            assert got == 2 and closed == []
+        else:
+            assert got is None
+            assert closed and not any(closed)  # closed, and never with a barrier
+    assert {r[0] for r in res} == {0, 1}
