@@ -115,9 +115,16 @@ __device__ __forceinline__ uint16_t float_to_bf16_sr(float f, uint32_t rnd) {
     return static_cast<uint16_t>((__float_as_uint(f) + (rnd & 0xFFFFu)) >> 16);
 }
 
+// The primitive that element i of the group belongs to: a 32-bit division where the group's element count allows
+// (every group of a scene below 2^32 elements), a 64-bit one otherwise.
+__device__ __forceinline__ long long primitive_of(const LeanGroup& G, long long i) {
+    if (G.n <= 0xFFFFFFFFll) return static_cast<uint32_t>(i) / static_cast<uint32_t>(G.features);
+    return i / G.features;
+}
+
 template <bool kLowp>
 __device__ __forceinline__ void lean_one(const LeanGroup& G, const LeanTable& t, long long i) {
-    if (t.visibility && t.visibility[i / G.features] == 0) return;
+    if (t.visibility && t.visibility[primitive_of(G, i)] == 0) return;
     const float g = G.grad[i];
     float m, v;
     if (kLowp) {
@@ -139,18 +146,34 @@ __device__ __forceinline__ void lean_one(const LeanGroup& G, const LeanTable& t,
     }
 }
 
-// Four consecutive elements with vector accesses; primitives that are not visible are skipped, and a run of
-// four invisible elements is not read at all.
-template <bool kLowp>
-__device__ __forceinline__ void lean_four(const LeanGroup& G, const LeanTable& t, long long e) {
-    bool on[kVec];
-    bool any = false;
+// Which of the four consecutive elements from e belong to visible primitives (bit k for element e + k): one
+// division per four elements, walking from the first element's primitive across the (at most four) primitives
+// they belong to and loading each one's visibility once.
+__device__ __forceinline__ unsigned lean_mask(const LeanGroup& G, const LeanTable& t, long long e) {
+    if (!t.visibility) return (1u << kVec) - 1u;
+    long long prim = primitive_of(G, e);
+    int r = static_cast<int>(e - prim * G.features);
+    bool vis = t.visibility[prim] != 0;
+    unsigned mask = 0u;
 #pragma unroll
     for (int k = 0; k < kVec; ++k) {
-        on[k] = !t.visibility || t.visibility[(e + k) / G.features] != 0;
-        any |= on[k];
+        mask |= static_cast<unsigned>(vis) << k;
+        if (++r == G.features && k + 1 < kVec) {
+            r = 0;
+            ++prim;
+            vis = t.visibility[prim] != 0;
+        }
     }
-    if (!any) return;
+    return mask;
+}
+
+// Four consecutive elements with vector accesses, `mask` from lean_mask (non-zero): elements of primitives that
+// are not visible keep their parameter and moments.
+template <bool kLowp>
+__device__ __forceinline__ void lean_four(const LeanGroup& G, const LeanTable& t, long long e, unsigned mask) {
+    bool on[kVec];
+#pragma unroll
+    for (int k = 0; k < kVec; ++k) on[k] = (mask >> k) & 1u;
     float4 p = *reinterpret_cast<const float4*>(G.param + e);
     const float4 g4 = __ldg(reinterpret_cast<const float4*>(G.grad + e));
     float pv[kVec] = {p.x, p.y, p.z, p.w}, gv[kVec] = {g4.x, g4.y, g4.z, g4.w}, mv[kVec], vv[kVec];
@@ -197,13 +220,23 @@ __device__ __forceinline__ void lean_four(const LeanGroup& G, const LeanTable& t
 template <bool kLowp>
 __device__ __forceinline__ void lean_block(const LeanGroup& G, const LeanTable& t, long long base) {
     if (G.vec) {
+        // the visibility of all of this thread's groups of four first, so that their loads overlap one another
+        // instead of each one delaying its group's data loads
+        constexpr int kIters = kPerBlock / (kThreads * kVec);
+        unsigned mask[kIters];
 #pragma unroll
-        for (int k = 0; k < kPerBlock / (kThreads * kVec); ++k) {
+        for (int k = 0; k < kIters; ++k) {
             const long long e = base + (static_cast<long long>(k) * kThreads + threadIdx.x) * kVec;
-            if (e + kVec <= G.n)
-                lean_four<kLowp>(G, t, e);
-            else
+            mask[k] = e + kVec <= G.n ? lean_mask(G, t, e) : 0u;
+        }
+#pragma unroll
+        for (int k = 0; k < kIters; ++k) {
+            const long long e = base + (static_cast<long long>(k) * kThreads + threadIdx.x) * kVec;
+            if (e + kVec <= G.n) {
+                if (mask[k]) lean_four<kLowp>(G, t, e, mask[k]);
+            } else {
                 for (long long j = e; j < G.n; ++j) lean_one<kLowp>(G, t, j);
+            }
         }
     } else {
         for (long long e = base + threadIdx.x; e < base + kPerBlock && e < G.n; e += kThreads)

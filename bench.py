@@ -169,10 +169,12 @@ def scene_for(workload: str, rank: int, world: int):
 class Trainer:
     """Replicated Gaussians, flat gradient buffer, Adam state; one training step per call."""
 
-    def __init__(self, sc: dict, dev, world: int, fuse: bool = False):
+    def __init__(self, sc: dict, dev, world: int, fuse: bool = False, lean: bool = False):
         self.dev = dev
         self.world = world
         self.fuse = fuse and world == 1  # preprocess backward + Adam in one kernel (N > 1: the exchange kernel)
+        # the reference's lean Adam: visibility-sparse, bfloat16 moments for the SH-rest group (N = 1 only)
+        self.lean = lean and world == 1 and not self.fuse
         self.bases = sc["active_sh_bases"]
         self.peer = None
         if world > 1:  # parameters and gradients in peer-addressable buffers, one fused exchange + Adam kernel
@@ -186,8 +188,9 @@ class Trainer:
             for p, w in zip(self.params, WIDTHS):
                 self.grads.append(self.flat[off:off + w * p.shape[0]].view(p.shape))
                 off += w * p.shape[0]
-            self.m = [torch.zeros_like(p) for p in self.params]
-            self.v = [torch.zeros_like(p) for p in self.params]
+            lowp = [self.lean and nm == "sh_rest" for nm in NAMES]
+            self.m = [torch.zeros_like(p, dtype=torch.bfloat16 if lo else p.dtype) for p, lo in zip(self.params, lowp)]
+            self.v = [torch.zeros_like(p, dtype=torch.bfloat16 if lo else p.dtype) for p, lo in zip(self.params, lowp)]
         self.n = self.params[0].shape[0]
         self.t = 0
         self.settings = {}
@@ -234,8 +237,13 @@ class Trainer:
         else:
             if timed:
                 e[3].record()
-            gs_adam.adam_step([(p, g, mm, vv, LRS[nm]) for p, g, mm, vv, nm in
-                               zip(self.params, self.grads, self.m, self.v, NAMES)], self.t, eps=1e-15)
+            groups = [(p, g, mm, vv, LRS[nm]) for p, g, mm, vv, nm in zip(self.params, self.grads, self.m, self.v,
+                                                                          NAMES)]
+            if self.lean:
+                gs_adam.adam_step_lean(groups, self.t, visibility=gs3d.primitive_views(prim, self.n)["n_touched"],
+                                       eps=1e-15)
+            else:
+                gs_adam.adam_step(groups, self.t, eps=1e-15)
         if timed:
             e[4].record()
             for k, (a, b) in zip(("fwd", "bwd", "comm", "adam"), zip(e[:-1], e[1:])):
@@ -248,7 +256,7 @@ def run_ours(args) -> None:
     dev = torch.device("cuda", local)
     sc, cams = scene_for(args.workload, rank, world)
     cam = cams[0]
-    tr = Trainer(sc, dev, world, fuse=args.fuse)
+    tr = Trainer(sc, dev, world, fuse=args.fuse, lean=args.lean)
     H, W = cam["height"], cam["width"]
     # The upstream gradient is the config's fixed random image with its sign alternating step to step: under Adam a
     # fixed gradient would move every parameter by about lr per step in one direction, and after a few hundred
@@ -311,7 +319,9 @@ def run_ours(args) -> None:
                        "gaussians": n, "width": W, "height": H, "views_per_gpu_per_step": views_per_step,
                        "instances_per_view": round(m_avg), "l2": "state (2.8 GB) larger than L2; no flush",
                        "parallelism": f"dp{world} (views)",
-                       "fused_preprocess_backward_adam": tr.fuse},
+                       "fused_preprocess_backward_adam": tr.fuse,
+                       "adam": "lean: visibility-sparse update, bfloat16 SH-rest moments with stochastic rounding"
+                               if tr.lean else "dense float32 (every Gaussian, every step)"},
             "stage_ms": {k: round(v, 4) for k, v in stage.items()},
             "fwd_bwd_ms": round(stage["fwd"] + stage["bwd"], 4),
             "wall_s": round(wall, 3),
@@ -348,8 +358,9 @@ def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
         leaves = [p.requires_grad_(True) for p in peer.params]
     else:  # with fuse_backward the rasterizer's preprocess backward runs inside the optimizer's fused step
         leaves = [p.requires_grad_(True) for p in start]
-        opt = gs_adam.FusedAdam([{"params": [p], "lr": LRS[nm]} for p, nm in zip(leaves, NAMES)], lr=0.0,
-                                eps=1e-15, fuse_backward=tr.fuse)
+        lean = {"sparse": True, "lowp_moment_groups": ("sh_rest",)} if tr.lean else {}
+        opt = gs_adam.FusedAdam([{"params": [p], "lr": LRS[nm], "name": nm} for p, nm in zip(leaves, NAMES)],
+                                lr=0.0, eps=1e-15, fuse_backward=tr.fuse, **lean)
     cam = cams[0]
     H, W = cam["height"], cam["width"]
     rank = torch.distributed.get_rank() if world > 1 else 0
@@ -452,6 +463,10 @@ def roofline(tr: Trainer, stage: dict, reach: dict, pixels: int) -> dict:
         Gaussian (accumulator clear). Its limiter is instruction issue (FP32, ex2, shuffles), not HBM: the HBM
         fraction it reports is low by nature; profiles/ holds its issue and pipe utilisation.
       k_adam: 59 floats x 4 B x 7 accesses (param, grad, m, v read; param, m, v written) = 1652 B per Gaussian.
+      k_adam_lean (--lean): per visible Gaussian 59 floats of parameter read and written and of gradient read
+        (708 B), the 14 float32 moments of the first five groups read and written (224 B) and the 45 bfloat16
+        SH-rest moments read and written (360 B): 1292 B, + 4 B of visibility per Gaussian; invisible Gaussians
+        are not touched.
       k_preprocess_backward fused with Adam (--fuse): 59 floats x 4 B x 6 accesses (param, m, v read and written)
         + 4 B (n_touched) per Gaussian, + 56 B per visible Gaussian (the blend backward's mean2d, conic + opacity
         and colour sums, colour + depth): 1420 N + 56 V."""
@@ -466,6 +481,10 @@ def roofline(tr: Trainer, stage: dict, reach: dict, pixels: int) -> dict:
              + 36.0 * tr.n, "traffic": BLEND_BWD_TRAFFIC, "limiter": "issue (FP32 / ex2 / shuffles)"}
     adam = {"kernel": "k_adam", "ms": stage["adam"], "bytes": 1652.0 * tr.n, "traffic": ADAM_TRAFFIC,
             "limiter": "HBM"}
+    if tr.lean:
+        visible = int((gs3d.primitive_views(tr.last[0], tr.n)["n_touched"] > 0).sum().item())
+        adam = {"kernel": "k_adam_lean", "ms": stage["adam"], "bytes": 1292.0 * visible + 4.0 * tr.n,
+                "traffic": None, "limiter": "HBM", "visible": visible}
     if tr.fuse:
         visible = int((gs3d.primitive_views(tr.last[0], tr.n)["n_touched"] > 0).sum().item())
         adam = {"kernel": "k_preprocess_backward (fused with Adam)", "ms": stage["adam"],
@@ -790,6 +809,9 @@ def main() -> None:
     ap.add_argument("--workload", choices=["c3", "c4", "c2", "c1", "c5", "gs2d"], default="c3")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for the baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--lean", action="store_true",
+                    help="N = 1: the reference's lean Adam (visibility-sparse, bfloat16 SH-rest moments) instead of "
+                         "the dense float32 update")
     ap.add_argument("--fuse", action="store_true",
                     help="N = 1: the preprocess backward fused with Adam (FusedAdam(fuse_backward=True)) instead of "
                          "separate launches; measured slower on C3 (1.01 ms against 0.24 + 0.74 ms)")
