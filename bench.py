@@ -1,6 +1,6 @@
 """Benchmark of the 3DGS training step on B200, one process per GPU.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c3|c4|c2|c1|c5|gs2d]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c3|c4|c2|c1|c5|gs2d|ssim]
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \
         bench.py --gpus N --steps K --warmup W
 
@@ -16,7 +16,8 @@ The Gaussian state (2.8 GB with moments) is far larger than the 126 MB L2, so no
 ``e2e`` runs the same step through the public API (diff_rasterize + autograd + FusedAdam, PeerAdam for N > 1)
 with the upstream gradient copied from pinned host memory every step and the loss read back, starting from the same
 configured parameters. --workload c1 / c5 measure the toy2d fit step and the render-only orbit instead, and
---workload gs2d the reference's toy2d kernel sweep (their own metric lines).
+--workload gs2d the reference's toy2d kernel sweep and --workload ssim the fused L1 + SSIM loss (their own metric
+lines).
 
 --impl reference times the CPU restatement of the same step (oracle/liboracle.so, OpenMP over all host cores)
 on rank 0 only, over a bounded sample (a horizontal band of the image), and reports the same metric.
@@ -549,9 +550,9 @@ def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    if args.workload in ("c1", "c5"):
+    if args.workload in ("c1", "c5", "gs2d", "ssim"):
         print(json.dumps({"impl": "reference", "unavailable": "the reference arm is defined for the C3 headline; "
-                                                              "run --workload c1/c5 for their cpu_baseline"}))
+                                                              "the other workloads report their own baselines"}))
         return
     sc, cams = scene_for(args.workload, 0, 1)
     res = cpu_baseline(args, sc, cams[0])
@@ -731,6 +732,86 @@ def run_c5(args) -> None:
         torch.distributed.destroy_process_group()
 
 
+def run_ssim(args) -> None:
+    """The fused L1 + SSIM loss beside the rasterizer (the fused-ssim step of the reference's training loop, with
+    lambda_dssim = 0.2): forward and backward of gs_b200.loss.l1_ssim_loss on one 3 x 1080 x 1920 image per step,
+    through the autograd op as a training loop calls it. The two images (50 MB) fit in L2, so a 256 MB buffer is
+    written before every timed step, and the step's own CUDA events bracket it alone (a short device-side sleep
+    after the flush lets the host queue the step, so host overhead is not timed as device time). Algorithmic
+    bytes per element of the image: forward 8 read (image, target) + 12 written (three derivative maps), backward
+    20 read (maps, image, target) + 4 written (gradient): 44 B."""
+    from gs_b200 import loss as gs_loss
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    H, W = 1080, 1920
+    g = torch.Generator().manual_seed(11)
+    gt_h = torch.rand(1, 3, H, W, generator=g)
+    img_h = (gt_h + 0.05 * torch.randn(1, 3, H, W, generator=g)).clamp(0.0, 1.0)
+    gt = gt_h.to(dev)
+    img = img_h.to(dev).requires_grad_(True)
+
+    def step(y):
+        img.grad = None
+        loss = gs_loss.l1_ssim_loss(img, y, 0.2)
+        loss.backward()
+        return loss
+
+    for _ in range(args.warmup):
+        step(gt)
+    torch.cuda.synchronize()
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MB, twice the L2
+    pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with Clocks(0) as clk:
+        launches0 = L.query("splat_launch_count")
+        clk.mark_start()
+        for a, b in pairs:
+            flush.zero_()
+            torch.cuda._sleep(200_000)
+            a.record()
+            step(gt)
+            b.record()
+        torch.cuda.synchronize()
+        clk.mark_end()
+        launches = L.query("splat_launch_count") - launches0
+    ms = sum(a.elapsed_time(b) for a, b in pairs) / args.steps
+    # end to end: the target copied from pinned host memory every step (as a training loop loads it), the loss
+    # copied back into pinned host memory, steps back to back
+    host = gt_h.contiguous().pin_memory()
+    gt_d = torch.empty_like(gt)
+    losses = torch.empty(args.steps, dtype=torch.float32).pin_memory()
+    a2, b2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a2.record()
+    for k in range(args.steps):
+        gt_d.copy_(host, non_blocking=True)
+        losses[k:k + 1].copy_(step(gt_d).detach().view(1), non_blocking=True)
+    b2.record()
+    torch.cuda.synchronize()
+    ms_e2e = a2.elapsed_time(b2) / args.steps
+    elems = 3 * H * W
+    peaks_path = ROOT / "MEASURED_PEAKS.json"
+    hbm, src = 6650.0, "fallback"
+    if peaks_path.exists():
+        v = json.loads(peaks_path.read_text()).get("hbm_gbs")
+        if v:
+            hbm, src = float(v), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    achieved = 44.0 * elems / (ms / 1000.0) / 1e9
+    line = {"metric": "fused L1 + SSIM loss, forward + backward, 3 x 1080 x 1920: evaluations/s",
+            "value": round(1000.0 / ms, 2), "unit": "evaluations/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "replicas only",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded target, image = target + noise)",
+            "config": {"workload": "ssim: l1_ssim_loss(img, gt, 0.2) forward + backward per step, 11x11 window",
+                       "l2": "256 MB written before every timed step (the images fit in L2)"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(achieved / hbm, 4), "traffic": None,
+                         "kernel": "k_ssim_forward + k_ssim_backward (one step)",
+                         "algorithmic_bytes": int(44 * elems), "peak_source": src},
+            "e2e": {"value": round(1000.0 / ms_e2e, 2), "unit": "evaluations/s",
+                    "h2d_bytes_per_step": int(host.numel() * 4), "d2h_bytes_per_step": 4},
+            "clocks": clk.summary(), "gpu_launches": launches}
+    print(json.dumps(line), flush=True)
+
+
 # The reference's toy2d kernel timings on an H100 (toy2d/results/bench-cfda5b4-4473561.json): (size, n) ->
 # (forward, forward saving buckets, backward pixel, backward splat) in ms, CUDA-event medians.
 GS2D_H100_MS = {
@@ -806,7 +887,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c3", "c4", "c2", "c1", "c5", "gs2d"], default="c3")
+    ap.add_argument("--workload", choices=["c3", "c4", "c2", "c1", "c5", "gs2d", "ssim"], default="c3")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for the baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--lean", action="store_true",
@@ -826,6 +907,8 @@ def main() -> None:
         run_c5(args)
     elif args.workload == "gs2d":
         run_gs2d(args)
+    elif args.workload == "ssim":
+        run_ssim(args)
     else:
         run_ours(args)
 
