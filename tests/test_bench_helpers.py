@@ -63,3 +63,20 @@ def test_clock_summary_of_a_short_region_takes_the_nearest_sample():
     out = _clocks(rows, t + 40 * ms, t + 45 * ms).summary()
     assert out["samples"] == 1 and out["sm_mhz"] == 1900.0 and "nearest" in out["note"]
     assert _clocks([], None, None).summary()["reasons"] == ["unsampled"]
+
+
+@pytest.mark.parametrize("workload", ["c1", "c5", "gs2d", "ssim"])
+def test_reference_arm_of_the_other_workloads_says_unavailable(workload):
+    """The reference arm is defined for the C3 headline; on the other workloads it prints one JSON line saying so
+    and exits 0 (without touching a GPU)."""
+    import json
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(bench.__file__).resolve().parent
+    out = subprocess.run([sys.executable, str(root / "bench.py"), "--impl", "reference", "--workload", workload],
+                         capture_output=True, text=True, timeout=300, cwd=root)
+    assert out.returncode == 0, out.stderr[-2000:]
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and "unavailable" in line
