@@ -54,6 +54,32 @@ void note_launch();
 
 constexpr unsigned int kFullMask = 0xffffffffu;
 
+// One halving step of a warp sum of N values per lane: lanes with the `off` bit clear keep the first ceil(N/2)
+// partial sums, the others the rest, each adding its partner's copy of the half it keeps. Four steps (16, 8, 4,
+// 2) and a last exchange (1) leave value k's total in the lanes whose bits 4..1 spell k's position.
+template <int N>
+__device__ __forceinline__ void fold_half(const float (&v)[N], float (&out)[(N + 1) / 2], int off, bool upper) {
+    constexpr int H = (N + 1) / 2;
+#pragma unroll
+    for (int i = 0; i < H; ++i) {
+        const float hi = i + H < N ? v[i + H] : 0.f;
+        const float recv = __shfl_xor_sync(kFullMask, upper ? v[i] : hi, off);
+        out[i] = (upper ? hi : v[i]) + recv;
+    }
+}
+
+// Warp sums of nine values: after the call, every lane's t holds one total; the totals of values 0..8 are in
+// lanes 0, 2, 4, 8, 10, 16, 18, 20, 24 (kFold9Lane).
+__device__ __forceinline__ float warp_fold9(const float (&v9)[9], int lane) {
+    float f5[5], f3[3], f2[2], f1[1];
+    fold_half<9>(v9, f5, 16, lane & 16);
+    fold_half<5>(f5, f3, 8, lane & 8);
+    fold_half<3>(f3, f2, 4, lane & 4);
+    fold_half<2>(f2, f1, 2, lane & 2);
+    return f1[0] + __shfl_xor_sync(kFullMask, f1[0], 1);
+}
+constexpr int kFold9Lane[9] = {0, 2, 4, 8, 10, 16, 18, 20, 24};
+
 // ---- workspace carving: one caller-owned byte buffer split into 256-byte aligned pieces ----
 struct Carver {
     char* base;

@@ -9,10 +9,13 @@
 //   * bucket_state[b][p] = (T, C) of pixel p at the start of the tile's 32-splat bucket b, written
 //     for every bucket of every 256-splat round the tile block executes (rasterize.cu:131-147)
 //
-// Differences in mechanism (not in results):
+// Mechanism (this library's own; results are the reference's):
 //   * binning runs on the GPU: radix sort of depth keys, duplication, radix sort of (tile, rank) keys
 //   * bg is read on the device (the reference copies it to the host, one sync per call)
-//   * colours are staged in shared memory with the geometry
+//   * forward and per-pixel backward: 128 threads per 16x16 tile, two pixels per thread; warp w owns the
+//     8x8 subtile (w & 1, w >> 1). Each staged splat carries the box of pixels its alpha can lift to 1/255,
+//     and a warp evaluates only the splats whose box meets its subtile (one ballot per 32 splats). The
+//     per-pixel backward sums a splat's terms over the warp's 64 pixels before its atomics
 //   * backward_splat uses the warp-per-bucket layout in which a lane owns 8 pixels of the tile and
 //     replays (T, rho = G . (out - C)) from the bucket checkpoint; per splat the warp sums the lanes'
 //     terms with shuffles and lane 0 issues one atomic set per (splat, bucket). It computes the same
@@ -32,40 +35,69 @@ constexpr float kAlphaMin = 1.0f / 255.0f;
 constexpr float kAlphaMax = 0.99f;
 constexpr float kTMin = 1e-4f;
 
-struct Splat {
-    float mx, my;
-    float A, B, C;
-    float o;
-    float r, g, b;
-};
+constexpr int kThreads = kBlock / 2;  // forward and per-pixel backward: two pixels per thread
+constexpr int kRound = 256;           // splats staged per round (the reference's round, which the checkpoints follow)
 
-__device__ __forceinline__ Splat load_splat(int id, const float* __restrict__ means, const float* __restrict__ conic,
-                                            const float* __restrict__ color, const float* __restrict__ opacity) {
-    Splat s;
-    s.mx = means[2 * id];
-    s.my = means[2 * id + 1];
-    s.A = conic[3 * id];
-    s.B = conic[3 * id + 1];
-    s.C = conic[3 * id + 2];
-    s.o = opacity[id];
-    s.r = color[3 * id];
-    s.g = color[3 * id + 1];
-    s.b = color[3 * id + 2];
-    return s;
+// toy2d's per-(pixel, splat) exponent, d = mean - pixel at integer pixel coordinates, written as the single
+// expression of rasterize.cu:40-48 so that it rounds the same way: the alpha >= 1/255 and T >= 1e-4 decisions,
+// and with them the contributor counts, are bit-exact only with that rounding.
+__device__ __forceinline__ float toy_power(float A, float B, float C, float dx, float dy) {
+    return -0.5f * (A * dx * dx + C * dy * dy) - B * dx * dy;
 }
 
-// Same expression order as rasterize.cu:40-48.
-__device__ __forceinline__ bool eval_splat(const Splat& s, float px, float py, float& dx, float& dy, float& G,
-                                           float& alpha, bool& clamped) {
-    dx = s.mx - px;
-    dy = s.my - py;
-    const float power = -0.5f * (s.A * dx * dx + s.C * dy * dy) - s.B * dx * dy;
-    if (power > 0.0f) return false;
-    G = expf(power);
-    const float a = s.o * G;
-    clamped = a > kAlphaMax;
-    alpha = fminf(kAlphaMax, a);
-    return alpha >= kAlphaMin;
+// Box (x0, x1, y0, y1) of the integer pixels where alpha = min(0.99, o e^power) can reach 1/255: those lie in
+// the ellipse q = -2 power <= R = 2 ln(255 o), whose half-extents are sqrt(R C / det) and sqrt(R A / det),
+// det = AC - B^2. R is widened by 0.1% and the box by one pixel, so the rounding of the per-pixel evaluation
+// never reaches outside it. An opacity below 1/255 reaches nothing; a conic that is not positive definite, or
+// values that are not finite (which the per-pixel rules turn into alpha = 0.99), give the unbounded box.
+__device__ __forceinline__ float4 reach_box(float mx, float my, float A, float B, float C, float o) {
+    const float inf = __int_as_float(0x7f800000);
+    const float4 all = make_float4(-inf, inf, -inf, inf);
+    if (o != o || !isfinite(mx) || !isfinite(my)) return all;
+    if (!(o * 255.f >= 1.f)) return make_float4(inf, -inf, inf, -inf);
+    const float det = A * C - B * B;
+    if (!(det > 0.f && A > 0.f && C > 0.f)) return all;
+    const float R = 2.002f * logf(255.f * o) + 1e-3f;
+    const float ex = sqrtf(R * C / det) + 1.f, ey = sqrtf(R * A / det) + 1.f;
+    if (!(ex == ex && ey == ey)) return all;
+    return make_float4(mx - ex, mx + ex, my - ey, my + ey);
+}
+
+// The splats of one round in shared memory, structure of arrays: (mx, my, A, B), (C, opacity, r, g), b, box.
+struct Stage {
+    float4 geo[kRound];
+    float4 cor[kRound];
+    float blue[kRound];
+    float4 box[kRound];
+    int id[kRound];
+};
+
+__device__ __forceinline__ void stage_splat(Stage& st, int slot, int g, const float* __restrict__ means,
+                                            const float* __restrict__ conic, const float* __restrict__ color,
+                                            const float* __restrict__ opacity) {
+    const float2 m = reinterpret_cast<const float2*>(means)[g];
+    const float A = conic[3 * g], B = conic[3 * g + 1], C = conic[3 * g + 2], o = opacity[g];
+    st.geo[slot] = make_float4(m.x, m.y, A, B);
+    st.cor[slot] = make_float4(C, o, color[3 * g], color[3 * g + 1]);
+    st.blue[slot] = color[3 * g + 2];
+    st.box[slot] = reach_box(m.x, m.y, A, B, C, o);
+    st.id[slot] = g;
+}
+
+// Value k (0..8) of warp_fold9 lands in lane kFold9Lane[k]; this is the inverse map (-1: no value).
+__device__ __forceinline__ int fold9_value(int lane) {
+    switch (lane) {
+        case 0: return 0;
+        case 2: return 1;
+        case 4: return 2;
+        case 8: return 3;
+        case 10: return 4;
+        case 16: return 5;
+        case 18: return 6;
+        case 20: return 7;
+        case 24: return 8;
+        default: return -1;
+    }
 }
 
 // Tables handed in by the caller are clamped so that an inconsistent list can give wrong pixels but
@@ -279,157 +311,240 @@ static FillScratch carve_fill(Carver& c, long long m, int T) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// Forward: one 256-thread block per 16x16 tile, one pixel per thread (rasterize.cu:106-177)
+// Forward: 128 threads per 16x16 tile, two pixels per thread (lane: column lane & 7, rows lane >> 3 and
+// (lane >> 3) + 4 of its warp's 8x8 subtile). A round stages 256 splats of the tile's list; each warp walks them
+// 32 at a time and evaluates, in list order, only those whose reach box meets its subtile.
+// kSave: the (T, C) state of both pixels is written at the start of each 32-splat bucket of every round the
+// block executes (bucket_state non-null).
 // ---------------------------------------------------------------------------------------------
-// kSave: the (T, C) state of every pixel is written at the start of each 32-splat bucket (bucket_state non-null).
-// The splats of a staged batch are walked bucket by bucket, so the save is decided once per bucket.
 template <bool kSave>
-__global__ void __launch_bounds__(kBlock) k_forward(const int2* __restrict__ ranges,
-                                                    const int32_t* __restrict__ point_list,
-                                                    const float* __restrict__ means, const float* __restrict__ conic,
-                                                    const float* __restrict__ color,
-                                                    const float* __restrict__ opacity, const float* __restrict__ bg,
-                                                    int N, int M, int num_buckets, int W, int H, int tiles_x,
-                                                    float* __restrict__ out,
-                                                    float* __restrict__ final_T, int32_t* __restrict__ n_contrib,
-                                                    const int32_t* __restrict__ bucket_offsets,
-                                                    float4* __restrict__ bucket_state) {
-    __shared__ Splat s_splat[kBlock];
+__global__ void __launch_bounds__(kThreads) k_render(const int2* __restrict__ ranges,
+                                                     const int32_t* __restrict__ point_list,
+                                                     const float* __restrict__ means, const float* __restrict__ conic,
+                                                     const float* __restrict__ color,
+                                                     const float* __restrict__ opacity, const float* __restrict__ bg,
+                                                     int N, int M, int num_buckets, int W, int H, int tiles_x,
+                                                     float* __restrict__ out, float* __restrict__ final_T,
+                                                     int32_t* __restrict__ n_contrib,
+                                                     const int32_t* __restrict__ bucket_offsets,
+                                                     float4* __restrict__ bucket_state) {
+    __shared__ Stage st;
     const int tile = blockIdx.y * tiles_x + blockIdx.x;
-    const int tid = threadIdx.x;
-    const int px = blockIdx.x * kTile + (tid % kTile);
-    const int py = blockIdx.y * kTile + (tid / kTile);
-    const bool inside = px < W && py < H;
-    bool done = !inside;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tx0 = blockIdx.x * kTile, ty0 = blockIdx.y * kTile;
+    const int sx0 = tx0 + (warp & 1) * 8, sy0 = ty0 + (warp >> 1) * 8;
+    const int x = sx0 + (lane & 7), ya = sy0 + (lane >> 3), yb = ya + 4;
+    const int la = (ya - ty0) * kTile + (x - tx0), lb = la + 4 * kTile;  // tile-local pixel indices
+    const bool in_a = x < W && ya < H, in_b = x < W && yb < H;
+    bool done_a = !in_a, done_b = !in_b;
+    const float fx = static_cast<float>(x), fya = static_cast<float>(ya), fyb = static_cast<float>(yb);
 
-    const int2 range = clamp_range(ranges[tile], M);
-    const int todo = range.y - range.x;
-    const int rounds = (todo + kBlock - 1) / kBlock;
-    const int bbase = bucket_state ? bucket_offsets[tile] : 0;
-    const float fpx = static_cast<float>(px), fpy = static_cast<float>(py);
-
-    float T = 1.0f;
-    float Cr = 0.0f, Cg = 0.0f, Cb = 0.0f;
-    int last = 0;
-    for (int r = 0; r < rounds; ++r) {
-        if (__syncthreads_count(done) == kBlock) break;
-        const int k = range.x + r * kBlock + tid;
-        if (k < range.y) s_splat[tid] = load_splat(clamp_id(point_list[k], N), means, conic, color, opacity);
+    const int2 rg = clamp_range(ranges[tile], M);
+    const int count = rg.y - rg.x;
+    const int bbase = kSave ? bucket_offsets[tile] : 0;
+    float Ta = 1.f, Ra = 0.f, Ga = 0.f, Ba = 0.f, Tb = 1.f, Rb = 0.f, Gb = 0.f, Bb = 0.f;
+    int last_a = 0, last_b = 0;
+    for (int base = 0; base < count; base += kRound) {
+        if (__syncthreads_count(!(done_a && done_b)) == 0) break;
+#pragma unroll
+        for (int h = 0; h < kRound / kThreads; ++h) {
+            const int slot = tid + h * kThreads;
+            if (base + slot < count)
+                stage_splat(st, slot, clamp_id(point_list[rg.x + base + slot], N), means, conic, color, opacity);
+        }
         __syncthreads();
-        const int n = min(kBlock, todo - r * kBlock);
-        for (int j0 = 0; j0 < n; j0 += kBucket) {  // kBlock is a whole number of buckets
+        const int n = min(kRound, count - base);
+        for (int j0 = 0; j0 < n; j0 += kBucket) {
             if (kSave) {
-                const int bkt = bbase + (r * kBlock + j0) / kBucket;
-                if (bkt >= 0 && bkt < num_buckets)
-                    bucket_state[static_cast<size_t>(bkt) * kBlock + tid] = make_float4(T, Cr, Cg, Cb);
-            }
-            if (done) continue;
-            const int j1 = min(j0 + kBucket, n);
-            for (int j = j0; j < j1; ++j) {
-                const Splat& s = s_splat[j];
-                float dx, dy, G, alpha;
-                bool clamped;
-                if (!eval_splat(s, fpx, fpy, dx, dy, G, alpha, clamped)) continue;
-                const float test_T = T * (1.0f - alpha);
-                if (test_T < kTMin) {
-                    done = true;
-                    break;
+                const int bkt = bbase + (base + j0) / kBucket;
+                if (bkt >= 0 && bkt < num_buckets) {
+                    float4* ck = bucket_state + static_cast<size_t>(bkt) * kBlock;
+                    ck[la] = make_float4(Ta, Ra, Ga, Ba);
+                    ck[lb] = make_float4(Tb, Rb, Gb, Bb);
                 }
-                const float w = alpha * T;
-                Cr += s.r * w;
-                Cg += s.g * w;
-                Cb += s.b * w;
-                T = test_T;
-                last = r * kBlock + j + 1;
+            }
+            if (__all_sync(kFullMask, done_a && done_b)) continue;
+            bool hit = false;
+            if (lane < n - j0) {
+                const float4 bx = st.box[j0 + lane];
+                hit = bx.x <= sx0 + 7 && bx.y >= sx0 && bx.z <= sy0 + 7 && bx.w >= sy0;
+            }
+            unsigned pending = __ballot_sync(kFullMask, hit);
+            while (pending != 0u && !(done_a && done_b)) {
+                const int j = j0 + __ffs(pending) - 1;
+                pending &= pending - 1u;
+                const float4 ge = st.geo[j], co = st.cor[j];
+                const float dx = ge.x - fx;
+                if (!done_a) {
+                    const float pw = toy_power(ge.z, ge.w, co.x, dx, ge.y - fya);
+                    if (!(pw > 0.f)) {
+                        const float al = fminf(kAlphaMax, co.y * expf(pw));
+                        if (al >= kAlphaMin) {
+                            const float t = Ta * (1.f - al);
+                            if (t < kTMin) {
+                                done_a = true;
+                            } else {
+                                const float w = al * Ta;
+                                Ra += co.z * w;
+                                Ga += co.w * w;
+                                Ba += st.blue[j] * w;
+                                Ta = t;
+                                last_a = base + j + 1;
+                            }
+                        }
+                    }
+                }
+                if (!done_b) {
+                    const float pw = toy_power(ge.z, ge.w, co.x, dx, ge.y - fyb);
+                    if (!(pw > 0.f)) {
+                        const float al = fminf(kAlphaMax, co.y * expf(pw));
+                        if (al >= kAlphaMin) {
+                            const float t = Tb * (1.f - al);
+                            if (t < kTMin) {
+                                done_b = true;
+                            } else {
+                                const float w = al * Tb;
+                                Rb += co.z * w;
+                                Gb += co.w * w;
+                                Bb += st.blue[j] * w;
+                                Tb = t;
+                                last_b = base + j + 1;
+                            }
+                        }
+                    }
+                }
             }
         }
+        __syncthreads();
     }
-    if (inside) {
-        const int pix = py * W + px;
-        const int HW = H * W;
-        out[pix] = Cr + T * bg[0];
-        out[HW + pix] = Cg + T * bg[1];
-        out[2 * HW + pix] = Cb + T * bg[2];
-        final_T[pix] = T;
-        n_contrib[pix] = last;
+    const size_t HW = static_cast<size_t>(H) * W;
+    if (in_a) {
+        const size_t pix = static_cast<size_t>(ya) * W + x;
+        out[pix] = Ra + Ta * bg[0];
+        out[HW + pix] = Ga + Ta * bg[1];
+        out[2 * HW + pix] = Ba + Ta * bg[2];
+        final_T[pix] = Ta;
+        n_contrib[pix] = last_a;
+    }
+    if (in_b) {
+        const size_t pix = static_cast<size_t>(yb) * W + x;
+        out[pix] = Rb + Tb * bg[0];
+        out[HW + pix] = Gb + Tb * bg[1];
+        out[2 * HW + pix] = Bb + Tb * bg[2];
+        final_T[pix] = Tb;
+        n_contrib[pix] = last_b;
     }
 }
 
 // ---------------------------------------------------------------------------------------------
-// Backward, per pixel (rasterize.cu:182-258): kept as the parity mode
+// Backward, per pixel (the reference's backward_pixel mode): the forward's thread layout walking the tile's list
+// back to front from the block's largest contributor count, 256 splats per round. Each pixel recovers T in front
+// of a splat by division and keeps B = G . (colour behind the splat, background included), so that
+// dL/dalpha = T (G . c) - B / (1 - alpha). Per splat, the warp sums its 64 pixels' nine terms with halving
+// exchanges and nine lanes issue the nine atomics at once.
 // ---------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(kBlock) k_backward_pixel(
+__global__ void __launch_bounds__(kThreads) k_backward_pixel(
     const int2* __restrict__ ranges, const int32_t* __restrict__ point_list, const float* __restrict__ means,
     const float* __restrict__ conic, const float* __restrict__ color, const float* __restrict__ opacity,
     const float* __restrict__ bg, int N, int M, int W, int H, int tiles_x, const float* __restrict__ final_T,
     const int32_t* __restrict__ n_contrib, const float* __restrict__ dL_dout, float* __restrict__ dmeans,
     float* __restrict__ dconic, float* __restrict__ dcolor, float* __restrict__ dopacity) {
-    __shared__ Splat s_splat[kBlock];
-    __shared__ int s_id[kBlock];
+    __shared__ Stage st;
+    __shared__ int s_last[kThreads / 32];
     const int tile = blockIdx.y * tiles_x + blockIdx.x;
-    const int tid = threadIdx.x;
-    const int px = blockIdx.x * kTile + (tid % kTile);
-    const int py = blockIdx.y * kTile + (tid / kTile);
-    const bool inside = px < W && py < H;
-    const int pix = py * W + px;
-    const int HW = H * W;
-    const int2 range = clamp_range(ranges[tile], M);
-    const int todo = range.y - range.x;
-    const int rounds = (todo + kBlock - 1) / kBlock;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int sx0 = blockIdx.x * kTile + (warp & 1) * 8, sy0 = blockIdx.y * kTile + (warp >> 1) * 8;
+    const int x = sx0 + (lane & 7), ya = sy0 + (lane >> 3), yb = ya + 4;
+    const bool in_a = x < W && ya < H, in_b = x < W && yb < H;
+    const float fx = static_cast<float>(x), fya = static_cast<float>(ya), fyb = static_cast<float>(yb);
+    const size_t HW = static_cast<size_t>(H) * W;
+    const size_t pa = in_a ? static_cast<size_t>(ya) * W + x : 0, pb = in_b ? static_cast<size_t>(yb) * W + x : 0;
 
-    const float T_final = inside ? final_T[pix] : 0.0f;
-    const int last = inside ? n_contrib[pix] : 0;
-    const float gr = inside ? dL_dout[pix] : 0.0f;
-    const float gg = inside ? dL_dout[HW + pix] : 0.0f;
-    const float gb = inside ? dL_dout[2 * HW + pix] : 0.0f;
-    const float bg_dot = bg[0] * gr + bg[1] * gg + bg[2] * gb;
-    const float fpx = static_cast<float>(px), fpy = static_cast<float>(py);
+    const float3 ga = in_a ? make_float3(dL_dout[pa], dL_dout[HW + pa], dL_dout[2 * HW + pa]) : make_float3(0.f, 0.f, 0.f);
+    const float3 gb = in_b ? make_float3(dL_dout[pb], dL_dout[HW + pb], dL_dout[2 * HW + pb]) : make_float3(0.f, 0.f, 0.f);
+    const float bg0 = bg[0], bg1 = bg[1], bg2 = bg[2];
+    float Ta = in_a ? final_T[pa] : 0.f, Tb = in_b ? final_T[pb] : 0.f;
+    float Ba = Ta * (ga.x * bg0 + ga.y * bg1 + ga.z * bg2), Bb = Tb * (gb.x * bg0 + gb.y * bg1 + gb.z * bg2);
+    const int last_a = in_a ? n_contrib[pa] : 0, last_b = in_b ? n_contrib[pb] : 0;
 
-    float T = T_final;
-    float ar = 0.0f, ag = 0.0f, ab = 0.0f;
-    float last_alpha = 0.0f, lr = 0.0f, lg = 0.0f, lb = 0.0f;
-    int contributor = todo;
-    for (int r = 0; r < rounds; ++r) {
+    const int2 rg = clamp_range(ranges[tile], M);
+    const int wlast = __reduce_max_sync(kFullMask, max(last_a, last_b));
+    if (lane == 0) s_last[warp] = wlast;
+    __syncthreads();
+    int top = 0;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) top = max(top, s_last[w]);
+    top = min(top, rg.y - rg.x);  // list positions >= top are used by no pixel of the tile
+    const int value = fold9_value(lane);
+
+    for (int hi = top; hi > 0; hi -= kRound) {
+        const int lo = max(hi - kRound, 0);
         __syncthreads();
-        const int k = range.y - 1 - (r * kBlock + tid);
-        if (k >= range.x) {
-            const int id = clamp_id(point_list[k], N);
-            s_id[tid] = id;
-            s_splat[tid] = load_splat(id, means, conic, color, opacity);
+#pragma unroll
+        for (int h = 0; h < kRound / kThreads; ++h) {
+            const int slot = tid + h * kThreads;
+            if (lo + slot < hi)
+                stage_splat(st, slot, clamp_id(point_list[rg.x + lo + slot], N), means, conic, color, opacity);
         }
         __syncthreads();
-        const int n = min(kBlock, todo - r * kBlock);
-        for (int j = 0; j < n; ++j) {
-            --contributor;
-            if (!inside || contributor >= last) continue;
-            const Splat& s = s_splat[j];
-            float dx, dy, G, alpha;
-            bool clamped;
-            if (!eval_splat(s, fpx, fpy, dx, dy, G, alpha, clamped)) continue;
-            const float one_minus = 1.0f - alpha;
-            T = T / one_minus;
-            ar = last_alpha * lr + (1.0f - last_alpha) * ar;
-            ag = last_alpha * lg + (1.0f - last_alpha) * ag;
-            ab = last_alpha * lb + (1.0f - last_alpha) * ab;
-            last_alpha = alpha;
-            lr = s.r;
-            lg = s.g;
-            lb = s.b;
-            float dL_dalpha = ((s.r - ar) * gr + (s.g - ag) * gg + (s.b - ab) * gb) * T;
-            dL_dalpha += (-T_final / one_minus) * bg_dot;
-            const float w = alpha * T;
-            const int id = s_id[j];
-            atomicAdd(&dcolor[3 * id + 0], w * gr);
-            atomicAdd(&dcolor[3 * id + 1], w * gg);
-            atomicAdd(&dcolor[3 * id + 2], w * gb);
-            if (!clamped) {
-                const float dpow = s.o * G * dL_dalpha;
-                atomicAdd(reinterpret_cast<float2*>(dmeans) + id,
-                          make_float2((-s.A * dx - s.B * dy) * dpow, (-s.C * dy - s.B * dx) * dpow));
-                atomicAdd(&dconic[3 * id + 0], -0.5f * dx * dx * dpow);
-                atomicAdd(&dconic[3 * id + 1], -dx * dy * dpow);
-                atomicAdd(&dconic[3 * id + 2], -0.5f * dy * dy * dpow);
-                atomicAdd(&dopacity[id], G * dL_dalpha);
+        for (int j0 = ((hi - lo - 1) / kBucket) * kBucket; j0 >= 0; j0 -= kBucket) {
+            if (lo + j0 >= wlast) continue;  // warp-uniform: none of this warp's pixels reached the bucket
+            bool hit = false;
+            if (lane < hi - lo - j0) {
+                const float4 bx = st.box[j0 + lane];
+                hit = bx.x <= sx0 + 7 && bx.y >= sx0 && bx.z <= sy0 + 7 && bx.w >= sy0;
+            }
+            unsigned pending = __ballot_sync(kFullMask, hit);
+            while (pending != 0u) {  // back to front: highest list position first
+                const int b = 31 - __clz(pending);
+                pending &= ~(1u << b);
+                const int j = j0 + b, pos = lo + j;
+                const float4 ge = st.geo[j], co = st.cor[j];
+                const float blue = st.blue[j];
+                const float dx = ge.x - fx;
+                float v[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // mx, my, A, B, C, r, g, b, opacity
+                bool used = false;
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    if (pos >= (q ? last_b : last_a)) continue;
+                    const float dy = ge.y - (q ? fyb : fya);
+                    const float pw = toy_power(ge.z, ge.w, co.x, dx, dy);
+                    if (pw > 0.f) continue;
+                    const float G = expf(pw), a0 = co.y * G, al = fminf(kAlphaMax, a0);
+                    if (!(al >= kAlphaMin)) continue;
+                    used = true;
+                    const float3 g = q ? gb : ga;
+                    float& T = q ? Tb : Ta;
+                    float& B = q ? Bb : Ba;
+                    const float om = 1.f - al;
+                    T = T / om;  // transmittance in front of this splat
+                    const float gc = g.x * co.z + g.y * co.w + g.z * blue;
+                    const float w = al * T;
+                    v[5] += w * g.x;
+                    v[6] += w * g.y;
+                    v[7] += w * g.z;
+                    const float dL_dalpha = T * gc - B / om;
+                    B += w * gc;
+                    if (!(a0 > kAlphaMax)) {  // the 0.99 clamp passes no gradient
+                        const float dpw = a0 * dL_dalpha;
+                        v[0] += (-ge.z * dx - ge.w * dy) * dpw;
+                        v[1] += (-co.x * dy - ge.w * dx) * dpw;
+                        v[2] += -0.5f * dx * dx * dpw;
+                        v[3] += -dx * dy * dpw;
+                        v[4] += -0.5f * dy * dy * dpw;
+                        v[8] += G * dL_dalpha;
+                    }
+                }
+                if (__ballot_sync(kFullMask, used) == 0u) continue;
+                const float t = warp_fold9(v, lane);
+                if (value >= 0) {
+                    const int g = st.id[j];
+                    float* dst = value < 2 ? dmeans + 2 * g + value
+                               : value < 5 ? dconic + 3 * g + (value - 2)
+                               : value < 8 ? dcolor + 3 * g + (value - 5)
+                                           : dopacity + g;
+                    atomicAdd(dst, t);
+                }
             }
         }
     }
@@ -445,7 +560,10 @@ __global__ void __launch_bounds__(32 * kBwdWarps) k_backward_splat(
     int M, int W, int H, int tiles_x, const float* __restrict__ out, const int32_t* __restrict__ n_contrib,
     const float* __restrict__ dL_dout, const float4* __restrict__ bucket_state, float* __restrict__ dmeans,
     float* __restrict__ dconic, float* __restrict__ dcolor, float* __restrict__ dopacity) {
-    __shared__ Splat s_splat[kBwdWarps][kBucket];
+    __shared__ float4 s_geo[kBwdWarps][kBucket];  // (mx, my, A, B)
+    __shared__ float4 s_cor[kBwdWarps][kBucket];  // (C, opacity, r, g)
+    __shared__ float4 s_box[kBwdWarps][kBucket];
+    __shared__ float s_blue[kBwdWarps][kBucket];
     __shared__ int s_id[kBwdWarps][kBucket];
     __shared__ float3 s_grad[kBwdWarps][kBlock];
 
@@ -460,7 +578,7 @@ __global__ void __launch_bounds__(32 * kBwdWarps) k_backward_splat(
     const int bsize = min(kBucket, range.y - range.x - bucket_start);
     const int tile_x0 = (tile % tiles_x) * kTile;
     const int tile_y0 = (tile / tiles_x) * kTile;
-    const int HW = H * W;
+    const size_t HW = static_cast<size_t>(H) * W;
 
     const int x = tile_x0 + (lane % kTile);
     const int y0 = tile_y0 + (lane / kTile);
@@ -476,7 +594,7 @@ __global__ void __launch_bounds__(32 * kBwdWarps) k_backward_splat(
         rho[r] = 0.0f;
         lim[r] = 0;
         if (x < W && y < H) {
-            const int pix = y * W + x;
+            const size_t pix = static_cast<size_t>(y) * W + x;
             lim[r] = n_contrib[pix] - bucket_start;
             if (lim[r] > 0) {
                 G = make_float3(dL_dout[pix], dL_dout[HW + pix], dL_dout[2 * HW + pix]);
@@ -492,66 +610,65 @@ __global__ void __launch_bounds__(32 * kBwdWarps) k_backward_splat(
     if (lim_max <= 0) return;  // no pixel of the tile reaches this bucket
     const int n_splats = min(bsize, lim_max);
     if (lane < n_splats) {
-        const int id = clamp_id(point_list[range.x + bucket_start + lane], N);
-        s_id[warp][lane] = id;
-        s_splat[warp][lane] = load_splat(id, means, conic, color, opacity);
+        const int g = clamp_id(point_list[range.x + bucket_start + lane], N);
+        const float2 m = reinterpret_cast<const float2*>(means)[g];
+        const float A = conic[3 * g], B = conic[3 * g + 1], C = conic[3 * g + 2], o = opacity[g];
+        s_id[warp][lane] = g;
+        s_geo[warp][lane] = make_float4(m.x, m.y, A, B);
+        s_cor[warp][lane] = make_float4(C, o, color[3 * g], color[3 * g + 1]);
+        s_blue[warp][lane] = color[3 * g + 2];
+        s_box[warp][lane] = reach_box(m.x, m.y, A, B, C, o);
     }
     __syncwarp();
     const float fx = static_cast<float>(x);
+    const int value = fold9_value(lane);
 
     for (int j = 0; j < n_splats; ++j) {
-        const Splat s = s_splat[warp][j];
-        float g_mx = 0.f, g_my = 0.f, g_A = 0.f, g_B = 0.f, g_C = 0.f, g_r = 0.f, g_g = 0.f, g_b = 0.f, g_o = 0.f;
+        const float4 ge = s_geo[warp][j], co = s_cor[warp][j], bx = s_box[warp][j];
+        const float blue = s_blue[warp][j];
+        const bool col_hit = fx >= bx.x && fx <= bx.y;
+        const float dx = ge.x - fx;
+        float v[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // mx, my, A, B, C, r, g, b, opacity
         bool used = false;
 #pragma unroll
         for (int r = 0; r < kPxPerLane; ++r) {
-            if (j >= lim[r]) continue;
-            float dx, dy, G, alpha;
-            bool clamped;
-            if (!eval_splat(s, fx, static_cast<float>(y0 + 2 * r), dx, dy, G, alpha, clamped)) continue;
+            const float yr = static_cast<float>(tile_y0 + 2 * r);  // this lane row pair: yr, yr + 1
+            if (bx.z > yr + 1.f || bx.w < yr) continue;           // warp-uniform
+            if (!col_hit || j >= lim[r]) continue;
+            const float dy = ge.y - static_cast<float>(y0 + 2 * r);
+            const float pw = toy_power(ge.z, ge.w, co.x, dx, dy);
+            if (pw > 0.f) continue;
+            const float G = expf(pw), a0 = co.y * G, al = fminf(kAlphaMax, a0);
+            if (!(al >= kAlphaMin)) continue;
             used = true;
             const float3 gp = s_grad[warp][r * 32 + lane];
-            const float w = alpha * T[r];
-            const float dot_c = gp.x * s.r + gp.y * s.g + gp.z * s.b;
-            g_r += w * gp.x;
-            g_g += w * gp.y;
-            g_b += w * gp.z;
+            const float w = al * T[r];
+            const float dot_c = gp.x * co.z + gp.y * co.w + gp.z * blue;
+            v[5] += w * gp.x;
+            v[6] += w * gp.y;
+            v[7] += w * gp.z;
             rho[r] -= w * dot_c;
-            const float dL_dalpha = T[r] * dot_c - rho[r] / (1.0f - alpha);
-            if (!clamped) {
-                g_o += G * dL_dalpha;
-                const float dpow = s.o * G * dL_dalpha;
-                g_mx += (-s.A * dx - s.B * dy) * dpow;
-                g_my += (-s.C * dy - s.B * dx) * dpow;
-                g_A += -0.5f * dx * dx * dpow;
-                g_B += -dx * dy * dpow;
-                g_C += -0.5f * dy * dy * dpow;
+            const float dL_dalpha = T[r] * dot_c - rho[r] / (1.0f - al);
+            if (!(a0 > kAlphaMax)) {  // the 0.99 clamp passes no gradient
+                v[8] += G * dL_dalpha;
+                const float dpw = a0 * dL_dalpha;
+                v[0] += (-ge.z * dx - ge.w * dy) * dpw;
+                v[1] += (-co.x * dy - ge.w * dx) * dpw;
+                v[2] += -0.5f * dx * dx * dpw;
+                v[3] += -dx * dy * dpw;
+                v[4] += -0.5f * dy * dy * dpw;
             }
-            T[r] = T[r] * (1.0f - alpha);
+            T[r] = T[r] * (1.0f - al);
         }
         if (__ballot_sync(kFullMask, used) == 0u) continue;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            g_mx += __shfl_down_sync(kFullMask, g_mx, o);
-            g_my += __shfl_down_sync(kFullMask, g_my, o);
-            g_A += __shfl_down_sync(kFullMask, g_A, o);
-            g_B += __shfl_down_sync(kFullMask, g_B, o);
-            g_C += __shfl_down_sync(kFullMask, g_C, o);
-            g_r += __shfl_down_sync(kFullMask, g_r, o);
-            g_g += __shfl_down_sync(kFullMask, g_g, o);
-            g_b += __shfl_down_sync(kFullMask, g_b, o);
-            g_o += __shfl_down_sync(kFullMask, g_o, o);
-        }
-        if (lane == 0) {
-            const int id = s_id[warp][j];
-            atomicAdd(reinterpret_cast<float2*>(dmeans) + id, make_float2(g_mx, g_my));
-            atomicAdd(&dconic[3 * id + 0], g_A);
-            atomicAdd(&dconic[3 * id + 1], g_B);
-            atomicAdd(&dconic[3 * id + 2], g_C);
-            atomicAdd(&dcolor[3 * id + 0], g_r);
-            atomicAdd(&dcolor[3 * id + 1], g_g);
-            atomicAdd(&dcolor[3 * id + 2], g_b);
-            atomicAdd(&dopacity[id], g_o);
+        const float t = warp_fold9(v, lane);
+        if (value >= 0) {
+            const int g = s_id[warp][j];
+            float* dst = value < 2 ? dmeans + 2 * g + value
+                       : value < 5 ? dconic + 3 * g + (value - 2)
+                       : value < 8 ? dcolor + 3 * g + (value - 5)
+                                   : dopacity + g;
+            atomicAdd(dst, t);
         }
     }
 }
@@ -666,9 +783,9 @@ int gs2d_forward(const float* means, const float* conic, const float* color, con
     SPLAT_REQUIRE(N > 0 || num_instances == 0, "gs2d_forward: instances without Gaussians");
     SPLAT_REQUIRE(!save_buckets || num_buckets == 0 || bucket_state, "gs2d_forward: bucket_state missing");
     const int tiles_x = (W + kTile - 1) / kTile, tiles_y = (H + kTile - 1) / kTile;
-    const dim3 grid(tiles_x, tiles_y), block(kBlock);
+    const dim3 grid(tiles_x, tiles_y), block(kThreads);
     const bool save = save_buckets && num_buckets > 0;
-    auto kernel = save ? k_forward<true> : k_forward<false>;
+    auto kernel = save ? k_render<true> : k_render<false>;
     kernel<<<grid, block, 0, as_stream(stream)>>>(
         reinterpret_cast<const int2*>(ranges), point_list, means, conic, color, opacity, bg, N,
         static_cast<int>(num_instances), num_buckets, W, H, tiles_x, out, final_T, n_contrib, bucket_offsets,
@@ -691,7 +808,7 @@ int gs2d_backward_pixel(const float* means, const float* conic, const float* col
     SPLAT_CUDA(cudaMemsetAsync(dcolor, 0, sizeof(float) * 3 * N, st));
     SPLAT_CUDA(cudaMemsetAsync(dopacity, 0, sizeof(float) * N, st));
     const int tiles_x = (W + kTile - 1) / kTile, tiles_y = (H + kTile - 1) / kTile;
-    k_backward_pixel<<<dim3(tiles_x, tiles_y), kBlock, 0, st>>>(
+    k_backward_pixel<<<dim3(tiles_x, tiles_y), kThreads, 0, st>>>(
         reinterpret_cast<const int2*>(ranges), point_list, means, conic, color, opacity, bg, N,
         static_cast<int>(num_instances), W, H, tiles_x, final_T, n_contrib, dL_dout, dmeans, dconic, dcolor, dopacity);
     note_launch();

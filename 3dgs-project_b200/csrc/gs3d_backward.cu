@@ -57,19 +57,6 @@ inline GradAcc carve_grad(Carver& c, int n) {
     return g;
 }
 
-// One halving step of a warp sum of N values per lane: lanes with the `off` bit clear keep the first ceil(N/2)
-// partial sums, the others the rest, each adding its partner's copy of the half it keeps.
-template <int N>
-__device__ __forceinline__ void fold_half(const float (&v)[N], float (&out)[(N + 1) / 2], int off, bool upper) {
-    constexpr int H = (N + 1) / 2;
-#pragma unroll
-    for (int i = 0; i < H; ++i) {
-        const float hi = i + H < N ? v[i + H] : 0.f;
-        const float recv = __shfl_xor_sync(kFullMask, upper ? v[i] : hi, off);
-        out[i] = (upper ? hi : v[i]) + recv;
-    }
-}
-
 // kAbs: also accumulate the per-pixel absolute values of the mean2d gradient (the third densification row).
 template <bool kAbs>
 __global__ void __launch_bounds__(32 * kBwdWarps, SPLAT_BWD_MIN_BLOCKS) k_blend_backward(
@@ -207,12 +194,7 @@ __global__ void __launch_bounds__(32 * kBwdWarps, SPLAT_BWD_MIN_BLOCKS) k_blend_
                 // halving exchanges: 9 -> 5 -> 3 -> 2 -> 1 partial sums per lane (11 shuffles), a last exchange,
                 // then lane 0 collects the nine totals from the lanes that hold them (8 shuffles)
                 const float v9[9] = {s_x, s_y, s_xx, s_xy, s_yy, g_o, g_r, g_g, g_bl};
-                float f5[5], f3[3], f2[2], f1[1];
-                fold_half<9>(v9, f5, 16, lane & 16);
-                fold_half<5>(f5, f3, 8, lane & 8);
-                fold_half<3>(f3, f2, 4, lane & 4);
-                fold_half<2>(f2, f1, 2, lane & 2);
-                const float t = f1[0] + __shfl_xor_sync(kFullMask, f1[0], 1);
+                const float t = warp_fold9(v9, lane);
                 s_x = t;
                 s_y = __shfl_sync(kFullMask, t, 2);
                 s_xx = __shfl_sync(kFullMask, t, 4);

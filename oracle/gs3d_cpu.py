@@ -47,7 +47,7 @@ def load():
         lib.gs3o_preprocess_backward.argtypes = [_P] * 12
         lib.gs3o_adam.argtypes = [_P] * 4 + [ctypes.c_longlong, ctypes.c_int] + [ctypes.c_double] * 4
         for name in ("mean2d", "conic_o", "color_z", "thr", "n_touched", "point_list", "keys_sorted", "ranges",
-                     "image", "final_T", "n_contrib"):
+                     "image", "final_T", "n_contrib", "near"):
             getattr(lib, f"gs3o_{name}").restype = _P
             getattr(lib, f"gs3o_{name}").argtypes = [_P]
         _lib = lib
@@ -117,10 +117,13 @@ class Oracle:
     def blend(self, row0=0, row1=None):
         self.lib.gs3o_blend(self.ctx, row0, self.tiles_y if row1 is None else row1)
 
-    def backward(self, grad_image: np.ndarray, row0=0, row1=None):
+    def backward(self, grad_image: np.ndarray, row0=0, row1=None, bands=None):
+        """The six parameter gradients of the blend backward over tile rows [row0, row1) (or over each
+        (row0, row1) of ``bands``), chained through the preprocess backward."""
         g = np.ascontiguousarray(grad_image, np.float32)
         self.lib.gs3o_backward_reset(self.ctx)
-        self.lib.gs3o_blend_backward(self.ctx, _ptr(g), row0, self.tiles_y if row1 is None else row1)
+        for r0, r1 in (bands or [(row0, self.tiles_y if row1 is None else row1)]):
+            self.lib.gs3o_blend_backward(self.ctx, _ptr(g), r0, r1)
         n, rest = self.n, self.rest
         out = [np.zeros((n, 3), np.float32), np.zeros((n, 3), np.float32), np.zeros((n, 4), np.float32),
                np.zeros((n, 1), np.float32), np.zeros((n, 1, 3), np.float32), np.zeros((n, rest, 3), np.float32)]
@@ -146,7 +149,8 @@ class Oracle:
         P = self.W * self.H
         return {"image": self._arr("image", np.float32, 3 * P).reshape(3, self.H, self.W),
                 "final_T": self._arr("final_T", np.float32, P).reshape(self.H, self.W),
-                "n_contrib": self._arr("n_contrib", np.int32, P).reshape(self.H, self.W)}
+                "n_contrib": self._arr("n_contrib", np.int32, P).reshape(self.H, self.W),
+                "near": self._arr("near", np.uint8, P).reshape(self.H, self.W).astype(bool)}
 
 
 def time_training_step(sc: dict, cam: dict, budget_s: float = 20.0) -> dict:

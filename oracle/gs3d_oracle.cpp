@@ -10,7 +10,9 @@
 //                   and sum rounded separately (compile with -ffp-contract=off), so the tiles match the device
 //   sort            std::stable_sort on (tile << 32 | order-preserving depth bits), ties by Gaussian id
 //   blend           per pixel, front to back over its tile's list; alpha = o exp2(min(q2, 0)), skip < 1/255,
-//                   stop after T < 1e-4; image = C + T bg
+//                   stop after T < 1e-4; image = C + T bg. A pixel is flagged "near" when one of its decisions
+//                   (alpha >= 1/255, T < 1e-4) lies within the error bound of two exp2 implementations (the
+//                   device's hardware ex2 and the C library's exp2f); counts are compared on the others
 //   blend backward  per pixel, back to front from its last contributor, T recovered by division (the
 //                   3DGS per-pixel scheme) in double precision, gradients into mean2d / conic / opacity /
 //                   colour accumulated in double
@@ -40,6 +42,9 @@ constexpr float kDilation = 0.3f;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kCullMargin = 0.01f;
 constexpr double kOneMinusAlphaEps = 1e-6;
+// Relative difference allowed between two float exp2 evaluations of the same argument (a few ulp: the
+// device's ex2.approx is within 2 ulp, the C library's exp2f within 1), times a safety factor of 4.
+constexpr float kExp2Tol = 0x1p-19f;
 
 const float SH0 = 0.28209479177387814f, SH1 = 0.4886025119029199f;
 const float SH2[5] = {1.0925484305920792f, -1.0925484305920792f, 0.31539156525252005f, -1.0925484305920792f,
@@ -74,6 +79,7 @@ struct gs3o_ctx {
     // forward per pixel
     std::vector<float> image, final_T;
     std::vector<int> n_contrib;
+    std::vector<unsigned char> near;  // 1 = a decision of this pixel is within exp2 rounding of its threshold
     // backward accumulators (double)
     std::vector<double> g_mean2d, g_conic_o, g_color;
 };
@@ -347,6 +353,7 @@ long long gs3o_bin(gs3o_ctx* c) {
     c->image.assign(3 * P, 0.f);
     c->final_T.assign(P, 1.f);
     c->n_contrib.assign(P, 0);
+    c->near.assign(P, 0);
     return m;
 }
 
@@ -364,6 +371,8 @@ void gs3o_blend(gs3o_ctx* c, int row0, int row1) {
                 const float pxf = x + 0.5f, pyf = y + 0.5f;
                 float T = 1.f, C[3] = {0.f, 0.f, 0.f};
                 int last = 0;
+                unsigned char near = 0;
+                double eT = 0.0;  // bound on the relative difference of T between two exp2 implementations
                 for (int64_t k = s0; k < s1; ++k) {
                     const int64_t g = c->point_list[k];
                     const float* co = &c->conic_o[4 * g];
@@ -371,14 +380,18 @@ void gs3o_blend(gs3o_ctx* c, int row0, int row1) {
                     const float a2 = -0.5f * kLog2e * co[0], b2 = -kLog2e * co[1], c2 = -0.5f * kLog2e * co[2];
                     const float q2 = fmaf(dx, fmaf(a2, dx, b2 * dy), c2 * (dy * dy));  // the device's blend_q2
                     const float alpha = co[3] * exp2f(std::min(q2, 0.f));
+                    if (fabsf(alpha - kAlphaMin) <= kExp2Tol * kAlphaMin) near = 1;
                     if (alpha < kAlphaMin) continue;
                     const float w = alpha * T;
                     for (int ch = 0; ch < 3; ++ch) C[ch] += w * std::max(c->color_z[4 * g + ch], 0.f);
                     T *= 1.f - alpha;
+                    eT += (double)kExp2Tol * alpha / std::max(1.0 - alpha, 1e-30) + 0x1p-22;
                     last = (int)(k - s0 + 1);
+                    if (fabs((double)T - kTMin) <= eT * kTMin) near = 1;
                     if (T < kTMin) break;
                 }
                 const size_t pix = (size_t)y * W + x;
+                c->near[pix] = near;
                 for (int ch = 0; ch < 3; ++ch) c->image[ch * P + pix] = C[ch] + T * c->s.bg[ch];
                 c->final_T[pix] = T;
                 c->n_contrib[pix] = last;
@@ -658,5 +671,6 @@ const int64_t* gs3o_ranges(gs3o_ctx* c) { return c->ranges.data(); }
 const float* gs3o_image(gs3o_ctx* c) { return c->image.data(); }
 const float* gs3o_final_T(gs3o_ctx* c) { return c->final_T.data(); }
 const int* gs3o_n_contrib(gs3o_ctx* c) { return c->n_contrib.data(); }
+const unsigned char* gs3o_near(gs3o_ctx* c) { return c->near.data(); }
 
 }  // extern "C"
