@@ -541,6 +541,25 @@ int noalloc_scan_partials(uint32_t** out) {
     return SPLAT_OK;
 }
 
+// The array's address is the current device's, so the buffers must be device memory of that device (or managed
+// memory): anything else would have the kernels mix this device's scratch with another device's data.
+int noalloc_check_pointer(const void* p, const char* name) {
+    if (p == nullptr) return SPLAT_OK;
+    int dev = -1;
+    SPLAT_CUDA(cudaGetDevice(&dev));
+    cudaPointerAttributes a{};
+    const cudaError_t e = cudaPointerGetAttributes(&a, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_error("splat_scan_exclusive_u32_noalloc: %s is not a CUDA pointer (%s)", name, cudaGetErrorString(e));
+        return SPLAT_ERR_ARG;
+    }
+    const bool ok = a.type == cudaMemoryTypeManaged || (a.type == cudaMemoryTypeDevice && a.device == dev);
+    SPLAT_REQUIRE(ok, "splat_scan_exclusive_u32_noalloc: %s must be device memory of the current device %d "
+                      "(memory type %d on device %d)", name, dev, static_cast<int>(a.type), a.device);
+    return SPLAT_OK;
+}
+
 }  // namespace
 
 int scan_exclusive_u32_noalloc(const uint32_t* in, uint32_t* out, long long n, uint32_t* total,
@@ -555,6 +574,9 @@ int scan_exclusive_u32_noalloc(const uint32_t* in, uint32_t* out, long long n, u
         if (total) SPLAT_CUDA(cudaMemsetAsync(total, 0, sizeof(uint32_t), stream));
         return SPLAT_OK;
     }
+    SPLAT_TRY(noalloc_check_pointer(in, "in"));
+    SPLAT_TRY(noalloc_check_pointer(out, "out"));
+    SPLAT_TRY(noalloc_check_pointer(total, "total"));
     uint32_t* partial = nullptr;
     SPLAT_TRY(noalloc_scan_partials(&partial));
     const unsigned int nb = div_up(n, kScanTile);  // <= kNoAllocScanPartials

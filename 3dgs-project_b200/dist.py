@@ -126,7 +126,8 @@ class PeerFlat:
 class MulticastFlat:
     """A flat float32 vector allocated as PyTorch symmetric memory: this rank's buffer as a tensor, every rank's
     buffer address (`ptrs`) and the NVLink multicast address bound to all of them (`mc`, 0 when the node has no
-    NVLS)."""
+    NVLS). Made in two steps: the constructor allocates this rank's buffer (local, no collective); bind() is the
+    collective rendezvous that exchanges the addresses, which every rank must enter."""
 
     def __init__(self, numel: int, group=None, device=None):
         import torch.distributed._symmetric_memory as symm_mem
@@ -135,7 +136,14 @@ class MulticastFlat:
         self.numel = numel
         self.tensor = symm_mem.empty(max(numel, 4), dtype=torch.float32, device=device)
         self.tensor.zero_()
-        self._handle = symm_mem.rendezvous(self.tensor, group if group is not None else dist.group.WORLD)
+        self._handle = None
+        self.ptrs: list = []
+        self.mc = 0
+
+    def bind(self) -> None:
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self._handle = symm_mem.rendezvous(self.tensor, self.group if self.group is not None else dist.group.WORLD)
         self.ptrs = list(self._handle.buffer_ptrs)
         self.mc = int(self._handle.multicast_ptr)
 
@@ -148,21 +156,40 @@ class MulticastFlat:
         self._handle = None
 
 
+_SETUP_ERRORS = (RuntimeError, ImportError, AttributeError, OSError)
+
+
+def _all_ranks(flag: int, group, device) -> bool:
+    ok = torch.tensor([int(flag)], device=device)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+    return bool(int(ok.item()))
+
+
 def agree_on_buffers(make, count: int, group=None, device=None):
-    """Make `count` multicast buffers with `make()` on every rank and return them where every rank made them all
-    with a multicast address; otherwise close this rank's (no rank has addressed them, so without a barrier) and
-    return None. Every rank gets the same answer, also when the buffers failed on some ranks only."""
+    """Make `count` multicast buffers on every rank and return them where every rank has them all with a multicast
+    address; otherwise close this rank's (no rank has addressed them, so without a barrier) and return None. Every
+    rank gets the same answer, also when the buffers fail on some ranks only.
+
+    Two agreement points keep the ranks' collectives in step: `make()` allocates one buffer locally (no
+    collective), and the ranks agree that every allocation succeeded before any of them enters the buffers'
+    collective `bind()` (the rendezvous), in the same order on every rank; they agree again on the multicast
+    addresses. A rank whose allocation fails therefore never leaves the others waiting inside a rendezvous."""
     made = []
     try:
         for _ in range(count):
             made.append(make())
-        usable = int(all(b.mc != 0 for b in made))
-    except (RuntimeError, ImportError, AttributeError):
-        usable = 0
-    ok = torch.tensor([usable], device=device)
-    dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
-    if int(ok.item()):
-        return made
+        allocated = 1
+    except _SETUP_ERRORS:
+        allocated = 0
+    if _all_ranks(allocated, group, device):
+        try:
+            for b in made:
+                b.bind()
+            usable = int(all(b.mc != 0 for b in made))
+        except _SETUP_ERRORS:
+            usable = 0
+        if _all_ranks(usable, group, device):
+            return made
     for b in made:
         b.close(barrier=False)
     return None

@@ -473,5 +473,36 @@ def instance_views(inst_buf: torch.Tensor, m: int, prim_buf: torch.Tensor | None
     return out
 
 
+def bucket_views(bucket_buf: torch.Tensor, bcap: int) -> dict[str, torch.Tensor]:
+    """tile [B] (tile of each bucket), reached [B] (the buckets the forward reached, in no set order), ckpt [B, 256, 4]
+    ((C.r, C.g, C.b, T) of each tile pixel, row-major, at the bucket's start): the layout of carve_bucket in
+    csrc/gs3d_common.cuh. Only the first counters[1] buckets exist; the rest of the capacity is unused."""
+    bb = max(bcap, 1)
+    off = 0
+    out = {}
+    for name, count in (("tile", bb), ("reached", bb)):
+        off = _align(off)
+        out[name] = bucket_buf[off:off + 4 * count].view(torch.int32)
+        off += 4 * count
+    off = _align(off)
+    out["ckpt"] = bucket_buf[off:off + 16 * TILE * TILE * bb].view(torch.float32).view(bb, TILE * TILE, 4)
+    return out
+
+
+def backward_workspace_views(ws: torch.Tensor, n: int) -> dict[str, torch.Tensor]:
+    """The per-Gaussian sums the blend backward leaves in its workspace (carve_grad in csrc/gs3d_backward.cu):
+    mean2d [N, 2] (dL/dmean2d, pixels), conic_o [N, 4] (dL/dA, dL/dB, dL/dC, dL/dopacity), color [N, 4]
+    (dL/d max(colour, 0), w unused), mean2d_abs [N, 2] (sums of |per-pixel dL/dmean2d|, written with three
+    densification rows only)."""
+    nn = max(n, 1)
+    off = _align(4)
+    out = {}
+    for name, width in (("mean2d", 2), ("conic_o", 4), ("color", 4), ("mean2d_abs", 2)):
+        off = _align(off)
+        out[name] = ws[off:off + 4 * width * nn].view(torch.float32).view(nn, width)[:n]
+        off += 4 * width * nn
+    return out
+
+
 def focal_from_fov(fov_y_deg: float, height: int) -> float:
     return 0.5 * height / math.tan(math.radians(fov_y_deg) / 2.0)

@@ -58,6 +58,8 @@ int splat_scan_exclusive_u32(const uint32_t* in, uint32_t* out, long long n, uin
  *  - n > SPLAT_SCAN_NOALLOC_MAX_N returns SPLAT_ERR_OVERFLOW before any launch.
  *  - The first call on each device looks up the array's address (cudaGetSymbolAddress on the current
  *    device, which must be the device of in, out and stream); make that first call before any stream capture.
+ *    Every call checks that in, out and total are device memory of the current device (or managed memory)
+ *    and returns SPLAT_ERR_ARG before any launch otherwise.
  *  - Every call on a device uses the same array. Nothing in it has to start at zero (each call writes every
  *    block sum it reads), but calls whose executions overlap in time (other streams, other host threads)
  *    race on it and give wrong results: serialise them. */

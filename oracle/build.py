@@ -17,6 +17,14 @@
                              kernels (phase0/csrc/macrotile: bindings.cpp, splat2d_cpu.cpp, splat2d_fwd.cu,
                              splat2d_bwd_pixel.cu, splat2d_bwd_splat.cu, the sources and -DWITH_CUDA build of
                              phase0/splat2d/ops.py:33-45 with an sm_100a target), built the same way
+  oracle/_ref/fastergs_macro/libfastergs_macro_ref.so   the reference's own Faster-GS blend backward
+                             (blend_backward_macro_cu): its source exists only as the lines
+                             phase1/fastergs_macro.patch adds to kernels_backward.cuh, which are extracted into
+                             that folder and compiled for sm_100a with nvcc behind oracle/fastergs_macro_ref.cu,
+                             under the names oracle/fastergs_ref_config.cuh supplies
+
+The reference tree is found through --reference, the REFERENCE_ROOT environment variable, or a folder named
+"reference" beside this repository's root; without one only liboracle.so is built.
 
 Built files are git-ignored; they travel to the GPU box with the working tree.
 """
@@ -55,8 +63,8 @@ def _compile(out: Path, sources: list[Path], flags: list[str], extra_inputs: lis
 def reference_root(arg: str | None = None) -> Path | None:
     root = arg or os.environ.get("REFERENCE_ROOT")
     if root is None:
-        guess = Path("/") / "root" / "reference"
-        root = str(guess) if guess.is_dir() else None
+        sibling = HERE.parent.parent / "reference"
+        root = str(sibling) if sibling.is_dir() else None
     return Path(root) if root and Path(root).is_dir() else None
 
 
@@ -69,6 +77,7 @@ def build(reference: str | None = None) -> None:
     if ref is not None:
         build_toy2d_cuda_ref(ref)
         build_splat2d_cuda_ref(ref)
+        build_fastergs_macro_ref(ref)
         mt = ref / "phase0" / "csrc" / "macrotile"
         if (mt / "splat2d_cpu.cpp").exists():
             REF_OUT.mkdir(exist_ok=True)
@@ -116,6 +125,57 @@ def build_splat2d_cuda_ref(ref: Path) -> Path | None:
          extra_include_paths=[str(mt)], with_cuda=True, verbose=False)
     built = out_dir / f"{SPLAT2D_REF_NAME}.so"
     return built if built.exists() else None
+
+
+FASTERGS_MACRO_DIR = REF_OUT / "fastergs_macro"
+FASTERGS_MACRO_LIB = FASTERGS_MACRO_DIR / "libfastergs_macro_ref.so"
+
+
+def extract_added_lines(patch: Path, target: str) -> str:
+    """The lines a unified diff adds to the file whose path ends with ``target`` (the '+' prefix removed)."""
+    out, inside = [], False
+    for line in patch.read_text().splitlines():
+        if line.startswith("diff --git"):
+            inside = line.endswith(target)
+            continue
+        if not inside or line.startswith("+++") or line.startswith("---"):
+            continue
+        if line.startswith("+"):
+            out.append(line[1:])
+    return "\n".join(out) + "\n"
+
+
+def build_fastergs_macro_ref(ref: Path) -> Path | None:
+    """The reference's blend_backward_macro_cu, extracted from phase1/fastergs_macro.patch and compiled for sm_100a
+    into oracle/_ref/fastergs_macro/libfastergs_macro_ref.so (C entry point: oracle/fastergs_macro_ref.cu)."""
+    patch = ref / "phase1" / "fastergs_macro.patch"
+    if not patch.exists():
+        return None
+    FASTERGS_MACRO_DIR.mkdir(parents=True, exist_ok=True)
+    kernel = extract_added_lines(patch, "rasterization/include/kernels_backward.cuh")
+    if "blend_backward_macro_cu" not in kernel:
+        raise RuntimeError("phase1/fastergs_macro.patch: blend_backward_macro_cu not found in its added lines")
+    inc = FASTERGS_MACRO_DIR / "blend_backward_macro.inc"
+    if not inc.exists() or inc.read_text() != kernel:
+        inc.write_text(kernel)
+    srcs = [HERE / "fastergs_macro_ref.cu", HERE / "fastergs_ref_config.cuh", inc]
+    flags = ["-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-Xcompiler", "-fPIC", "-shared",
+             f"-I{HERE}", f"-I{FASTERGS_MACRO_DIR}"]
+    stamp = FASTERGS_MACRO_LIB.with_suffix(".so.stamp")
+    h = hashlib.sha256(" ".join(flags).encode())
+    for p in srcs:
+        h.update(p.read_bytes())
+    if FASTERGS_MACRO_LIB.exists() and stamp.exists() and stamp.read_text() == h.hexdigest():
+        return FASTERGS_MACRO_LIB
+    import shutil
+
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    cmd = [nvcc, *flags, str(HERE / "fastergs_macro_ref.cu"), "-o", str(FASTERGS_MACRO_LIB)]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"reference blend backward build failed:\n{' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+    stamp.write_text(h.hexdigest())
+    return FASTERGS_MACRO_LIB
 
 
 def main() -> int:

@@ -47,7 +47,7 @@ def load():
         lib.gs3o_preprocess_backward.argtypes = [_P] * 12
         lib.gs3o_adam.argtypes = [_P] * 4 + [ctypes.c_longlong, ctypes.c_int] + [ctypes.c_double] * 4
         for name in ("mean2d", "conic_o", "color_z", "thr", "n_touched", "point_list", "keys_sorted", "ranges",
-                     "image", "final_T", "n_contrib", "near"):
+                     "image", "final_T", "n_contrib", "near", "g_mean2d", "g_conic_o", "g_color"):
             getattr(lib, f"gs3o_{name}").restype = _P
             getattr(lib, f"gs3o_{name}").argtypes = [_P]
         _lib = lib
@@ -131,6 +131,18 @@ class Oracle:
         self.lib.gs3o_preprocess_backward(self.ctx, _ptr(p[0]), _ptr(p[1]), _ptr(p[2]), _ptr(p[3]), _ptr(p[5]),
                                           *map(_ptr, out))
         return out
+
+    def blend_backward_sums(self, grad_image: np.ndarray, bands=None) -> dict:
+        """The blend backward alone, in float64: per-Gaussian dL/dmean2d [N, 2], (dL/dA, dL/dB, dL/dC, dL/dopacity)
+        [N, 4] and dL/dcolour [N, 3] summed over tile rows [r0, r1) of ``bands`` (default: all rows)."""
+        g = np.ascontiguousarray(grad_image, np.float32)
+        self.lib.gs3o_backward_reset(self.ctx)
+        for r0, r1 in (bands or [(0, self.tiles_y)]):
+            self.lib.gs3o_blend_backward(self.ctx, _ptr(g), r0, r1)
+        n = self.n
+        return {"mean2d": self._arr("g_mean2d", np.float64, 2 * n).reshape(n, 2),
+                "conic_o": self._arr("g_conic_o", np.float64, 4 * n).reshape(n, 4),
+                "color": self._arr("g_color", np.float64, 3 * n).reshape(n, 3)}
 
     def primitives(self) -> dict:
         n = self.n

@@ -13,9 +13,10 @@
 //                   stop after T < 1e-4; image = C + T bg. A pixel is flagged "near" when one of its decisions
 //                   (alpha >= 1/255, T < 1e-4) lies within the error bound of two exp2 implementations (the
 //                   device's hardware ex2 and the C library's exp2f); counts are compared on the others
-//   blend backward  per pixel, back to front from its last contributor, T recovered by division (the
-//                   3DGS per-pixel scheme) in double precision, gradients into mean2d / conic / opacity /
-//                   colour accumulated in double
+//   blend backward  per pixel: the forward's splat set (its float alpha >= 1/255 decisions before the pixel's
+//                   contributor count), then exact float64 values of the float inputs (exponent, G, alpha, T as
+//                   the product of (1 - alpha)); back to front with T recovered by division (the 3DGS per-pixel
+//                   scheme); gradients into mean2d / conic / opacity / colour accumulated in double
 //   preprocess bwd  the analytic chain to means, scales, rotations, opacity logits, sh0, sh_rest
 //   adam            the update of cluster/patches/fastergs_lean_adam.patch:112-117
 // OpenMP parallelises over Gaussians and over tile rows; a row range [row0, row1) bounds the blend work so
@@ -412,59 +413,80 @@ void gs3o_blend_backward(gs3o_ctx* c, const float* grad_image, int row0, int row
     const size_t P = (size_t)W * H;
     row0 = std::max(row0, 0);
     row1 = std::min(row1, c->tiles_y);
-#pragma omp parallel for schedule(dynamic, 1)
-    for (int t = row0 * c->tiles_x; t < row1 * c->tiles_x; ++t) {
-        const int tx0 = (t % c->tiles_x) * kTile, ty0 = (t / c->tiles_x) * kTile;
-        const int64_t s0 = c->ranges[2 * t];
-        for (int y = ty0; y < std::min(ty0 + kTile, H); ++y)
-            for (int x = tx0; x < std::min(tx0 + kTile, W); ++x) {
-                const size_t pix = (size_t)y * W + x;
-                const double G[3] = {grad_image[pix], grad_image[P + pix], grad_image[2 * P + pix]};
-                double T = c->final_T[pix];
-                double acc[3] = {0.0, 0.0, 0.0};  // colour behind the current splat, background included, / T
-                for (int ch = 0; ch < 3; ++ch) acc[ch] = c->s.bg[ch];
-                const double pxf = x + 0.5, pyf = y + 0.5;
-                for (int64_t k = s0 + c->n_contrib[pix] - 1; k >= s0; --k) {
-                    const int64_t g = c->point_list[k];
-                    const float* co = &c->conic_o[4 * g];
-                    // same float evaluation as the forward, so the same splats pass
-                    const float dxf = c->mean2d[2 * g] - (float)pxf, dyf = c->mean2d[2 * g + 1] - (float)pyf;
-                    const float a2 = -0.5f * kLog2e * co[0], b2 = -kLog2e * co[1], c2 = -0.5f * kLog2e * co[2];
-                    const float q2 = fmaf(dxf, fmaf(a2, dxf, b2 * dyf), c2 * (dyf * dyf));
-                    const float Gs = exp2f(std::min(q2, 0.f));
-                    const float alpha_f = co[3] * Gs;
-                    if (alpha_f < kAlphaMin) continue;
-                    const double alpha = alpha_f;
-                    const double om = std::max(1.0 - alpha, kOneMinusAlphaEps);
-                    T = T / om;  // T before this splat
-                    double col[3], dot = 0.0;
-                    for (int ch = 0; ch < 3; ++ch) {
-                        col[ch] = std::max(c->color_z[4 * g + ch], 0.f);
-                        dot += G[ch] * (col[ch] - acc[ch]);
+#pragma omp parallel
+    {
+        std::vector<double> alpha_d, G_d;  // this thread's per-contributor values of one pixel
+        std::vector<int64_t> ids;
+#pragma omp for schedule(dynamic, 1)
+        for (int t = row0 * c->tiles_x; t < row1 * c->tiles_x; ++t) {
+            const int tx0 = (t % c->tiles_x) * kTile, ty0 = (t / c->tiles_x) * kTile;
+            const int64_t s0 = c->ranges[2 * t];
+            for (int y = ty0; y < std::min(ty0 + kTile, H); ++y)
+                for (int x = tx0; x < std::min(tx0 + kTile, W); ++x) {
+                    const size_t pix = (size_t)y * W + x;
+                    const double Gr[3] = {grad_image[pix], grad_image[P + pix], grad_image[2 * P + pix]};
+                    const float pxf = x + 0.5f, pyf = y + 0.5f;
+                    // The forward's splat set: its float decisions (the same evaluation as the blend) over the
+                    // positions before its contributor count. The values are then exact float64 functions of the
+                    // float inputs: the exponent -0.5 d^T K d from the float conic and offsets, G = e^min(., 0),
+                    // alpha = opacity G, and T as the product of (1 - alpha) in front.
+                    alpha_d.clear();
+                    G_d.clear();
+                    ids.clear();
+                    double T = 1.0;
+                    for (int64_t k = s0; k < s0 + c->n_contrib[pix]; ++k) {
+                        const int64_t g = c->point_list[k];
+                        const float* co = &c->conic_o[4 * g];
+                        const float dxf = c->mean2d[2 * g] - pxf, dyf = c->mean2d[2 * g + 1] - pyf;
+                        const float a2 = -0.5f * kLog2e * co[0], b2 = -kLog2e * co[1], c2 = -0.5f * kLog2e * co[2];
+                        const float q2 = fmaf(dxf, fmaf(a2, dxf, b2 * dyf), c2 * (dyf * dyf));
+                        if (co[3] * exp2f(std::min(q2, 0.f)) < kAlphaMin) continue;
+                        const double dx = (double)c->mean2d[2 * g] - (x + 0.5), dy = (double)c->mean2d[2 * g + 1] - (y + 0.5);
+                        const double pw = -0.5 * ((double)co[0] * dx * dx + 2.0 * (double)co[1] * dx * dy +
+                                                  (double)co[2] * dy * dy);
+                        const double Gs = exp(std::min(pw, 0.0));
+                        ids.push_back(g);
+                        G_d.push_back(Gs);
+                        alpha_d.push_back((double)co[3] * Gs);
+                        T *= 1.0 - alpha_d.back();
                     }
-                    const double dL_dalpha = T * dot;
-                    for (int ch = 0; ch < 3; ++ch) {
+                    double acc[3];  // colour behind the current splat, background included, / T
+                    for (int ch = 0; ch < 3; ++ch) acc[ch] = c->s.bg[ch];
+                    for (int64_t i = (int64_t)ids.size() - 1; i >= 0; --i) {
+                        const int64_t g = ids[i];
+                        const float* co = &c->conic_o[4 * g];
+                        const double alpha = alpha_d[i], Gs = G_d[i];
+                        const double om = std::max(1.0 - alpha, kOneMinusAlphaEps);
+                        T = T / om;  // T before this splat
+                        double col[3], dot = 0.0;
+                        for (int ch = 0; ch < 3; ++ch) {
+                            col[ch] = std::max(c->color_z[4 * g + ch], 0.f);
+                            dot += Gr[ch] * (col[ch] - acc[ch]);
+                        }
+                        const double dL_dalpha = T * dot;
+                        for (int ch = 0; ch < 3; ++ch) {
 #pragma omp atomic
-                        c->g_color[3 * g + ch] += G[ch] * alpha * T;
-                        acc[ch] = alpha * col[ch] + (1.0 - alpha) * acc[ch];
+                            c->g_color[3 * g + ch] += Gr[ch] * alpha * T;
+                            acc[ch] = alpha * col[ch] + (1.0 - alpha) * acc[ch];
+                        }
+                        const double dx = (double)c->mean2d[2 * g] - (x + 0.5), dy = (double)c->mean2d[2 * g + 1] - (y + 0.5);
+                        const double h = alpha * dL_dalpha;  // dL/dpower (power = -0.5 d^T K d)
+                        const double A = co[0], B = co[1], C = co[2];
+#pragma omp atomic
+                        c->g_mean2d[2 * g] += -h * (A * dx + B * dy);
+#pragma omp atomic
+                        c->g_mean2d[2 * g + 1] += -h * (B * dx + C * dy);
+#pragma omp atomic
+                        c->g_conic_o[4 * g] += -0.5 * h * dx * dx;
+#pragma omp atomic
+                        c->g_conic_o[4 * g + 1] += -h * dx * dy;
+#pragma omp atomic
+                        c->g_conic_o[4 * g + 2] += -0.5 * h * dy * dy;
+#pragma omp atomic
+                        c->g_conic_o[4 * g + 3] += Gs * dL_dalpha;
                     }
-                    const double dx = dxf, dy = dyf;
-                    const double h = alpha * dL_dalpha;  // dL/dpower (power = -0.5 d^T K d)
-                    const double A = co[0], B = co[1], C = co[2];
-#pragma omp atomic
-                    c->g_mean2d[2 * g] += -h * (A * dx + B * dy);
-#pragma omp atomic
-                    c->g_mean2d[2 * g + 1] += -h * (B * dx + C * dy);
-#pragma omp atomic
-                    c->g_conic_o[4 * g] += -0.5 * h * dx * dx;
-#pragma omp atomic
-                    c->g_conic_o[4 * g + 1] += -h * dx * dy;
-#pragma omp atomic
-                    c->g_conic_o[4 * g + 2] += -0.5 * h * dy * dy;
-#pragma omp atomic
-                    c->g_conic_o[4 * g + 3] += (double)Gs * dL_dalpha;
                 }
-            }
+        }
     }
 }
 
@@ -672,5 +694,10 @@ const float* gs3o_image(gs3o_ctx* c) { return c->image.data(); }
 const float* gs3o_final_T(gs3o_ctx* c) { return c->final_T.data(); }
 const int* gs3o_n_contrib(gs3o_ctx* c) { return c->n_contrib.data(); }
 const unsigned char* gs3o_near(gs3o_ctx* c) { return c->near.data(); }
+// The blend backward's float64 per-Gaussian sums: dL/dmean2d [N, 2], (dL/dA, dL/dB, dL/dC, dL/dopacity) [N, 4],
+// dL/dcolour [N, 3] (before the colour >= 0 mask).
+const double* gs3o_g_mean2d(gs3o_ctx* c) { return c->g_mean2d.data(); }
+const double* gs3o_g_conic_o(gs3o_ctx* c) { return c->g_conic_o.data(); }
+const double* gs3o_g_color(gs3o_ctx* c) { return c->g_color.data(); }
 
 }  // extern "C"

@@ -128,12 +128,20 @@ def test_owned_slices_tile_the_vector():
 
 
 class _FakeMulticast:
-    """Stands in for MulticastFlat on the host: a multicast address, or none, and a record of how it was closed."""
+    """Stands in for MulticastFlat on the host: allocation in the constructor, then a bind() that runs one
+    collective per buffer (as the rendezvous does) and yields a multicast address, or none; a record of how it was
+    closed."""
 
     closed: list = []
 
     def __init__(self, mc: int):
-        self.mc = mc
+        self._mc = mc
+        self.mc = 0
+
+    def bind(self) -> None:
+        t = torch.tensor([1.0])
+        dist.all_reduce(t)  # the rendezvous is a collective: a rank missing here would leave the others waiting
+        self.mc = self._mc
 
     def close(self, barrier: bool = True) -> None:
         _FakeMulticast.closed.append(barrier)
@@ -146,8 +154,8 @@ def _agree_worker(rank, world, port, q, case):
 
         def make():
             made[0] += 1
-            if case == "raises" and rank == 1 and made[0] == 2:  # the second buffer fails on one rank only
-                raise RuntimeError("no multicast object")
+            if case == "raises" and rank == 1 and made[0] == 2:  # the second allocation fails on one rank only
+                raise RuntimeError("out of memory")
             return _FakeMulticast(0 if case == "no_mc" and rank == 0 else 0x1000 * made[0])
 
         got = gdist.agree_on_buffers(make, 2)
@@ -162,9 +170,10 @@ def _agree_worker(rank, world, port, q, case):
 
 @pytest.mark.parametrize("case", ["ok", "raises", "no_mc"])
 def test_ranks_agree_on_the_multicast_buffers(case):
-    """PeerAdam's choice of the multicast form: the same answer on every rank, also when the buffers fail or lack a
-    multicast address on one rank only; what was made is closed without a barrier (a failure injected on the
-    host, in the buffer factory)."""
+    """PeerAdam's choice of the multicast form: the same answer on every rank, also when an allocation fails or a
+    buffer lacks a multicast address on one rank only; what was made is closed without a barrier. The failure is
+    injected on the host, in the buffer factory, whose bind() runs a collective as the rendezvous does: a rank
+    that skipped it while the other entered it would leave the test waiting for the process-group timeout."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()

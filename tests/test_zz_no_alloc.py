@@ -12,6 +12,7 @@ from gs_b200 import _lib as L
 pytestmark = pytest.mark.gpu
 
 MAX_N = 1 << 28  # SPLAT_SCAN_NOALLOC_MAX_N
+SPLAT_ERR_ARG = 1
 SPLAT_ERR_OVERFLOW = 3
 
 
@@ -56,3 +57,18 @@ def test_noalloc_scan_rejects_sizes_above_the_maximum(cuda):
     status = lib.splat_scan_exclusive_u32_noalloc(None, None, MAX_N + 1, None, None)
     assert status == SPLAT_ERR_OVERFLOW
     assert b"exceeds its maximum" in lib.splat_last_error()
+
+
+def test_noalloc_scan_rejects_buffers_that_are_not_on_the_current_device(cuda):
+    """The fixed array is the current device's, so host memory is refused before any launch."""
+    import ctypes
+
+    import numpy as np
+
+    lib = L.load()
+    host = np.zeros(64, dtype=np.uint32)
+    dev_out = torch.empty(64, dtype=torch.int32, device=cuda)
+    status = lib.splat_scan_exclusive_u32_noalloc(host.ctypes.data_as(ctypes.c_void_p), L.ptr(dev_out), 64, None,
+                                                  None)
+    assert status == SPLAT_ERR_ARG
+    assert b"in " in lib.splat_last_error() or b"in must" in lib.splat_last_error()
