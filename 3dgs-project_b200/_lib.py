@@ -25,6 +25,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "splat_last_error": (ctypes.c_char_p, []),
     "splat_abi_version": (_I, []),
     "splat_launch_count": (_LL, []),
+    "splat_time_kernel": (_I, [ctypes.c_char_p, _P, _P]),
     "splat_scan_workspace_size": (_SZ, [_LL]),
     "splat_scan_exclusive_u32": (_I, [_P, _P, _LL, _P, _P, _SZ, _P]),
     "splat_scan_exclusive_u32_noalloc": (_I, [_P, _P, _LL, _P, _P]),
@@ -73,6 +74,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gs3d_backward": (_I, [_P] * 7 + [_I, _LL, _P] + [_P, _SZ] * 4 + [_LL, _P, _SZ] + [_P] * 7 + [_I, _P]),
     "gs3d_backward_blend": (_I, [_P, _P, _I, _LL, _P] + [_P, _SZ] * 4 + [_LL, _P, _SZ, _I, _P]),
     "gs3d_backward_preprocess": (_I, [_P] * 5 + [_I, _P, _P, _SZ, _P, _SZ] + [_P] * 7 + [_I, _P]),
+    "gs3d_backward_preprocess_accumulate": (_I, [_P] * 5 + [_I, _P, _P, _SZ, _P, _SZ] + [_P] * 7 + [_I, _P]),
     "gs3d_backward_densification": (_I, [_I, _P, _P, _SZ, _P, _SZ, _P, _I, _P]),
     "gs3d_backward_preprocess_adam": (_I, [_P] * 6 + [_I, _P, _P, _SZ, _P, _SZ, _P, _P]),
     "adam_step_multi": (_I, [_I, _P, _I, ctypes.c_double, ctypes.c_double, ctypes.c_double, _P]),
@@ -118,6 +120,39 @@ def check_device_waits(device: torch.device) -> None:
     Costs one small synchronous copy; call it where the host already waits for the device."""
     with torch.cuda.device(device):
         call("splat_check_device_waits")
+
+
+class KernelTimer:
+    """Live device times of named kernels (splat_time_kernel): before each step, arm() hands the library a fresh
+    pair of CUDA events per kernel, which it records on the launching stream around that kernel's next launches;
+    times() returns, per kernel, the milliseconds of each armed step (the last launch of the kernel in that step)."""
+
+    def __init__(self, *kernels: str):
+        self.kernels = kernels
+        self.pairs: dict[str, list] = {k: [] for k in kernels}
+
+    def arm(self) -> None:
+        for k in self.kernels:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()  # creates the CUDA events; the library records them again around the launch
+            b.record()
+            call("splat_time_kernel", k.encode(), ctypes.c_void_p(a.cuda_event), ctypes.c_void_p(b.cuda_event))
+            self.pairs[k].append((a, b))
+
+    def stop(self) -> None:
+        for k in self.kernels:
+            call("splat_time_kernel", k.encode(), None, None)
+
+    def times(self) -> dict[str, list[float]]:
+        torch.cuda.synchronize()
+        return {k: [a.elapsed_time(b) for a, b in v] for k, v in self.pairs.items()}
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.stop()
+        return False
 
 
 def query(name: str, *args) -> int:

@@ -303,7 +303,8 @@ int adam_step_multi(int count, const adam_group* groups, int step, double beta1,
     t.count = k;
     if (blocks == 0) return SPLAT_OK;
     SPLAT_REQUIRE(blocks < (1ll << 31), "adam_step_multi: too many elements");
-    adam::k_adam<<<static_cast<unsigned int>(blocks), adam::kThreads, 0, as_stream(stream)>>>(t);
+    SPLAT_TIMED_LAUNCH("k_adam", as_stream(stream),
+                       (adam::k_adam<<<static_cast<unsigned int>(blocks), adam::kThreads, 0, as_stream(stream)>>>(t)));
     note_launch();
     return check_launch("adam_step_multi");
 }

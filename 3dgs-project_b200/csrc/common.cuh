@@ -52,6 +52,18 @@ int sm_count();
 // Counts one kernel launch of this library (every launch site calls it; read by splat_launch_count).
 void note_launch();
 
+// Records the caller's CUDA events (splat_time_kernel) on `st` just before (begin) and after (end) a launch of the
+// named kernel; a no-op unless a timer is set. `kernel` must be the literal name the timer table lists.
+void timer_mark(const char* kernel, bool begin, cudaStream_t st);
+
+// Launches `launch` (a kernel launch statement) on stream `st` between the timer marks of `name`.
+#define SPLAT_TIMED_LAUNCH(name, st, launch)    \
+    do {                                        \
+        ::splat::timer_mark(name, true, st);    \
+        launch;                                 \
+        ::splat::timer_mark(name, false, st);   \
+    } while (0)
+
 constexpr unsigned int kFullMask = 0xffffffffu;
 
 // One halving step of a warp sum of N values per lane: lanes with the `off` bit clear keep the first ceil(N/2)

@@ -786,10 +786,11 @@ int gs2d_forward(const float* means, const float* conic, const float* color, con
     const dim3 grid(tiles_x, tiles_y), block(kThreads);
     const bool save = save_buckets && num_buckets > 0;
     auto kernel = save ? k_render<true> : k_render<false>;
-    kernel<<<grid, block, 0, as_stream(stream)>>>(
-        reinterpret_cast<const int2*>(ranges), point_list, means, conic, color, opacity, bg, N,
-        static_cast<int>(num_instances), num_buckets, W, H, tiles_x, out, final_T, n_contrib, bucket_offsets,
-        save ? reinterpret_cast<float4*>(bucket_state) : nullptr);
+    SPLAT_TIMED_LAUNCH("gs2d_k_render", as_stream(stream),
+                       (kernel<<<grid, block, 0, as_stream(stream)>>>(
+                           reinterpret_cast<const int2*>(ranges), point_list, means, conic, color, opacity, bg, N,
+                           static_cast<int>(num_instances), num_buckets, W, H, tiles_x, out, final_T, n_contrib,
+                           bucket_offsets, save ? reinterpret_cast<float4*>(bucket_state) : nullptr)));
     note_launch();
     return check_launch("gs2d_forward");
 }
@@ -831,11 +832,12 @@ int gs2d_backward_splat(const float* means, const float* conic, const float* col
     SPLAT_CUDA(cudaMemsetAsync(dopacity, 0, sizeof(float) * N, st));
     if (num_buckets == 0 || num_instances == 0) return SPLAT_OK;  // zero gradients (rasterize.cu:434)
     const int tiles_x = (W + kTile - 1) / kTile;
-    k_backward_splat<<<div_up(num_buckets, kBwdWarps), 32 * kBwdWarps, 0, st>>>(
-        num_buckets, bucket_to_tile, bucket_offsets, reinterpret_cast<const int2*>(ranges), point_list, means, conic,
-        color, opacity, N, static_cast<int>(num_instances), W, H, tiles_x, out, n_contrib, dL_dout,
-        reinterpret_cast<const float4*>(bucket_state), dmeans,
-        dconic, dcolor, dopacity);
+    SPLAT_TIMED_LAUNCH("gs2d_k_backward_splat", st,
+                       (k_backward_splat<<<div_up(num_buckets, kBwdWarps), 32 * kBwdWarps, 0, st>>>(
+                           num_buckets, bucket_to_tile, bucket_offsets, reinterpret_cast<const int2*>(ranges),
+                           point_list, means, conic, color, opacity, N, static_cast<int>(num_instances), W, H,
+                           tiles_x, out, n_contrib, dL_dout, reinterpret_cast<const float4*>(bucket_state), dmeans,
+                           dconic, dcolor, dopacity)));
     note_launch();
     return check_launch("gs2d_backward_splat");
 }

@@ -239,7 +239,8 @@ struct PParams {
 // The six gradient outputs (means, scales, rotations, opacities, sh0, sh_rest) of the unfused preprocess backward.
 struct Grads {
     float* ptr[6];
-    int vec;  // the SH-rest output 16-byte aligned
+    int vec;         // the SH-rest output 16-byte aligned
+    int accumulate;  // add into the outputs instead of storing (the gradients of several views of one batch)
 };
 
 __device__ __forceinline__ void sh_backward(float x, float y, float z, int bases, const float* v, float& gx, float& gy,
@@ -459,6 +460,8 @@ __global__ void __launch_bounds__(kPbThreads, SPLAT_PB_MIN_BLOCKS) k_preprocess_
     auto emit = [&](int gi, size_t e, float g) {
         if (A.fused)
             sg[small_offset(gi) + static_cast<int>(e - static_cast<size_t>(group_width(gi, rest3)) * first)] = g;
+        else if (out.accumulate)
+            out.ptr[gi][e] += g;
         else
             out.ptr[gi][e] = g;
     };
@@ -685,7 +688,7 @@ __global__ void __launch_bounds__(kPbThreads, SPLAT_PB_MIN_BLOCKS) k_preprocess_
         emit(2, 4 * i + 1, (gx - qx * qd) * inv_n);
         emit(2, 4 * i + 2, (gy - qy * qd) * inv_n);
         emit(2, 4 * i + 3, (gz - qz * qd) * inv_n);
-    } else if (valid) {
+    } else if (valid && !out.accumulate) {  // zero gradients: nothing to add when accumulating
 #pragma unroll
         for (int k = 0; k < 3; ++k) {
             emit(0, 3 * i + k, 0.f);
@@ -705,7 +708,25 @@ __global__ void __launch_bounds__(kPbThreads, SPLAT_PB_MIN_BLOCKS) k_preprocess_
         return;
     }
     // the warp's SH-rest gradients as one contiguous block
-    if (rest3 > 0) {
+    if (rest3 > 0 && out.accumulate) {
+        if (!sh_staged) return;  // all zeros
+        float* dst = out.ptr[5] + static_cast<size_t>(first) * rest3;
+        int done = 0;
+        if (out.vec) {
+            const int n4 = nfl / 4;
+            for (int k = lane; k < n4; k += 32) {
+                float4 d = reinterpret_cast<float4*>(dst)[k];
+                const float4 a = reinterpret_cast<const float4*>(sh)[k];
+                d.x += a.x;
+                d.y += a.y;
+                d.z += a.z;
+                d.w += a.w;
+                reinterpret_cast<float4*>(dst)[k] = d;
+            }
+            done = n4 * 4;
+        }
+        for (int k = done + lane; k < nfl; k += 32) dst[k] += sh[k];
+    } else if (rest3 > 0) {
         float* dst = out.ptr[5] + static_cast<size_t>(first) * rest3;
         int done = 0;
         if (out.vec) {
@@ -768,22 +789,23 @@ int gs3d_backward_blend(const float* grad_image, const float* image, int n, long
         const long long blocks = std::min<long long>(static_cast<long long>(sm_count()) * SPLAT_BWD_MIN_BLOCKS,
                                                      div_up(bucket_capacity, kBwdWarps));
         auto kernel = abs_grad ? k_blend_backward<true> : k_blend_backward<false>;
-        kernel<<<static_cast<unsigned>(blocks), 32 * kBwdWarps, 0, st>>>(
-            cam, pb.counters, bb.reached, acc.work, bb.tile, tb.ranges, tb.bstart, tb.max_contrib, ib.point_list,
-            pb.mean2d, pb.conic_o, pb.color_z, pb.rect, grad_image, image, tb.n_contrib, bb.ckpt, n,
-            static_cast<int>(m), bucket_capacity, acc);
+        SPLAT_TIMED_LAUNCH("k_blend_backward", st,
+                           (kernel<<<static_cast<unsigned>(blocks), 32 * kBwdWarps, 0, st>>>(
+                               cam, pb.counters, bb.reached, acc.work, bb.tile, tb.ranges, tb.bstart, tb.max_contrib,
+                               ib.point_list, pb.mean2d, pb.conic_o, pb.color_z, pb.rect, grad_image, image,
+                               tb.n_contrib, bb.ckpt, n, static_cast<int>(m), bucket_capacity, acc)));
         note_launch();
         SPLAT_TRY(check_launch("gs3d_blend_backward"));
     }
     return SPLAT_OK;
 }
 
-int gs3d_backward_preprocess(const float* means, const float* scales, const float* rotations,
-                             const float* opacities, const float* sh_rest, int n, const gs3d_settings* settings,
-                             void* prim_buf, size_t prim_bytes_, void* workspace, size_t workspace_bytes,
-                             float* grad_means, float* grad_scales, float* grad_rotations, float* grad_opacities,
-                             float* grad_sh0, float* grad_sh_rest, float* densification_info,
-                             int densification_rows, void* stream) {
+namespace {
+int preprocess_backward(const float* means, const float* scales, const float* rotations, const float* opacities,
+                        const float* sh_rest, int n, const gs3d_settings* settings, void* prim_buf, size_t prim_bytes_,
+                        void* workspace, size_t workspace_bytes, float* grad_means, float* grad_scales,
+                        float* grad_rotations, float* grad_opacities, float* grad_sh0, float* grad_sh_rest,
+                        float* densification_info, int densification_rows, int accumulate, void* stream) {
     Cam cam;
     SPLAT_TRY(fill_cam(settings, cam));
     SPLAT_REQUIRE(n >= 0, "gs3d_backward: bad size n=%d", n);
@@ -797,16 +819,41 @@ int gs3d_backward_preprocess(const float* means, const float* scales, const floa
     PrimBuffers pb = carve_prim(cp, n);
     GradAcc acc = carve_grad(cw, n);
     PParams P{means, scales, rotations, opacities, sh_rest, settings->w2c, settings->cam_position, n};
-    Grads g{{grad_means, grad_scales, grad_rotations, grad_opacities, grad_sh0, grad_sh_rest}, 0};
+    Grads g{{grad_means, grad_scales, grad_rotations, grad_opacities, grad_sh0, grad_sh_rest}, 0, accumulate};
     for (int gi = 0; gi < 6; ++gi)
         SPLAT_REQUIRE(g.ptr[gi] || (gi == 5 && cam.rest_bases == 0), "gs3d_backward: gradient output %d is null", gi);
     g.vec = (reinterpret_cast<uintptr_t>(grad_sh_rest) & 15u) == 0;
     const size_t smem = static_cast<size_t>(kPbWarps) * 32 * cam.rest_bases * 3 * sizeof(float);
     const Densification dens{densification_info, densification_rows};
-    k_preprocess_backward<<<div_up(n, kPbThreads), kPbThreads, smem, as_stream(stream)>>>(P, cam, pb, acc, g, dens,
-                                                                                           AdamArgs{});
+    SPLAT_TIMED_LAUNCH("k_preprocess_backward", as_stream(stream),
+                       (k_preprocess_backward<<<div_up(n, kPbThreads), kPbThreads, smem, as_stream(stream)>>>(
+                           P, cam, pb, acc, g, dens, AdamArgs{})));
     note_launch();
     return check_launch("gs3d_preprocess_backward");
+}
+}  // namespace
+
+int gs3d_backward_preprocess(const float* means, const float* scales, const float* rotations,
+                             const float* opacities, const float* sh_rest, int n, const gs3d_settings* settings,
+                             void* prim_buf, size_t prim_bytes_, void* workspace, size_t workspace_bytes,
+                             float* grad_means, float* grad_scales, float* grad_rotations, float* grad_opacities,
+                             float* grad_sh0, float* grad_sh_rest, float* densification_info,
+                             int densification_rows, void* stream) {
+    return preprocess_backward(means, scales, rotations, opacities, sh_rest, n, settings, prim_buf, prim_bytes_,
+                               workspace, workspace_bytes, grad_means, grad_scales, grad_rotations, grad_opacities,
+                               grad_sh0, grad_sh_rest, densification_info, densification_rows, 0, stream);
+}
+
+int gs3d_backward_preprocess_accumulate(const float* means, const float* scales, const float* rotations,
+                                        const float* opacities, const float* sh_rest, int n,
+                                        const gs3d_settings* settings, void* prim_buf, size_t prim_bytes_,
+                                        void* workspace, size_t workspace_bytes, float* grad_means,
+                                        float* grad_scales, float* grad_rotations, float* grad_opacities,
+                                        float* grad_sh0, float* grad_sh_rest, float* densification_info,
+                                        int densification_rows, void* stream) {
+    return preprocess_backward(means, scales, rotations, opacities, sh_rest, n, settings, prim_buf, prim_bytes_,
+                               workspace, workspace_bytes, grad_means, grad_scales, grad_rotations, grad_opacities,
+                               grad_sh0, grad_sh_rest, densification_info, densification_rows, 1, stream);
 }
 
 int gs3d_backward_densification(int n, const gs3d_settings* settings, void* prim_buf, size_t prim_bytes_,

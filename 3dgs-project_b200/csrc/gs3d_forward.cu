@@ -657,7 +657,7 @@ int bin_instances(int n, long long m, const Cam& cam, const PrimBuffers& pb, con
                   cudaStream_t st) {
     const int T = cam.tiles_x * cam.tiles_y;
     if (m > 0) {
-        k_duplicate<<<div_up(n, kDupThreads), kDupThreads, 0, st>>>(n, cam, pb, ib);
+        SPLAT_TIMED_LAUNCH("k_duplicate", st, (k_duplicate<<<div_up(n, kDupThreads), kDupThreads, 0, st>>>(n, cam, pb, ib)));
         note_launch();
         SPLAT_TRY(check_launch("gs3d_duplicate"));
         // the tile-digit passes (the pad key T needs bit_width(T) bits)
@@ -714,7 +714,7 @@ int gs3d_preprocess_count(const float* means, const float* scales, const float* 
                                             kPreWarps * 32 * kMaxRestBases * 3 * static_cast<int>(sizeof(float))));
             configured = true;
         }
-        k_preprocess<<<div_up(n, kPreThreads), kPreThreads, smem, st>>>(P, cam, pb);
+        SPLAT_TIMED_LAUNCH("k_preprocess", st, (k_preprocess<<<div_up(n, kPreThreads), kPreThreads, smem, st>>>(P, cam, pb)));
         note_launch();
         SPLAT_TRY(check_launch("gs3d_preprocess"));
         k_count_instances<<<div_up(n, kCountThreads * kCountItems), kCountThreads, 0, st>>>(pb.n_touched, n,
@@ -771,10 +771,11 @@ int gs3d_render(int n, long long num_instances, const gs3d_settings* settings, v
     BucketBuffers bb = carve_bucket(cb, bucket_capacity);
     SPLAT_CUDA(cudaMemsetAsync(pb.counters + 2, 0, sizeof(uint32_t), st));  // k_blend counts the replayed buckets
     SPLAT_TRY(bin_instances(n, m, cam, pb, tb, ib, bucket_capacity, bb.tile, pb.counters + 1, st));
-    k_blend<true><<<T, kTilePixels / 2, 0, st>>>(cam, tb.ranges, tb.bstart, ib.point_list, pb.mean2d, pb.conic_o,
-                                                 pb.color_z, pb.rect, settings->bg, image, tb.final_T, tb.n_contrib,
-                                                 tb.max_contrib, bb.ckpt, pb.counters, bb.reached, n < 1 ? 1 : n,
-                                                 static_cast<int>(m), bucket_capacity);
+    SPLAT_TIMED_LAUNCH("k_blend", st,
+                       (k_blend<true><<<T, kTilePixels / 2, 0, st>>>(
+                           cam, tb.ranges, tb.bstart, ib.point_list, pb.mean2d, pb.conic_o, pb.color_z, pb.rect,
+                           settings->bg, image, tb.final_T, tb.n_contrib, tb.max_contrib, bb.ckpt, pb.counters,
+                           bb.reached, n < 1 ? 1 : n, static_cast<int>(m), bucket_capacity)));
     note_launch();
     return check_launch("gs3d_blend");
 }
@@ -797,9 +798,11 @@ int gs3d_render_inference(int n, long long num_instances, const gs3d_settings* s
     TileBuffers tb = carve_tile(ct, cam.width, cam.height);
     InstBuffers ib = carve_inst(ci, m);
     SPLAT_TRY(bin_instances(n, m, cam, pb, tb, ib, 0, nullptr, nullptr, st));
-    k_blend<false><<<T, kTilePixels / 2, 0, st>>>(cam, tb.ranges, nullptr, ib.point_list, pb.mean2d, pb.conic_o,
-                                                  pb.color_z, pb.rect, settings->bg, image, nullptr, nullptr, nullptr,
-                                                  nullptr, nullptr, nullptr, n < 1 ? 1 : n, static_cast<int>(m), 0);
+    SPLAT_TIMED_LAUNCH("k_blend", st,
+                       (k_blend<false><<<T, kTilePixels / 2, 0, st>>>(
+                           cam, tb.ranges, nullptr, ib.point_list, pb.mean2d, pb.conic_o, pb.color_z, pb.rect,
+                           settings->bg, image, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                           n < 1 ? 1 : n, static_cast<int>(m), 0)));
     note_launch();
     return check_launch("gs3d_blend_inference");
 }

@@ -210,8 +210,7 @@ class PeerAdam:
     (G + 1) / G slices-worth of the vector against 2 (G - 1) / G for peer loads and stores: more at G = 2 (1.5 vs
     1), fewer from G = 4 on (1.25 vs 1.5; 1.125 vs 1.75 at G = 8). Measured on the 3M-Gaussian C3 scene: at G = 2
     1.84 ms multicast against 1.17 ms peer; at G = 4 1.73 ms multicast (513 GB/s per direction) against 1.84 ms
-    peer (577 GB/s). The default is therefore the multicast form from 4 ranks on and peer loads / stores below;
-    the SPLAT_NVLS environment variable ("0" / "1") overrides it.
+    peer (577 GB/s). Without an explicit `nvls`, the form exchange_for() picks for the rank count is taken.
     """
 
     def __init__(self, tensors, lrs, group=None, betas=(0.9, 0.999), eps: float = 1e-15, nvls: bool | None = None):
@@ -228,10 +227,7 @@ class PeerAdam:
         sizes = [t.numel() for t in tensors]
         self.total = sum(sizes)
         if nvls is None:
-            import os
-
-            env = os.environ.get("SPLAT_NVLS")
-            nvls = (env == "1") if env in ("0", "1") else self.world >= 4
+            nvls = exchange_for(self.world) == "nvls"
         self.nvls = False
         if nvls and self.world > 1:
             padded = (self.total + 3) // 4 * 4  # the multicast kernel moves whole 16-byte groups
@@ -289,6 +285,93 @@ class PeerAdam:
         self.params = self.grads = []
         self.param_buf.close()
         self.grad_buf.close()
+
+
+class NcclAdam:
+    """PeerAdam's step through NCCL collectives, for comparison and for nodes without peer access: a reduce-scatter
+    of the flat gradient vector (rank r receives the summed slice it owns), Adam on that slice with the slice's
+    moments (the exchange kernels' segmented Adam on one rank: adam_step_dp_fused with G = 1), and an all-gather
+    of the updated parameter slices into every rank's flat parameter vector. The same interface as PeerAdam
+    (`params`, `grads` as per-group views of flat buffers, step(), close()); the vector is padded to G equal
+    slices of a multiple of 4 elements. Gradient sums follow NCCL's reduction order (at G = 2 one addition, the
+    same bits as PeerAdam)."""
+
+    def __init__(self, tensors, lrs, group=None, betas=(0.9, 0.999), eps: float = 1e-15):
+        from . import _lib as L
+
+        self._L = L
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        dev = tensors[0].device
+        self.shapes = [tuple(t.shape) for t in tensors]
+        sizes = [t.numel() for t in tensors]
+        self.total = sum(sizes)
+        self.chunk = ((self.total + self.world - 1) // self.world + 3) // 4 * 4
+        padded = self.chunk * self.world
+        self.param_flat = torch.zeros(padded, dtype=torch.float32, device=dev)
+        self.grad_flat = torch.zeros(padded, dtype=torch.float32, device=dev)
+        self.params, self.grads, self.segments, off = [], [], [], 0
+        for t, n, lr in zip(tensors, sizes, lrs):
+            pv = self.param_flat[off:off + n].view(t.shape)
+            pv.copy_(t.detach())
+            self.params.append(pv)
+            self.grads.append(self.grad_flat[off:off + n].view(t.shape))
+            self.segments.append((off, off + n, float(lr)))
+            off += n
+        self.lo = self.rank * self.chunk
+        self.hi = min(self.lo + self.chunk, self.total) if self.lo < self.total else self.lo
+        self.grad_slice = torch.zeros(self.chunk, dtype=torch.float32, device=dev)
+        self.exp_avg = torch.zeros(self.chunk, dtype=torch.float32, device=dev)
+        self.exp_avg_sq = torch.zeros_like(self.exp_avg)
+        self.betas, self.eps, self.t = betas, eps, 0
+        self._seg = (_Segment * len(self.segments))(*[_Segment(a, b, lr) for a, b, lr in self.segments])
+        # The kernel reads gradient element e (lo <= e < hi) at grads[0] + e: the slice's base, moved back by lo.
+        self._gptr = (ctypes.c_void_p * 8)(self.grad_slice.data_ptr() - 4 * self.lo)
+        self._pptr = (ctypes.c_void_p * 8)(self.param_flat.data_ptr())
+        dist.barrier(group=group)
+
+    @torch.no_grad()
+    def step(self, grads=None) -> None:
+        if grads is not None:
+            for v, g in zip(self.grads, grads):
+                v.copy_(g.reshape(v.shape))
+        self.t += 1
+        dist.reduce_scatter_tensor(self.grad_slice, self.grad_flat, op=dist.ReduceOp.SUM, group=self.group)
+        stream = torch.cuda.current_stream(self.exp_avg.device).cuda_stream
+        self._L.call("adam_step_dp_fused", 1, 0, ctypes.addressof(self._gptr), ctypes.addressof(self._pptr), self.lo,
+                     self.hi, self._L.ptr(self.exp_avg), self._L.ptr(self.exp_avg_sq), len(self.segments),
+                     ctypes.addressof(self._seg), self.t, float(self.betas[0]), float(self.betas[1]), float(self.eps),
+                     stream)
+        mine = self.param_flat[self.rank * self.chunk:(self.rank + 1) * self.chunk]
+        dist.all_gather_into_tensor(self.param_flat, mine, group=self.group)
+
+    def close(self) -> None:
+        torch.cuda.synchronize()
+        self.params = self.grads = []
+
+
+def exchange_for(world: int, form: str = "auto") -> str:
+    """The exchange form a step of `world` ranks uses: "peer" (peer loads and stores, adam_step_dp_fused), "nvls"
+    (NVLink multicast, adam_step_dp_nvls) or "nccl" (NcclAdam). "auto" picks the form measured fastest at that
+    rank count on this pool's B200 nodes (see DESIGN)."""
+    if form != "auto":
+        if form not in ("peer", "nvls", "nccl"):
+            raise ValueError(f"unknown exchange form {form!r}")
+        return form
+    return AUTO_EXCHANGE.get(world, "nvls" if world >= 4 else "peer")
+
+
+# The fastest form per rank count, measured on the C3 training step (3M Gaussians: a 708 MB vector).
+AUTO_EXCHANGE = {2: "peer", 4: "nvls", 8: "nvls"}
+
+
+def make_exchange(tensors, lrs, form: str = "auto", group=None, betas=(0.9, 0.999), eps: float = 1e-15):
+    """PeerAdam (peer or multicast form) or NcclAdam for the replicated parameter tensors, by exchange_for()."""
+    kind = exchange_for(dist.get_world_size(group), form)
+    if kind == "nccl":
+        return NcclAdam(tensors, lrs, group=group, betas=betas, eps=eps)
+    return PeerAdam(tensors, lrs, group=group, betas=betas, eps=eps, nvls=(kind == "nvls"))
 
 
 class _Segment(ctypes.Structure):

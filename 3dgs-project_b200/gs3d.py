@@ -182,12 +182,14 @@ def forward(means, scales, rotations, opacities, sh0, sh_rest, w2c, cam_position
 def backward(densification_info, grad_image, image, means, scales, rotations, opacities, sh_rest, prim_buf,
              tile_buf, inst_buf, bucket_buf, w2c, cam_position, bg_color, active_sh_bases, width, height, focal_x,
              focal_y, center_x, center_y, near_plane, far_plane, proper_antialiasing, n_instances, n_buckets,
-             selector, *mode, out: tuple | None = None, stage_event: torch.cuda.Event | None = None):
+             selector, *mode, out: tuple | None = None, stage_event: torch.cuda.Event | None = None,
+             accumulate: bool = False):
     """Faster-GS `_C.backward` (the trailing blend-backward mode of the phase1 patch is accepted and ignored:
     there is one blend backward here). Returns (means, scales, rotations, opacities[N,1], sh0[N,1,3], sh_rest) and
     accumulates densification_info ([0 | 2 | 3, N]) in place: visible count, |dL/dmean2d| in normalised device
     units, and with three rows the norm of the summed per-pixel absolute mean2d gradients.
-    ``out`` may supply the six contiguous float32 result tensors (e.g. views of one flat gradient buffer).
+    ``out`` may supply the six contiguous float32 result tensors (e.g. views of one flat gradient buffer);
+    with ``accumulate`` the gradients are added into them (the views of one batch into one buffer).
     It runs as its two launches (gs3d_backward_blend, gs3d_backward_preprocess); ``stage_event``, if given, is
     recorded on the stream between them."""
     pending = backward_blend(densification_info, grad_image, image, means, scales, rotations, opacities, sh_rest,
@@ -196,7 +198,7 @@ def backward(densification_info, grad_image, image, means, scales, rotations, op
                              proper_antialiasing, n_instances, n_buckets, selector, defer_densification=True)
     if stage_event is not None:
         stage_event.record(torch.cuda.current_stream(means.device))
-    return pending.preprocess(out=out)
+    return pending.preprocess(out=out, accumulate=accumulate)
 
 
 class PendingBackward:
@@ -209,9 +211,12 @@ class PendingBackward:
         self.means, self.scales, self.rotations, self.opacities, self.sh_rest = tensors
         self.n, self.rest, self.rows, self.dinfo, self.stream = n, rest, rows, dinfo, stream
 
-    def preprocess(self, out: tuple | None = None) -> tuple:
+    def preprocess(self, out: tuple | None = None, accumulate: bool = False) -> tuple:
         """The six parameter gradients (gs3d_backward_preprocess), with the densification rows when they were
-        deferred to this call."""
+        deferred to this call. accumulate (with ``out``): add them into ``out`` instead
+        (gs3d_backward_preprocess_accumulate), as the views of one batch do."""
+        if accumulate and out is None:
+            raise RuntimeError("accumulate needs the out tensors to add into")
         n, rest, dev = self.n, self.rest, self.means.device
         if out is not None:
             grads = tuple(out)
@@ -223,7 +228,8 @@ class PendingBackward:
             grads = (torch.empty(n, 3, device=dev), torch.empty(n, 3, device=dev), torch.empty(n, 4, device=dev),
                      torch.empty(n, 1, device=dev), torch.empty(n, 1, 3, device=dev),
                      torch.empty(n, rest, 3, device=dev))
-        L.call("gs3d_backward_preprocess", L.ptr(self.means), L.ptr(self.scales), L.ptr(self.rotations),
+        L.call("gs3d_backward_preprocess_accumulate" if accumulate else "gs3d_backward_preprocess",
+               L.ptr(self.means), L.ptr(self.scales), L.ptr(self.rotations),
                L.ptr(self.opacities), L.ptr(self.sh_rest), n, ctypes.byref(self.s), L.ptr(self.prim),
                self.prim.numel(), L.ptr(self.ws), self.ws.numel(), *map(L.ptr, grads), L.ptr(self.dinfo), self.rows,
                self.stream)

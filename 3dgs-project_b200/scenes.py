@@ -47,6 +47,24 @@ def gs2d_c1(seed: int = 0) -> dict:
                 depth=depth, target=sinusoid_target(H, W, seed + 1))
 
 
+def splat2d_bench_scene(n: int, h: int, w: int, seed: int = 0, sigma=(2.0, 10.0), opacity=(0.05, 0.6)):
+    """The scene generator of the reference's splat2d backward benchmark (bench/phase0/backward_bench.py:35-49):
+    float64 means over the image +-2%, Cholesky factors of per-axis sigma in [2, 10] px with a bounded shear,
+    opacity logits of U(0.05, 0.6), colours U(0, 1); index order is depth order."""
+    g = torch.Generator().manual_seed(seed)
+
+    def u(lo, hi, *shape):
+        return lo + (hi - lo) * torch.rand(*shape, generator=g, dtype=torch.float64)
+
+    means = torch.stack([u(-0.02 * w, 1.02 * w, n), u(-0.02 * h, 1.02 * h, n)], dim=-1)
+    l0 = 1.0 / u(sigma[0], sigma[1], n)
+    l2 = 1.0 / u(sigma[0], sigma[1], n)
+    l1 = u(-0.5, 0.5, n) * torch.minimum(l0, l2)
+    o = u(opacity[0], opacity[1], n)
+    colors = u(0.0, 1.0, n, 3)
+    return means, torch.stack([l0, l1, l2], dim=-1), torch.log(o / (1.0 - o)), colors
+
+
 # ---------------------------------------------------------------------------------------------
 # 3DGS scenes
 # ---------------------------------------------------------------------------------------------

@@ -39,6 +39,13 @@ int splat_abi_version(void);
 /* Kernels this library has launched in this process so far (all threads and devices). No counterpart in
  * the reference; benchmarks read it before and after a timed region. */
 long long splat_launch_count(void);
+/* Kernel timing for benchmarks (no counterpart in the reference): until called again for the same kernel, the
+ * library records begin_event just before and end_event just after every launch of `kernel`, on the stream it
+ * launches on (cudaEvent_t handles created by the caller, passed as void*; NULL events stop the timing). Kernels:
+ * "k_preprocess", "k_duplicate", "k_blend" (training and render-only forward), "k_blend_backward",
+ * "k_preprocess_backward", "k_adam", "gs2d_k_render" (gs2d forward), "gs2d_k_backward_splat". At most four
+ * kernels at once. The events are re-recorded by every launch: read them before the kernel runs again. */
+int splat_time_kernel(const char* kernel, void* begin_event, void* end_event);
 
 /* ---------------------------------------------------------------------------------------------
  * Device-wide primitives (replace the CUB DeviceScan / DeviceRadixSort calls inside Faster-GS's
@@ -253,6 +260,17 @@ int gs3d_backward_preprocess(const float* means, const float* scales, const floa
                              float* grad_means, float* grad_scales, float* grad_rotations, float* grad_opacities,
                              float* grad_sh0, float* grad_sh_rest, float* densification_info,
                              int densification_rows, void* stream);
+/* gs3d_backward_preprocess adding its gradients into the six outputs instead of storing them (no counterpart in
+ * the reference, whose multi-view batches sum the views' gradients in autograd): the gradients of a batch's
+ * views accumulate in one buffer, one view after the other on one stream. Gaussians a view does not see add
+ * nothing (their zeros are not written). */
+int gs3d_backward_preprocess_accumulate(const float* means, const float* scales, const float* rotations,
+                                        const float* opacities, const float* sh_rest, int n,
+                                        const gs3d_settings* settings, void* prim_buf, size_t prim_bytes,
+                                        void* workspace, size_t workspace_bytes, float* grad_means,
+                                        float* grad_scales, float* grad_rotations, float* grad_opacities,
+                                        float* grad_sh0, float* grad_sh_rest, float* densification_info,
+                                        int densification_rows, void* stream);
 /* The densification rows of gs3d_backward_preprocess alone, from the blend backward's workspace (the same
  * arithmetic, so the rows equal those gs3d_backward_preprocess accumulates). For callers that defer the
  * preprocess backward to gs3d_backward_preprocess_adam but read the statistics before the optimizer step. */

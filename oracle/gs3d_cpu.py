@@ -44,6 +44,7 @@ def load():
         lib.gs3o_blend.argtypes = [_P, ctypes.c_int, ctypes.c_int]
         lib.gs3o_backward_reset.argtypes = [_P]
         lib.gs3o_blend_backward.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int]
+        lib.gs3o_blend_backward_fast.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int]
         lib.gs3o_preprocess_backward.argtypes = [_P] * 12
         lib.gs3o_adam.argtypes = [_P] * 4 + [ctypes.c_longlong, ctypes.c_int] + [ctypes.c_double] * 4
         for name in ("mean2d", "conic_o", "color_z", "thr", "n_touched", "point_list", "keys_sorted", "ranges",
@@ -165,69 +166,101 @@ class Oracle:
                 "near": self._arr("near", np.uint8, P).reshape(self.H, self.W).astype(bool)}
 
 
-def time_training_step(sc: dict, cam: dict, budget_s: float = 20.0) -> dict:
-    """One training step of one view on the CPU: preprocess, binning, blend and blend backward over a band of
-    tile rows (grown until about ``budget_s`` of work), preprocess backward, Adam over every parameter.
-    The blend parts are extrapolated from the band to the whole view."""
-    import torch
+def use_all_threads(threads: int | None = None) -> int:
+    """Sets the oracle's OpenMP thread count (default: every host CPU; torch.distributed.run sets OMP_NUM_THREADS=1,
+    which would otherwise leave it single-threaded) and returns the count now in effect."""
+    lib = load()
+    lib.gs3o_set_threads(int(threads or os.cpu_count() or 1))
+    return int(lib.gs3o_threads())
 
-    params = [sc[k].numpy() if torch.is_tensor(sc[k]) else sc[k]
-              for k in ("means", "scales", "rotations", "opacities", "sh0", "sh_rest")]
-    o = Oracle(params, {k: (v.numpy() if torch.is_tensor(v) else v) for k, v in cam.items()}, sc["active_sh_bases"])
-    threads = o.lib.gs3o_threads()
-    t0 = time.perf_counter()
-    o.preprocess()
-    t1 = time.perf_counter()
-    o.bin()
-    t2 = time.perf_counter()
-    rng = np.random.default_rng(0)
-    grad = (1e-3 * rng.standard_normal((3, o.H, o.W))).astype(np.float32)
-    # blend + backward over growing bands from the middle of the image
-    mid = o.tiles_y // 2
-    rows, blend_s = 0, 0.0
-    band = 1
-    while True:
-        r0 = max(mid - band // 2, 0)
-        r1 = min(r0 + band, o.tiles_y)
-        ta = time.perf_counter()
-        o.blend(r0, r1)
+
+class TrainingStepSample:
+    """One training step of one view on the CPU, on a bounded sample: preprocess, binning, preprocess backward and
+    Adam over every parameter in full; blend + blend backward on ``rows`` tile rows spread evenly over the image,
+    extrapolated to the whole view. Gradient outputs and optimiser state are allocated and touched once,
+    untimed, as a training loop holds them."""
+
+    def __init__(self, sc: dict, cam: dict, threads: int | None = None):
+        import torch
+
+        self.threads = use_all_threads(threads)
+        params = [sc[k].numpy() if torch.is_tensor(sc[k]) else sc[k]
+                  for k in ("means", "scales", "rotations", "opacities", "sh0", "sh_rest")]
+        self.o = Oracle(params, {k: (v.numpy() if torch.is_tensor(v) else v) for k, v in cam.items()},
+                        sc["active_sh_bases"])
+        o = self.o
+        rng = np.random.default_rng(0)
+        self.grad = (1e-3 * rng.standard_normal((3, o.H, o.W))).astype(np.float32)
+        n, rest = o.n, o.rest
+        self.out = [np.zeros((n, 3), np.float32), np.zeros((n, 3), np.float32), np.zeros((n, 4), np.float32),
+                    np.zeros((n, 1), np.float32), np.zeros((n, 1, 3), np.float32), np.zeros((n, rest, 3), np.float32)]
+        self.state = []
+        for prm in o.params:
+            q, m, v = prm.copy(), np.empty_like(prm), np.empty_like(prm)
+            m.fill(0.0)
+            v.fill(0.0)
+            self.state.append((q, m, v))
+        self.rows = 1
+        self.t = 0
+
+    def step(self) -> dict:
+        o, p = self.o, self.o.params
+        t0 = time.perf_counter()
+        o.preprocess()
+        t1 = time.perf_counter()
+        o.bin()
+        t2 = time.perf_counter()
+        rows = self.sample_rows()
+        for r in rows:
+            o.blend(r, r + 1)
         o.lib.gs3o_backward_reset(o.ctx)
-        o.lib.gs3o_blend_backward(o.ctx, _ptr(grad), r0, r1)
-        tb = time.perf_counter()
-        rows, blend_s = r1 - r0, tb - ta
-        if tb - t0 > budget_s * 0.6 or r1 - r0 >= o.tiles_y:
-            break
-        band = min(band * 2, o.tiles_y)
-    # gradient outputs and optimiser state exist before a training step: allocate and touch them untimed
-    n, rest = o.n, o.rest
-    out = [np.zeros((n, 3), np.float32), np.zeros((n, 3), np.float32), np.zeros((n, 4), np.float32),
-           np.zeros((n, 1), np.float32), np.zeros((n, 1, 3), np.float32), np.zeros((n, rest, 3), np.float32)]
-    for a in out:
-        a.fill(0.0)
-    p = o.params
-    state = []
-    for prm in p:
-        q, m, v = prm.copy(), np.empty_like(prm), np.empty_like(prm)
-        m.fill(0.0)
-        v.fill(0.0)
-        state.append((q, m, v))
-    t3 = time.perf_counter()
-    o.lib.gs3o_preprocess_backward(o.ctx, _ptr(p[0]), _ptr(p[1]), _ptr(p[2]), _ptr(p[3]), _ptr(p[5]),
-                                   *map(_ptr, out))
-    t4 = time.perf_counter()
-    for (q, m, v), g in zip(state, out):
-        o.lib.gs3o_adam(_ptr(q), _ptr(g), _ptr(m), _ptr(v), q.size, 1, 1e-3, 0.9, 0.999, 1e-15)
-    t5 = time.perf_counter()
-    full_blend = blend_s * o.tiles_y / max(rows, 1)
-    step_s = (t1 - t0) + (t2 - t1) + full_blend + (t4 - t3) + (t5 - t4)
-    return {"value": round(1.0 / step_s, 5), "unit": "views/s", "cores": threads, "kind": "port",
-            "sample": f"one training step of one {o.W}x{o.H} view, {n} Gaussians: preprocess, binning "
-                      f"({o.m} instances), preprocess backward and Adam in full; blend + blend backward on "
-                      f"{rows} of {o.tiles_y} tile rows ({blend_s:.2f} s), scaled to the whole view",
-            "seconds": {"preprocess": round(t1 - t0, 3), "binning": round(t2 - t1, 3),
-                        "blend_fwd_bwd_full_view_est": round(full_blend, 3),
-                        "preprocess_backward": round(t4 - t3, 3), "adam": round(t5 - t4, 3)},
-            "threads": os.cpu_count()}
+        for r in rows:
+            o.lib.gs3o_blend_backward_fast(o.ctx, _ptr(self.grad), r, r + 1)
+        t3 = time.perf_counter()
+        o.lib.gs3o_preprocess_backward(o.ctx, _ptr(p[0]), _ptr(p[1]), _ptr(p[2]), _ptr(p[3]), _ptr(p[5]),
+                                       *map(_ptr, self.out))
+        t4 = time.perf_counter()
+        self.t += 1
+        for (q, m, v), g in zip(self.state, self.out):
+            o.lib.gs3o_adam(_ptr(q), _ptr(g), _ptr(m), _ptr(v), q.size, self.t, 1e-3, 0.9, 0.999, 1e-15)
+        t5 = time.perf_counter()
+        blend_full = (t3 - t2) * o.tiles_y / len(rows)
+        parts = {"preprocess": t1 - t0, "binning": t2 - t1, "blend_fwd_bwd_band": t3 - t2,
+                 "blend_fwd_bwd_full_view_est": blend_full, "preprocess_backward": t4 - t3, "adam": t5 - t4}
+        return {"seconds": (t1 - t0) + (t2 - t1) + blend_full + (t4 - t3) + (t5 - t4), "parts": parts,
+                "rows": len(rows), "instances": o.m}
+
+    def sample_rows(self) -> list[int]:
+        """``rows`` tile rows spread evenly over the image (the middle of each of ``rows`` equal bands), so the
+        sample's blend cost is an unbiased estimate of the view's."""
+        ty = self.o.tiles_y
+        k = min(max(self.rows, 1), ty)
+        return sorted({min(int((i + 0.5) * ty / k), ty - 1) for i in range(k)})
+
+    def calibrate(self, target_s: float) -> dict:
+        """One step on one tile row, then the band widened so that a step takes about ``target_s``."""
+        self.rows = 1
+        s = self.step()
+        fixed = s["seconds"] - s["parts"]["blend_fwd_bwd_full_view_est"]
+        per_row = max(s["parts"]["blend_fwd_bwd_band"], 1e-6)
+        self.rows = int(min(max((target_s - fixed) / per_row, 1), self.o.tiles_y))
+        return s
+
+    def describe(self) -> str:
+        o = self.o
+        return (f"one training step of one {o.W}x{o.H} view, {o.n} Gaussians: preprocess, binning ({o.m} instances), "
+                f"preprocess backward and Adam in full; blend + blend backward on {len(self.sample_rows())} of "
+                f"{o.tiles_y} tile rows spread evenly over the image, scaled to the whole view")
+
+
+def time_training_step(sc: dict, cam: dict, budget_s: float = 20.0) -> dict:
+    """One training step of one view on the CPU (TrainingStepSample), its band sized for about ``budget_s``."""
+    smp = TrainingStepSample(sc, cam)
+    smp.calibrate(budget_s * 0.6)
+    res = smp.step()
+    return {"value": round(1.0 / res["seconds"], 5), "unit": "views/s", "cores": smp.threads, "kind": "port",
+            "sample": smp.describe(), "seconds": {k: round(v, 3) for k, v in res["parts"].items()},
+            "threads": smp.threads}
 
 
 def time_render_frame(sc: dict, cam: dict, budget_s: float = 20.0) -> dict:
@@ -237,8 +270,8 @@ def time_render_frame(sc: dict, cam: dict, budget_s: float = 20.0) -> dict:
 
     params = [sc[k].numpy() if torch.is_tensor(sc[k]) else sc[k]
               for k in ("means", "scales", "rotations", "opacities", "sh0", "sh_rest")]
+    threads = use_all_threads()
     o = Oracle(params, {k: (v.numpy() if torch.is_tensor(v) else v) for k, v in cam.items()}, sc["active_sh_bases"])
-    threads = o.lib.gs3o_threads()
     t0 = time.perf_counter()
     o.preprocess()
     t1 = time.perf_counter()

@@ -490,6 +490,69 @@ void gs3o_blend_backward(gs3o_ctx* c, const float* grad_image, int row0, int row
     }
 }
 
+// The same sums by the 3DGS per-pixel scheme in its float form, for the timed CPU baseline: alpha and G in float
+// (the forward's evaluation), T recovered by division from the forward's final T, accumulation in double.
+void gs3o_blend_backward_fast(gs3o_ctx* c, const float* grad_image, int row0, int row1) {
+    const int W = c->s.width, H = c->s.height;
+    const size_t P = (size_t)W * H;
+    row0 = std::max(row0, 0);
+    row1 = std::min(row1, c->tiles_y);
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int t = row0 * c->tiles_x; t < row1 * c->tiles_x; ++t) {
+        const int tx0 = (t % c->tiles_x) * kTile, ty0 = (t / c->tiles_x) * kTile;
+        const int64_t s0 = c->ranges[2 * t];
+        for (int y = ty0; y < std::min(ty0 + kTile, H); ++y)
+            for (int x = tx0; x < std::min(tx0 + kTile, W); ++x) {
+                const size_t pix = (size_t)y * W + x;
+                const double G[3] = {grad_image[pix], grad_image[P + pix], grad_image[2 * P + pix]};
+                double T = c->final_T[pix];
+                double acc[3] = {0.0, 0.0, 0.0};  // colour behind the current splat, background included, / T
+                for (int ch = 0; ch < 3; ++ch) acc[ch] = c->s.bg[ch];
+                const double pxf = x + 0.5, pyf = y + 0.5;
+                for (int64_t k = s0 + c->n_contrib[pix] - 1; k >= s0; --k) {
+                    const int64_t g = c->point_list[k];
+                    const float* co = &c->conic_o[4 * g];
+                    // same float evaluation as the forward, so the same splats pass
+                    const float dxf = c->mean2d[2 * g] - (float)pxf, dyf = c->mean2d[2 * g + 1] - (float)pyf;
+                    const float a2 = -0.5f * kLog2e * co[0], b2 = -kLog2e * co[1], c2 = -0.5f * kLog2e * co[2];
+                    const float q2 = fmaf(dxf, fmaf(a2, dxf, b2 * dyf), c2 * (dyf * dyf));
+                    const float Gs = exp2f(std::min(q2, 0.f));
+                    const float alpha_f = co[3] * Gs;
+                    if (alpha_f < kAlphaMin) continue;
+                    const double alpha = alpha_f;
+                    const double om = std::max(1.0 - alpha, kOneMinusAlphaEps);
+                    T = T / om;  // T before this splat
+                    double col[3], dot = 0.0;
+                    for (int ch = 0; ch < 3; ++ch) {
+                        col[ch] = std::max(c->color_z[4 * g + ch], 0.f);
+                        dot += G[ch] * (col[ch] - acc[ch]);
+                    }
+                    const double dL_dalpha = T * dot;
+                    for (int ch = 0; ch < 3; ++ch) {
+#pragma omp atomic
+                        c->g_color[3 * g + ch] += G[ch] * alpha * T;
+                        acc[ch] = alpha * col[ch] + (1.0 - alpha) * acc[ch];
+                    }
+                    const double dx = dxf, dy = dyf;
+                    const double h = alpha * dL_dalpha;  // dL/dpower (power = -0.5 d^T K d)
+                    const double A = co[0], B = co[1], C = co[2];
+#pragma omp atomic
+                    c->g_mean2d[2 * g] += -h * (A * dx + B * dy);
+#pragma omp atomic
+                    c->g_mean2d[2 * g + 1] += -h * (B * dx + C * dy);
+#pragma omp atomic
+                    c->g_conic_o[4 * g] += -0.5 * h * dx * dx;
+#pragma omp atomic
+                    c->g_conic_o[4 * g + 1] += -h * dx * dy;
+#pragma omp atomic
+                    c->g_conic_o[4 * g + 2] += -0.5 * h * dy * dy;
+#pragma omp atomic
+                    c->g_conic_o[4 * g + 3] += (double)Gs * dL_dalpha;
+                }
+            }
+    }
+}
+
 // Chain rule from the accumulated (mean2d, conic, opacity, colour) gradients to the parameters.
 void gs3o_preprocess_backward(gs3o_ctx* c, const float* means, const float* scales, const float* rotations,
                               const float* opacities, const float* sh_rest, float* g_means, float* g_scales,

@@ -54,6 +54,8 @@ def _prototypes() -> dict[str, tuple[str, list[str]]]:
 
 
 def _kind(decl: str):
+    if re.match(r"const char\s*\*", decl):
+        return ctypes.c_char_p
     if "*" in decl:
         return ctypes.c_void_p
     if "size_t" in decl:

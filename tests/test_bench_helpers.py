@@ -10,18 +10,20 @@ import pytest
 import bench
 
 
-def _trainer(world: int, lo: int, hi: int, total: int, nvls: bool):
-    peer = types.SimpleNamespace(lo=lo, hi=hi, total=total, nvls=nvls)
-    return types.SimpleNamespace(world=world, peer=peer)
+def _trainer(world: int, lo: int, hi: int, total: int, form: str):
+    peer = types.SimpleNamespace(lo=lo, hi=hi, total=total)
+    return types.SimpleNamespace(world=world, peer=peer, exchange=form)
 
 
-@pytest.mark.parametrize("world,nvls,slices", [(2, False, 2), (2, True, 3), (4, False, 6), (4, True, 5),
-                                               (8, False, 14), (8, True, 9)])
-def test_exchange_bytes_per_direction(world, nvls, slices):
+@pytest.mark.parametrize("world,form,slices", [(2, "peer", 2), (2, "nvls", 3), (2, "nccl", 2), (4, "peer", 6),
+                                               (4, "nvls", 5), (4, "nccl", 6), (8, "peer", 14), (8, "nvls", 9),
+                                               (8, "nccl", 14)])
+def test_exchange_bytes_per_direction(world, form, slices):
     total = 8_000_000
     chunk = total // world
-    tr = _trainer(world, 0, chunk, total, nvls)
+    tr = _trainer(world, 0, chunk, total, form)
     out = bench.exchange_figures(tr, {"comm": 1.0})
+    assert out["form"] == form
     assert out["bytes_each_direction"] == slices * 4 * chunk
     assert out["achieved"] == pytest.approx(slices * 4 * chunk / 1e-3 / 1e9, rel=1e-6)
     assert out["frac"] == pytest.approx(out["achieved"] / 770.0, abs=1e-4)
@@ -65,18 +67,29 @@ def test_clock_summary_of_a_short_region_takes_the_nearest_sample():
     assert _clocks([], None, None).summary()["reasons"] == ["unsampled"]
 
 
-@pytest.mark.parametrize("workload", ["c1", "c5", "gs2d", "ssim"])
-def test_reference_arm_of_the_other_workloads_says_unavailable(workload):
-    """The reference arm is defined for the C3 headline; on the other workloads it prints one JSON line saying so
-    and exits 0 (without touching a GPU)."""
+def _reference_line(*extra: str) -> dict:
     import json
     import subprocess
     import sys
     from pathlib import Path
 
     root = Path(bench.__file__).resolve().parent
-    out = subprocess.run([sys.executable, str(root / "bench.py"), "--impl", "reference", "--workload", workload],
-                         capture_output=True, text=True, timeout=300, cwd=root)
+    out = subprocess.run([sys.executable, str(root / "bench.py"), "--impl", "reference", *extra],
+                         capture_output=True, text=True, timeout=600, cwd=root)
     assert out.returncode == 0, out.stderr[-2000:]
-    line = json.loads(out.stdout.strip().splitlines()[-1])
+    return json.loads(out.stdout.strip().splitlines()[-1])
+
+
+@pytest.mark.parametrize("workload", ["ssim", "gs2d", "splat2d", "blend-bwd"])
+def test_reference_arm_without_its_kernels_says_unavailable(workload):
+    """The reference's SSIM is not vendored, and its CUDA kernels need a GPU: those reference arms print one JSON
+    line saying why and exit 0 (here, without a GPU)."""
+    line = _reference_line("--workload", workload)
     assert line["impl"] == "reference" and "unavailable" in line
+
+
+def test_reference_arm_of_c1_times_the_cpu_path():
+    """The c1 reference arm times the numpy restatement of the reference's CPU path for K steps."""
+    line = _reference_line("--workload", "c1", "--steps", "1", "--warmup", "3")
+    assert line["impl"] == "reference" and line["steps"] == 1 and line["value"] > 0
+    assert line["config"] == bench.C1_CONFIG

@@ -264,3 +264,30 @@ def test_inputs_must_be_cuda():
     params = [sc[k] for k in ("means", "scales", "rotations", "opacities", "sh0", "sh_rest")]
     with pytest.raises(RuntimeError, match="CUDA"):
         gs3d.forward(*params, *scenes.settings_tuple(cam, 16, "cpu"))
+
+
+def test_backward_accumulates_the_views_of_a_batch(cuda):
+    """backward(..., out=grads, accumulate=True) adds a view's gradients into ``out``
+    (gs3d_backward_preprocess_accumulate): two views summed in one buffer equal the two views' separate gradients
+    added, up to the atomic-order noise of the blend backward."""
+    sc = scenes.gs3d_config("c2", seed=3)
+    params = [sc[k].to(cuda).contiguous() for k in GRAD_NAMES]
+    cams = [sc["cameras"][0], scenes.camera(1297, 840, (3.0, -1.0, -7.0))]
+    n = params[0].shape[0]
+    outs, douts, fwd = [], [], []
+    for k, cam in enumerate(cams):
+        s = scenes.settings_tuple(cam, sc["active_sh_bases"], cuda)
+        f = gs3d.forward(*params, *s)
+        d = torch.randn(f[0].shape, generator=torch.Generator().manual_seed(40 + k)).to(cuda)
+        fwd.append((s, f))
+        douts.append(d)
+        outs.append(gs3d.backward(None, d, f[0], params[0], params[1], params[2], params[3], params[5], *f[1:5], *s,
+                                  *f[5:]))
+    acc = tuple(torch.full_like(g, float("nan")) for g in outs[0])
+    for k, ((s, f), d) in enumerate(zip(fwd, douts)):
+        gs3d.backward(None, d, f[0], params[0], params[1], params[2], params[3], params[5], *f[1:5], *s, *f[5:],
+                      out=acc, accumulate=k > 0)
+    for name, a, g0, g1 in zip(GRAD_NAMES, acc, outs[0], outs[1]):
+        assert bool(torch.isfinite(a).all()), name
+        assert rel(a, g0 + g1) < 1e-5, f"{name}: {rel(a, g0 + g1):.2e}"
+    assert n > 0

@@ -18,7 +18,7 @@ from pathlib import Path
 import pytest
 import torch
 
-from gs_b200 import splat2d
+from gs_b200 import scenes, splat2d
 
 pytestmark = pytest.mark.gpu
 
@@ -38,18 +38,7 @@ def ref_ext():
 
 def scene(n, h, w, seed=0, sigma=(2.0, 10.0), opacity=(0.05, 0.6)):
     """The scene generator of bench/phase0/backward_bench.py:35-49 (float64, index order = depth order)."""
-    g = torch.Generator().manual_seed(seed)
-
-    def u(lo, hi, *shape):
-        return lo + (hi - lo) * torch.rand(*shape, generator=g, dtype=torch.float64)
-
-    means = torch.stack([u(-0.02 * w, 1.02 * w, n), u(-0.02 * h, 1.02 * h, n)], dim=-1)
-    l0 = 1.0 / u(sigma[0], sigma[1], n)
-    l2 = 1.0 / u(sigma[0], sigma[1], n)
-    l1 = u(-0.5, 0.5, n) * torch.minimum(l0, l2)
-    o = u(opacity[0], opacity[1], n)
-    colors = u(0.0, 1.0, n, 3)
-    return means, torch.stack([l0, l1, l2], dim=-1), torch.log(o / (1.0 - o)), colors
+    return scenes.splat2d_bench_scene(n, h, w, seed, sigma, opacity)
 
 
 def rel(a, b) -> float:
