@@ -32,6 +32,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "splat_sort_workspace_size": (_SZ, [_LL, _I]),
     "splat_radix_sort_pairs": (_I, [_P, _P, _P, _P, _LL, _I, _I, _I, _P, _SZ, _P]),
     "splat_check_device_waits": (_I, []),
+    "splat_set_lookback_poll_limit": (_I, [_I]),
     "splat_l1_ssim_workspace_size": (_SZ, [_I, _I, _I, _I]),
     "splat_peer_alloc": (_I, [_SZ, _P, _P]),
     "splat_peer_open": (_I, [_P, _P]),

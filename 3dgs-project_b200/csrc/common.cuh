@@ -27,6 +27,16 @@ int check_launch(const char* what);
         }                                        \
     } while (0)
 
+// A size bound of the caller's inputs is exceeded (e.g. more instances than 32-bit lists index, a capacity
+// below its bound): SPLAT_ERR_OVERFLOW before any device work.
+#define SPLAT_BOUND(cond, ...)                   \
+    do {                                         \
+        if (!(cond)) {                           \
+            ::splat::set_error(__VA_ARGS__);     \
+            return SPLAT_ERR_OVERFLOW;           \
+        }                                        \
+    } while (0)
+
 #define SPLAT_CUDA(call)                                                           \
     do {                                                                           \
         cudaError_t e_ = (call);                                                   \

@@ -688,16 +688,19 @@ __global__ void __launch_bounds__(kPbThreads, SPLAT_PB_MIN_BLOCKS) k_preprocess_
         emit(2, 4 * i + 1, (gx - qx * qd) * inv_n);
         emit(2, 4 * i + 2, (gy - qy * qd) * inv_n);
         emit(2, 4 * i + 3, (gz - qz * qd) * inv_n);
-    } else if (valid && !out.accumulate) {  // zero gradients: nothing to add when accumulating
+    } else if (valid) {
+        if (!out.accumulate) {  // zero gradients (nothing to add when accumulating)
 #pragma unroll
-        for (int k = 0; k < 3; ++k) {
-            emit(0, 3 * i + k, 0.f);
-            emit(1, 3 * i + k, 0.f);
-            emit(4, 3 * i + k, 0.f);
+            for (int k = 0; k < 3; ++k) {
+                emit(0, 3 * i + k, 0.f);
+                emit(1, 3 * i + k, 0.f);
+                emit(4, 3 * i + k, 0.f);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) emit(2, 4 * i + k, 0.f);
+            emit(3, i, 0.f);
         }
-#pragma unroll
-        for (int k = 0; k < 4; ++k) emit(2, 4 * i + k, 0.f);
-        emit(3, i, 0.f);
+        // this Gaussian's row of the warp's staged block still holds its SH coefficients: its gradients are zeros
         if (rest3 > 0 && any_vis && cam.active_sh_bases > 1)
             for (int k = 0; k < rest3; ++k) my_sh[k] = 0.f;
     }

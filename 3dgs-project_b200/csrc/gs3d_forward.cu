@@ -756,11 +756,14 @@ int gs3d_render(int n, long long num_instances, const gs3d_settings* settings, v
     SPLAT_TRY(fill_cam(settings, cam));
     const long long m = num_instances;
     const int T = cam.tiles_x * cam.tiles_y;
-    SPLAT_REQUIRE(n >= 0 && m >= 0 && m < (1ll << 31), "gs3d_render: bad sizes n=%d M=%lld", n, m);
+    SPLAT_REQUIRE(n >= 0 && m >= 0, "gs3d_render: bad sizes n=%d M=%lld", n, m);
+    SPLAT_BOUND(m < (1ll << 31), "gs3d_render: %lld instances exceed the 2^31 the 32-bit lists index", m);
+    SPLAT_BOUND(bucket_capacity >= bucket_bound(m, T),
+                "gs3d_render: bucket capacity %lld is below the bound %lld for %lld instances in %d tiles",
+                bucket_capacity, bucket_bound(m, T), m, T);
     SPLAT_REQUIRE(n > 0 || m == 0, "gs3d_render: instances without Gaussians");
     SPLAT_REQUIRE(prim_bytes_ >= prim_bytes(n) && tile_bytes_ >= tile_bytes(cam.width, cam.height) &&
-                      inst_bytes_ >= inst_bytes(m) && bucket_capacity >= bucket_bound(m, T) &&
-                      bucket_bytes_ >= bucket_bytes(bucket_capacity),
+                      inst_bytes_ >= inst_bytes(m) && bucket_bytes_ >= bucket_bytes(bucket_capacity),
                   "gs3d_render: a buffer is smaller than its size query");
     cudaStream_t st = as_stream(stream);
     Carver cp(prim_buf, prim_bytes_), ct(tile_buf, tile_bytes_), ci(inst_buf, inst_bytes_),
@@ -787,7 +790,8 @@ int gs3d_render_inference(int n, long long num_instances, const gs3d_settings* s
     SPLAT_TRY(fill_cam(settings, cam));
     const long long m = num_instances;
     const int T = cam.tiles_x * cam.tiles_y;
-    SPLAT_REQUIRE(n >= 0 && m >= 0 && m < (1ll << 31), "gs3d_render_inference: bad sizes n=%d M=%lld", n, m);
+    SPLAT_REQUIRE(n >= 0 && m >= 0, "gs3d_render_inference: bad sizes n=%d M=%lld", n, m);
+    SPLAT_BOUND(m < (1ll << 31), "gs3d_render_inference: %lld instances exceed the 2^31 the 32-bit lists index", m);
     SPLAT_REQUIRE(n > 0 || m == 0, "gs3d_render_inference: instances without Gaussians");
     SPLAT_REQUIRE(prim_bytes_ >= prim_bytes(n) && tile_bytes_ >= tile_bytes(cam.width, cam.height) &&
                       inst_bytes_ >= inst_bytes(m),

@@ -8,6 +8,7 @@
 // earlier tiles publish, and writes the pairs out digit run by digit run, so consecutive threads store
 // consecutive addresses.
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "sort.cuh"
@@ -18,6 +19,7 @@ namespace {
 // Bounded device-side waits that gave up (look-back of the radix sort), per device; read and cleared by
 // splat_check_device_waits.
 __device__ unsigned int g_wait_timeouts = 0u;
+
 
 __device__ __forceinline__ uint32_t warp_inclusive_scan(uint32_t v, int lane) {
 #pragma unroll
@@ -217,6 +219,9 @@ constexpr uint32_t kCountMask = kAggregateFlag - 1u;
 // Polls of one digit's look-back before it gives up (about a second with the back-off below; a tile
 // normally waits a few microseconds).
 constexpr int kLookbackPollLimit = 1 << 20;
+// Empty polls a look-back wait makes before it gives up; passed to every scatter launch. Changed only through
+// splat_set_lookback_poll_limit (failure-detection tests).
+std::atomic<int> g_poll_limit{kLookbackPollLimit};
 #ifndef SPLAT_LOOKBACK_WINDOW
 #define SPLAT_LOOKBACK_WINDOW 4
 #endif
@@ -238,7 +243,7 @@ constexpr size_t scatter_smem_bytes() {
 
 // Number of earlier pairs of digit `tid` over all tiles before `tile`: walks back over the status words,
 // kLookbackWindow tiles per round trip, summing counts up to and including the first inclusive prefix.
-__device__ __forceinline__ uint32_t look_back(const uint32_t* status, long long tile, int tid) {
+__device__ __forceinline__ uint32_t look_back(const uint32_t* status, long long tile, int tid, int poll_limit) {
     uint32_t excl = 0u;
     long long j = tile - 1;
     int polls = 0;
@@ -261,7 +266,7 @@ __device__ __forceinline__ uint32_t look_back(const uint32_t* status, long long 
         if (done) break;
         j -= used;
         if (used == 0) {
-            if (++polls >= kLookbackPollLimit) {
+            if (++polls >= poll_limit) {
                 atomicAdd(&g_wait_timeouts, 1u);
                 break;
             }
@@ -291,7 +296,7 @@ __global__ void __launch_bounds__(kSortThreads, kSortMinBlocks) k_sort_scatter(c
                                                                uint32_t* __restrict__ status,
                                                                uint32_t* __restrict__ ticket,
                                                                const uint32_t* __restrict__ gather_table,
-                                                               uint32_t* __restrict__ gather_out) {
+                                                               uint32_t* __restrict__ gather_out, int poll_limit) {
     static_assert(kRadix == kSortThreads, "one thread per digit");
     constexpr int kWarps = kSortThreads / 32;
     constexpr int kWarpItems = 32 * kSortRounds;
@@ -353,7 +358,7 @@ __global__ void __launch_bounds__(kSortThreads, kSortMinBlocks) k_sort_scatter(c
         s_goff[tid] = digit_base[tid];
     } else {
         store_status(mine, kAggregateFlag | count);
-        const uint32_t excl = look_back(status, tile, tid);
+        const uint32_t excl = look_back(status, tile, tid, poll_limit);
         store_status(mine, kPrefixFlag | (excl + count));
         s_goff[tid] = digit_base[tid] + excl;
     }
@@ -486,7 +491,8 @@ int radix_sort_pairs(const K* keys_in, const uint32_t* vals_in, K* keys_out, uin
         auto kernel = gather ? k_sort_scatter<K, true> : k_sort_scatter<K, false>;
         kernel<<<static_cast<unsigned>(nb), kSortThreads, scatter_smem_bytes<K>(), stream>>>(
             src_k, src_v, dst_k, dst_v, n, shift, mask, hist + p * kRadix,
-            status + static_cast<size_t>(p) * nb * kRadix, tickets + p, gather_table, gather_out);
+            status + static_cast<size_t>(p) * nb * kRadix, tickets + p, gather_table, gather_out,
+            g_poll_limit.load(std::memory_order_relaxed));
         note_launch();
         SPLAT_TRY(check_launch("radix_sort_pairs"));
         src_k = dst_k;
@@ -609,6 +615,14 @@ size_t splat_scan_workspace_size(long long n) { return splat::scan_workspace_byt
 int splat_scan_exclusive_u32(const uint32_t* in, uint32_t* out, long long n, uint32_t* total, void* workspace,
                              size_t workspace_bytes, void* stream) {
     return splat::scan_exclusive_u32(in, out, n, total, workspace, workspace_bytes, splat::as_stream(stream));
+}
+
+int splat_set_lookback_poll_limit(int polls) {
+    if (polls < 1) {
+        splat::set_error("splat_set_lookback_poll_limit: %d polls (at least 1)", polls);
+        return -1;
+    }
+    return splat::g_poll_limit.exchange(polls);
 }
 
 int splat_scan_exclusive_u32_noalloc(const uint32_t* in, uint32_t* out, long long n, uint32_t* total, void* stream) {

@@ -5,19 +5,21 @@
 //   q = (l0 dx + l1 dy)^2 + (l2 dy)^2 with (dx, dy) = pixel centre (x + 0.5, y + 0.5) - mean,
 //   o = sigmoid(z), alpha = min(0.99, o exp(-q / 2)), skipped below 1/255; front to back,
 //   C += c alpha T, T *= (1 - alpha); a pixel stops once T < 1e-4 (checked before each splat).
-// Outputs as phase0/csrc/macrotile/bindings.cpp:554-576: image [H,W,3], t_final, n_contrib (count),
+// Outputs as phase0/csrc/macrotile/bindings.cpp:156-178: image [H,W,3], t_final, n_contrib (count),
 // last_contrib (list position + 1), ckpt [B,256,4] = (C, T) at every bucket start, every slot written.
 //
 // Kernels (own design, same arithmetic per (pixel, splat) as splat2d_common.h:132-246):
-//   forward          one 256-thread block per 16x16 tile, batches of 256 splats staged in shared
-//                    memory with the sigmoid applied once per splat; once every pixel of the tile has
-//                    stopped, the block only fills the remaining checkpoints
+//   forward          one 128-thread block per 16x16 tile, two pixels per thread (warp per 8x8 subtile);
+//                    batches of 256 splats staged in shared memory with the sigmoid applied once per splat
+//                    and the box of pixels each can reach (alpha >= 1/255); a warp evaluates only the splats
+//                    whose box meets its subtile; once every pixel of the tile has stopped, the block only
+//                    fills the remaining checkpoints
 //   backward_pixel   one thread per pixel walking back from last_contrib (T by division), 9 atomics
 //                    per (pixel, splat): the baseline mode
 //   backward_splat   one warp per (tile, 32-splat bucket), lane owns the 8 pixels r*32 + lane, keeps
 //                    (T, rho = G . (C_final - C)) replayed from the checkpoint, warp-reduces the 9
 //                    parameter sums per splat and issues one atomic per parameter from lane 0
-// Op counters (get_counters / reset_counters, bindings.cpp:620-627) count on the device when enabled.
+// Op counters (get_counters / reset_counters, bindings.cpp:222-230) count on the device when enabled.
 #include "common.cuh"
 #include "sort.cuh"
 
@@ -143,71 +145,159 @@ __device__ __forceinline__ int safe_id(const Tables& t, int k) { return min(max(
 // ---------------------------------------------------------------------------------------------
 // Forward
 // ---------------------------------------------------------------------------------------------
+constexpr int kFwdThreads = kBlock / 2;  // two pixels per thread
+
+// Box (x0, x1, y0, y1) of the pixel centres where alpha = min(0.99, o e^(-q/2)) can reach 1/255: those satisfy
+// q = (l0 dx + l1 dy)^2 + (l2 dy)^2 <= R = 2 ln(255 o), an ellipse with half-extents sqrt(R (l1^2 + l2^2)) / |l0 l2|
+// in x and sqrt(R) / |l2| in y. R is widened by 0.1% and the box by one pixel, so the rounding of the per-pixel
+// evaluation never reaches outside it. An opacity below 1/255 reaches nothing; a degenerate factor or values that
+// are not finite (which the per-pixel rules may turn into alpha = 0.99) give the unbounded box.
+template <typename S>
+__device__ __forceinline__ void reach_box(const P<S>& p, S (&box)[4]) {
+    const S inf = S(INFINITY);
+    box[0] = -inf;
+    box[1] = inf;
+    box[2] = -inf;
+    box[3] = inf;
+    if (!isfinite(p.mx) || !isfinite(p.my) || p.o != p.o) return;
+    if (!(p.o * S(255) >= S(1))) {
+        box[0] = inf;
+        box[1] = -inf;
+        return;
+    }
+    const S d = fabs(p.l0 * p.l2);
+    if (!(d > S(0)) || !isfinite(d)) return;
+    const S R = S(2.002) * log(S(255) * p.o) + S(1e-3);
+    const S ex = sqrt(R * (p.l1 * p.l1 + p.l2 * p.l2)) / d + S(1), ey = sqrt(R) / fabs(p.l2) + S(1);
+    if (!(ex == ex && ey == ey)) return;
+    box[0] = p.mx - ex;
+    box[1] = p.mx + ex;
+    box[2] = p.my - ey;
+    box[3] = p.my + ey;
+}
+
+// 128 threads per 16x16 tile, two pixels per thread: warp w owns the 8x8 subtile (w & 1, w >> 1), lane (column
+// lane & 7, rows lane >> 3 and (lane >> 3) + 4). A round stages 256 splats of the tile's list (two per thread) with
+// their reach boxes; each warp walks them 32 at a time, evaluating in list order only those whose box meets its
+// subtile. The (C, T) checkpoint of both pixels is written at every bucket start; once every pixel of the tile
+// has stopped, the remaining checkpoints are filled with the final (C, T), so every slot is written.
 template <typename S, bool kCount>
-__global__ void __launch_bounds__(kBlock) k_forward(Tables t, const S* __restrict__ means, const S* __restrict__ chol,
-                                                    const S* __restrict__ zlogit, const S* __restrict__ colors,
-                                                    S* __restrict__ image, S* __restrict__ t_final,
-                                                    int32_t* __restrict__ n_contrib, int32_t* __restrict__ last_contrib,
-                                                    S* __restrict__ ckpt) {
+__global__ void __launch_bounds__(kFwdThreads) k_forward(Tables t, const S* __restrict__ means,
+                                                         const S* __restrict__ chol, const S* __restrict__ zlogit,
+                                                         const S* __restrict__ colors, S* __restrict__ image,
+                                                         S* __restrict__ t_final, int32_t* __restrict__ n_contrib,
+                                                         int32_t* __restrict__ last_contrib, S* __restrict__ ckpt) {
     __shared__ P<S> s_p[kBlock];
+    __shared__ S s_box[kBlock][4];
     const int tile = blockIdx.x;
-    const int lane = threadIdx.x;
-    const int x = (tile % t.tiles_x) * kTile + lane % kTile;
-    const int y = (tile / t.tiles_x) * kTile + lane / kTile;
-    const bool inside = x < t.W && y < t.H;
-    const S px = S(x) + S(0.5), py = S(y) + S(0.5);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tx0 = (tile % t.tiles_x) * kTile, ty0 = (tile / t.tiles_x) * kTile;
+    const int sx0 = tx0 + (warp & 1) * 8, sy0 = ty0 + (warp >> 1) * 8;
+    const int x = sx0 + (lane & 7), ya = sy0 + (lane >> 3), yb = ya + 4;
+    const int la = (ya - ty0) * kTile + (x - tx0), lb = la + 4 * kTile;
+    const bool in_a = x < t.W && ya < t.H, in_b = x < t.W && yb < t.H;
+    const S px = S(x) + S(0.5), pya = S(ya) + S(0.5), pyb = S(yb) + S(0.5);
+    const S bx0 = S(sx0) + S(0.5), bx1 = S(sx0) + S(7.5), by0 = S(sy0) + S(0.5), by1 = S(sy0) + S(7.5);
     const int2 rg = tile_range(t, tile);
     const int bucket0 = t.bucket_off[tile];
-    S Cr = S(0), Cg = S(0), Cb = S(0), T = S(1);
-    int cnt = 0, last = 0;
+    S Ra = S(0), Ga = S(0), Ba = S(0), Ta = S(1), Rb = S(0), Gb = S(0), Bb = S(0), Tb = S(1);
+    int cnt_a = 0, cnt_b = 0, last_a = 0, last_b = 0;
     unsigned long long evals = 0;
     auto store_ckpt = [&](int local) {
         const int bk = bucket0 + local / kBucket;
         if (bk >= 0 && bk < t.B) {
-            S* d = ckpt + (static_cast<size_t>(bk) * kBlock + lane) * 4;
-            d[0] = Cr;
-            d[1] = Cg;
-            d[2] = Cb;
-            d[3] = T;
+            S* d = ckpt + (static_cast<size_t>(bk) * kBlock + la) * 4;
+            d[0] = Ra;
+            d[1] = Ga;
+            d[2] = Ba;
+            d[3] = Ta;
+            d = ckpt + (static_cast<size_t>(bk) * kBlock + lb) * 4;
+            d[0] = Rb;
+            d[1] = Gb;
+            d[2] = Bb;
+            d[3] = Tb;
         }
     };
     for (int batch = rg.x; batch < rg.y; batch += kBlock) {
-        const bool live = inside && !(T < S(1e-4));
+        const bool live = (in_a && !(Ta < S(1e-4))) || (in_b && !(Tb < S(1e-4)));
         if (__syncthreads_count(live) == 0) {
             // every pixel has stopped: the remaining checkpoints all hold the final (C, T)
             for (int local = (batch - rg.x + kBucket - 1) / kBucket * kBucket; local < rg.y - rg.x; local += kBucket)
                 store_ckpt(local);
             break;
         }
-        if (batch + lane < rg.y) s_p[lane] = load_params<S>(safe_id(t, batch + lane), means, chol, zlogit, colors);
+#pragma unroll
+        for (int h = 0; h < kBlock / kFwdThreads; ++h) {
+            const int slot = tid + h * kFwdThreads;
+            if (batch + slot < rg.y) {
+                const P<S> p = load_params<S>(safe_id(t, batch + slot), means, chol, zlogit, colors);
+                s_p[slot] = p;
+                reach_box<S>(p, s_box[slot]);
+            }
+        }
         __syncthreads();
         const int nb = min(kBlock, rg.y - batch);
-        for (int j = 0; j < nb; ++j) {
-            const int local = batch - rg.x + j;
-            if (local % kBucket == 0) store_ckpt(local);
-            if (!inside || T < S(1e-4)) continue;
-            const P<S>& p = s_p[j];
-            const Eval<S> e = eval<S>(p, px, py);
-            if (kCount) ++evals;
-            if (e.alpha < S(1.0 / 255.0)) continue;
-            Cr = Cr + p.cr * e.alpha * T;
-            Cg = Cg + p.cg * e.alpha * T;
-            Cb = Cb + p.cb * e.alpha * T;
-            T = T * (S(1) - e.alpha);
-            ++cnt;
-            last = local + 1;
+        for (int j0 = 0; j0 < nb; j0 += kBucket) {
+            store_ckpt(batch - rg.x + j0);
+            const bool run_a = in_a && !(Ta < S(1e-4)), run_b = in_b && !(Tb < S(1e-4));
+            if (!__any_sync(kFullMask, run_a || run_b)) continue;
+            bool hit = false;
+            if (lane < nb - j0) {
+                const S* bx = s_box[j0 + lane];
+                hit = bx[0] <= bx1 && bx[1] >= bx0 && bx[2] <= by1 && bx[3] >= by0;
+            }
+            unsigned pending = __ballot_sync(kFullMask, hit);
+            while (pending != 0u) {
+                const int j = j0 + __ffs(pending) - 1;
+                pending &= pending - 1u;
+                const P<S>& p = s_p[j];
+                const int local = batch - rg.x + j;
+                if (in_a && !(Ta < S(1e-4))) {
+                    const Eval<S> e = eval<S>(p, px, pya);
+                    if (kCount) ++evals;
+                    if (!(e.alpha < S(1.0 / 255.0))) {
+                        Ra = Ra + p.cr * e.alpha * Ta;
+                        Ga = Ga + p.cg * e.alpha * Ta;
+                        Ba = Ba + p.cb * e.alpha * Ta;
+                        Ta = Ta * (S(1) - e.alpha);
+                        ++cnt_a;
+                        last_a = local + 1;
+                    }
+                }
+                if (in_b && !(Tb < S(1e-4))) {
+                    const Eval<S> e = eval<S>(p, px, pyb);
+                    if (kCount) ++evals;
+                    if (!(e.alpha < S(1.0 / 255.0))) {
+                        Rb = Rb + p.cr * e.alpha * Tb;
+                        Gb = Gb + p.cg * e.alpha * Tb;
+                        Bb = Bb + p.cb * e.alpha * Tb;
+                        Tb = Tb * (S(1) - e.alpha);
+                        ++cnt_b;
+                        last_b = local + 1;
+                    }
+                }
+            }
         }
         __syncthreads();
     }
     if (kCount) count(kEvals, evals);
-    if (inside) {
-        const int pix = y * t.W + x;
-        image[3 * pix] = Cr;
-        image[3 * pix + 1] = Cg;
-        image[3 * pix + 2] = Cb;
-        t_final[pix] = T;
-        n_contrib[pix] = cnt;
-        last_contrib[pix] = last;
+    if (in_a) {
+        const int pix = ya * t.W + x;
+        image[3 * pix] = Ra;
+        image[3 * pix + 1] = Ga;
+        image[3 * pix + 2] = Ba;
+        t_final[pix] = Ta;
+        n_contrib[pix] = cnt_a;
+        last_contrib[pix] = last_a;
+    }
+    if (in_b) {
+        const int pix = yb * t.W + x;
+        image[3 * pix] = Rb;
+        image[3 * pix + 1] = Gb;
+        image[3 * pix + 2] = Bb;
+        t_final[pix] = Tb;
+        n_contrib[pix] = cnt_b;
+        last_contrib[pix] = last_b;
     }
 }
 
@@ -530,7 +620,7 @@ int forward_impl(const void* means, const void* chol, const void* zl, const void
     Tables t = make_tables<S>(tile_off, tile_ids, bucket_off, bucket_tile, N, M, B, H, W);
     if (g_counting) g_ckpt_bytes += static_cast<long long>(B) * kBlock * 4 * sizeof(S);
     auto kern = g_counting ? k_forward<S, true> : k_forward<S, false>;
-    kern<<<t.T, kBlock, 0, st>>>(t, static_cast<const S*>(means), static_cast<const S*>(chol),
+    kern<<<t.T, kFwdThreads, 0, st>>>(t, static_cast<const S*>(means), static_cast<const S*>(chol),
                                  static_cast<const S*>(zl), static_cast<const S*>(colors), static_cast<S*>(image),
                                  static_cast<S*>(t_final), n_contrib, last_contrib, static_cast<S*>(ckpt));
     note_launch();

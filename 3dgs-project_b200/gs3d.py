@@ -331,7 +331,7 @@ class _Rasterize(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx: Any, means, scales, rotations, opacities, sh0, sh_rest, densification_info,
-                settings: RasterizerSettings):
+                settings: RasterizerSettings, want_radii: bool = False):
         params = [t.contiguous() for t in (means, scales, rotations, opacities, sh0, sh_rest)]
         image, prim, tile, inst, bucket, m, nb, sel = forward(*params, *settings.as_tuple())
         if _Rasterize.track_visibility:
@@ -342,10 +342,14 @@ class _Rasterize(torch.autograd.Function):
         ctx.shapes = (opacities.shape, sh0.shape, sh_rest.shape)
         ctx.save_for_backward(image, params[0], params[1], params[2], params[3], params[5], prim, tile, inst, bucket,
                               params[4])
+        if want_radii:
+            radii = screen_radii(prim, params[0].shape[0])
+            ctx.mark_non_differentiable(radii)
+            return image, radii
         return image
 
     @staticmethod
-    def backward(ctx: Any, grad_image):
+    def backward(ctx: Any, grad_image, *unused):
         image, means, scales, rotations, opacities, sh_rest, prim, tile, inst, bucket, sh0 = ctx.saved_tensors
         opt = _Rasterize.fused_optimizer
         six = (means, scales, rotations, opacities, sh0, sh_rest)
@@ -353,12 +357,12 @@ class _Rasterize(torch.autograd.Function):
             pending = backward_blend(ctx.densification_info, grad_image, image, means, scales, rotations, opacities,
                                      sh_rest, prim, tile, inst, bucket, *ctx.settings.as_tuple(), *ctx.buffer_state)
             opt._defer(pending, six)
-            return (None,) * 8
+            return (None,) * 9
         g = backward(ctx.densification_info, grad_image, image, means, scales, rotations, opacities, sh_rest, prim,
                      tile, inst, bucket, *ctx.settings.as_tuple(), *ctx.buffer_state)
         op_shape, sh0_shape, rest_shape = ctx.shapes
         return (g[0], g[1], g[2], g[3].reshape(op_shape), g[4].reshape(sh0_shape), g[5].reshape(rest_shape), None,
-                None)
+                None, None)
 
 
 def diff_rasterize(means, scales, rotations, opacities, sh0, sh_rest, densification_info,
@@ -371,12 +375,17 @@ def rasterize_gaussians(means3D, scales, rotations, opacities, shs, viewmatrix, 
                         image_height, image_width, sh_degree, campos, scale_modifier=1.0, near_plane=0.2,
                         far_plane=1000.0):
     """graphdeco-style entry: activated inputs (scales > 0, opacities in (0, 1), any quaternions, shs [N, K, 3]);
-    viewmatrix is the transposed world-to-view matrix as graphdeco passes it (p_view = p_h @ viewmatrix).
-    projmatrix is accepted for signature compatibility; the pinhole model uses tanfovx / tanfovy.
-    Returns (image [3, H, W], radii int32 [N]: half the culling rectangle's larger side, 0 = not visible)."""
+    viewmatrix is the transposed world-to-view matrix as graphdeco passes it (p_view = p_h @ viewmatrix) and
+    projmatrix its full projection (viewmatrix @ P^T). The rasterizer is the pinhole model with the principal point
+    at the image centre and focal lengths W / (2 tanfovx), H / (2 tanfovy); projmatrix must be that projection of
+    viewmatrix (its x, y and w columns are checked; the depth column carries graphdeco's znear / zfar, which the
+    model does not use), else ValueError. Returns (image [3, H, W], radii int32 [N]): graphdeco's screen radius,
+    ceil(3 sqrt(largest eigenvalue of the dilated 2D covariance)), taken from the forward's own primitive buffer,
+    0 for Gaussians the view does not list."""
     W, H = int(image_width), int(image_height)
     fx = W / (2.0 * float(tanfovx))
     fy = H / (2.0 * float(tanfovy))
+    check_projmatrix(viewmatrix, projmatrix, float(tanfovx), float(tanfovy))
     w2c = viewmatrix.transpose(0, 1).contiguous()
     bases = (int(sh_degree) + 1) ** 2
     settings = RasterizerSettings(w2c, campos, bg, bases, W, H, fx, fy, W / 2.0, H / 2.0, near_plane, far_plane,
@@ -384,29 +393,36 @@ def rasterize_gaussians(means3D, scales, rotations, opacities, shs, viewmatrix, 
     log_scales = torch.log(scales * scale_modifier)
     logits = torch.logit(opacities.reshape(-1, 1).clamp(1e-7, 1 - 1e-7))
     sh0, sh_rest = shs[:, :1].contiguous(), shs[:, 1:].contiguous()
-    image = diff_rasterize(means3D, log_scales, rotations, logits, sh0, sh_rest, torch.empty(0), settings)
-    with torch.no_grad():
-        prim = _last_visibility(means3D, log_scales, rotations, logits, sh0, sh_rest, settings)
-    return image, prim
+    return _Rasterize.apply(means3D, log_scales, rotations, logits, sh0, sh_rest, torch.empty(0), settings, True)
+
+
+def check_projmatrix(viewmatrix: torch.Tensor, projmatrix: torch.Tensor, tanfovx: float, tanfovy: float,
+                     rtol: float = 1e-4) -> None:
+    """projmatrix = viewmatrix @ P^T for graphdeco's pinhole P: its columns 0, 1 and 3 are viewmatrix's columns 0 and
+    1 divided by tanfovx and tanfovy and its column 2. Raises ValueError otherwise (an off-centre or other
+    projection, which the pinhole settings cannot express)."""
+    v = viewmatrix.detach().double().cpu().reshape(4, 4)
+    p = projmatrix.detach().double().cpu().reshape(4, 4)
+    want = torch.stack([v[:, 0] / tanfovx, v[:, 1] / tanfovy, v[:, 2]], 1)
+    got = torch.stack([p[:, 0], p[:, 1], p[:, 3]], 1)
+    err = float((got - want).abs().max()) / max(float(want.abs().max()), 1e-30)
+    if not err <= rtol:
+        raise ValueError(f"projmatrix is not the centred pinhole projection of viewmatrix with tanfovx={tanfovx} and "
+                         f"tanfovy={tanfovy} (relative difference {err:.2e}); use the Faster-GS entry (forward / "
+                         f"diff_rasterize) with explicit focal lengths and principal point")
 
 
 @torch.no_grad()
-def _last_visibility(means, scales, rotations, opacities, sh0, sh_rest, settings):
-    """Per-Gaussian screen radius from a preprocess pass (rasterize_gaussians' second output)."""
-    n, rest = _check_params(means.contiguous(), scales.contiguous(), rotations.contiguous(), opacities.contiguous(),
-                            sh0, sh_rest)
-    dev = means.device
-    keep: list = []
-    s = _settings(dev, *settings.as_tuple()[:3], settings.active_sh_bases, settings.width, settings.height,
-                  settings.focal_x, settings.focal_y, settings.center_x, settings.center_y, settings.near_plane,
-                  settings.far_plane, settings.proper_antialiasing, rest, keep)
-    prim = torch.empty(L.query("gs3d_primitive_buffer_size", n), dtype=torch.uint8, device=dev)
-    L.call("gs3d_preprocess", L.ptr(means.contiguous()), L.ptr(scales.contiguous()), L.ptr(rotations.contiguous()),
-           L.ptr(opacities.contiguous()), L.ptr(sh0), L.ptr(sh_rest), n, ctypes.byref(s), L.ptr(prim), prim.numel(),
-           None, L.stream_of(means))
-    v = primitive_views(prim, n)
-    r = v["rect"].to(torch.int32)
-    radii = torch.maximum(r[:, 2] - r[:, 0], r[:, 3] - r[:, 1]).div(2, rounding_mode="floor") + 1
+def screen_radii(prim_buf: torch.Tensor, n: int) -> torch.Tensor:
+    """graphdeco's per-Gaussian screen radius from a forward's primitive buffer: ceil(3 sqrt(lambda_max)) of the dilated
+    2D covariance (the inverse of the stored conic), int32, 0 where the Gaussian is not listed in any tile."""
+    v = primitive_views(prim_buf, n)
+    A, B, C = (v["conic_o"][:, k].double() for k in range(3))
+    det = A * C - B * B
+    a, b, c = C / det, -B / det, A / det  # covariance = conic^-1
+    mid = 0.5 * (a + c)
+    lam = mid + torch.sqrt(torch.clamp(mid * mid - (a * c - b * b), min=0.1))
+    radii = torch.ceil(3.0 * torch.sqrt(lam)).to(torch.int32)
     return torch.where(v["n_touched"] > 0, radii, torch.zeros_like(radii))
 
 

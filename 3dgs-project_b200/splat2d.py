@@ -3,7 +3,7 @@
     from gs_b200.splat2d import render, bin_tiles, load_extension
     image = render(means, chol, opacity_logit, colors, H, W, mode="splat")   # [H, W, 3]
 
-float32 and float64 parameters are both supported (bindings.cpp:568-574 dispatches on the dtype).
+float32 and float64 parameters are both supported (bindings.cpp:170 dispatches on the dtype).
 Binning (ops.py:206-255) runs on the GPU in float64 like the reference's CPU loop; forward,
 backward_pixel and backward_splat run in libsplat_b200.so. There is no CPU build: CPU tensors raise.
 The pure-PyTorch ground truth ``ref_render`` / ``ref_state`` (ops.py:358-398) is test infrastructure
@@ -55,7 +55,7 @@ class Extension(Protocol):
 
 
 def _check_scene(means, chol, opacity_logit, colors, tables, height, width):
-    """bindings.cpp:448-482: shapes, one floating dtype, int32 tables, one device, non-empty image."""
+    """bindings.cpp:50-84 (make_scene): shapes, one floating dtype, int32 tables, one device, non-empty image."""
     if means.dim() != 2 or means.shape[1] != 2:
         raise RuntimeError("means must be [N, 2]")
     n = means.shape[0]

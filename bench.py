@@ -383,6 +383,7 @@ def run_ours(args) -> None:
              for k, c in enumerate(cams)]
     douts = ([h.to(dev) for h in hosts], [(-h).to(dev) for h in hosts])
     r = time_steps(tr, cams, lambda t: douts[t % 2], args.steps, args.warmup, world, local)
+    L.check_device_waits(dev)  # a sort wait of the last forward that gave up is reported here, not after the run
     stage = r["stage"]
     reach = blend_reach(tr, cam["width"], cam["height"])
     checksum = tr.checksum()
@@ -441,6 +442,7 @@ def c4_strong(args, world: int, rank: int, local: int, dev) -> dict:
     douts = ([h.to(dev) for h in hosts], [(-h).to(dev) for h in hosts])
     steps = max(args.steps // 4, 10)
     r = time_steps(tr, cams, lambda t: douts[t % 2], steps, args.warmup, world, local, with_clocks=False)
+    L.check_device_waits(dev)
     checksum = tr.checksum()
     stage = {k: round(v, 4) for k, v in r["stage"].items()}
     exch = tr.exchange
@@ -925,6 +927,7 @@ def run_c5(args, ref: bool = False) -> None:
         clk.mark_end()
         launches = L.query("splat_launch_count") - launches0
     timer.stop()
+    L.check_device_waits(dev)
     ms = torch.tensor([a.elapsed_time(b)], device=dev)
     if world > 1:
         torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)

@@ -83,6 +83,11 @@ int splat_radix_sort_pairs(const void* keys_in, const uint32_t* vals_in, void* k
  * (results produced since then are unreliable), else SPLAT_OK. Synchronises the device; clears the count.
  * No counterpart in the reference (CUB's single-sweep sort waits without a bound). */
 int splat_check_device_waits(void);
+/* Failure-detection hook (no counterpart in the reference): sets the number of empty polls after which a
+ * radix-sort look-back wait gives up (default 2^20, about a second of back-off) and returns the previous value,
+ * or -1 for polls < 1. A tiny limit makes waits give up on purpose, so that tests see SPLAT_ERR_TIMEOUT from
+ * splat_check_device_waits; the pass still completes and writes within its output (its order is then wrong). */
+int splat_set_lookback_poll_limit(int polls);
 /* The same count without a synchronisation: enqueues on `stream` a copy of it into dst (device uint32) and
  * clears it, so a caller that reads dst at a point where it waits anyway learns of a wait that gave up in
  * the work enqueued before. No counterpart in the reference. */
@@ -133,7 +138,7 @@ int gs2d_backward_splat(const float* means, const float* conic, const float* col
 
 /* ---------------------------------------------------------------------------------------------
  * splat2d: phase0 2D op, float (is_f64 = 0) or double (is_f64 = 1). Replaces the extension of
- * phase0/csrc/macrotile/bindings.cpp:554-637 and the CPU binning of phase0/splat2d/ops.py:206-255.
+ * phase0/csrc/macrotile/bindings.cpp:50-84,156-239 and the CPU binning of phase0/splat2d/ops.py:206-255.
  * means S[N,2], chol S[N,3] (l0,l1,l2), opacity_logit S[N], colors S[N,3]; CSR tile tables:
  * tile_offsets i32[T+1], tile_ids i32[M], bucket_offsets i32[T+1], bucket_tile i32[B].
  * ------------------------------------------------------------------------------------------- */
@@ -150,14 +155,14 @@ int splat2d_bin_fill(int n, int H, int W, long long num_instances, void* count_w
                      size_t count_workspace_bytes, void* fill_workspace, size_t fill_workspace_bytes,
                      int32_t* tile_offsets, int32_t* tile_ids, int32_t* bucket_offsets, int32_t* bucket_tile,
                      uint32_t* num_buckets, void* stream);
-/* bindings.cpp:554-576 `forward`: image S[H,W,3], t_final S[H,W], n_contrib i32[H,W] (count),
+/* bindings.cpp:156-178 `forward`: image S[H,W,3], t_final S[H,W], n_contrib i32[H,W] (count),
  * last_contrib i32[H,W] (position + 1), ckpt S[B,256,4] = (C, T); every checkpoint slot is written. */
 int splat2d_forward(int is_f64, const void* means, const void* chol, const void* opacity_logit, const void* colors,
                     const int32_t* tile_offsets, const int32_t* tile_ids, const int32_t* bucket_offsets,
                     const int32_t* bucket_tile, int N, long long num_instances, int num_buckets, int H, int W,
                     void* image, void* t_final, int32_t* n_contrib, int32_t* last_contrib, void* ckpt,
                     void* stream);
-/* bindings.cpp:578-618 `backward_pixel` (splat_mode = 0: uses t_final, last_contrib) and
+/* bindings.cpp:180-220 `backward_pixel` (splat_mode = 0: uses t_final, last_contrib) and
  * `backward_splat` (splat_mode = 1: uses image, ckpt). grad_image S[H,W,3]; gradients S, same shapes
  * as the parameters. */
 int splat2d_backward(int is_f64, int splat_mode, const void* grad_image, const void* means, const void* chol,
@@ -166,7 +171,7 @@ int splat2d_backward(int is_f64, int splat_mode, const void* grad_image, const v
                      long long num_instances, int num_buckets, int H, int W, const void* t_final,
                      const int32_t* last_contrib, const void* image, const void* ckpt, void* grad_means,
                      void* grad_chol, void* grad_opacity_logit, void* grad_colors, void* stream);
-/* Op counters (bindings.cpp:620-627), counted on the device while enabled: out3 = {atomic_adds,
+/* Op counters (bindings.cpp:222-230), counted on the device while enabled: out3 = {atomic_adds,
  * checkpoint_bytes, splat_pixel_evals}. get synchronises the device. */
 int splat2d_set_counting(int on);
 int splat2d_reset_counters(void);

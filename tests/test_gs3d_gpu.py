@@ -239,23 +239,47 @@ def test_back_to_back_calls_without_sync(cuda):
         assert torch.equal(img, outs[k])
 
 
+def _graphdeco_proj(view: torch.Tensor, tanfovx: float, tanfovy: float, znear=0.01, zfar=100.0) -> torch.Tensor:
+    """graphdeco's full projection: viewmatrix @ P^T with its pinhole P (getProjectionMatrix, centred)."""
+    P = torch.zeros(4, 4, dtype=view.dtype, device=view.device)
+    P[0, 0], P[1, 1] = 1.0 / tanfovx, 1.0 / tanfovy
+    P[3, 2] = 1.0
+    P[2, 2], P[2, 3] = zfar / (zfar - znear), -(zfar * znear) / (zfar - znear)
+    return view @ P.T
+
+
 def test_rasterize_gaussians_graphdeco_entry(cuda):
     sc, cam, params, settings = _setup("tiny", seed=4)
     means, scales, rot, op, sh0, shr = params
     shs = torch.cat([sh0, shr], 1)
     view = settings[0].T.contiguous()
     W, H = cam["width"], cam["height"]
-    img, radii = gs3d.rasterize_gaussians(means, torch.exp(scales), rot, torch.sigmoid(op), shs, view, view,
-                                          settings[2], W / (2 * cam["focal_x"]), H / (2 * cam["focal_y"]), H, W, 3,
-                                          settings[1])
+    tx, ty = W / (2 * cam["focal_x"]), H / (2 * cam["focal_y"])
+    img, radii = gs3d.rasterize_gaussians(means, torch.exp(scales), rot, torch.sigmoid(op), shs, view,
+                                          _graphdeco_proj(view, tx, ty), settings[2], tx, ty, H, W, 3, settings[1])
     # same camera with a centred principal point through the Faster-GS entry
     s2 = list(settings)
     s2[8], s2[9] = W / 2.0, H / 2.0
-    ref = gs3d.forward(*params, *s2)[0]
+    ref, prim = gs3d.forward(*params, *s2)[:2]
     # log(exp(s)) and logit(sigmoid(o)) round differently, so a pixel may flip a threshold decision
     err = (img.detach() - ref).abs().amax(0)
     assert float((err > 1e-4).double().mean()) < 1e-3 and float(err.mean()) < 1e-5
-    assert radii.shape == (means.shape[0],) and int((radii > 0).sum()) > 0
+    # graphdeco's radius: ceil(3 sqrt(lambda_max)) of the dilated 2D covariance, 0 where not listed
+    n = means.shape[0]
+    pv = gs3d.primitive_views(prim, n)
+    vis = pv["n_touched"] > 0
+    cov = torch.linalg.inv(torch.stack([torch.stack([pv["conic_o"][:, 0], pv["conic_o"][:, 1]], -1),
+                                        torch.stack([pv["conic_o"][:, 1], pv["conic_o"][:, 2]], -1)], -2).double())
+    lam = torch.linalg.eigvalsh(cov)[:, 1]
+    want = torch.where(vis, torch.ceil(3 * torch.sqrt(lam)).int(), torch.zeros_like(radii))
+    assert radii.shape == (n,) and radii.dtype == torch.int32 and int((radii > 0).sum()) > 0
+    assert float((radii != want).double().mean()) < 1e-3  # log/logit round trip: a few may differ by one
+    # a projection that is not the centred pinhole of viewmatrix is refused
+    bad = _graphdeco_proj(view, tx, ty).clone()
+    bad[0, 0] *= 1.1
+    with pytest.raises(ValueError, match="projmatrix"):
+        gs3d.rasterize_gaussians(means, torch.exp(scales), rot, torch.sigmoid(op), shs, view, bad, settings[2], tx,
+                                 ty, H, W, 3, settings[1])
 
 
 def test_inputs_must_be_cuda():

@@ -104,9 +104,11 @@ def _float64_replay(sc, cam, ref: RefInputs, dout: torch.Tensor) -> dict:
     return o.blend_backward_sums(dout.cpu().numpy())
 
 
-def _as_dict(ref: RefInputs, mean2d, conic_abc, opacity, color) -> dict:
+def _as_dict(ref: RefInputs, mean2d, conic_abc, opacity, color, factored: bool = False) -> dict:
+    """The four sums in the reference kernel's convention: opacity with the sigmoid derivative applied (unless
+    proper antialiasing; ``factored``: already applied), colour masked where the colour is negative."""
     o = ref.conic_o[:, 3].double().cpu()
-    factor = torch.ones_like(o) if ref.aa else o * (1 - o)
+    factor = torch.ones_like(o) if ref.aa or factored else o * (1 - o)
     return {"mean2d": torch.as_tensor(mean2d).double().cpu(), "conic": torch.as_tensor(conic_abc).double().cpu(),
             "opacity": torch.as_tensor(opacity).double().cpu() * factor,
             "color": torch.as_tensor(color).double().cpu() * ref.color_mask.double().cpu()}
@@ -126,7 +128,7 @@ def test_blend_backward_against_reference_kernel_and_float64_replay(case, cuda):
     ex = _float64_replay(sc, cam, ref, dout)
     ours = _as_dict(ref, acc["mean2d"], acc["conic_o"][:, :3], acc["conic_o"][:, 3], acc["color"][:, :3])
     theirs = _as_dict(ref, out["mean2d"], torch.stack([out["conic"][0], 2 * out["conic"][1], out["conic"][2]], 1),
-                      out["opacity"], out["color"])
+                      out["opacity"], out["color"], factored=True)
     exact = _as_dict(ref, ex["mean2d"], ex["conic_o"][:, :3], ex["conic_o"][:, 3], ex["color"])
     for k in ours:
         e_ours, e_ref = _rel(ours[k], exact[k]), _rel(theirs[k], exact[k])
