@@ -243,7 +243,8 @@ constexpr size_t scatter_smem_bytes() {
 
 // Number of earlier pairs of digit `tid` over all tiles before `tile`: walks back over the status words,
 // kLookbackWindow tiles per round trip, summing counts up to and including the first inclusive prefix.
-__device__ __forceinline__ uint32_t look_back(const uint32_t* status, long long tile, int tid, int poll_limit) {
+__device__ __forceinline__ uint32_t look_back(const uint32_t* status, long long tile, int tid, int poll_limit,
+                                              bool& gave_up) {
     uint32_t excl = 0u;
     long long j = tile - 1;
     int polls = 0;
@@ -268,6 +269,7 @@ __device__ __forceinline__ uint32_t look_back(const uint32_t* status, long long 
         if (used == 0) {
             if (++polls >= poll_limit) {
                 atomicAdd(&g_wait_timeouts, 1u);
+                gave_up = true;
                 break;
             }
             if (polls > 32) __nanosleep(64);
@@ -283,7 +285,8 @@ __device__ __forceinline__ uint32_t look_back(const uint32_t* status, long long 
 // totals are published, and the number of earlier pairs of each digit is found by looking back over the
 // totals of the tiles before (stopping at the first tile that has published an inclusive prefix). A tile
 // only waits on tiles that took their ticket earlier, which are running; every wait is bounded, and on
-// timeout the wait counter is raised and the pass completes (with wrong offsets) instead of hanging.
+// timeout the wait counter is raised and the tile counts the earlier tiles' digits from the keys themselves (slow,
+// exact) instead of hanging.
 // Pairs are then placed in digit order in shared memory and written out digit run by digit run.
 // kGather: the last pass also writes gather_out[i] = gather_table[value] for every output slot i.
 template <typename K, bool kGather>
@@ -358,7 +361,19 @@ __global__ void __launch_bounds__(kSortThreads, kSortMinBlocks) k_sort_scatter(c
         s_goff[tid] = digit_base[tid];
     } else {
         store_status(mine, kAggregateFlag | count);
-        const uint32_t excl = look_back(status, tile, tid, poll_limit);
+        bool gave_up = false;
+        uint32_t excl = look_back(status, tile, tid, poll_limit, gave_up);
+        if (__syncthreads_or(gave_up)) {
+            // A wait gave up (it is counted and reported). The earlier tiles' digit counts are taken from the pass's
+            // input itself instead, so the offsets, and the sort, stay exact: the block counts the digits of every
+            // key before this tile (s_start is free until the scan below).
+            s_start[tid] = 0u;
+            __syncthreads();
+            for (long long i = tid; i < base; i += kSortThreads) atomicAdd(&s_start[digit_of(keys_in[i], shift, mask)], 1u);
+            __syncthreads();
+            excl = s_start[tid];
+            __syncthreads();
+        }
         store_status(mine, kPrefixFlag | (excl + count));
         s_goff[tid] = digit_base[tid] + excl;
     }
@@ -645,8 +660,8 @@ int splat_check_device_waits(void) {
     unsigned int n = 0u;
     SPLAT_TRY(splat::take_wait_timeouts(&n));
     if (n) {
-        splat::set_error("%u bounded device-side wait(s) gave up (radix sort look-back); results since the last "
-                         "check are unreliable",
+        splat::set_error("%u bounded device-side wait(s) gave up (radix sort look-back; their tiles recounted "
+                         "their offsets from the keys, so the sorts are exact, but the device stalled that long)",
                          n);
         return SPLAT_ERR_TIMEOUT;
     }

@@ -142,7 +142,8 @@ def _preprocess(means, scales, rotations, opacities, sh0, sh_rest, settings_args
     counted.synchronize()
     m, waits = host.tolist()
     if waits:
-        raise RuntimeError(f"{waits} bounded device-side wait(s) in the radix sort gave up; results are unreliable")
+        raise RuntimeError(f"{waits} bounded device-side wait(s) in the radix sort gave up: the device stalled (the "
+                           f"sorts recounted their offsets and stayed exact)")
     return n, dev, s, keep, stream, prim, tile, m
 
 

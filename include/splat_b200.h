@@ -80,13 +80,15 @@ int splat_radix_sort_pairs(const void* keys_in, const uint32_t* vals_in, void* k
                            long long n, int key_bytes, int begin_bit, int end_bit, void* workspace,
                            size_t workspace_bytes, void* stream);
 /* SPLAT_ERR_TIMEOUT if a bounded device-side wait on the current device gave up since the last call
- * (results produced since then are unreliable), else SPLAT_OK. Synchronises the device; clears the count.
+ * (about a second of polling without progress: the device stalled; the sorts themselves stay exact, their
+ * tiles having recounted their offsets from the keys), else SPLAT_OK. Synchronises the device; clears the count.
  * No counterpart in the reference (CUB's single-sweep sort waits without a bound). */
 int splat_check_device_waits(void);
 /* Failure-detection hook (no counterpart in the reference): sets the number of empty polls after which a
  * radix-sort look-back wait gives up (default 2^20, about a second of back-off) and returns the previous value,
  * or -1 for polls < 1. A tiny limit makes waits give up on purpose, so that tests see SPLAT_ERR_TIMEOUT from
- * splat_check_device_waits; the pass still completes and writes within its output (its order is then wrong). */
+ * splat_check_device_waits; a tile whose wait gave up counts the earlier tiles' digits from the keys instead
+ * (slow but exact), so the sort's result stays right. */
 int splat_set_lookback_poll_limit(int polls);
 /* The same count without a synchronisation: enqueues on `stream` a copy of it into dst (device uint32) and
  * clears it, so a caller that reads dst at a point where it waits anyway learns of a wait that gave up in

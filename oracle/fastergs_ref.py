@@ -46,6 +46,7 @@ class RefInputs:
         self.mean2d, self.conic_o = pv["mean2d"], pv["conic_o"]
         self.color3 = pv["color_z"][:, :3].contiguous()
         self.color_mask = pv["color_z"][:, :3] >= 0
+        self.visible = pv["n_touched"] > 0  # the primitive entries of the others are not written by the forward
         r = pv["rect"]  # (x0, y0, x1, y1) inclusive -> Faster-GS screen bounds (x0, x1 + 1, y0, y1 + 1)
         self.bounds = torch.stack([r[:, 0], r[:, 2] + 1, r[:, 1], r[:, 3] + 1], 1).to(torch.int16).contiguous()
         self.image = image

@@ -268,12 +268,15 @@ def test_rasterize_gaussians_graphdeco_entry(cuda):
     n = means.shape[0]
     pv = gs3d.primitive_views(prim, n)
     vis = pv["n_touched"] > 0
-    cov = torch.linalg.inv(torch.stack([torch.stack([pv["conic_o"][:, 0], pv["conic_o"][:, 1]], -1),
-                                        torch.stack([pv["conic_o"][:, 1], pv["conic_o"][:, 2]], -1)], -2).double())
+    co = pv["conic_o"][vis].double()  # the other Gaussians' entries are not written by the forward
+    cov = torch.linalg.inv(torch.stack([torch.stack([co[:, 0], co[:, 1]], -1), torch.stack([co[:, 1], co[:, 2]], -1)],
+                                       -2))
     lam = torch.linalg.eigvalsh(cov)[:, 1]
-    want = torch.where(vis, torch.ceil(3 * torch.sqrt(lam)).int(), torch.zeros_like(radii))
+    want = torch.zeros_like(radii)
+    want[vis] = torch.ceil(3 * torch.sqrt(lam)).int()
     assert radii.shape == (n,) and radii.dtype == torch.int32 and int((radii > 0).sum()) > 0
-    assert float((radii != want).double().mean()) < 1e-3  # log/logit round trip: a few may differ by one
+    # rasterize_gaussians renders log(exp(s)) and logit(sigmoid(o)): a ceil may flip, by one pixel at most
+    assert int((radii - want).abs().max()) <= 1 and float((radii != want).double().mean()) < 1e-2
     # a projection that is not the centred pinhole of viewmatrix is refused
     bad = _graphdeco_proj(view, tx, ty).clone()
     bad[0, 0] *= 1.1

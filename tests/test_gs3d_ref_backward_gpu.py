@@ -58,18 +58,23 @@ def forward_and_ours(sc, cam, seed: int, rows: int, scale: float = 1.0):
 
 
 def compare(ref: RefInputs, acc: dict, out: dict, abs_grad: bool) -> dict:
-    o = ref.conic_o[:, 3]
+    """Relative differences over the Gaussians the view lists (both kernels leave the others at zero; their
+    primitive entries are not written)."""
+    v = ref.visible
+    o = ref.conic_o[v, 3]
     factor = torch.ones_like(o) if ref.aa else o * (1 - o)
-    mask = ref.color_mask.float()
+    mask = ref.color_mask[v].float()
     errs = {
-        "mean2d": _rel(acc["mean2d"], out["mean2d"]),
-        "conic": _rel(torch.stack([acc["conic_o"][:, 0], 0.5 * acc["conic_o"][:, 1], acc["conic_o"][:, 2]]),
-                      out["conic"]),
-        "opacity": _rel(acc["conic_o"][:, 3] * factor, out["opacity"]),
-        "color": _rel(acc["color"][:, :3] * mask, out["color"]),
+        "mean2d": _rel(acc["mean2d"][v], out["mean2d"][v]),
+        "conic": _rel(torch.stack([acc["conic_o"][v, 0], 0.5 * acc["conic_o"][v, 1], acc["conic_o"][v, 2]]),
+                      out["conic"][:, v]),
+        "opacity": _rel(acc["conic_o"][v, 3] * factor, out["opacity"][v]),
+        "color": _rel(acc["color"][v, :3] * mask, out["color"][v]),
     }
     if abs_grad:
-        errs["mean2d_abs"] = _rel(acc["mean2d_abs"], out["mean2d_abs"])
+        errs["mean2d_abs"] = _rel(acc["mean2d_abs"][v], out["mean2d_abs"][v])
+    for k in ("mean2d", "opacity", "color"):
+        assert float(out[k][~v].abs().sum()) == 0.0, f"the reference kernel wrote {k} of an unlisted Gaussian"
     return errs
 
 
@@ -105,13 +110,15 @@ def _float64_replay(sc, cam, ref: RefInputs, dout: torch.Tensor) -> dict:
 
 
 def _as_dict(ref: RefInputs, mean2d, conic_abc, opacity, color, factored: bool = False) -> dict:
-    """The four sums in the reference kernel's convention: opacity with the sigmoid derivative applied (unless
-    proper antialiasing; ``factored``: already applied), colour masked where the colour is negative."""
-    o = ref.conic_o[:, 3].double().cpu()
+    """The four sums of the listed Gaussians in the reference kernel's convention: opacity with the sigmoid
+    derivative applied (unless proper antialiasing; ``factored``: already applied), colour masked where the colour
+    is negative."""
+    v = ref.visible.cpu()
+    o = ref.conic_o[:, 3].double().cpu()[v]
     factor = torch.ones_like(o) if ref.aa or factored else o * (1 - o)
-    return {"mean2d": torch.as_tensor(mean2d).double().cpu(), "conic": torch.as_tensor(conic_abc).double().cpu(),
-            "opacity": torch.as_tensor(opacity).double().cpu() * factor,
-            "color": torch.as_tensor(color).double().cpu() * ref.color_mask.double().cpu()}
+    return {"mean2d": torch.as_tensor(mean2d).double().cpu()[v], "conic": torch.as_tensor(conic_abc).double().cpu()[v],
+            "opacity": torch.as_tensor(opacity).double().cpu()[v] * factor,
+            "color": torch.as_tensor(color).double().cpu()[v] * ref.color_mask.double().cpu()[v]}
 
 
 @pytest.mark.parametrize("case", ["garden_res", "garden_res+aa", "c2", "c3"])
