@@ -354,7 +354,7 @@ class NcclAdam:
 def exchange_for(world: int, form: str = "auto") -> str:
     """The exchange form a step of `world` ranks uses: "peer" (peer loads and stores, adam_step_dp_fused), "nvls"
     (NVLink multicast, adam_step_dp_nvls) or "nccl" (NcclAdam). "auto" picks the form measured fastest at that
-    rank count on this pool's B200 nodes (see DESIGN)."""
+    rank count on 8-GPU B200 nodes (AUTO_EXCHANGE), the multicast form from 4 ranks on otherwise."""
     if form != "auto":
         if form not in ("peer", "nvls", "nccl"):
             raise ValueError(f"unknown exchange form {form!r}")

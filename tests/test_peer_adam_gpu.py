@@ -1,7 +1,8 @@
-"""PeerAdam (csrc/dp_adam.cu) on 2 GPUs, with peer loads / stores and with NVLink multicast, against an NCCL
-all-reduce of the gradients followed by adam_step_multi on every rank. With two ranks the gradient sum g0 + g1 is
-the same single addition in all of them, so parameters and the owned moments must agree bit for bit. Skipped with
-fewer than two GPUs."""
+"""The exchange + Adam forms on 2 GPUs - PeerAdam (csrc/dp_adam.cu) with peer loads / stores and with NVLink
+multicast, and NcclAdam (NCCL reduce-scatter, Adam on the owned slice, all-gather) - against an NCCL all-reduce of
+the gradients followed by adam_step_multi on every rank. With two ranks the gradient sum g0 + g1 is the same single
+addition in all of them, so parameters and the owned moments must agree bit for bit. Skipped with fewer than two
+GPUs. NVLS is left to NCCL's default here; the ranks exchange only on the host between steps."""
 from __future__ import annotations
 
 import datetime
@@ -15,7 +16,7 @@ import torch.multiprocessing as mp
 pytestmark = pytest.mark.gpu
 
 
-def _worker(rank: int, world: int, port: int, q, nvls: bool) -> None:
+def _worker(rank: int, world: int, port: int, q, form: str) -> None:
     try:
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
@@ -35,7 +36,7 @@ def _worker(rank: int, world: int, port: int, q, nvls: bool) -> None:
         init = [torch.randn(n, 3, device=dev, generator=g0), torch.randn(n, 4, device=dev, generator=g0),
                 torch.randn(n, 1, device=dev, generator=g0), torch.randn(n, 15, 3, device=dev, generator=g0)]
         lrs = [1e-3, 2e-3, 5e-2, 2.5e-3]
-        opt = D.PeerAdam(init, lrs, nvls=nvls)
+        opt = D.NcclAdam(init, lrs) if form == "nccl" else D.PeerAdam(init, lrs, nvls=form == "nvls")
         ref = [t.clone() for t in init]
         m = [torch.zeros_like(t) for t in init]
         v = [torch.zeros_like(t) for t in init]
@@ -54,22 +55,22 @@ def _worker(rank: int, world: int, port: int, q, nvls: bool) -> None:
         flat_m = torch.cat([x.flatten() for x in m])[opt.lo:opt.hi]  # the multicast path pads the vector to 4
         ok_m = torch.equal(opt.exp_avg[:flat_m.numel()], flat_m)
         # the copied-in path: step(grads=...) gives the same as writing into opt.grads
-        used_nvls = opt.nvls
+        used_nvls = getattr(opt, "nvls", False)
         opt.close()
-        q.put((rank, ok_p, ok_m, None if used_nvls or not nvls else "no NVLS"))
+        q.put((rank, ok_p, ok_m, None if used_nvls or form != "nvls" else "no NVLS"))
         dist.destroy_process_group()
     except Exception as exc:  # report instead of hanging the parent
         q.put((rank, False, False, repr(exc)))
 
 
-@pytest.mark.parametrize("nvls", [False, True], ids=["peer_loads", "multicast"])
-def test_peer_adam_matches_allreduce_adam(nvls):
+@pytest.mark.parametrize("form", ["peer", "nvls", "nccl"])
+def test_exchange_matches_allreduce_adam(form):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29600 + os.getpid() % 300 + (7 if nvls else 0)
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, nvls)) for r in range(2)]
+    port = 29600 + os.getpid() % 300 + {"peer": 0, "nvls": 7, "nccl": 13}[form]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, form)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]
