@@ -271,7 +271,10 @@ def test_rasterize_gaussians_graphdeco_entry(cuda):
     co = pv["conic_o"][vis].double()  # the other Gaussians' entries are not written by the forward
     cov = torch.linalg.inv(torch.stack([torch.stack([co[:, 0], co[:, 1]], -1), torch.stack([co[:, 1], co[:, 2]], -1)],
                                        -2))
-    lam = torch.linalg.eigvalsh(cov)[:, 1]
+    # graphdeco's larger eigenvalue: mid + sqrt(max(mid^2 - det, 0.1)) of the 2D covariance
+    a, b, c = cov[:, 0, 0], cov[:, 0, 1], cov[:, 1, 1]
+    mid = 0.5 * (a + c)
+    lam = mid + torch.sqrt(torch.clamp(mid * mid - (a * c - b * b), min=0.1))
     want = torch.zeros_like(radii)
     want[vis] = torch.ceil(3 * torch.sqrt(lam)).int()
     assert radii.shape == (n,) and radii.dtype == torch.int32 and int((radii > 0).sum()) > 0
