@@ -148,7 +148,8 @@ __global__ void __launch_bounds__(32 * kBwdWarps, SPLAT_BWD_MIN_BLOCKS) k_blend_
             const float4 co = s_con[warp][j];
             const float4 c = s_col[warp][j];
             const ushort4 rc = s_rect[warp][j];
-            // per-lane sums over its pixels: h = dL/dq2 moments (for mean2d and conic), opacity, colour
+            // per-lane sums over its pixels of t = G dL/dalpha: its moments (for mean2d and conic; dL/dq2 is
+            // t opacity ln 2, a per-splat factor applied once to the warp's totals), t itself (opacity), colour
             float s_x = 0.f, s_y = 0.f, s_xx = 0.f, s_xy = 0.f, s_yy = 0.f, g_o = 0.f, g_r = 0.f, g_g = 0.f, g_bl = 0.f;
             float a_x = 0.f, a_y = 0.f;  // kAbs: sums of |per-pixel dL/dmean2d|
             bool used = false;
@@ -173,17 +174,17 @@ __global__ void __launch_bounds__(32 * kBwdWarps, SPLAT_BWD_MIN_BLOCKS) k_blend_
                 rho[r] -= w * dot_c;
                 const float one_minus = 1.f - alpha;
                 const float dL_dalpha = T[r] * dot_c - __fdividef(rho[r], fmaxf(one_minus, kOneMinusAlphaEps));
-                g_o += G * dL_dalpha;
-                const float h = alpha * dL_dalpha * kLn2;  // dL/dq2
-                const float hx = h * dx, hy = h * dy;
-                s_x += hx;
-                s_y += hy;
-                s_xx += hx * dx;
-                s_xy += hx * dy;
-                s_yy += hy * dy;
+                const float t = G * dL_dalpha;
+                g_o += t;
+                const float tx = t * dx, ty = t * dy;
+                s_x += tx;
+                s_y += ty;
+                s_xx += tx * dx;
+                s_xy += tx * dy;
+                s_yy += ty * dy;
                 if (kAbs) {
-                    a_x += fabsf(2.f * co.x * hx + co.y * hy);
-                    a_y += fabsf(co.y * hx + 2.f * co.z * hy);
+                    a_x += fabsf(2.f * co.x * tx + co.y * ty);
+                    a_y += fabsf(co.y * tx + 2.f * co.z * ty);
                 }
                 T[r] *= one_minus;
             }
@@ -213,13 +214,16 @@ __global__ void __launch_bounds__(32 * kBwdWarps, SPLAT_BWD_MIN_BLOCKS) k_blend_
                 }
             }
             if (lane == 0) {
-                // q2 = a2 dx^2 + b2 dx dy + c2 dy^2: dq2/dmx = 2 a2 dx + b2 dy, dq2/dmy = b2 dx + 2 c2 dy; then back
-                // from the exp2-scaled conic (a2, b2, c2) = log2(e) (-0.5 A, -B, -0.5 C) to (A, B, C)
-                atomicAdd(acc.mean2d + g, make_float2(2.f * co.x * s_x + co.y * s_y, co.y * s_x + 2.f * co.z * s_y));
+                // dL/dq2 = t opacity ln 2 (alpha = opacity 2^q2). q2 = a2 dx^2 + b2 dx dy + c2 dy^2: dq2/dmx =
+                // 2 a2 dx + b2 dy, dq2/dmy = b2 dx + 2 c2 dy; back from the exp2-scaled conic (a2, b2, c2) =
+                // log2(e) (-0.5 A, -B, -0.5 C) to (A, B, C), log2(e) ln 2 = 1
+                const float k = co.w * kLn2;
+                atomicAdd(acc.mean2d + g,
+                          make_float2(k * (2.f * co.x * s_x + co.y * s_y), k * (co.y * s_x + 2.f * co.z * s_y)));
                 atomicAdd(acc.conic_o + g,
-                          make_float4(-0.5f * kLog2e * s_xx, -kLog2e * s_xy, -0.5f * kLog2e * s_yy, g_o));
+                          make_float4(-0.5f * co.w * s_xx, -co.w * s_xy, -0.5f * co.w * s_yy, g_o));
                 atomicAdd(acc.color + g, make_float4(g_r, g_g, g_bl, 0.f));
-                if (kAbs) atomicAdd(acc.mean2d_abs + g, make_float2(a_x, a_y));
+                if (kAbs) atomicAdd(acc.mean2d_abs + g, make_float2(k * a_x, k * a_y));
             }
         }
     }
