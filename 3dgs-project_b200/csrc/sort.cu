@@ -144,20 +144,6 @@ __device__ __forceinline__ uint32_t digit_of(K key, int shift, uint32_t mask) {
     return static_cast<uint32_t>(key >> shift) & mask;
 }
 
-// Lanes of the warp whose digit equals this lane's (among the lanes in `valid`): one ballot per digit bit.
-__device__ __forceinline__ unsigned digit_peers(uint32_t d, int bits, unsigned valid) {
-    unsigned peers = valid;
-#pragma unroll
-    for (int b = 0; b < kRadixBits; ++b) {
-        if (b < bits) {
-            const bool set = (d >> b) & 1u;
-            const unsigned m = __ballot_sync(kFullMask, set);
-            peers &= set ? m : ~m;
-        }
-    }
-    return peers;
-}
-
 // Digit counts of every pass in one read of the keys: per-warp shared counters (dynamic shared memory,
 // [passes][warp][digit]), loads batched kHistUnroll deep, then one global atomic per (pass, digit) and block.
 constexpr int kHistUnroll = 4;
@@ -165,8 +151,10 @@ constexpr int kHistUnroll = 4;
 template <typename K>
 __global__ void __launch_bounds__(kSortThreads) k_sort_global_hist(const K* __restrict__ keys, long long n,
                                                                    int begin_bit, int end_bit, int passes,
-                                                                   uint32_t* __restrict__ hist) {
+                                                                   uint32_t* __restrict__ hist,
+                                                                   const uint32_t* __restrict__ n_dev) {
     constexpr int kWarps = kSortThreads / 32;
+    if (n_dev) n = min(n, static_cast<long long>(*n_dev));  // the count on the device, within the capacity
     extern __shared__ uint32_t s_whist[];
     uint32_t* mine = s_whist + (threadIdx.x >> 5) * kRadix;
     for (int i = threadIdx.x; i < passes * kWarps * kRadix; i += kSortThreads) s_whist[i] = 0u;
@@ -238,7 +226,7 @@ __device__ __forceinline__ void store_status(uint32_t* p, uint32_t v) {
 template <typename K>
 constexpr size_t scatter_smem_bytes() {
     return kSortTile * sizeof(K) + kSortTile * sizeof(uint32_t) +
-           ((kSortThreads / 32) * kRadix + 2 * kRadix) * sizeof(uint32_t);
+           (2 * (kSortThreads / 32) * kRadix + 2 * kRadix) * sizeof(uint32_t);
 }
 
 // Number of earlier pairs of digit `tid` over all tiles before `tile`: walks back over the status words,
@@ -280,7 +268,8 @@ __device__ __forceinline__ uint32_t look_back(const uint32_t* status, long long 
 
 // One digit pass in one launch. Tiles are taken in launch order from a ticket counter. Warp w of a tile
 // owns the tile's pairs [w * 32 * kSortRounds, (w + 1) * 32 * kSortRounds) and ranks them round by round
-// against its own per-digit counters (ballot-based peers, no atomics, no block barrier); one block
+// against its own per-digit counters (no block barrier): in a round, each lane ORs its lane bit into its
+// digit's match word, so that reading the word back gives the lanes holding the same digit; one block
 // barrier later the per-warp counts give each warp's base per digit and the tile's per-digit totals. The
 // totals are published, and the number of earlier pairs of each digit is found by looking back over the
 // totals of the tiles before (stopping at the first tile that has published an inclusive prefix). A tile
@@ -299,7 +288,8 @@ __global__ void __launch_bounds__(kSortThreads, kSortMinBlocks) k_sort_scatter(c
                                                                uint32_t* __restrict__ status,
                                                                uint32_t* __restrict__ ticket,
                                                                const uint32_t* __restrict__ gather_table,
-                                                               uint32_t* __restrict__ gather_out, int poll_limit) {
+                                                               uint32_t* __restrict__ gather_out, int poll_limit,
+                                                               const uint32_t* __restrict__ n_dev) {
     static_assert(kRadix == kSortThreads, "one thread per digit");
     constexpr int kWarps = kSortThreads / 32;
     constexpr int kWarpItems = 32 * kSortRounds;
@@ -307,19 +297,24 @@ __global__ void __launch_bounds__(kSortThreads, kSortMinBlocks) k_sort_scatter(c
     K* s_keys = reinterpret_cast<K*>(smem_raw);
     uint32_t* s_vals = reinterpret_cast<uint32_t*>(s_keys + kSortTile);
     uint32_t* s_cnt = s_vals + kSortTile;          // [kWarps][kRadix]: running counts, then warp bases
-    uint32_t* s_start = s_cnt + kWarps * kRadix;   // first slot of each digit in the sorted tile
+    uint32_t* s_match = s_cnt + kWarps * kRadix;   // [kWarps][kRadix]: lanes of the round holding each digit
+    uint32_t* s_start = s_match + kWarps * kRadix; // first slot of each digit in the sorted tile
     uint32_t* s_goff = s_start + kRadix;           // first global slot of each digit for this tile
     __shared__ uint32_t s_warp[33];
     __shared__ uint32_t s_tile;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int bits = __popc(mask);
     if (tid == 0) s_tile = atomicAdd(ticket, 1u);
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) s_cnt[w * kRadix + tid] = 0u;
+    for (int w = 0; w < kWarps; ++w) {
+        s_cnt[w * kRadix + tid] = 0u;
+        s_match[w * kRadix + tid] = 0u;
+    }
     __syncthreads();
     const long long tile = s_tile;
     const long long base = tile * kSortTile;
+    if (n_dev) n = min(n, static_cast<long long>(*n_dev));  // the count on the device, within the capacity
+    if (base >= n) return;  // a tile past the pairs on the device: no later tile looks back at it
     const int tile_n = static_cast<int>(min(static_cast<long long>(kSortTile), n - base));
     const int wbase = warp * kWarpItems;
 
@@ -333,17 +328,22 @@ __global__ void __launch_bounds__(kSortThreads, kSortMinBlocks) k_sort_scatter(c
         val[r] = li < tile_n ? vals_in[base + li] : 0u;
     }
     uint32_t* cnt = s_cnt + warp * kRadix;
+    uint32_t* match = s_match + warp * kRadix;
     const unsigned lanes_below = (1u << lane) - 1u;
 #pragma unroll
     for (int r = 0; r < kSortRounds; ++r) {
         const bool ok = wbase + r * 32 + lane < tile_n;
-        const unsigned okm = __ballot_sync(kFullMask, ok);
-        const uint32_t d = ok ? digit_of(key[r], shift, mask) : 0u;
-        const unsigned peers = digit_peers(d, bits, okm);
+        const uint32_t d = digit_of(key[r], shift, mask);
+        if (ok) atomicOr(&match[d], 1u << lane);
+        __syncwarp();
+        const unsigned peers = ok ? match[d] : 0u;  // lanes of this round with digit d (this lane included)
         const uint32_t below = __popc(peers & lanes_below);
         const uint32_t prior = ok ? cnt[d] : 0u;
         __syncwarp();
-        if (ok && below == 0u) cnt[d] = prior + __popc(peers);
+        if (ok && below == 0u) {  // the lowest lane of the group advances the counter and clears the word
+            cnt[d] = prior + __popc(peers);
+            match[d] = 0u;
+        }
         __syncwarp();
         rank[r] = prior + below;
     }
@@ -356,30 +356,12 @@ __global__ void __launch_bounds__(kSortThreads, kSortMinBlocks) k_sort_scatter(c
         count += c;
     }
     uint32_t* mine = status + tile * kRadix + tid;
-    if (tile == 0) {
-        store_status(mine, kPrefixFlag | count);
-        s_goff[tid] = digit_base[tid];
-    } else {
-        store_status(mine, kAggregateFlag | count);
-        bool gave_up = false;
-        uint32_t excl = look_back(status, tile, tid, poll_limit, gave_up);
-        if (__syncthreads_or(gave_up)) {
-            // A wait gave up (it is counted and reported). The earlier tiles' digit counts are taken from the pass's
-            // input itself instead, so the offsets, and the sort, stay exact: the block counts the digits of every
-            // key before this tile (s_start is free until the scan below).
-            s_start[tid] = 0u;
-            __syncthreads();
-            for (long long i = tid; i < base; i += kSortThreads) atomicAdd(&s_start[digit_of(keys_in[i], shift, mask)], 1u);
-            __syncthreads();
-            excl = s_start[tid];
-            __syncthreads();
-        }
-        store_status(mine, kPrefixFlag | (excl + count));
-        s_goff[tid] = digit_base[tid] + excl;
-    }
+    store_status(mine, (tile == 0 ? kPrefixFlag : kAggregateFlag) | count);  // before anything else of the tile
     uint32_t btotal;
-    s_start[tid] = block_exclusive_scan(count, s_warp, btotal);  // its barriers publish s_cnt and s_goff too
+    s_start[tid] = block_exclusive_scan(count, s_warp, btotal);  // its barriers publish s_cnt too
     __syncthreads();
+    // The tile's pairs in digit order in shared memory first, so that the registers holding them are free during
+    // the look-back (its window of status words in flight).
 #pragma unroll
     for (int r = 0; r < kSortRounds; ++r) {
         if (wbase + r * 32 + lane < tile_n) {
@@ -389,6 +371,23 @@ __global__ void __launch_bounds__(kSortThreads, kSortMinBlocks) k_sort_scatter(c
             s_vals[pos] = val[r];
         }
     }
+    uint32_t excl = 0u;
+    if (tile != 0) {
+        bool gave_up = false;
+        excl = look_back(status, tile, tid, poll_limit, gave_up);
+        if (__syncthreads_or(gave_up)) {
+            // A wait gave up (it is counted and reported). The earlier tiles' digit counts are taken from the pass's
+            // input itself instead, so the offsets, and the sort, stay exact: the block counts the digits of every
+            // key before this tile (in the match words, unused after the ranking).
+            s_match[tid] = 0u;
+            __syncthreads();
+            for (long long i = tid; i < base; i += kSortThreads) atomicAdd(&s_match[digit_of(keys_in[i], shift, mask)], 1u);
+            __syncthreads();
+            excl = s_match[tid];
+        }
+        store_status(mine, kPrefixFlag | (excl + count));
+    }
+    s_goff[tid] = digit_base[tid] + excl;
     __syncthreads();
     for (int li = tid; li < tile_n; li += kSortThreads) {
         const K k = s_keys[li];
@@ -459,7 +458,7 @@ size_t sort_workspace_bytes(long long n) {
 template <typename K>
 int radix_sort_pairs(const K* keys_in, const uint32_t* vals_in, K* keys_out, uint32_t* vals_out, long long n,
                      int begin_bit, int end_bit, void* ws, size_t ws_bytes, cudaStream_t stream,
-                     const uint32_t* gather_table, uint32_t* gather_out) {
+                     const uint32_t* gather_table, uint32_t* gather_out, const uint32_t* n_dev) {
     constexpr int kKeyBits = static_cast<int>(sizeof(K) * 8);
     SPLAT_REQUIRE(0 <= begin_bit && begin_bit <= end_bit && end_bit <= kKeyBits, "bad bit range [%d, %d)",
                   begin_bit, end_bit);
@@ -489,7 +488,7 @@ int radix_sort_pairs(const K* keys_in, const uint32_t* vals_in, K* keys_out, uin
     SPLAT_CUDA(cudaMemsetAsync(hist, 0, zero_bytes, stream));
     const long long hist_blocks = std::min<long long>(div_up(n, kSortThreads * 8), 4ll * sm_count());
     k_sort_global_hist<K><<<static_cast<unsigned>(hist_blocks), kSortThreads, global_hist_smem_bytes(passes),
-                            stream>>>(keys_in, n, begin_bit, end_bit, passes, hist);
+                            stream>>>(keys_in, n, begin_bit, end_bit, passes, hist, n_dev);
     note_launch();
     k_sort_digit_base<<<1, kSortThreads, 0, stream>>>(hist, passes);
     note_launch();
@@ -507,7 +506,7 @@ int radix_sort_pairs(const K* keys_in, const uint32_t* vals_in, K* keys_out, uin
         kernel<<<static_cast<unsigned>(nb), kSortThreads, scatter_smem_bytes<K>(), stream>>>(
             src_k, src_v, dst_k, dst_v, n, shift, mask, hist + p * kRadix,
             status + static_cast<size_t>(p) * nb * kRadix, tickets + p, gather_table, gather_out,
-            g_poll_limit.load(std::memory_order_relaxed));
+            g_poll_limit.load(std::memory_order_relaxed), n_dev);
         note_launch();
         SPLAT_TRY(check_launch("radix_sort_pairs"));
         src_k = dst_k;
@@ -613,10 +612,11 @@ int scan_exclusive_u32_noalloc(const uint32_t* in, uint32_t* out, long long n, u
 template size_t sort_workspace_bytes<uint32_t>(long long);
 template size_t sort_workspace_bytes<unsigned long long>(long long);
 template int radix_sort_pairs<uint32_t>(const uint32_t*, const uint32_t*, uint32_t*, uint32_t*, long long, int,
-                                        int, void*, size_t, cudaStream_t, const uint32_t*, uint32_t*);
+                                        int, void*, size_t, cudaStream_t, const uint32_t*, uint32_t*,
+                                        const uint32_t*);
 template int radix_sort_pairs<unsigned long long>(const unsigned long long*, const uint32_t*, unsigned long long*,
                                                   uint32_t*, long long, int, int, void*, size_t, cudaStream_t,
-                                                  const uint32_t*, uint32_t*);
+                                                  const uint32_t*, uint32_t*, const uint32_t*);
 
 }  // namespace splat
 

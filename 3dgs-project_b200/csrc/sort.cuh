@@ -21,7 +21,7 @@ constexpr int kSortThreads = 256;
 #endif
 constexpr int kSortRounds = SPLAT_SORT_ROUNDS;
 #ifndef SPLAT_SORT_MIN_BLOCKS
-#define SPLAT_SORT_MIN_BLOCKS 2
+#define SPLAT_SORT_MIN_BLOCKS 3
 #endif
 constexpr int kSortMinBlocks = SPLAT_SORT_MIN_BLOCKS;  // resident scatter blocks per SM to budget registers for
 constexpr int kSortTile = kSortThreads * kSortRounds;  // pairs per sort block
@@ -48,11 +48,13 @@ size_t sort_workspace_bytes(long long n);
 // Stable sort of (key, value) pairs by key bits [begin_bit, end_bit). keys_in/vals_in are not
 // modified; results land in keys_out/vals_out (which must not alias the inputs). With gather_out
 // (device, n entries), the last pass also writes gather_out[i] = gather_table[vals_out[i]].
+// With n_dev (device), n is a capacity: the pairs sorted are the first min(*n_dev, n), a count that
+// the host never reads; the launches are sized for n.
 template <typename K>
 int radix_sort_pairs(const K* keys_in, const uint32_t* vals_in, K* keys_out, uint32_t* vals_out,
                      long long n, int begin_bit, int end_bit, void* ws, size_t ws_bytes,
                      cudaStream_t stream, const uint32_t* gather_table = nullptr,
-                     uint32_t* gather_out = nullptr);
+                     uint32_t* gather_out = nullptr, const uint32_t* n_dev = nullptr);
 
 // Number of significant bits needed to represent v (0 for v == 0).
 inline int bit_width(unsigned long long v) {
