@@ -179,9 +179,10 @@ __global__ void k_bin_rank(const uint32_t* __restrict__ sorted_ids, int n, int64
 __global__ void k_bin_duplicate(const int4* __restrict__ rect, const uint32_t* __restrict__ counts,
                                 const uint32_t* __restrict__ offsets, const uint32_t* __restrict__ rank, int n,
                                 int tiles_x, int rank_bits, unsigned long long* __restrict__ keys,
-                                uint32_t* __restrict__ vals) {
+                                uint32_t* __restrict__ vals, const uint32_t* __restrict__ m_eff) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
+    if (m_eff && *m_eff == 0u) return;  // bounded fill past its capacity: no list (flagged by k_bin_clamp)
     const uint32_t c = counts[i];
     if (c == 0) return;
     const int4 rc = rect[i];
@@ -200,8 +201,9 @@ __global__ void k_bin_duplicate(const int4* __restrict__ rect, const uint32_t* _
 // Run boundaries of the sorted keys give each tile's [first, last) (zero for empty tiles).
 __global__ void k_bin_runs(const unsigned long long* __restrict__ keys, const uint32_t* __restrict__ vals, int m,
                            int rank_bits, uint32_t* __restrict__ first, uint32_t* __restrict__ last,
-                           int32_t* __restrict__ point_list) {
+                           int32_t* __restrict__ point_list, const uint32_t* __restrict__ m_dev) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (m_dev) m = min(m, static_cast<int>(*m_dev));
     if (i >= m) return;
     const unsigned long long t = keys[i] >> rank_bits;
     if (i == 0 || (keys[i - 1] >> rank_bits) != t) first[t] = static_cast<uint32_t>(i);
@@ -230,6 +232,21 @@ __global__ void k_bin_ranges(const uint32_t* __restrict__ count, const uint32_t*
     bucket_offsets[t] = static_cast<int32_t>(bstart[t]);
 }
 
+// The bounded fill's instance count: M from the count, or 0 with *overflow set when M exceeds the capacity (the list
+// is then empty rather than written past its buffers).
+__global__ void k_bin_clamp(const uint32_t* __restrict__ m, long long capacity, uint32_t* __restrict__ m_eff,
+                            uint32_t* __restrict__ overflow) {
+    const uint32_t v = *m;
+    const bool over = static_cast<long long>(v) > capacity;
+    *m_eff = over ? 0u : v;
+    if (over) *overflow = 1u;
+}
+// Buckets past the count up to the capacity name no tile (-1), so that a launch over the capacity skips them.
+__global__ void k_bin_bucket_tail(const uint32_t* __restrict__ total, long long capacity,
+                                  int32_t* __restrict__ bucket_to_tile) {
+    const long long b = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (b < capacity && b >= static_cast<long long>(*total)) bucket_to_tile[b] = -1;
+}
 __global__ void k_bin_bucket_tiles(const uint32_t* __restrict__ nb, const uint32_t* __restrict__ bstart, int T,
                                    int32_t* __restrict__ bucket_to_tile) {
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
@@ -285,6 +302,7 @@ struct FillScratch {
     uint32_t* start;
     uint32_t* nb;
     uint32_t* bstart;
+    uint32_t* m_eff;  // bounded fill: the instance count used (M, or 0 when M exceeds the capacity)
     void* sort_ws;
     size_t sort_ws_bytes;
     void* scan_ws;
@@ -303,6 +321,7 @@ static FillScratch carve_fill(Carver& c, long long m, int T) {
     s.start = c.take<uint32_t>(T + 1);
     s.nb = c.take<uint32_t>(T + 1);
     s.bstart = c.take<uint32_t>(T + 1);
+    s.m_eff = c.take<uint32_t>(1);
     s.sort_ws_bytes = sort_workspace_bytes<unsigned long long>(m);
     s.sort_ws = c.take<unsigned char>(s.sort_ws_bytes);
     s.scan_ws_bytes = scan_workspace_bytes(T > m ? T : m);
@@ -728,32 +747,42 @@ int gs2d_bin_count(const float* means, const int32_t* radii, const void* depth, 
     return SPLAT_OK;
 }
 
-int gs2d_bin_fill(const int32_t* rect, int n, int H, int W, long long m, void* count_ws, size_t count_ws_bytes,
-                  void* fill_ws, size_t fill_ws_bytes, int32_t* point_list, int32_t* ranges, int32_t* bucket_offsets,
-                  int32_t* bucket_to_tile, uint32_t* num_buckets, void* stream) {
-    SPLAT_REQUIRE(n >= 0 && m >= 0 && H > 0 && W > 0, "gs2d_bin_fill: bad sizes");
-    SPLAT_REQUIRE(m < (1ll << 31), "gs2d_bin_fill: %lld instances exceed int32 indexing", m);
+}  // extern "C"
+
+namespace {
+// The fill shared by the exact and the bounded entry points. m: the instance count (exact), or the capacity with
+// m_dev the count on the device (bounded); bucket_capacity > 0: fill the buckets past the count with -1.
+int bin_fill(const int32_t* rect, int n, int H, int W, long long m, const uint32_t* m_dev, void* count_ws,
+             size_t count_ws_bytes, void* fill_ws, size_t fill_ws_bytes, int32_t* point_list, int32_t* ranges,
+             int32_t* bucket_offsets, int32_t* bucket_to_tile, uint32_t* num_buckets, long long bucket_capacity,
+             uint32_t* overflow, cudaStream_t st) {
     const int tiles_x = (W + kTile - 1) / kTile, tiles_y = (H + kTile - 1) / kTile;
     const int T = tiles_x * tiles_y;
-    SPLAT_REQUIRE(fill_ws_bytes >= gs2d_bin_fill_workspace_size(m, H, W), "gs2d_bin_fill: workspace too small");
-    cudaStream_t st = as_stream(stream);
     Carver cc(count_ws, count_ws_bytes);
     BinScratch s = carve_count(cc, n < 1 ? 1 : n);
     Carver cf(fill_ws, fill_ws_bytes);
     FillScratch f = carve_fill(cf, m < 1 ? 1 : m, T);
     SPLAT_CUDA(cudaMemsetAsync(f.first, 0, sizeof(uint32_t) * T, st));
     SPLAT_CUDA(cudaMemsetAsync(f.last, 0, sizeof(uint32_t) * T, st));
+    const uint32_t* m_eff = nullptr;
+    if (m_dev) {
+        k_bin_clamp<<<1, 1, 0, st>>>(m_dev, m, f.m_eff, overflow);
+        note_launch();
+        SPLAT_TRY(check_launch("gs2d_bin_clamp"));
+        m_eff = f.m_eff;
+    }
     const int rank_bits = bit_width(static_cast<unsigned long long>(n > 1 ? n - 1 : 1));
     const int tile_bits = bit_width(static_cast<unsigned long long>(T > 1 ? T - 1 : 1));
     if (m > 0) {
         k_bin_duplicate<<<div_up(n, 256), 256, 0, st>>>(reinterpret_cast<const int4*>(rect), s.counts, s.offsets,
-                                                        s.rank, n, tiles_x, rank_bits, f.keys, f.vals);
+                                                        s.rank, n, tiles_x, rank_bits, f.keys, f.vals, m_eff);
         note_launch();
         SPLAT_TRY(check_launch("gs2d_bin_duplicate"));
         SPLAT_TRY(radix_sort_pairs<unsigned long long>(f.keys, f.vals, f.keys_sorted, f.vals_sorted, m, 0,
-                                                       rank_bits + tile_bits, f.sort_ws, f.sort_ws_bytes, st));
+                                                       rank_bits + tile_bits, f.sort_ws, f.sort_ws_bytes, st,
+                                                       nullptr, nullptr, m_eff));
         k_bin_runs<<<div_up(m, 256), 256, 0, st>>>(f.keys_sorted, f.vals_sorted, static_cast<int>(m), rank_bits,
-                                                   f.first, f.last, point_list);
+                                                   f.first, f.last, point_list, m_eff);
         note_launch();
         SPLAT_TRY(check_launch("gs2d_bin_runs"));
     }
@@ -766,11 +795,51 @@ int gs2d_bin_fill(const int32_t* rect, int n, int H, int W, long long m, void* c
     note_launch();
     SPLAT_TRY(check_launch("gs2d_bin_ranges"));
     if (bucket_to_tile) {
+        if (bucket_capacity > 0) {
+            k_bin_bucket_tail<<<static_cast<unsigned>(div_up(bucket_capacity, 256ll)), 256, 0, st>>>(
+                num_buckets, bucket_capacity, bucket_to_tile);
+            note_launch();
+            SPLAT_TRY(check_launch("gs2d_bin_bucket_tail"));
+        }
         k_bin_bucket_tiles<<<div_up(T, 256), 256, 0, st>>>(f.nb, f.bstart, T, bucket_to_tile);
         note_launch();
         SPLAT_TRY(check_launch("gs2d_bin_bucket_tiles"));
     }
     return SPLAT_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int gs2d_bin_fill(const int32_t* rect, int n, int H, int W, long long m, void* count_ws, size_t count_ws_bytes,
+                  void* fill_ws, size_t fill_ws_bytes, int32_t* point_list, int32_t* ranges, int32_t* bucket_offsets,
+                  int32_t* bucket_to_tile, uint32_t* num_buckets, void* stream) {
+    SPLAT_REQUIRE(n >= 0 && m >= 0 && H > 0 && W > 0, "gs2d_bin_fill: bad sizes");
+    SPLAT_REQUIRE(m < (1ll << 31), "gs2d_bin_fill: %lld instances exceed int32 indexing", m);
+    SPLAT_REQUIRE(fill_ws_bytes >= gs2d_bin_fill_workspace_size(m, H, W), "gs2d_bin_fill: workspace too small");
+    return bin_fill(rect, n, H, W, m, nullptr, count_ws, count_ws_bytes, fill_ws, fill_ws_bytes, point_list, ranges,
+                    bucket_offsets, bucket_to_tile, num_buckets, 0, nullptr, as_stream(stream));
+}
+
+int gs2d_bin_fill_bounded(const int32_t* rect, int n, int H, int W, long long instance_capacity,
+                          const uint32_t* num_instances, void* count_ws, size_t count_ws_bytes, void* fill_ws,
+                          size_t fill_ws_bytes, int32_t* point_list, int32_t* ranges, int32_t* bucket_offsets,
+                          int32_t* bucket_to_tile, long long bucket_capacity, uint32_t* num_buckets,
+                          uint32_t* overflow, void* stream) {
+    const long long T = static_cast<long long>((W + kTile - 1) / kTile) * ((H + kTile - 1) / kTile);
+    SPLAT_REQUIRE(n >= 0 && instance_capacity >= 0 && H > 0 && W > 0, "gs2d_bin_fill_bounded: bad sizes");
+    SPLAT_REQUIRE(instance_capacity < (1ll << 31), "gs2d_bin_fill_bounded: capacity %lld exceeds int32 indexing",
+                  instance_capacity);
+    SPLAT_REQUIRE(num_instances && num_buckets && overflow && bucket_to_tile,
+                  "gs2d_bin_fill_bounded: null count, bucket table or overflow word");
+    SPLAT_REQUIRE(bucket_capacity >= instance_capacity / kBucket + T,
+                  "gs2d_bin_fill_bounded: bucket capacity %lld below the bound %lld", bucket_capacity,
+                  instance_capacity / kBucket + T);
+    SPLAT_REQUIRE(fill_ws_bytes >= gs2d_bin_fill_workspace_size(instance_capacity, H, W),
+                  "gs2d_bin_fill_bounded: workspace too small");
+    return bin_fill(rect, n, H, W, instance_capacity, num_instances, count_ws, count_ws_bytes, fill_ws,
+                    fill_ws_bytes, point_list, ranges, bucket_offsets, bucket_to_tile, num_buckets, bucket_capacity,
+                    overflow, as_stream(stream));
 }
 
 int gs2d_forward(const float* means, const float* conic, const float* color, const float* opacity, const float* bg,

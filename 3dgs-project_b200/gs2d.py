@@ -40,6 +40,15 @@ class Bins:
     bucket_offsets: torch.Tensor  # (T,) int32 first bucket of each tile
     bucket_to_tile: torch.Tensor  # (B,) int32 tile of each bucket
     num_buckets: int
+    # bounded binning (bin_gaussians with a capacity): int32 [1] on the device, 1 if the instances exceeded the
+    # capacity (the list is then empty); None for exact binning
+    overflow: torch.Tensor | None = None
+
+    def check(self) -> None:
+        """Bounded binning: raise if the instances exceeded the capacity (one host read; exact binning: no-op)."""
+        if self.overflow is not None and int(self.overflow.item()):
+            raise RuntimeError("bin_gaussians: the (tile, Gaussian) instances exceeded the capacity; the tile lists "
+                               "were left empty - bin again with a larger capacity")
 
     def to(self, device):
         kw = {k: (v.to(device) if torch.is_tensor(v) else v) for k, v in self.__dict__.items()}
@@ -91,11 +100,18 @@ def radii_from_cov(cov: torch.Tensor) -> torch.Tensor:
 
 
 @torch.no_grad()
-def bin_gaussians(means: torch.Tensor, radii: torch.Tensor, depth: torch.Tensor, H: int, W: int) -> Bins:
+def bin_gaussians(means: torch.Tensor, radii: torch.Tensor, depth: torch.Tensor, H: int, W: int,
+                  capacity: int | None = None) -> Bins:
     """Tile binning on the GPU; bit-identical to toy2d/gs2d/binning.py:35-88.
 
-    Two host reads, as in the reference: the instance count (to size point_list) and the bucket
-    count (to size the per-bucket state)."""
+    Exact (capacity None): two host reads, as in the reference - the instance count (to size point_list) and the
+    bucket count (to size the per-bucket state).
+    Bounded (capacity = the most (tile, Gaussian) instances to hold): no host read. The buffers are sized from the
+    capacity (point_list holds `capacity` entries, of which the tile ranges index the first M; bucket_to_tile and
+    num_buckets the bound capacity // 32 + tiles + 1, the buckets past the count naming tile -1), the counts stay on
+    the device, and the same tile lists and buckets result. If M exceeds the capacity the lists are left empty and
+    Bins.overflow is set (Bins.check() raises). Nothing in this path waits on the device, so a training step that
+    uses it can be captured in a CUDA graph."""
     L.check_cuda("means", means)
     dev = means.device
     n = int(means.shape[0])
@@ -114,6 +130,22 @@ def bin_gaussians(means: torch.Tensor, radii: torch.Tensor, depth: torch.Tensor,
     cws = L.workspace(L.query("gs2d_bin_count_workspace_size", n), dev)
     L.call("gs2d_bin_count", L.ptr(m), L.ptr(r), L.ptr(d), int(d.dtype == torch.float64), n, H, W, L.ptr(rect),
            L.ptr(order), L.ptr(counts), L.ptr(cws), cws.numel(), stream)
+    if capacity is not None:
+        cap = int(capacity)
+        if cap < 0 or cap >= 2 ** 31:
+            raise ValueError(f"capacity {cap} out of range")
+        cap_b = cap // BUCKET + T + 1
+        fws = L.workspace(L.query("gs2d_bin_fill_workspace_size", cap, H, W), dev)
+        point_list = torch.empty(max(cap, 1), dtype=torch.int32, device=dev)
+        ranges = torch.empty(T, 2, dtype=torch.int32, device=dev)
+        bucket_offsets = torch.empty(T, dtype=torch.int32, device=dev)
+        bucket_to_tile = torch.empty(cap_b, dtype=torch.int32, device=dev)
+        overflow = torch.zeros(1, dtype=torch.int32, device=dev)
+        L.call("gs2d_bin_fill_bounded", L.ptr(rect), n, H, W, cap, L.ptr(counts), L.ptr(cws), cws.numel(), L.ptr(fws),
+               fws.numel(), L.ptr(point_list), L.ptr(ranges), L.ptr(bucket_offsets), L.ptr(bucket_to_tile), cap_b,
+               L.ptr(counts[1:]), L.ptr(overflow), stream)
+        return Bins(H, W, tiles_x, tiles_y, rect, order, point_list[:cap] if cap else point_list[:0], ranges,
+                    bucket_offsets, bucket_to_tile, cap_b, overflow)
     M = int(counts[0].item())
     fws = L.workspace(L.query("gs2d_bin_fill_workspace_size", M, H, W), dev)
     point_list = torch.empty(M, dtype=torch.int32, device=dev)

@@ -128,3 +128,54 @@ def test_cpu_tensors_are_rejected():
         gs2d.ext().forward(torch.zeros(1, 2), torch.zeros(1, 3), torch.zeros(1, 3), torch.zeros(1),
                            torch.zeros(3), torch.zeros(1, 2, dtype=torch.int32), torch.zeros(0, dtype=torch.int32),
                            torch.zeros(1, dtype=torch.int32), 0, 16, 16, False)
+
+
+def _bins_bounded(g, dev, capacity):
+    return gs2d.bin_gaussians(torch.tensor(g["means"], dtype=torch.float32, device=dev),
+                              torch.tensor(g["radii"], device=dev), torch.tensor(g["depth"], device=dev),
+                              int(g["H"]), int(g["W"]), capacity=capacity)
+
+
+@pytest.mark.parametrize("scene", ALL)
+def test_bounded_binning_same_lists(scene, cuda):
+    """Bounded binning (no host read) gives the reference's lists: the first M entries of point_list, the same
+    ranges and bucket offsets, the reference's buckets followed by -1 up to the bound, and no overflow."""
+    g = golden(f"gs2d_{scene}")
+    M, B = len(g["point_list"]), int(g["num_buckets"])
+    b = _bins_bounded(g, cuda, capacity=M + 37)
+    for key in ("rect", "order", "ranges", "bucket_offsets"):
+        assert np.array_equal(getattr(b, key).cpu().numpy(), g[key]), key
+    assert np.array_equal(b.point_list.cpu().numpy()[:M], g["point_list"])
+    btt = b.bucket_to_tile.cpu().numpy()
+    assert b.num_buckets == btt.size >= B
+    assert np.array_equal(btt[:B], g["bucket_to_tile"]) and (btt[B:] == -1).all()
+    b.check()
+
+
+@pytest.mark.parametrize("scene", ["dense", "c1"])
+def test_bounded_binning_same_render_and_gradients(scene, cuda):
+    """The image and the gradients of a bounded binning equal the exact binning's (same lists; the extra buckets
+    name no tile); the splat backward's atomics allow 1e-6."""
+    g = golden(f"gs2d_{scene}")
+    res = []
+    for b in (_bins(g, cuda), _bins_bounded(g, cuda, capacity=2 * len(g["point_list"]))):
+        x, bg = _inputs(g, cuda)
+        out = gs2d.rasterize(*x, b, bg, backend="splat")
+        grads = torch.autograd.grad(out, x, torch.tensor(g["dout"], dtype=torch.float32, device=cuda))
+        res.append((out.detach(), grads))
+    assert torch.equal(res[0][0], res[1][0])
+    for name, a, c in zip(NAMES, res[0][1], res[1][1]):
+        assert O.rel_err(c.cpu().numpy(), a.cpu().numpy()) < 1e-6, name
+
+
+def test_bounded_binning_overflow_is_flagged(cuda):
+    """More instances than the capacity: the lists are left empty (background image, zero gradients), nothing is
+    written past the buffers, and Bins.check() raises."""
+    g = golden("gs2d_dense")
+    b = _bins_bounded(g, cuda, capacity=len(g["point_list"]) // 2)
+    assert b.ranges.cpu().numpy().tolist() == [[0, 0]] * b.ranges.shape[0]
+    x, bg = _inputs(g, cuda)
+    out = gs2d.rasterize(*x, b, bg, backend="splat")
+    assert torch.allclose(out, bg[:, None, None].expand_as(out))
+    with pytest.raises(RuntimeError, match="capacity"):
+        b.check()
