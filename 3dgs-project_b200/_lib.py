@@ -42,12 +42,15 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                ctypes.c_double, _P]),
     "adam_step_dp_fused": (_I, [_I, _I, _P, _P, _LL, _LL, _P, _P, _I, _P, _I, ctypes.c_double, ctypes.c_double,
                                 ctypes.c_double, _P]),
+    "adam_step_dp_compact": (_I, [_I, _I, _P, _P, _LL, _LL, _LL, _I, _I, _I, _P, _P, _P, _I, ctypes.c_double,
+                                  ctypes.c_double, ctypes.c_double, _P]),
     "splat_l1_ssim_forward": (_I, [_P, _P, _I, _I, _I, _I, ctypes.c_float, _I, _P, _P, _P, _SZ, _P]),
     "splat_l1_ssim_backward": (_I, [_P, _P, _I, _I, _I, _I, ctypes.c_float, _I, _P, _P, _P, _SZ, _P]),
     "splat_take_device_waits_async": (_I, [_P, _P]),
     "gs2d_bin_count_workspace_size": (_SZ, [_I]),
     "gs2d_bin_fill_workspace_size": (_SZ, [_LL, _I, _I]),
     "gs2d_bin_count": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _SZ, _P]),
+    "gs2d_bin_fill_bounded": (_I, [_P, _I, _I, _I, _LL, _P, _P, _SZ, _P, _SZ, _P, _P, _P, _P, _LL, _P, _P, _P]),
     "gs2d_bin_fill": (_I, [_P, _I, _I, _I, _LL, _P, _SZ, _P, _SZ, _P, _P, _P, _P, _P, _P]),
     "gs2d_forward": (_I, [_P] * 8 + [_I, _LL, _I, _I, _I, _I] + [_P] * 5),
     "gs2d_backward_pixel": (_I, [_P] * 7 + [_I, _LL, _I, _I] + [_P] * 8),
@@ -76,6 +79,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gs3d_backward_blend": (_I, [_P, _P, _I, _LL, _P] + [_P, _SZ] * 4 + [_LL, _P, _SZ, _I, _P]),
     "gs3d_backward_preprocess": (_I, [_P] * 5 + [_I, _P, _P, _SZ, _P, _SZ] + [_P] * 7 + [_I, _P]),
     "gs3d_backward_preprocess_accumulate": (_I, [_P] * 5 + [_I, _P, _P, _SZ, _P, _SZ] + [_P] * 7 + [_I, _P]),
+    "gs3d_backward_preprocess_records": (_I, [_P] * 5 + [_I, _P, _P, _SZ, _P, _SZ] + [_P] * 5 + [_I, _P, _I, _P]),
     "gs3d_backward_densification": (_I, [_I, _P, _P, _SZ, _P, _SZ, _P, _I, _P]),
     "gs3d_backward_preprocess_adam": (_I, [_P] * 6 + [_I, _P, _P, _SZ, _P, _SZ, _P, _P]),
     "adam_step_multi": (_I, [_I, _P, _I, ctypes.c_double, ctypes.c_double, ctypes.c_double, _P]),

@@ -245,6 +245,10 @@ struct Grads {
     float* ptr[6];
     int vec;         // the SH-rest output 16-byte aligned
     int accumulate;  // add into the outputs instead of storing (the gradients of several views of one batch)
+    // When set, the SH gradients are not formed: per Gaussian, six floats (dL/dcolour masked by the colour clamp,
+    // then the unit view direction) are stored here instead, zeros for a Gaussian the view does not see; ptr[4]
+    // and ptr[5] are unused. Always stored, also with accumulate (each view has its own records).
+    float* records;
 };
 
 __device__ __forceinline__ void sh_backward(float x, float y, float z, int bases, const float* v, float& gx, float& gy,
@@ -462,6 +466,7 @@ __global__ void __launch_bounds__(kPbThreads, SPLAT_PB_MIN_BLOCKS) k_preprocess_
     const int nfl = cnt * rest3;
     // one gradient element of group gi: stored, or staged for the warp's Adam phase
     auto emit = [&](int gi, size_t e, float g) {
+        if (gi == 4 && out.records) return;  // the records carry the SH gradients
         if (A.fused)
             sg[small_offset(gi) + static_cast<int>(e - static_cast<size_t>(group_width(gi, rest3)) * first)] = g;
         else if (out.accumulate)
@@ -510,10 +515,20 @@ __global__ void __launch_bounds__(kPbThreads, SPLAT_PB_MIN_BLOCKS) k_preprocess_
         const float inv_len = rsqrtf(ux * ux + uy * uy + uz * uz);
         const float dx = ux * inv_len, dy = uy * inv_len, dz = uz * inv_len;
         float bas[16];
-        sh_basis(dx, dy, dz, cam.active_sh_bases, bas);
-        emit(4, 3 * i, bas[0] * gr);
-        emit(4, 3 * i + 1, bas[0] * gg);
-        emit(4, 3 * i + 2, bas[0] * gb);
+        sh_basis_rn(dx, dy, dz, cam.active_sh_bases, bas);
+        // each product rounded on its own, as the compact exchange forms it from the records
+        emit(4, 3 * i, __fmul_rn(bas[0], gr));
+        emit(4, 3 * i + 1, __fmul_rn(bas[0], gg));
+        emit(4, 3 * i + 2, __fmul_rn(bas[0], gb));
+        if (out.records) {
+            float* rec = out.records + 6 * static_cast<size_t>(i);
+            rec[0] = gr;
+            rec[1] = gg;
+            rec[2] = gb;
+            rec[3] = dx;
+            rec[4] = dy;
+            rec[5] = dz;
+        }
         float v[16];
         v[0] = 0.f;
         const int nb = min(cam.active_sh_bases, cam.rest_bases + 1);
@@ -523,9 +538,9 @@ __global__ void __launch_bounds__(kPbThreads, SPLAT_PB_MIN_BLOCKS) k_preprocess_
             if (k < nb) {
                 const float cr = my_sh[3 * (k - 1)], cg = my_sh[3 * (k - 1) + 1], cb = my_sh[3 * (k - 1) + 2];
                 v[k] = gr * cr + gg * cg + gb * cb;
-                my_sh[3 * (k - 1)] = bas[k] * gr;
-                my_sh[3 * (k - 1) + 1] = bas[k] * gg;
-                my_sh[3 * (k - 1) + 2] = bas[k] * gb;
+                my_sh[3 * (k - 1)] = __fmul_rn(bas[k], gr);
+                my_sh[3 * (k - 1) + 1] = __fmul_rn(bas[k], gg);
+                my_sh[3 * (k - 1) + 2] = __fmul_rn(bas[k], gb);
             }
         }
         for (int k = max(nb, 1); k <= cam.rest_bases; ++k) {
@@ -704,6 +719,11 @@ __global__ void __launch_bounds__(kPbThreads, SPLAT_PB_MIN_BLOCKS) k_preprocess_
             for (int k = 0; k < 4; ++k) emit(2, 4 * i + k, 0.f);
             emit(3, i, 0.f);
         }
+        if (out.records) {  // not seen by this view: its records are zeros
+            float* rec = out.records + 6 * static_cast<size_t>(i);
+#pragma unroll
+            for (int k = 0; k < 6; ++k) rec[k] = 0.f;
+        }
         // this Gaussian's row of the warp's staged block still holds its SH coefficients: its gradients are zeros
         if (rest3 > 0 && any_vis && cam.active_sh_bases > 1)
             for (int k = 0; k < rest3; ++k) my_sh[k] = 0.f;
@@ -714,6 +734,7 @@ __global__ void __launch_bounds__(kPbThreads, SPLAT_PB_MIN_BLOCKS) k_preprocess_
         warp_adam(A, first, cnt, rest3, sh, sh_staged, sg, lane);
         return;
     }
+    if (out.records) return;  // no SH-rest gradients are formed
     // the warp's SH-rest gradients as one contiguous block
     if (rest3 > 0 && out.accumulate) {
         if (!sh_staged) return;  // all zeros
@@ -812,7 +833,8 @@ int preprocess_backward(const float* means, const float* scales, const float* ro
                         const float* sh_rest, int n, const gs3d_settings* settings, void* prim_buf, size_t prim_bytes_,
                         void* workspace, size_t workspace_bytes, float* grad_means, float* grad_scales,
                         float* grad_rotations, float* grad_opacities, float* grad_sh0, float* grad_sh_rest,
-                        float* densification_info, int densification_rows, int accumulate, void* stream) {
+                        float* densification_info, int densification_rows, int accumulate, void* stream,
+                        float* records = nullptr) {
     Cam cam;
     SPLAT_TRY(fill_cam(settings, cam));
     SPLAT_REQUIRE(n >= 0, "gs3d_backward: bad size n=%d", n);
@@ -826,9 +848,11 @@ int preprocess_backward(const float* means, const float* scales, const float* ro
     PrimBuffers pb = carve_prim(cp, n);
     GradAcc acc = carve_grad(cw, n);
     PParams P{means, scales, rotations, opacities, sh_rest, settings->w2c, settings->cam_position, n};
-    Grads g{{grad_means, grad_scales, grad_rotations, grad_opacities, grad_sh0, grad_sh_rest}, 0, accumulate};
+    Grads g{{grad_means, grad_scales, grad_rotations, grad_opacities, grad_sh0, grad_sh_rest}, 0, accumulate,
+            records};
     for (int gi = 0; gi < 6; ++gi)
-        SPLAT_REQUIRE(g.ptr[gi] || (gi == 5 && cam.rest_bases == 0), "gs3d_backward: gradient output %d is null", gi);
+        SPLAT_REQUIRE(g.ptr[gi] || (gi >= 4 && records) || (gi == 5 && cam.rest_bases == 0),
+                      "gs3d_backward: gradient output %d is null", gi);
     g.vec = (reinterpret_cast<uintptr_t>(grad_sh_rest) & 15u) == 0;
     const size_t smem = static_cast<size_t>(kPbWarps) * 32 * cam.rest_bases * 3 * sizeof(float);
     const Densification dens{densification_info, densification_rows};
@@ -861,6 +885,20 @@ int gs3d_backward_preprocess_accumulate(const float* means, const float* scales,
     return preprocess_backward(means, scales, rotations, opacities, sh_rest, n, settings, prim_buf, prim_bytes_,
                                workspace, workspace_bytes, grad_means, grad_scales, grad_rotations, grad_opacities,
                                grad_sh0, grad_sh_rest, densification_info, densification_rows, 1, stream);
+}
+
+int gs3d_backward_preprocess_records(const float* means, const float* scales, const float* rotations,
+                                     const float* opacities, const float* sh_rest, int n,
+                                     const gs3d_settings* settings, void* prim_buf, size_t prim_bytes_,
+                                     void* workspace, size_t workspace_bytes, float* grad_means, float* grad_scales,
+                                     float* grad_rotations, float* grad_opacities, float* sh_records,
+                                     int accumulate, float* densification_info, int densification_rows,
+                                     void* stream) {
+    SPLAT_REQUIRE(sh_records != nullptr, "gs3d_backward_preprocess_records: sh_records is null");
+    return preprocess_backward(means, scales, rotations, opacities, sh_rest, n, settings, prim_buf, prim_bytes_,
+                               workspace, workspace_bytes, grad_means, grad_scales, grad_rotations, grad_opacities,
+                               nullptr, nullptr, densification_info, densification_rows, accumulate ? 1 : 0, stream,
+                               sh_records);
 }
 
 int gs3d_backward_densification(int n, const gs3d_settings* settings, void* prim_buf, size_t prim_bytes_,

@@ -249,6 +249,38 @@ __device__ __forceinline__ void sh_basis(float x, float y, float z, int bases, f
     }
 }
 
+// sh_basis with every operation rounded on its own (no contraction into fused multiply-adds), so that the basis of
+// a direction has the same bits in every kernel that evaluates it: the preprocess backward forms the SH gradients
+// basis_k(d) * dL/dcolour from it, and the compact exchange (dp_adam.cu) forms the same products again from the
+// direction and the colour gradient that a rank sends in their place.
+__device__ __forceinline__ void sh_basis_rn(float x, float y, float z, int bases, float* b) {
+    b[0] = kSH0;
+    if (bases > 1) {
+        b[1] = __fmul_rn(-kSH1, y);
+        b[2] = __fmul_rn(kSH1, z);
+        b[3] = __fmul_rn(-kSH1, x);
+    }
+    if (bases > 4) {
+        const float xx = __fmul_rn(x, x), yy = __fmul_rn(y, y), zz = __fmul_rn(z, z);
+        b[4] = __fmul_rn(__fmul_rn(kSH2_0, x), y);
+        b[5] = __fmul_rn(__fmul_rn(kSH2_1, y), z);
+        b[6] = __fmul_rn(kSH2_2, __fsub_rn(__fsub_rn(__fmul_rn(2.f, zz), xx), yy));
+        b[7] = __fmul_rn(__fmul_rn(kSH2_3, x), z);
+        b[8] = __fmul_rn(kSH2_4, __fsub_rn(xx, yy));
+        if (bases > 9) {
+            const float t4 = __fsub_rn(__fsub_rn(__fmul_rn(4.f, zz), xx), yy);
+            b[9] = __fmul_rn(__fmul_rn(kSH3_0, y), __fsub_rn(__fmul_rn(3.f, xx), yy));
+            b[10] = __fmul_rn(__fmul_rn(__fmul_rn(kSH3_1, x), y), z);
+            b[11] = __fmul_rn(__fmul_rn(kSH3_2, y), t4);
+            b[12] = __fmul_rn(__fmul_rn(kSH3_3, z),
+                              __fsub_rn(__fsub_rn(__fmul_rn(2.f, zz), __fmul_rn(3.f, xx)), __fmul_rn(3.f, yy)));
+            b[13] = __fmul_rn(__fmul_rn(kSH3_4, x), t4);
+            b[14] = __fmul_rn(__fmul_rn(kSH3_5, z), __fsub_rn(xx, yy));
+            b[15] = __fmul_rn(__fmul_rn(kSH3_6, x), __fsub_rn(xx, __fmul_rn(3.f, yy)));
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------------------------
 // Blend evaluation shared by the forward and the backward, with explicit fused multiply-adds so both
 // kernels take the same alpha >= 1/255 decisions bit for bit. (a2, b2, c2) is the conic scaled by

@@ -268,6 +268,7 @@ class PeerAdam:
         self.t += 1
         stream = torch.cuda.current_stream(self.exp_avg.device).cuda_stream
         self._barrier()
+        ev = _kernel_events(self)
         if self.nvls:
             self._L.call("adam_step_dp_nvls", self.lo, self.hi, self.grad_buf.mc, self.param_buf.mc,
                          self._L.ptr(self.param_buf.tensor), self._L.ptr(self.exp_avg), self._L.ptr(self.exp_avg_sq),
@@ -278,6 +279,8 @@ class PeerAdam:
                          ctypes.addressof(self._pptr), self.lo, self.hi, self._L.ptr(self.exp_avg),
                          self._L.ptr(self.exp_avg_sq), len(self.segments), ctypes.addressof(self._seg), self.t,
                          float(self.betas[0]), float(self.betas[1]), float(self.eps), stream)
+        if ev:
+            ev[1].record()
         self._barrier()
 
     def close(self) -> None:
@@ -285,6 +288,17 @@ class PeerAdam:
         self.params = self.grads = []
         self.param_buf.close()
         self.grad_buf.close()
+
+
+def _kernel_events(ex):
+    """When ex.kernel_events is a list (a caller timing the exchange kernel apart from the barriers around it): a
+    pair of CUDA events, the first recorded now on the current stream, appended to it; else None."""
+    if not isinstance(getattr(ex, "kernel_events", None), list):
+        return None
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    ex.kernel_events.append((a, b))
+    return a, b
 
 
 class NcclAdam:
@@ -337,6 +351,7 @@ class NcclAdam:
             for v, g in zip(self.grads, grads):
                 v.copy_(g.reshape(v.shape))
         self.t += 1
+        ev = _kernel_events(self)
         dist.reduce_scatter_tensor(self.grad_slice, self.grad_flat, op=dist.ReduceOp.SUM, group=self.group)
         stream = torch.cuda.current_stream(self.exp_avg.device).cuda_stream
         self._L.call("adam_step_dp_fused", 1, 0, ctypes.addressof(self._gptr), ctypes.addressof(self._pptr), self.lo,
@@ -345,18 +360,157 @@ class NcclAdam:
                      stream)
         mine = self.param_flat[self.rank * self.chunk:(self.rank + 1) * self.chunk]
         dist.all_gather_into_tensor(self.param_flat, mine, group=self.group)
+        if ev:
+            ev[1].record()
 
     def close(self) -> None:
         torch.cuda.synchronize()
         self.params = self.grads = []
 
 
+def owned_gaussians(n: int, rank: int, world: int) -> tuple[int, int]:
+    """The Gaussians [lo, hi) of n whose parameters rank `rank` of `world` updates in the compact exchange: equal
+    chunks rounded up to a multiple of 4 Gaussians, the last ones possibly short or empty."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of {world}")
+    chunk = ((n + world - 1) // world + 3) // 4 * 4
+    lo = min(rank * chunk, n)
+    return lo, min(lo + chunk, n)
+
+
+def compact_layout(n: int, rest_bases: int, views: int) -> dict:
+    """Element offsets of the compact exchange's flat buffers for n Gaussians (adam_step_dp_compact): the parameter
+    vector (means, scales, rotations, opacities, sh0, sh_rest) and the gradient vector (the four non-SH groups,
+    then one block of six-float records per view)."""
+    p_off, off = {}, 0
+    for name, w in zip(GROUPS, widths(rest_bases)):
+        p_off[name] = (off, off + w * n)
+        off += w * n
+    g_off = {name: p_off[name] for name in GROUPS[:4]}
+    rec = [(11 * n + 6 * n * v, 11 * n + 6 * n * (v + 1)) for v in range(views)]
+    return {"params": p_off, "param_total": off, "grads": g_off, "records": rec, "grad_total": (11 + 6 * views) * n}
+
+
+class CompactPeerAdam:
+    """PeerAdam with compact SH gradients (adam_step_dp_compact). A view's SH gradients are the products
+    basis_k(view direction) x colour gradient, so each rank stores per view and Gaussian six floats (the colour
+    gradient and the direction: gs3d.PendingBackward.preprocess_records) in place of its 3 (rest_bases + 1) SH
+    gradients; the owner of a Gaussian forms every rank's products with the preprocess backward's rounding and
+    sums them (views in view order, ranks in rank order). The non-SH groups are summed as in PeerAdam. Per step a
+    rank's links carry (11 + 6 views) floats per Gaussian of gradients instead of 59, and the full parameter
+    vector. Rank r owns whole Gaussians (owned_gaussians) and updates all of their parameters.
+
+    `params`: the six parameter tensors as views of the peer-addressable parameter buffer; `grads`: the four
+    non-SH gradient tensors; `records[v]`: view v's record block (6n floats). Every step must write all `views`
+    record blocks (the first view stores its gradients, the others accumulate into `grads`): through
+    gs3d.backward(..., out=grads, records=records[v], accumulate=v > 0), or through autograd - while this object is
+    open, the backward of a diff_rasterize call on its six parameter tensors writes the next record block and the
+    non-SH gradients here and leaves the tensors' .grad untouched (the hook FusedAdam's fuse_backward uses)."""
+
+    def __init__(self, tensors, lrs, views: int, active_sh_bases: int, group=None, betas=(0.9, 0.999),
+                 eps: float = 1e-15):
+        from . import _lib as L
+
+        self._L = L
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise RuntimeError("CompactPeerAdam supports at most 8 ranks")
+        if views < 1:
+            raise ValueError("views must be >= 1")
+        tensors = list(tensors)
+        dev = tensors[0].device
+        self.n = n = tensors[0].shape[0]
+        self.rest = tensors[5].shape[1] if tensors[5].dim() == 3 else 0
+        self.views, self.active_sh_bases = int(views), int(active_sh_bases)
+        self.shapes = [tuple(t.shape) for t in tensors]
+        lay = compact_layout(n, self.rest, self.views)
+        self.param_buf = PeerFlat(lay["param_total"], group, dev)
+        self.grad_buf = PeerFlat(lay["grad_total"], group, dev)
+        self.params, self.grads = [], []
+        for name, t in zip(GROUPS, tensors):
+            a, b = lay["params"][name]
+            pv = self.param_buf.tensor[a:b].view(t.shape)
+            pv.copy_(t.detach())
+            self.params.append(pv)
+            if name in lay["grads"]:
+                a, b = lay["grads"][name]
+                self.grads.append(self.grad_buf.tensor[a:b].view(t.shape))
+        self.records = [self.grad_buf.tensor[a:b] for a, b in lay["records"]]
+        self.lo, self.hi = owned_gaussians(n, self.rank, self.world)
+        cpad = (self.hi - self.lo + 3) // 4 * 4
+        self.exp_avg = torch.zeros(max(sum(widths(self.rest)) * cpad, 1), dtype=torch.float32, device=dev)
+        self.exp_avg_sq = torch.zeros_like(self.exp_avg)
+        self.betas, self.eps, self.t = betas, eps, 0
+        self._lr = (ctypes.c_double * 6)(*[float(x) for x in lrs])
+        self._tiny = torch.zeros(1, dtype=torch.float32, device=dev)
+        self._gptr = (ctypes.c_void_p * 8)(*self.grad_buf.ptrs)
+        self._pptr = (ctypes.c_void_p * 8)(*self.param_buf.ptrs)
+        self._written = 0  # record blocks written through autograd this step
+        from . import gs3d
+
+        gs3d._Rasterize.fused_optimizer = self
+        dist.barrier(group=group)
+
+    # ---- the autograd hook of gs3d._Rasterize (the same one FusedAdam(fuse_backward=True) uses) ----
+    def _owns(self, six) -> bool:
+        return len(self.params) == 6 and all(t.data_ptr() == p.data_ptr() and t.shape == p.shape
+                                             for t, p in zip(six, self.params))
+
+    def _defer(self, pending, six) -> None:
+        if self._written >= self.views:
+            raise RuntimeError(f"more than {self.views} views rendered for one step of the compact exchange")
+        pending.preprocess_records(self.grads, self.records[self._written], accumulate=self._written > 0)
+        self._written += 1
+
+    def _barrier(self) -> None:
+        dist.all_reduce(self._tiny, group=self.group)
+
+    @torch.no_grad()
+    def step(self, grads=None) -> None:
+        """One step. `grads` (e.g. the leaves' .grad after an autograd backward): None, or per group a tensor to add
+        to the gradient of the four non-SH groups; SH gradients other than the records cannot be carried."""
+        if grads is not None:
+            grads = list(grads)
+            if any(g is not None for g in grads[4:]):
+                raise RuntimeError("the compact exchange carries SH gradients only as the views' records")
+            for v, g in zip(self.grads, grads[:4]):
+                if g is not None:
+                    v.add_(g.reshape(v.shape))
+        if 0 < self._written < self.views:
+            raise RuntimeError(f"{self._written} of {self.views} views rendered before the step")
+        self._written = 0
+        self.t += 1
+        stream = torch.cuda.current_stream(self.exp_avg.device).cuda_stream
+        self._barrier()
+        ev = _kernel_events(self)
+        self._L.call("adam_step_dp_compact", self.world, self.rank, ctypes.addressof(self._gptr),
+                     ctypes.addressof(self._pptr), self.n, self.lo, self.hi, self.views, self.active_sh_bases,
+                     self.rest, self._L.ptr(self.exp_avg), self._L.ptr(self.exp_avg_sq), ctypes.addressof(self._lr),
+                     self.t, float(self.betas[0]), float(self.betas[1]), float(self.eps), stream)
+        if ev:
+            ev[1].record()
+        self._barrier()
+
+    def close(self) -> None:
+        from . import gs3d
+
+        if gs3d._Rasterize.fused_optimizer is self:
+            gs3d._Rasterize.fused_optimizer = None
+        torch.cuda.synchronize()
+        self.params = self.grads = self.records = []
+        self.param_buf.close()
+        self.grad_buf.close()
+
+
 def exchange_for(world: int, form: str = "auto") -> str:
     """The exchange form a step of `world` ranks uses: "peer" (peer loads and stores, adam_step_dp_fused), "nvls"
-    (NVLink multicast, adam_step_dp_nvls) or "nccl" (NcclAdam). "auto" picks the form measured fastest at that
-    rank count on 8-GPU B200 nodes (AUTO_EXCHANGE), the multicast form from 4 ranks on otherwise."""
+    (NVLink multicast, adam_step_dp_nvls), "compact" (peer form with compact SH gradients, CompactPeerAdam) or
+    "nccl" (NcclAdam). "auto" picks the form measured fastest at that rank count on 8-GPU B200 nodes
+    (AUTO_EXCHANGE), the multicast form from 4 ranks on otherwise."""
     if form != "auto":
-        if form not in ("peer", "nvls", "nccl"):
+        if form not in ("peer", "nvls", "compact", "nccl"):
             raise ValueError(f"unknown exchange form {form!r}")
         return form
     return AUTO_EXCHANGE.get(world, "nvls" if world >= 4 else "peer")
@@ -366,9 +520,13 @@ def exchange_for(world: int, form: str = "auto") -> str:
 AUTO_EXCHANGE = {2: "peer", 4: "nvls", 8: "nvls"}
 
 
-def make_exchange(tensors, lrs, form: str = "auto", group=None, betas=(0.9, 0.999), eps: float = 1e-15):
-    """PeerAdam (peer or multicast form) or NcclAdam for the replicated parameter tensors, by exchange_for()."""
+def make_exchange(tensors, lrs, form: str = "auto", group=None, betas=(0.9, 0.999), eps: float = 1e-15,
+                  views: int = 1, active_sh_bases: int = 16):
+    """PeerAdam (peer or multicast form), CompactPeerAdam or NcclAdam for the replicated parameter tensors, by
+    exchange_for(). views / active_sh_bases: the compact form's views per rank and step, and SH bases."""
     kind = exchange_for(dist.get_world_size(group), form)
+    if kind == "compact":
+        return CompactPeerAdam(tensors, lrs, views, active_sh_bases, group=group, betas=betas, eps=eps)
     if kind == "nccl":
         return NcclAdam(tensors, lrs, group=group, betas=betas, eps=eps)
     return PeerAdam(tensors, lrs, group=group, betas=betas, eps=eps, nvls=(kind == "nvls"))

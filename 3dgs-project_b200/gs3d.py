@@ -184,7 +184,7 @@ def backward(densification_info, grad_image, image, means, scales, rotations, op
              tile_buf, inst_buf, bucket_buf, w2c, cam_position, bg_color, active_sh_bases, width, height, focal_x,
              focal_y, center_x, center_y, near_plane, far_plane, proper_antialiasing, n_instances, n_buckets,
              selector, *mode, out: tuple | None = None, stage_event: torch.cuda.Event | None = None,
-             accumulate: bool = False):
+             accumulate: bool = False, records: torch.Tensor | None = None):
     """Faster-GS `_C.backward` (the trailing blend-backward mode of the phase1 patch is accepted and ignored:
     there is one blend backward here). Returns (means, scales, rotations, opacities[N,1], sh0[N,1,3], sh_rest) and
     accumulates densification_info ([0 | 2 | 3, N]) in place: visible count, |dL/dmean2d| in normalised device
@@ -192,13 +192,19 @@ def backward(densification_info, grad_image, image, means, scales, rotations, op
     ``out`` may supply the six contiguous float32 result tensors (e.g. views of one flat gradient buffer);
     with ``accumulate`` the gradients are added into them (the views of one batch into one buffer).
     It runs as its two launches (gs3d_backward_blend, gs3d_backward_preprocess); ``stage_event``, if given, is
-    recorded on the stream between them."""
+    recorded on the stream between them. ``records`` (with ``out`` holding the four non-SH gradient tensors): the
+    compact exchange's form, PendingBackward.preprocess_records; returns None."""
     pending = backward_blend(densification_info, grad_image, image, means, scales, rotations, opacities, sh_rest,
                              prim_buf, tile_buf, inst_buf, bucket_buf, w2c, cam_position, bg_color, active_sh_bases,
                              width, height, focal_x, focal_y, center_x, center_y, near_plane, far_plane,
                              proper_antialiasing, n_instances, n_buckets, selector, defer_densification=True)
     if stage_event is not None:
         stage_event.record(torch.cuda.current_stream(means.device))
+    if records is not None:
+        if out is None:
+            raise RuntimeError("records need the four non-SH gradient tensors in out")
+        pending.preprocess_records(out, records, accumulate=accumulate)
+        return None
     return pending.preprocess(out=out, accumulate=accumulate)
 
 
@@ -236,6 +242,28 @@ class PendingBackward:
                self.stream)
         self.rows, self.dinfo = 0, None
         return grads
+
+    def preprocess_records(self, out4, records: torch.Tensor, accumulate: bool = False) -> None:
+        """The preprocess backward for the compact exchange (gs3d_backward_preprocess_records): the gradients of
+        means, scales, rotations and opacities into ``out4`` (stored, or added with ``accumulate``), and in place of
+        the SH gradients six floats per Gaussian into ``records`` (float32, 6n elements): the colour gradient where
+        the colour clamp passes it, then the unit view direction; zeros for Gaussians this view does not see."""
+        n = self.n
+        out4 = tuple(out4)
+        if len(out4) != 4:
+            raise RuntimeError("four gradient tensors (means, scales, rotations, opacities) expected")
+        for t, numel in zip(out4, (3 * n, 3 * n, 4 * n, n)):
+            L.check_cuda("out", t, torch.float32)
+            if t.numel() != numel:
+                raise RuntimeError("out tensors must match the parameter shapes")
+        L.check_cuda("records", records, torch.float32)
+        if records.numel() != 6 * n:
+            raise RuntimeError(f"records must hold 6 floats per Gaussian ({6 * n}), got {records.numel()}")
+        L.call("gs3d_backward_preprocess_records", L.ptr(self.means), L.ptr(self.scales), L.ptr(self.rotations),
+               L.ptr(self.opacities), L.ptr(self.sh_rest), n, ctypes.byref(self.s), L.ptr(self.prim),
+               self.prim.numel(), L.ptr(self.ws), self.ws.numel(), *map(L.ptr, out4), L.ptr(records),
+               int(bool(accumulate)), L.ptr(self.dinfo), self.rows, self.stream)
+        self.rows, self.dinfo = 0, None
 
     def preprocess_adam(self, params, exp_avg, exp_avg_sq, lrs, steps, betas=(0.9, 0.999), eps: float = 1e-15,
                         grad_in=None) -> None:

@@ -162,12 +162,10 @@ def setup_dist(n_gpus: int):
 
 def scene_for(workload: str, rank: int, world: int):
     if workload == "c3":
+        # Weak scaling: every rank trains on the configured view with its own upstream gradient (view_seed), so a
+        # GPU's work per step is the N = 1 step's and the scaling measures what the exchange costs. (Distinct views
+        # per rank, whose costs differ, are the C4 batch of the c4_strong_scaling object.)
         sc = scenes.gs3d_config("c3", seed=0)
-        if rank > 0:  # another seeded view at the same radius
-            g = torch.Generator().manual_seed(5000 + rank)
-            d = torch.randn(3, generator=g)
-            d = d / d.norm() * 12.0
-            sc["cameras"] = [scenes.camera(1920, 1080, tuple(d.tolist()))]
         return sc, sc["cameras"][:1]
     if workload == "c4":
         sc = scenes.gs3d_config("c4", seed=0)
@@ -182,7 +180,8 @@ def scene_for(workload: str, rank: int, world: int):
 class Trainer:
     """Replicated Gaussians, flat gradient buffer, Adam state; one training step (of one or several views) per call."""
 
-    def __init__(self, sc: dict, dev, world: int, fuse: bool = False, lean: bool = False, exchange: str = "auto"):
+    def __init__(self, sc: dict, dev, world: int, fuse: bool = False, lean: bool = False, exchange: str = "auto",
+                 views: int = 1):
         self.dev = dev
         self.world = world
         self.fuse = fuse and world == 1  # preprocess backward + Adam in one kernel (N > 1: the exchange kernel)
@@ -194,7 +193,8 @@ class Trainer:
         if world > 1:  # the gradient exchange and Adam: peer-memory kernel, NVLink multicast kernel or NCCL
             self.exchange = gs_dist.exchange_for(world, exchange)
             self.peer = gs_dist.make_exchange([sc[k].to(dev).contiguous() for k in NAMES], [LRS[k] for k in NAMES],
-                                              form=self.exchange, eps=1e-15)
+                                              form=self.exchange, eps=1e-15, views=views,
+                                              active_sh_bases=self.bases)
             self.params, self.grads = self.peer.params, self.peer.grads
         else:
             self.params = [sc[k].to(dev).contiguous() for k in NAMES]
@@ -209,7 +209,7 @@ class Trainer:
         self.n = self.params[0].shape[0]
         self.t = 0
         self.settings = {}
-        self.ev = {k: [] for k in ("fwd", "bwd", "comm", "adam", "blend_bwd")}
+        self.ev = {k: [] for k in ("fwd", "bwd", "comm", "xkernel", "adam", "blend_bwd")}
         self.last = None
 
     def _settings(self, cam: dict):
@@ -253,9 +253,10 @@ class Trainer:
                                        ("comm", []), ("adam", [(bs, be)])):
                         self.ev[key].append(pairs)
                 return insts
+            records = self.peer.records[k] if self.exchange == "compact" else None
             gs3d.backward(None, dout, image, self.params[0], self.params[1], self.params[2], self.params[3],
                           self.params[5], prim, tile, inst, bucket, *s, m, nb, sel, out=self.grads,
-                          stage_event=bs, accumulate=k > 0)
+                          stage_event=bs, accumulate=k > 0, records=records)
             if timed:
                 be.record()
             views.append((fs, fe, bs, be))
@@ -263,6 +264,7 @@ class Trainer:
         if timed:
             cs.record()
         if self.peer is not None:  # the exchange and Adam
+            self.peer.kernel_events = [] if timed else None  # the exchange kernel alone, without its barriers
             self.peer.step()
         else:
             groups = [(p, g, mm, vv, LRS[nm]) for p, g, mm, vv, nm in zip(self.params, self.grads, self.m, self.v,
@@ -278,6 +280,7 @@ class Trainer:
             self.ev["bwd"].append([(b, d) for _, b, _, d in views])
             self.ev["blend_bwd"].append([(b, c) for _, b, c, _ in views])
             self.ev["comm"].append([(cs, ce)] if self.peer is not None else [])
+            self.ev["xkernel"].append(list(self.peer.kernel_events) if self.peer is not None else [])
             self.ev["adam"].append([] if self.peer is not None else [(cs, ce)])
         return insts
 
@@ -373,7 +376,7 @@ def run_ours(args) -> None:
     dev = torch.device("cuda", local)
     sc, cams = scene_for(args.workload, rank, world)
     cam = cams[0]
-    tr = Trainer(sc, dev, world, fuse=args.fuse, lean=args.lean, exchange=args.exchange)
+    tr = Trainer(sc, dev, world, fuse=args.fuse, lean=args.lean, exchange=args.exchange, views=len(cams))
     # Each view's upstream gradient is the config's fixed random image with its sign alternating step to step: under
     # Adam a fixed gradient would move every parameter by about lr per step in one direction, and after a few hundred
     # steps the scene (visible Gaussians, instances, blend depth) would no longer be the configured one. Alternating
@@ -391,7 +394,7 @@ def run_ours(args) -> None:
     # end to end through the public API: pinned host upstream gradients in, loss out, every step
     e2e = run_e2e(sc, cams, dev, world, args, tr)
     roof = roofline(tr, stage, reach, cam["width"] * cam["height"])
-    exch = exchange_figures(tr, stage) if tr.peer is not None else None
+    exch = exchange_figures(tr, stage, world, dev) if tr.peer is not None else None
     tr.close()
     del tr
     torch.cuda.empty_cache()
@@ -437,7 +440,7 @@ def c4_strong(args, world: int, rank: int, local: int, dev) -> dict:
     The batch is fixed as N grows (strong scaling): views/s = 8 x steps / (max over ranks of the device time)."""
     sc = scenes.gs3d_config("c4", seed=0)
     cams = gs_dist.shard_views(sc["cameras"], rank, world)
-    tr = Trainer(sc, dev, world, exchange=args.exchange)
+    tr = Trainer(sc, dev, world, exchange=args.exchange, views=len(cams))
     hosts = [upstream_gradient(rank + k * world, c["height"], c["width"]) for k, c in enumerate(cams)]
     douts = ([h.to(dev) for h in hosts], [(-h).to(dev) for h in hosts])
     steps = max(args.steps // 4, 10)
@@ -471,7 +474,8 @@ def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
     peer = None
     start = [sc[k].to(dev).contiguous() for k in NAMES]  # the configured scene, as the device-timed run started
     if world > 1:  # the leaves are views of the exchange's parameter buffer; step() takes their .grad
-        peer = gs_dist.make_exchange(start, [LRS[nm] for nm in NAMES], form=tr.exchange, eps=1e-15)
+        peer = gs_dist.make_exchange(start, [LRS[nm] for nm in NAMES], form=tr.exchange, eps=1e-15, views=len(cams),
+                                     active_sh_bases=sc["active_sh_bases"])
         leaves = [p.requires_grad_(True) for p in peer.params]
     else:  # with fuse_backward the rasterizer's preprocess backward runs inside the optimizer's fused step
         leaves = [p.requires_grad_(True) for p in start]
@@ -633,7 +637,7 @@ def roofline(tr: Trainer, stage: dict, reach: dict, pixels: int) -> dict:
     return {"roofline": out}
 
 
-def exchange_figures(tr: Trainer, stage: dict) -> dict:
+def exchange_figures(tr: Trainer, stage: dict, world: int, dev) -> dict:
     """N > 1: the exchange + Adam of one step, against NVLink (measured 770 GB/s per direction).
 
     Peer form (adam_step_dp_fused between two barriers): each rank reads its slice's gradients from the other G - 1
@@ -643,20 +647,35 @@ def exchange_figures(tr: Trainer, stage: dict) -> dict:
     buffer (G slices) out and takes its reduced slice in; its multicast store sends one slice out and the switch
     delivers all G slices in: G + 1 slices in each direction.
     NCCL form (reduce-scatter, Adam on the slice, all-gather): a ring reduce-scatter and all-gather each move
-    G - 1 slices in each direction: 2 (G - 1), as the peer form."""
+    G - 1 slices in each direction: 2 (G - 1), as the peer form.
+    Compact form (adam_step_dp_compact between two barriers): a rank owns whole Gaussians; per owned Gaussian it
+    reads 11 + 6 V gradient floats (V views per rank) from each of the G - 1 other ranks and writes its 59 parameters
+    to each of them."""
     g = tr.world
     form = tr.exchange
-    slice_bytes = 4.0 * (tr.peer.hi - tr.peer.lo)
-    cross = (g + 1) * slice_bytes if form == "nvls" else 2 * (g - 1) * slice_bytes
-    kernel = {"nvls": "adam_step_dp_nvls (+ 2 barriers)", "peer": "adam_step_dp_fused (+ 2 barriers)",
+    if form == "compact":
+        owned = tr.peer.hi - tr.peer.lo
+        width = sum(gs_dist.widths(tr.peer.rest))
+        cross = (g - 1) * 4.0 * owned * (11 + 6 * tr.peer.views + width)
+        vector = 4.0 * tr.peer.n * width
+    else:
+        slice_bytes = 4.0 * (tr.peer.hi - tr.peer.lo)
+        cross = (g + 1) * slice_bytes if form == "nvls" else 2 * (g - 1) * slice_bytes
+        vector = 4.0 * tr.peer.total
+    kernel = {"nvls": "adam_step_dp_nvls", "peer": "adam_step_dp_fused", "compact": "adam_step_dp_compact",
               "nccl": "ncclReduceScatter + adam_step_dp_fused on the slice + ncclAllGather"}[form]
-    t = stage["comm"]
+    # the kernel alone (its barriers excluded) and the whole stage with the barriers, each the maximum over the
+    # ranks; the stage also holds a rank's wait for slower ranks at the first barrier
+    both = torch.tensor([stage["xkernel"], stage["comm"]], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(both, op=torch.distributed.ReduceOp.MAX)
+    t, t_stage = float(both[0]), float(both[1])
     ach = cross / (t / 1000.0) / 1e9 if t > 0 else 0.0
     # the same exchange measured as an all-reduce: bus bandwidth 2 (G - 1) / G x vector bytes / time, against the
     # measured 8-rank NCCL all-reduce bus bandwidth of this pool (725 GB/s at 1 GiB), which also carries no Adam step
-    vector = 4.0 * tr.peer.total
     bus = 2.0 * (g - 1) / g * vector / (t / 1000.0) / 1e9 if t > 0 else 0.0
-    return {"form": form, "kernel": kernel, "ms": round(t, 4), "bytes_each_direction": int(cross),
+    return {"form": form, "kernel": kernel, "ms": round(t, 4), "stage_ms_with_barriers": round(t_stage, 4),
+            "bytes_each_direction": int(cross),
             "achieved": round(ach, 1), "peak": 770.0, "unit": "GB/s", "frac": round(ach / 770.0, 4),
             "peak_source": "measured peer copy, per direction",
             "allreduce_bus_gbs": round(bus, 1), "allreduce_bus_frac_of_nccl": round(bus / 725.0, 4)}
@@ -793,37 +812,59 @@ def run_c1(args, ref: bool = False) -> None:
     sc, means, conic, color, opacity, radii, depth, target = c1_inputs(dev)
     H, W = sc["H"], sc["W"]
     leaves = [t.clone().requires_grad_(True) for t in (means, conic, color, opacity)]
-    tgt = target.reshape(3, H, W).to(dev)
+    # One exact binning at setup sizes the step's bounded binning (no host read per step) and gives M and B for the
+    # byte counts below. The parameters do not change between steps (the step has no optimizer), so M does not
+    # either; the capacity leaves 50% headroom and any overflow is checked after the timed steps.
+    exact = gs2d.bin_gaussians(means, radii, depth, H, W)
+    M, B, P = int(exact.point_list.numel()), int(exact.num_buckets), H * W
+    capacity = M + M // 2 + 1024
+    static_tgt = target.reshape(3, H, W).to(dev).contiguous()
     last = {}
 
-    def step(tg):
-        bins = gs2d.bin_gaussians(leaves[0].detach(), radii, depth, H, W)
+    def step():
+        bins = gs2d.bin_gaussians(leaves[0].detach(), radii, depth, H, W, capacity=capacity)
         last["bins"] = bins
         img = gs2d.rasterize(*leaves, bins, backend="splat")
-        loss = ((img - tg) ** 2).mean()
+        loss = ((img - static_tgt) ** 2).mean()
         for p in leaves:
             p.grad = None
         loss.backward()
         return loss
 
-    for _ in range(args.warmup):
-        step(tgt)
+    # warm-up on a side stream (as CUDA graph capture asks), then the step captured once as a CUDA graph: a step is
+    # one replay, with no host work or host read inside it
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(max(args.warmup, 3)):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(side)
     torch.cuda.synchronize()
-    timer = L.KernelTimer("gs2d_k_render", "gs2d_k_backward_splat")
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    graph = torch.cuda.CUDAGraph()
     launches0 = L.query("splat_launch_count")
+    with torch.cuda.graph(graph):
+        static_loss = step()
+    per_step_launches = L.query("splat_launch_count") - launches0
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(args.steps):
-        timer.arm()
-        step(tgt)
+        graph.replay()
     b.record()
     torch.cuda.synchronize()
-    timer.stop()
-    launches = L.query("splat_launch_count") - launches0
     ms = a.elapsed_time(b) / args.steps
+    launches = per_step_launches * args.steps
+    last["bins"].check()  # no step's instances exceeded the capacity
+    # the two kernels' device times, from eager steps (event pairs around each launch)
+    timer = L.KernelTimer("gs2d_k_render", "gs2d_k_backward_splat")
+    for _ in range(min(args.steps, 50)):
+        timer.arm()
+        step()
+    torch.cuda.synchronize()
+    timer.stop()
     kt = {k: float(statistics.median(v)) for k, v in timer.times().items()}
-    bins = last["bins"]
-    M, B, P = int(bins.point_list.numel()), int(bins.num_buckets), H * W
     # forward (saving bucket states): 40 B per list entry (id + 9 splat floats), 20 B per pixel (image, T, count),
     # 4 KB per bucket of (T, C) states; backward: the states, 28 B per pixel, 40 B per list entry
     fwd = hbm_roofline("gs2d k_render (forward, bucket states saved)", kt["gs2d_k_render"],
@@ -834,12 +875,15 @@ def run_c1(args, ref: bool = False) -> None:
     top, other = (fwd, bwd) if fwd["kernel_ms"] >= bwd["kernel_ms"] else (bwd, fwd)
     top["next_kernel"] = other
     top["step_share"] = round((fwd["kernel_ms"] + bwd["kernel_ms"]) / ms, 4)
+    # end to end: each step copies its target from pinned host memory into the graph's input and reads its loss back
     host = target.reshape(3, H, W).contiguous().pin_memory()
     losses = torch.empty(args.steps, dtype=torch.float32).pin_memory()
     a2, b2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a2.record()
     for k in range(args.steps):
-        losses[k:k + 1].copy_(step(host.to(dev, non_blocking=True)).detach().view(1), non_blocking=True)
+        static_tgt.copy_(host, non_blocking=True)
+        graph.replay()
+        losses[k:k + 1].copy_(static_loss.detach().view(1), non_blocking=True)
     b2.record()
     torch.cuda.synchronize()
     ms_e2e = a2.elapsed_time(b2) / args.steps
@@ -849,14 +893,18 @@ def run_c1(args, ref: bool = False) -> None:
             "data": "synthetic (seeded, config-shaped)", "config": C1_CONFIG,
             "e2e": {"value": round(1000.0 / ms_e2e, 2), "unit": "fits/s", "h2d_bytes_per_step": int(host.numel() * 4),
                     "d2h_bytes_per_step": 4},
-            "gpu_launches": launches, "roofline": top}
+            "gpu_launches": launches, "host_reads_per_step": 0,
+            "binning": {"mode": "bounded (no host read)", "capacity": capacity, "instances": M, "buckets": B},
+            "roofline": top}
+    graph.reset()
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = c1_cpu(sc, means, conic, color, opacity, radii, depth, target)
     print(json.dumps(line), flush=True)
 
 
 C1_CONFIG = {"workload": "c1: binning + forward + splat backward of 4096 2D Gaussians, 256x256, L2 loss",
-             "l2": "the whole working set fits in L2; steps run back to back"}
+             "l2": "the whole working set fits in L2; steps run back to back",
+             "step": "one CUDA graph replay: bounded binning (no host read), forward, loss, splat backward"}
 
 
 def c1_cpu(sc, means, conic, color, opacity, radii, depth, target) -> dict:
@@ -1277,7 +1325,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["c3", "c4", "c2", "c1", "c5", "gs2d", "splat2d", "blend-bwd", "ssim"],
                     default="c3")
-    ap.add_argument("--exchange", choices=["auto", "peer", "nvls", "nccl"], default="auto",
+    ap.add_argument("--exchange", choices=["auto", "peer", "nvls", "compact", "nccl"], default="auto",
                     help="N > 1: the gradient exchange + Adam form (auto: the fastest measured at that rank count)")
     ap.add_argument("--no-c4", action="store_true", help="skip the C4 strong-scaling object of the c3 line")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for the baseline sample")

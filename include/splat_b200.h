@@ -117,6 +117,19 @@ int gs2d_bin_fill(const int32_t* rect, int n, int H, int W, long long num_instan
                   size_t count_workspace_bytes, void* fill_workspace, size_t fill_workspace_bytes,
                   int32_t* point_list, int32_t* ranges, int32_t* bucket_offsets, int32_t* bucket_to_tile,
                   uint32_t* num_buckets, void* stream);
+/* Binning phase 2 without a host read of M (no counterpart in the reference, which reads M and the bucket count
+ * back to size its tensors): buffers sized from instance_capacity (point_list i32[instance_capacity], the fill
+ * workspace from gs2d_bin_fill_workspace_size(instance_capacity, H, W)); M is read on the device from
+ * *num_instances (gs2d_bin_count's output). bucket_to_tile holds bucket_capacity >= instance_capacity / 32 + T
+ * entries: the first *num_buckets name their tiles, the rest -1 (so gs2d_forward / gs2d_backward_splat may be
+ * given instance_capacity and bucket_capacity as the instance and bucket counts). The lists are those of
+ * gs2d_bin_fill. If M > instance_capacity the lists are left empty and *overflow (device u32) is set to 1; the
+ * library never clears it. */
+int gs2d_bin_fill_bounded(const int32_t* rect, int n, int H, int W, long long instance_capacity,
+                          const uint32_t* num_instances, void* count_workspace, size_t count_workspace_bytes,
+                          void* fill_workspace, size_t fill_workspace_bytes, int32_t* point_list, int32_t* ranges,
+                          int32_t* bucket_offsets, int32_t* bucket_to_tile, long long bucket_capacity,
+                          uint32_t* num_buckets, uint32_t* overflow, void* stream);
 /* rasterize.cu:366-394 `forward`: out f32[3,H,W], final_T f32[H,W], n_contrib i32[H,W],
  * bucket_state f32[num_buckets,256,4] = (T, C) when save_buckets (untouched entries keep the caller's
  * zero fill, as in the reference). */
@@ -278,6 +291,18 @@ int gs3d_backward_preprocess_accumulate(const float* means, const float* scales,
                                         float* grad_scales, float* grad_rotations, float* grad_opacities,
                                         float* grad_sh0, float* grad_sh_rest, float* densification_info,
                                         int densification_rows, void* stream);
+/* gs3d_backward_preprocess for the compact exchange (adam_step_dp_compact): the four non-SH gradients as
+ * gs3d_backward_preprocess (accumulate = 0) or gs3d_backward_preprocess_accumulate (accumulate = 1) writes them,
+ * and in place of the SH gradients six floats per Gaussian in sh_records (device f32[6n]): dL/dcolour where the
+ * colour clamp passes it (0 elsewhere), then the unit view direction; zeros for a Gaussian this view does not see.
+ * The records are always stored (each view of a batch has its own). */
+int gs3d_backward_preprocess_records(const float* means, const float* scales, const float* rotations,
+                                     const float* opacities, const float* sh_rest, int n,
+                                     const gs3d_settings* settings, void* prim_buf, size_t prim_bytes,
+                                     void* workspace, size_t workspace_bytes, float* grad_means, float* grad_scales,
+                                     float* grad_rotations, float* grad_opacities, float* sh_records,
+                                     int accumulate, float* densification_info, int densification_rows,
+                                     void* stream);
 /* The densification rows of gs3d_backward_preprocess alone, from the blend backward's workspace (the same
  * arithmetic, so the rows equal those gs3d_backward_preprocess accumulates). For callers that defer the
  * preprocess backward to gs3d_backward_preprocess_adam but read the statistics before the optimizer step. */
@@ -383,6 +408,24 @@ int adam_step_dp_fused(int world, int rank, const float* const* grads, float* co
 int adam_step_dp_nvls(long long lo, long long hi, const float* grads_mc, float* params_mc, const float* params_local,
                       float* exp_avg, float* exp_avg_sq, int segment_count, const dp_adam_segment* segments, int step,
                       double beta1, double beta2, double eps, void* stream);
+
+/* The step with compact SH gradients (no counterpart in the reference, which has no multi-GPU path): per view
+ * and Gaussian a rank sends the six floats that gs3d_backward_preprocess_records stores (the colour gradient
+ * and the view direction) instead of its 3 (rest_bases + 1) SH gradients, and the owner forms the products
+ * basis_k(direction) * colour gradient itself, with the preprocess backward's rounding, summing a rank's views in
+ * view order and the ranks in rank order: the same gradients, so the same update, as gs3d_backward_preprocess(_
+ * accumulate) followed by adam_step_dp_fused, apart from the sign of zero sums (which Adam does not see).
+ * Rank `rank` owns the Gaussians [lo, hi) of n (lo a multiple of 4 unless empty) and updates all their
+ * parameters. Per rank k (as this GPU addresses it):
+ *   params[k]: means 3n | scales 3n | rotations 4n | opacities n | sh0 3n | sh_rest 3 rest_bases n floats
+ *   grads[k]:  means 3n | scales 3n | rotations 4n | opacities n | views x (6n floats of records)
+ * exp_avg / exp_avg_sq: the owned Gaussians' moments in the parameter layout, with c = hi - lo rounded up to a
+ * multiple of 4 in place of n. lr: six learning rates (means, scales, rotations, opacities, sh0, sh_rest); bias
+ * corrections as in adam_step_multi. Same ordering requirements as adam_step_dp_fused. */
+int adam_step_dp_compact(int world, int rank, const float* const* grads, float* const* params, long long n,
+                         long long lo, long long hi, int views, int active_sh_bases, int rest_bases, float* exp_avg,
+                         float* exp_avg_sq, const double* lr, int step, double beta1, double beta2, double eps,
+                         void* stream);
 
 /* ---------------------------------------------------------------------------------------------
  * Fused L1 + SSIM loss (the training loss around the rasterizer; replaces the external fused-ssim call of the

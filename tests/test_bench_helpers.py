@@ -22,13 +22,26 @@ def test_exchange_bytes_per_direction(world, form, slices):
     total = 8_000_000
     chunk = total // world
     tr = _trainer(world, 0, chunk, total, form)
-    out = bench.exchange_figures(tr, {"comm": 1.0})
-    assert out["form"] == form
+    out = bench.exchange_figures(tr, {"xkernel": 1.0, "comm": 1.25}, 1, "cpu")
+    assert out["form"] == form and out["ms"] == 1.0 and out["stage_ms_with_barriers"] == 1.25
     assert out["bytes_each_direction"] == slices * 4 * chunk
     assert out["achieved"] == pytest.approx(slices * 4 * chunk / 1e-3 / 1e9, rel=1e-6)
     assert out["frac"] == pytest.approx(out["achieved"] / 770.0, abs=1e-4)
     # as an all-reduce of the whole vector: 2 (G - 1) / G of it over the time
     assert out["allreduce_bus_gbs"] == pytest.approx(2.0 * (world - 1) / world * 4 * total / 1e-3 / 1e9, rel=1e-3)
+
+
+@pytest.mark.parametrize("world,views", [(2, 1), (4, 2), (8, 1)])
+def test_compact_exchange_bytes_per_direction(world, views):
+    """Per owned Gaussian the compact form reads 11 + 6 V gradient floats from each other rank and writes its 59
+    parameters to each of them."""
+    n = 1_000_000
+    owned = n // world
+    peer = types.SimpleNamespace(lo=0, hi=owned, n=n, rest=15, views=views)
+    tr = types.SimpleNamespace(world=world, peer=peer, exchange="compact")
+    out = bench.exchange_figures(tr, {"xkernel": 1.0, "comm": 1.0}, 1, "cpu")
+    assert out["bytes_each_direction"] == (world - 1) * 4 * owned * (11 + 6 * views + 59)
+    assert out["allreduce_bus_gbs"] == pytest.approx(2.0 * (world - 1) / world * 4 * 59 * n / 1e-3 / 1e9, rel=1e-3)
 
 
 def _clocks(rows, t0, t1):

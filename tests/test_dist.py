@@ -127,6 +127,23 @@ def test_owned_slices_tile_the_vector():
         gdist.owned_slice(10, 2, 2)
 
 
+def test_owned_gaussians_and_compact_layout():
+    """The compact exchange's ownership is by whole Gaussians (starts at multiples of 4) and its buffers hold the
+    parameter groups in the reference's order and one 6n-float record block per view after the non-SH gradients."""
+    for n in (0, 1, 5, 17, 4096, 3_000_001):
+        for world in (1, 2, 3, 8):
+            spans = [gdist.owned_gaussians(n, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(b == c for (_, b), (c, _) in zip(spans, spans[1:]))
+            assert all(lo <= hi and (lo % 4 == 0 or lo == hi) for lo, hi in spans)
+    lay = gdist.compact_layout(10, 15, 3)
+    assert lay["params"]["means"] == (0, 30) and lay["params"]["sh0"] == (110, 140)
+    assert lay["params"]["sh_rest"] == (140, 590) and lay["param_total"] == 590
+    assert lay["grads"] == {"means": (0, 30), "scales": (30, 60), "rotations": (60, 100), "opacities": (100, 110)}
+    assert lay["records"] == [(110, 170), (170, 230), (230, 290)] and lay["grad_total"] == 290
+    assert gdist.exchange_for(2, "compact") == "compact"
+
+
 class _FakeMulticast:
     """Stands in for MulticastFlat on the host: allocation in the constructor, then a bind() that runs one
     collective per buffer (as the rendezvous does) and yields a multicast address, or none; a record of how it was

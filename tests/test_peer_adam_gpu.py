@@ -83,3 +83,82 @@ def test_exchange_matches_allreduce_adam(form):
             pytest.skip("this node has no NVLink multicast")
         assert err is None, f"rank {rank}: {err}"
         assert ok_p and ok_m, f"rank {rank}: params equal {ok_p}, moments equal {ok_m}"
+
+
+def _compact_worker(rank: int, world: int, port: int, q, n: int, views: int) -> None:
+    """Each view's blend backward runs once; its preprocess backward runs twice from the same sums, into PeerAdam's
+    six gradient tensors and into CompactPeerAdam's four non-SH tensors and records (the preprocess backward is
+    deterministic; the blend backward's atomics are not, so two blend backwards would not give the same bits)."""
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=dev)
+        import math
+        import sys
+        sys.path.insert(0, os.getcwd())
+        import __graft_entry__ as ge
+        ge.load_package()
+        from gs_b200 import dist as D
+        from gs_b200 import gs3d, scenes
+
+        sc = scenes.gaussians_3d(n, 7, sigma=1.0)
+        names = ("means", "scales", "rotations", "opacities", "sh0", "sh_rest")
+        cams = [scenes.camera(256, 192, (6 * math.cos(2 * math.pi * k / (world * views)), 0.5,
+                                         6 * math.sin(2 * math.pi * k / (world * views))))
+                for k in range(world * views)]
+        mine = D.shard_views(cams, rank, world)
+        tensors = [sc[k].to(dev).contiguous() for k in names]
+        lrs = [1.6e-4, 5e-3, 1e-3, 5e-2, 2.5e-3, 2.5e-3]
+        full = D.PeerAdam(tensors, lrs, nvls=False)
+        compact = D.CompactPeerAdam(tensors, lrs, views=len(mine), active_sh_bases=16)
+        g = torch.Generator(device=dev).manual_seed(50 + rank)
+        same, seen_zero = [], 0
+        for step in range(3):
+            for k, cam in enumerate(mine):
+                s = scenes.settings_tuple(cam, 16, dev)
+                p = full.params
+                img, prim, tile, inst, bucket, m, nb, sel = gs3d.forward(*p, *s)
+                seen_zero += int((gs3d.n_touched_tiles(prim, n) == 0).sum())
+                dout = torch.randn(img.shape, device=dev, generator=g) * 1e-2
+                pend = gs3d.backward_blend(None, dout, img, p[0], p[1], p[2], p[3], p[5], prim, tile, inst, bucket,
+                                           *s, m, nb, sel, defer_densification=True)
+                pend.preprocess(out=full.grads, accumulate=k > 0)
+                pend.preprocess_records(compact.grads, compact.records[k], accumulate=k > 0)
+            full.step()
+            compact.step()
+            torch.cuda.synchronize()
+            same.append(all(torch.equal(a, b) for a, b in zip(full.params, compact.params)))
+        moved = not torch.equal(full.params[5], tensors[5])
+        full.close()
+        compact.close()
+        q.put((rank, all(same), moved and seen_zero > 0, None))
+        dist.destroy_process_group()
+    except Exception as exc:  # report instead of hanging the parent
+        q.put((rank, False, False, repr(exc)))
+
+
+@pytest.mark.parametrize("n, views", [(20_000, 2), (20_003, 1)])
+def test_compact_exchange_matches_peer(n, views):
+    """CompactPeerAdam (SH gradients sent as colour-gradient / direction records) gives bit-identical parameters to
+    PeerAdam over three steps: with two views per rank (the records of a rank summed in view order) and 16-byte
+    accesses, and with one view per rank and an odd Gaussian count (element-wise accesses)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29600 + os.getpid() % 300 + 20 + views
+    procs = [ctx.Process(target=_compact_worker, args=(r, 2, port, q, n, views)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    for rank, same, exercised, err in res:
+        assert err is None, f"rank {rank}: {err}"
+        assert exercised, f"rank {rank}: the SH parameters did not move or every Gaussian was seen"
+        assert same, f"rank {rank}: compact and full exchanges differ"
