@@ -208,9 +208,9 @@ class PeerAdam:
     nvls: use NVLink SHARP when the node has it (the buffers come from PyTorch's symmetric memory, the kernel sums
     through multimem.ld_reduce and writes through multimem.st). Per rank and direction its links then carry
     (G + 1) / G slices-worth of the vector against 2 (G - 1) / G for peer loads and stores: more at G = 2 (1.5 vs
-    1), fewer from G = 4 on (1.25 vs 1.5; 1.125 vs 1.75 at G = 8). Measured on the 3M-Gaussian C3 scene: at G = 2
-    1.84 ms multicast against 1.17 ms peer; at G = 4 1.73 ms multicast (513 GB/s per direction) against 1.84 ms
-    peer (577 GB/s). Without an explicit `nvls`, the form exchange_for() picks for the rank count is taken.
+    1), fewer from G = 4 on (1.25 vs 1.5; 1.125 vs 1.75 at G = 8). Measured on the 3M-Gaussian C3 state (the kernel
+    alone, maximum over the ranks): at G = 2 1.86 ms multicast against 1.07 ms peer; at G = 4 1.69 ms multicast
+    against 1.66 ms peer. Without an explicit `nvls`, the form exchange_for() picks for the rank count is taken.
     """
 
     def __init__(self, tensors, lrs, group=None, betas=(0.9, 0.999), eps: float = 1e-15, nvls: bool | None = None):
@@ -227,7 +227,7 @@ class PeerAdam:
         sizes = [t.numel() for t in tensors]
         self.total = sum(sizes)
         if nvls is None:
-            nvls = exchange_for(self.world) == "nvls"
+            nvls = exchange_for(self.world) == "nvls"  # the six-tensor forms' choice
         self.nvls = False
         if nvls and self.world > 1:
             padded = (self.total + 3) // 4 * 4  # the multicast kernel moves whole 16-byte groups
@@ -504,27 +504,34 @@ class CompactPeerAdam:
         self.grad_buf.close()
 
 
-def exchange_for(world: int, form: str = "auto") -> str:
+def exchange_for(world: int, form: str = "auto", records: bool = False) -> str:
     """The exchange form a step of `world` ranks uses: "peer" (peer loads and stores, adam_step_dp_fused), "nvls"
     (NVLink multicast, adam_step_dp_nvls), "compact" (peer form with compact SH gradients, CompactPeerAdam) or
-    "nccl" (NcclAdam). "auto" picks the form measured fastest at that rank count on 8-GPU B200 nodes
-    (AUTO_EXCHANGE), the multicast form from 4 ranks on otherwise."""
+    "nccl" (NcclAdam). "auto" picks the form measured fastest at that rank count on 8-GPU B200 nodes: among all
+    forms when the caller's backward writes the compact form's records (`records`: AUTO_EXCHANGE), else among the
+    forms that take the six gradient tensors (AUTO_EXCHANGE_FULL)."""
     if form != "auto":
         if form not in ("peer", "nvls", "compact", "nccl"):
             raise ValueError(f"unknown exchange form {form!r}")
         return form
-    return AUTO_EXCHANGE.get(world, "nvls" if world >= 4 else "peer")
+    if records:
+        return AUTO_EXCHANGE.get(world, "compact" if world >= 4 else "peer")
+    return AUTO_EXCHANGE_FULL.get(world, "nvls" if world >= 8 else "peer")
 
 
-# The fastest form per rank count, measured on the C3 training step (3M Gaussians: a 708 MB vector).
-AUTO_EXCHANGE = {2: "peer", 4: "nvls", 8: "nvls"}
+# The fastest form per rank count, exchange kernel alone on the C3 state (3M Gaussians, one view per rank), ms:
+#   2 ranks: peer 1.065, compact 1.010 (whole C3 step: peer 677 views/s, compact 660), multicast 1.86
+#   4 ranks: peer 1.662, multicast 1.685, compact 1.235, NCCL 2.159
+AUTO_EXCHANGE = {2: "peer", 4: "compact", 8: "compact"}
+AUTO_EXCHANGE_FULL = {2: "peer", 4: "peer", 8: "nvls"}
 
 
 def make_exchange(tensors, lrs, form: str = "auto", group=None, betas=(0.9, 0.999), eps: float = 1e-15,
-                  views: int = 1, active_sh_bases: int = 16):
+                  views: int = 1, active_sh_bases: int = 16, records: bool = False):
     """PeerAdam (peer or multicast form), CompactPeerAdam or NcclAdam for the replicated parameter tensors, by
-    exchange_for(). views / active_sh_bases: the compact form's views per rank and step, and SH bases."""
-    kind = exchange_for(dist.get_world_size(group), form)
+    exchange_for(world, form, records). views / active_sh_bases: the compact form's views per rank and step, and SH
+    bases; records: the caller's backward can write the compact form's records (so "auto" may choose it)."""
+    kind = exchange_for(dist.get_world_size(group), form, records)
     if kind == "compact":
         return CompactPeerAdam(tensors, lrs, views, active_sh_bases, group=group, betas=betas, eps=eps)
     if kind == "nccl":

@@ -191,7 +191,7 @@ class Trainer:
         self.peer = None
         self.exchange = None
         if world > 1:  # the gradient exchange and Adam: peer-memory kernel, NVLink multicast kernel or NCCL
-            self.exchange = gs_dist.exchange_for(world, exchange)
+            self.exchange = gs_dist.exchange_for(world, exchange, records=True)  # its backward writes records
             self.peer = gs_dist.make_exchange([sc[k].to(dev).contiguous() for k in NAMES], [LRS[k] for k in NAMES],
                                               form=self.exchange, eps=1e-15, views=views,
                                               active_sh_bases=self.bases)

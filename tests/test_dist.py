@@ -144,6 +144,18 @@ def test_owned_gaussians_and_compact_layout():
     assert gdist.exchange_for(2, "compact") == "compact"
 
 
+def test_auto_exchange_picks_compact_only_for_record_writers():
+    """"auto" may pick the compact form (whose backward writes records instead of SH gradients) only for callers that
+    say they write records; the others get a form that takes the six gradient tensors."""
+    for world in (2, 3, 4, 5, 8):
+        assert gdist.exchange_for(world) in ("peer", "nvls", "nccl")
+        assert gdist.exchange_for(world, records=True) in ("peer", "nvls", "nccl", "compact")
+    assert gdist.exchange_for(4, records=True) == gdist.AUTO_EXCHANGE[4]
+    assert gdist.exchange_for(4) == gdist.AUTO_EXCHANGE_FULL[4]
+    with pytest.raises(ValueError):
+        gdist.exchange_for(2, "ring")
+
+
 class _FakeMulticast:
     """Stands in for MulticastFlat on the host: allocation in the constructor, then a bind() that runs one
     collective per buffer (as the rendezvous does) and yields a multicast address, or none; a record of how it was
