@@ -316,7 +316,8 @@ def run_config(args, world: int, sc: dict, cams: list) -> dict:
     """The line's config: the same object for this library's arm and the reference arm of one command line."""
     cam = cams[0]
     W, H, n = cam["width"], cam["height"], sc["means"].shape[0]
-    what = {"c3": f"3DGS training step of one {W}x{H} view per GPU per step, {n} Gaussians, SH3; fwd + bwd + Adam",
+    what = {"c3": f"3DGS training step of one {W}x{H} view per GPU per step (every GPU the configured camera, with "
+                  f"its own upstream gradient), {n} Gaussians, SH3; fwd + bwd + Adam",
             "c2": f"3DGS training step of the {W}x{H} view, {n} Gaussians, SH3; fwd + bwd + Adam",
             "c4": f"3DGS training step of the 8-view {W}x{H} batch sharded over the GPUs, {n} Gaussians, SH3; "
                   f"fwd + bwd of each view, gradients summed, one exchange + Adam"}[args.workload]
@@ -327,7 +328,7 @@ def run_config(args, world: int, sc: dict, cams: list) -> dict:
                    if args.lean and world == 1 else "dense float32 (every Gaussian, every step)",
            "fused_preprocess_backward_adam": bool(args.fuse and world == 1)}
     if world > 1:
-        cfg["exchange"] = gs_dist.exchange_for(world, args.exchange)
+        cfg["exchange"] = gs_dist.exchange_for(world, args.exchange, records=True)  # the trainer's choice
     return cfg
 
 
