@@ -74,6 +74,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gs3d_preprocess_count": (_I, [_P] * 6 + [_I, _P, _P, _SZ, _P, _P]),
     "gs3d_preprocess_order": (_I, [_I, _P, _SZ, _P]),
     "gs3d_render": (_I, [_I, _LL, _P, _P, _SZ, _P, _SZ, _P, _SZ, _P, _SZ, _LL, _P, _P]),
+    "gs3d_render_bounded": (_I, [_I, _LL, _P, _P, _SZ, _P, _SZ, _P, _SZ, _P, _SZ, _LL, _P, _P, _P]),
     "gs3d_render_inference": (_I, [_I, _LL, _P, _P, _SZ, _P, _SZ, _P, _SZ, _P, _P]),
     "gs3d_backward": (_I, [_P] * 7 + [_I, _LL, _P] + [_P, _SZ] * 4 + [_LL, _P, _SZ] + [_P] * 7 + [_I, _P]),
     "gs3d_backward_blend": (_I, [_P, _P, _I, _LL, _P] + [_P, _SZ] * 4 + [_LL, _P, _SZ, _I, _P]),

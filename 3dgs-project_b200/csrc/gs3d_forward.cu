@@ -236,12 +236,14 @@ constexpr int kDupWarpMin = SPLAT_DUP_WARP_MIN;  // Gaussians listed in more til
 
 // Instance `slot` of the block (counted from the block's first output slot `base`): staged in shared memory
 // when it fits, else written straight to global memory.
+// cap: the instance buffer's capacity; slots at or past it are not written (a bounded render whose count exceeded
+// its capacity, which k_check_capacity flags).
 __device__ __forceinline__ void put_instance(uint32_t* s_key, uint32_t* s_val, const InstBuffers& ib,
-                                             uint32_t base, uint32_t slot, uint32_t key, uint32_t id) {
+                                             uint32_t base, uint32_t slot, uint32_t key, uint32_t id, uint32_t cap) {
     if (slot < kDupStage) {
         s_key[slot] = key;
         s_val[slot] = id;
-    } else {
+    } else if (base + slot < cap) {
         ib.keys[base + slot] = key;
         ib.vals[base + slot] = id;
     }
@@ -254,7 +256,8 @@ __device__ __forceinline__ void put_instance(uint32_t* s_key, uint32_t* s_val, c
 // so their instances are assembled in shared memory and stored with coalesced writes. A Gaussian listed in
 // at most kDupWarpMin tiles is enumerated by its own thread; a larger one by its whole warp, lane per tile
 // row, then lane per instance - the same rows and tiles in the same order.
-__global__ void __launch_bounds__(kDupThreads) k_duplicate(int n, Cam cam, PrimBuffers pb, InstBuffers ib) {
+__global__ void __launch_bounds__(kDupThreads) k_duplicate(int n, Cam cam, PrimBuffers pb, InstBuffers ib,
+                                                            uint32_t cap) {
     __shared__ uint32_t s_key[kDupStage > 0 ? kDupStage : 1];
     __shared__ uint32_t s_val[kDupStage > 0 ? kDupStage : 1];
     const int lane = threadIdx.x & 31;
@@ -286,9 +289,9 @@ __global__ void __launch_bounds__(kDupThreads) k_duplicate(int n, Cam cam, PrimB
         for (int ty = rows.x; ty <= rows.y && k < cnt; ++ty) {
             const int2 t = ellipse_row_tiles(e, ty, cam.width, cam.height, cam.tiles_x);
             for (int tx = t.x; tx <= t.y && k < cnt; ++tx, ++k)
-                put_instance(s_key, s_val, ib, base, slot + k, static_cast<uint32_t>(ty * cam.tiles_x + tx), id);
+                put_instance(s_key, s_val, ib, base, slot + k, static_cast<uint32_t>(ty * cam.tiles_x + tx), id, cap);
         }
-        for (; k < cnt; ++k) put_instance(s_key, s_val, ib, base, slot + k, pad_key, id);
+        for (; k < cnt; ++k) put_instance(s_key, s_val, ib, base, slot + k, pad_key, id, cap);
     }
     unsigned big = __ballot_sync(kFullMask, cnt > static_cast<uint32_t>(kDupWarpMin));
     while (big) {
@@ -334,16 +337,16 @@ __global__ void __launch_bounds__(kDupThreads) k_duplicate(int n, Cam cam, PrimB
                 if (j < chunk && k + j < gcnt) {
                     const uint32_t row_start = owner > 0 ? before : 0u;
                     const uint32_t key = static_cast<uint32_t>((ty0 + owner) * cam.tiles_x + tx0) + (j - row_start);
-                    put_instance(s_key, s_val, ib, base, gslot + k + j, key, gid);
+                    put_instance(s_key, s_val, ib, base, gslot + k + j, key, gid, cap);
                 }
             }
             k += min(chunk, gcnt - k);
         }
-        for (uint32_t p = k + lane; p < gcnt; p += 32u) put_instance(s_key, s_val, ib, base, gslot + p, pad_key, gid);
+        for (uint32_t p = k + lane; p < gcnt; p += 32u) put_instance(s_key, s_val, ib, base, gslot + p, pad_key, gid, cap);
     }
     __syncthreads();
     const uint32_t staged = min(end - base, static_cast<uint32_t>(kDupStage));
-    for (uint32_t j = threadIdx.x; j < staged; j += kDupThreads) {
+    for (uint32_t j = threadIdx.x; j < staged && base + j < cap; j += kDupThreads) {
         ib.keys[base + j] = s_key[j];
         ib.vals[base + j] = s_val[j];
     }
@@ -357,10 +360,12 @@ __global__ void __launch_bounds__(kDupThreads) k_duplicate(int n, Cam cam, PrimB
 constexpr int kBoundsThreads = 256;
 
 __global__ void __launch_bounds__(kBoundsThreads) k_tile_bounds(const uint32_t* __restrict__ keys, int m, int T,
-                                                                uint32_t* __restrict__ lb) {
+                                                                uint32_t* __restrict__ lb,
+                                                                const uint32_t* __restrict__ m_dev) {
     const int t = (blockIdx.x * kBoundsThreads + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (t > T) return;  // whole warps
+    if (m_dev) m = static_cast<int>(min(static_cast<long long>(m), static_cast<long long>(*m_dev)));
     int lo = 0, hi = m;  // lb[t] lies in [lo, hi]
     while (hi > lo) {
         const long long len = hi - lo;
@@ -652,21 +657,31 @@ int fill_cam(const gs3d_settings* s, Cam& cam) {
 
 // Duplication, the tile-digit sort passes and the per-tile tables (shared by the training and the render-only
 // path; the render-only path passes no bucket outputs).
+// A bounded render's count against its capacity: *overflow = 1 when the count exceeds it (the list then holds
+// only the instances of the first slots).
+__global__ void k_check_capacity(const uint32_t* __restrict__ count, long long capacity, uint32_t* __restrict__ overflow) {
+    if (static_cast<long long>(*count) > capacity) *overflow = 1u;
+}
+
+// bounded: m is the instance buffer's capacity and the count is read on the device (pb.counters[0], the offsets
+// scan's total), by the duplication, the tile sort and the tile bounds alike.
 int bin_instances(int n, long long m, const Cam& cam, const PrimBuffers& pb, const TileBuffers& tb,
                   const InstBuffers& ib, long long bcap, uint32_t* bucket_tile, uint32_t* total_buckets,
-                  cudaStream_t st) {
+                  cudaStream_t st, bool bounded = false) {
     const int T = cam.tiles_x * cam.tiles_y;
+    const uint32_t* m_dev = bounded ? pb.counters : nullptr;
     if (m > 0) {
-        SPLAT_TIMED_LAUNCH("k_duplicate", st, (k_duplicate<<<div_up(n, kDupThreads), kDupThreads, 0, st>>>(n, cam, pb, ib)));
+        SPLAT_TIMED_LAUNCH("k_duplicate", st, (k_duplicate<<<div_up(n, kDupThreads), kDupThreads, 0, st>>>(
+                                                  n, cam, pb, ib, static_cast<uint32_t>(m))));
         note_launch();
         SPLAT_TRY(check_launch("gs3d_duplicate"));
         // the tile-digit passes (the pad key T needs bit_width(T) bits)
         const int tile_bits = bit_width(static_cast<unsigned long long>(T));
         SPLAT_TRY(radix_sort_pairs<uint32_t>(ib.keys, ib.vals, ib.keys_sorted, ib.point_list, m, 0, tile_bits,
-                                             ib.sort_ws, ib.sort_bytes, st));
+                                             ib.sort_ws, ib.sort_bytes, st, nullptr, nullptr, m_dev));
     }
     k_tile_bounds<<<div_up(32ll * (T + 1), kBoundsThreads), kBoundsThreads, 0, st>>>(
-        ib.keys_sorted, static_cast<int>(m), T, tb.lb);
+        ib.keys_sorted, static_cast<int>(m), T, tb.lb, m_dev);
     note_launch();
     SPLAT_TRY(check_launch("gs3d_tile_bounds"));
     k_tile_tables<<<div_up(T, kTableTiles), kTableThreads, 0, st>>>(tb.lb, T, bcap, tb.ranges,
@@ -779,6 +794,46 @@ int gs3d_render(int n, long long num_instances, const gs3d_settings* settings, v
                            cam, tb.ranges, tb.bstart, ib.point_list, pb.mean2d, pb.conic_o, pb.color_z, pb.rect,
                            settings->bg, image, tb.final_T, tb.n_contrib, tb.max_contrib, bb.ckpt, pb.counters,
                            bb.reached, n < 1 ? 1 : n, static_cast<int>(m), bucket_capacity)));
+    note_launch();
+    return check_launch("gs3d_blend");
+}
+
+int gs3d_render_bounded(int n, long long instance_capacity, const gs3d_settings* settings, void* prim_buf,
+                        size_t prim_bytes_, void* tile_buf, size_t tile_bytes_, void* inst_buf, size_t inst_bytes_,
+                        void* bucket_buf, size_t bucket_bytes_, long long bucket_capacity, float* image,
+                        uint32_t* overflow, void* stream) {
+    Cam cam;
+    SPLAT_TRY(fill_cam(settings, cam));
+    const long long m = instance_capacity;
+    const int T = cam.tiles_x * cam.tiles_y;
+    SPLAT_REQUIRE(n >= 0 && m >= 0, "gs3d_render_bounded: bad sizes n=%d capacity=%lld", n, m);
+    SPLAT_REQUIRE(overflow != nullptr, "gs3d_render_bounded: overflow word is null");
+    SPLAT_BOUND(m < (1ll << 31), "gs3d_render_bounded: capacity %lld exceeds the 2^31 the 32-bit lists index", m);
+    SPLAT_BOUND(bucket_capacity >= bucket_bound(m, T),
+                "gs3d_render_bounded: bucket capacity %lld is below the bound %lld for %lld instances in %d tiles",
+                bucket_capacity, bucket_bound(m, T), m, T);
+    SPLAT_REQUIRE(prim_bytes_ >= prim_bytes(n) && tile_bytes_ >= tile_bytes(cam.width, cam.height) &&
+                      inst_bytes_ >= inst_bytes(m) && bucket_bytes_ >= bucket_bytes(bucket_capacity),
+                  "gs3d_render_bounded: a buffer is smaller than its size query");
+    if (n == 0)  // no Gaussians (the order step wrote no count): the exact form with no instances, the background
+        return gs3d_render(0, 0, settings, prim_buf, prim_bytes_, tile_buf, tile_bytes_, inst_buf, inst_bytes_,
+                           bucket_buf, bucket_bytes_, bucket_capacity, image, stream);
+    cudaStream_t st = as_stream(stream);
+    Carver cp(prim_buf, prim_bytes_), ct(tile_buf, tile_bytes_), ci(inst_buf, inst_bytes_),
+        cb(bucket_buf, bucket_bytes_);
+    PrimBuffers pb = carve_prim(cp, n);
+    TileBuffers tb = carve_tile(ct, cam.width, cam.height);
+    InstBuffers ib = carve_inst(ci, m);
+    BucketBuffers bb = carve_bucket(cb, bucket_capacity);
+    k_check_capacity<<<1, 1, 0, st>>>(pb.counters, m, overflow);
+    note_launch();
+    SPLAT_CUDA(cudaMemsetAsync(pb.counters + 2, 0, sizeof(uint32_t), st));  // k_blend counts the replayed buckets
+    SPLAT_TRY(bin_instances(n, m, cam, pb, tb, ib, bucket_capacity, bb.tile, pb.counters + 1, st, true));
+    SPLAT_TIMED_LAUNCH("k_blend", st,
+                       (k_blend<true><<<T, kTilePixels / 2, 0, st>>>(
+                           cam, tb.ranges, tb.bstart, ib.point_list, pb.mean2d, pb.conic_o, pb.color_z, pb.rect,
+                           settings->bg, image, tb.final_T, tb.n_contrib, tb.max_contrib, bb.ckpt, pb.counters,
+                           bb.reached, n, static_cast<int>(m), bucket_capacity)));
     note_launch();
     return check_launch("gs3d_blend");
 }

@@ -117,7 +117,9 @@ def _readback_slot(dev):
     return slots[key]
 
 
-def _preprocess(means, scales, rotations, opacities, sh0, sh_rest, settings_args):
+def _preprocess(means, scales, rotations, opacities, sh0, sh_rest, settings_args, read_count: bool = True):
+    """Preprocess and depth order of one view; returns M read back from the device, or None (read_count False: no
+    host read, the bounded render reads M on the device)."""
     n, rest = _check_params(means, scales, rotations, opacities, sh0, sh_rest)
     dev = means.device
     keep: list = []
@@ -129,6 +131,9 @@ def _preprocess(means, scales, rotations, opacities, sh0, sh_rest, settings_args
     count = torch.empty(2, dtype=torch.int32, device=dev)
     L.call("gs3d_preprocess_count", L.ptr(means), L.ptr(scales), L.ptr(rotations), L.ptr(opacities), L.ptr(sh0),
            L.ptr(sh_rest), n, ctypes.byref(s), L.ptr(prim), prim.numel(), L.ptr(count), stream)
+    if not read_count:
+        L.call("gs3d_preprocess_order", n, L.ptr(prim), prim.numel(), stream)
+        return n, dev, s, keep, stream, prim, tile, None
     # the device's count of look-back waits that gave up (the sorts of the forwards before this one)
     L.call("splat_take_device_waits_async", L.ptr(count[1:]), stream)
     host, side, ready, counted = _readback_slot(dev)
@@ -164,12 +169,30 @@ def inference(means, scales, rotations, opacities, sh0, sh_rest, w2c, cam_positi
 
 @torch.no_grad()
 def forward(means, scales, rotations, opacities, sh0, sh_rest, w2c, cam_position, bg_color, active_sh_bases, width,
-            height, focal_x, focal_y, center_x, center_y, near_plane, far_plane, proper_antialiasing):
-    """Faster-GS `_C.forward`: (image[3,H,W], prim_buf, tile_buf, inst_buf, bucket_buf, n_instances, n_buckets, 0)."""
+            height, focal_x, focal_y, center_x, center_y, near_plane, far_plane, proper_antialiasing, *,
+            capacity: int | None = None, overflow: torch.Tensor | None = None):
+    """Faster-GS `_C.forward`: (image[3,H,W], prim_buf, tile_buf, inst_buf, bucket_buf, n_instances, n_buckets, 0).
+
+    capacity (keyword, no counterpart in the reference): the bounded form, with no host read - buffers sized for
+    `capacity` instances, M read on the device (gs3d_render_bounded), n_instances returned as the capacity (which
+    the backward takes as it is). If M exceeds it, overflow (device int32 [1], required) is set to 1 and the image
+    lists only the first `capacity` instances; check it where a host read is acceptable."""
     n, dev, s, keep, stream, prim, tile, m = _preprocess(
         means, scales, rotations, opacities, sh0, sh_rest,
         (w2c, cam_position, bg_color, active_sh_bases, width, height, focal_x, focal_y, center_x, center_y,
-         near_plane, far_plane, proper_antialiasing))
+         near_plane, far_plane, proper_antialiasing), read_count=capacity is None)
+    if capacity is not None:
+        if overflow is None:
+            raise RuntimeError("the bounded forward needs an overflow word (device int32 [1])")
+        L.check_cuda("overflow", overflow, torch.int32)
+        m = int(capacity)
+        bcap = int(L.load().gs3d_bucket_bound(m, width, height))
+        inst = torch.empty(L.query("gs3d_instance_buffer_size", m), dtype=torch.uint8, device=dev)
+        bucket = torch.empty(L.query("gs3d_bucket_buffer_size", bcap), dtype=torch.uint8, device=dev)
+        image = torch.empty(3, height, width, dtype=torch.float32, device=dev)
+        L.call("gs3d_render_bounded", n, m, ctypes.byref(s), L.ptr(prim), prim.numel(), L.ptr(tile), tile.numel(),
+               L.ptr(inst), inst.numel(), L.ptr(bucket), bucket.numel(), bcap, L.ptr(image), L.ptr(overflow), stream)
+        return image, prim, tile, inst, bucket, m, bcap, 0
     bcap = int(L.load().gs3d_bucket_bound(m, width, height))
     inst = torch.empty(L.query("gs3d_instance_buffer_size", m), dtype=torch.uint8, device=dev)
     bucket = torch.empty(L.query("gs3d_bucket_buffer_size", bcap), dtype=torch.uint8, device=dev)

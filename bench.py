@@ -209,6 +209,11 @@ class Trainer:
         self.n = self.params[0].shape[0]
         self.t = 0
         self.settings = {}
+        # Bounded forwards (no host read of the instance count): a view's first forward reads M back; later ones
+        # size their instance buffers for 1.25 M + 64K and read M on the device. `overflow` is checked once after
+        # the timed steps (check_capacity).
+        self.capacity = {}
+        self.overflow = torch.zeros(1, dtype=torch.int32, device=dev)
         self.ev = {k: [] for k in ("fwd", "bwd", "comm", "xkernel", "adam", "blend_bwd")}
         self.last = None
 
@@ -235,7 +240,11 @@ class Trainer:
             fs, fe, bs, be = (mk(), mk(), mk(), mk()) if timed else (None, None, None, None)
             if timed:
                 fs.record()
-            image, prim, tile, inst, bucket, m, nb, sel = gs3d.forward(*self.params, *s)
+            cap = self.capacity.get(id(cam))
+            image, prim, tile, inst, bucket, m, nb, sel = gs3d.forward(*self.params, *s, capacity=cap,
+                                                                       overflow=self.overflow)
+            if cap is None:
+                self.capacity[id(cam)] = m + m // 4 + 65536
             if timed:
                 fe.record()
             self.last = (prim, tile, m, cam)
@@ -283,6 +292,16 @@ class Trainer:
             self.ev["xkernel"].append(list(self.peer.kernel_events) if self.peer is not None else [])
             self.ev["adam"].append([] if self.peer is not None else [(cs, ce)])
         return insts
+
+    def instances_of(self, prim) -> int:
+        """The instance count M of the view whose primitive buffer is `prim` (one host read): the bounded forward
+        returns its capacity as n_instances."""
+        return int(gs3d.primitive_views(prim, self.n)["counters"][0].item())
+
+    def check_capacity(self) -> None:
+        """One host read: raise if a bounded forward's instances exceeded its capacity."""
+        if int(self.overflow.item()):
+            raise RuntimeError("a bounded forward listed more instances than its capacity; the run is invalid")
 
     def stage_ms(self) -> dict:
         """Mean per-step milliseconds of each stage over the timed steps."""
@@ -388,6 +407,7 @@ def run_ours(args) -> None:
     douts = ([h.to(dev) for h in hosts], [(-h).to(dev) for h in hosts])
     r = time_steps(tr, cams, lambda t: douts[t % 2], args.steps, args.warmup, world, local)
     L.check_device_waits(dev)  # a sort wait of the last forward that gave up is reported here, not after the run
+    tr.check_capacity()
     stage = r["stage"]
     reach = blend_reach(tr, cam["width"], cam["height"])
     checksum = tr.checksum()
@@ -412,7 +432,7 @@ def run_ours(args) -> None:
             "warmup": args.warmup, "ms_per_step": round(r["ms_max"] / args.steps, 4), "higher_is_better": True,
             "scaling": "strong" if args.workload == "c4" else "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded, config-shaped)", "config": run_config(args, world, sc, cams),
-            "instances_per_view": round(float(np.mean(r["insts"]))) if r["insts"] else 0,
+            "instances_per_view": reach["instances"],
             "stage_ms": {k: round(v, 4) for k, v in stage.items()},
             "fwd_bwd_ms": round(stage["fwd"] + stage["bwd"], 4),
             "wall_s": round(r["wall"], 3), "clocks": r["clocks"], "e2e": e2e, "gpu_launches": r["launches"],
@@ -447,6 +467,7 @@ def c4_strong(args, world: int, rank: int, local: int, dev) -> dict:
     steps = max(args.steps // 4, 10)
     r = time_steps(tr, cams, lambda t: douts[t % 2], steps, args.warmup, world, local, with_clocks=False)
     L.check_device_waits(dev)
+    tr.check_capacity()
     checksum = tr.checksum()
     stage = {k: round(v, 4) for k, v in r["stage"].items()}
     exch = tr.exchange
@@ -576,7 +597,8 @@ def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
 def blend_reach(tr: Trainer, width: int, height: int) -> dict:
     """What the last step's blend backward had to touch: per tile the list positions up to its last contributor
     (min(max_contrib, range length)), the 32-splat buckets those make, and the bucket count of the whole view."""
-    prim, tile, m, _ = tr.last
+    prim, tile, _, _ = tr.last
+    m = tr.instances_of(prim)
     tv = gs3d.tile_views(tile, width, height)
     rg = tv["ranges"].long()
     reach = torch.minimum(tv["max_contrib"].long(), (rg[:, 1] - rg[:, 0]).clamp(min=0))

@@ -244,6 +244,17 @@ int gs3d_preprocess_order(int n, void* prim_buf, size_t prim_bytes, void* stream
 int gs3d_render(int n, long long num_instances, const gs3d_settings* settings, void* prim_buf, size_t prim_bytes,
                 void* tile_buf, size_t tile_bytes, void* inst_buf, size_t inst_bytes, void* bucket_buf,
                 size_t bucket_bytes, long long bucket_capacity, float* image, void* stream);
+/* gs3d_render without the host read of M (no counterpart in the reference, whose forward reads M back to size its
+ * buffers): the instance buffer is sized for instance_capacity (gs3d_instance_buffer_size(instance_capacity)) and
+ * the bucket buffer for gs3d_bucket_bound(instance_capacity, ...); M is read on the device from the primitive
+ * buffer (the total of gs3d_preprocess_order's offsets scan). The results are gs3d_render's when M <= capacity;
+ * otherwise only the instances in the first instance_capacity slots are listed and *overflow (device u32) is set
+ * to 1 (never cleared by the library). The backward takes instance_capacity and bucket_capacity as the instance and
+ * bucket counts. */
+int gs3d_render_bounded(int n, long long instance_capacity, const gs3d_settings* settings, void* prim_buf,
+                        size_t prim_bytes, void* tile_buf, size_t tile_bytes, void* inst_buf, size_t inst_bytes,
+                        void* bucket_buf, size_t bucket_bytes, long long bucket_capacity, float* image,
+                        uint32_t* overflow, void* stream);
 /* Render only (replaces Faster-GS's `_C.inference`, whose blend loop upstream/upstream_main_kernels.patch:131-165
  * shows): gs3d_preprocess, then this in place of gs3d_render. The same image as gs3d_render, without the
  * checkpoints, per-pixel counts and bucket tables a backward needs (no bucket buffer). */

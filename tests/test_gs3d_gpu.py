@@ -321,3 +321,46 @@ def test_backward_accumulates_the_views_of_a_batch(cuda):
         assert bool(torch.isfinite(a).all()), name
         assert rel(a, g0 + g1) < 1e-5, f"{name}: {rel(a, g0 + g1):.2e}"
     assert n > 0
+
+
+@pytest.mark.parametrize("name", ["micro", "tiny", "garden_res", "heavy_overlap", "empty"])
+def test_bounded_forward_matches_exact_forward(name, cuda):
+    """The bounded forward (no host read of M; buffers for a capacity) gives the exact forward's image, sorted list,
+    tile ranges, contributor counts and final T bit for bit, and the backward from either gives the same gradients
+    (the blend backward's atomic order allows 1e-5); the overflow word stays 0."""
+    sc, cam, params, settings = _setup(name, seed=5)
+    W, H = cam["width"], cam["height"]
+    ex = gs3d.forward(*params, *settings)
+    m = ex[5]
+    overflow = torch.zeros(1, dtype=torch.int32, device=cuda)
+    bd = gs3d.forward(*params, *settings, capacity=m + 1000, overflow=overflow)
+    assert bd[5] == m + 1000
+    assert torch.equal(ex[0], bd[0])
+    if m:  # the bounded buffer's slots past M are never written: compare the first M (and gather nothing by them)
+        ie, ib = gs3d.instance_views(ex[3], m), gs3d.instance_views(bd[3], m + 1000)
+        for key in ("tiles_sorted", "point_list"):
+            assert torch.equal(ie[key], ib[key][:m]), key
+    te, tb = gs3d.tile_views(ex[2], W, H), gs3d.tile_views(bd[2], W, H)
+    for key in ("ranges", "n_contrib", "final_T", "max_contrib"):
+        assert torch.equal(te[key], tb[key]), key
+    dout = torch.randn(3, H, W, device=cuda, generator=torch.Generator(device=cuda).manual_seed(2)) * 1e-2
+    grads = []
+    for r in (ex, bd):
+        image, prim, tile, inst, bucket, mm, nb, sel = r
+        grads.append(gs3d.backward(None, dout, image, params[0], params[1], params[2], params[3], params[5], prim,
+                                   tile, inst, bucket, *settings, mm, nb, sel))
+    for a, b in zip(*grads):  # atomic-order noise (heavy overlap stacks many atomics on each Gaussian)
+        assert rel(b, a) < 1e-5
+    assert int(overflow.item()) == 0
+
+
+def test_bounded_forward_overflow_is_flagged(cuda):
+    """A capacity below M: the overflow word is set, nothing is written past the buffers, and the call returns."""
+    sc, cam, params, settings = _setup("garden_res", seed=5)
+    m = gs3d.forward(*params, *settings)[5]
+    assert m > 1000
+    overflow = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = gs3d.forward(*params, *settings, capacity=m // 2, overflow=overflow)
+    torch.cuda.synchronize()
+    assert int(overflow.item()) == 1
+    assert bool(torch.isfinite(out[0]).all())
