@@ -195,7 +195,47 @@ def agree_on_buffers(make, count: int, group=None, device=None):
     return None
 
 
-class PeerAdam:
+class _BackwardInto:
+    """The autograd hook of gs3d._Rasterize (the one FusedAdam(fuse_backward=True) uses), for the exchanges that take
+    six gradient tensors: while the exchange is open, the backward of a diff_rasterize call on its six parameter
+    tensors writes its gradients into `grads` (a step's first view stores, later views add) instead of returning
+    them, and step() finds them in place with nothing to copy."""
+
+    def _hook_backward(self) -> None:
+        from . import gs3d
+
+        self._written = 0
+        gs3d._Rasterize.fused_optimizer = self
+
+    def _unhook_backward(self) -> None:
+        from . import gs3d
+
+        if gs3d._Rasterize.fused_optimizer is self:
+            gs3d._Rasterize.fused_optimizer = None
+
+    def _owns(self, six) -> bool:
+        return len(self.params) == 6 and all(t.data_ptr() == p.data_ptr() and t.shape == p.shape
+                                             for t, p in zip(six, self.params))
+
+    def _defer(self, pending, six) -> None:
+        pending.preprocess(out=self.grads, accumulate=self._written > 0)
+        self._written += 1
+
+    def _take_grads(self, grads) -> None:
+        """step()'s `grads` (e.g. the leaves' .grad): added to what the hooked backward wrote this step, or copied
+        into the buffer when it wrote nothing; None entries are skipped."""
+        if grads is not None:
+            for v, g in zip(self.grads, grads):
+                if g is None:
+                    continue
+                if self._written:
+                    v.add_(g.reshape(v.shape))
+                else:
+                    v.copy_(g.reshape(v.shape))
+        self._written = 0
+
+
+class PeerAdam(_BackwardInto):
     """Data-parallel Adam for replicated parameters, one fused kernel per step instead of an all-reduce of the
     gradients followed by the same Adam step on every rank.
 
@@ -253,6 +293,7 @@ class PeerAdam:
         self._seg = (_Segment * len(self.segments))(*[_Segment(a, b, lr) for a, b, lr in self.segments])
         self._gptr = (ctypes.c_void_p * 8)(*self.grad_buf.ptrs)
         self._pptr = (ctypes.c_void_p * 8)(*self.param_buf.ptrs)
+        self._hook_backward()
         dist.barrier(group=group)  # every rank's initial parameters are in place
 
     def _barrier(self) -> None:
@@ -261,10 +302,9 @@ class PeerAdam:
     @torch.no_grad()
     def step(self, grads=None) -> None:
         """One step. `grads` (a list of per-group tensors, e.g. the leaves' .grad) is first copied into this rank's
-        gradient buffer; leave it None when the backward wrote into `grads` directly."""
-        if grads is not None:
-            for v, g in zip(self.grads, grads):
-                v.copy_(g.reshape(v.shape))
+        gradient buffer (added, when a hooked diff_rasterize backward already wrote it); leave it None when the
+        backward wrote into `grads` directly."""
+        self._take_grads(grads)
         self.t += 1
         stream = torch.cuda.current_stream(self.exp_avg.device).cuda_stream
         self._barrier()
@@ -284,6 +324,7 @@ class PeerAdam:
         self._barrier()
 
     def close(self) -> None:
+        self._unhook_backward()
         torch.cuda.synchronize()
         self.params = self.grads = []
         self.param_buf.close()
@@ -301,7 +342,7 @@ def _kernel_events(ex):
     return a, b
 
 
-class NcclAdam:
+class NcclAdam(_BackwardInto):
     """PeerAdam's step through NCCL collectives, for comparison and for nodes without peer access: a reduce-scatter
     of the flat gradient vector (rank r receives the summed slice it owns), Adam on that slice with the slice's
     moments (the exchange kernels' segmented Adam on one rank: adam_step_dp_fused with G = 1), and an all-gather
@@ -343,13 +384,12 @@ class NcclAdam:
         # The kernel reads gradient element e (lo <= e < hi) at grads[0] + e: the slice's base, moved back by lo.
         self._gptr = (ctypes.c_void_p * 8)(self.grad_slice.data_ptr() - 4 * self.lo)
         self._pptr = (ctypes.c_void_p * 8)(self.param_flat.data_ptr())
+        self._hook_backward()
         dist.barrier(group=group)
 
     @torch.no_grad()
     def step(self, grads=None) -> None:
-        if grads is not None:
-            for v, g in zip(self.grads, grads):
-                v.copy_(g.reshape(v.shape))
+        self._take_grads(grads)
         self.t += 1
         ev = _kernel_events(self)
         dist.reduce_scatter_tensor(self.grad_slice, self.grad_flat, op=dist.ReduceOp.SUM, group=self.group)
@@ -364,6 +404,7 @@ class NcclAdam:
             ev[1].record()
 
     def close(self) -> None:
+        self._unhook_backward()
         torch.cuda.synchronize()
         self.params = self.grads = []
 

@@ -383,9 +383,11 @@ class _Rasterize(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx: Any, means, scales, rotations, opacities, sh0, sh_rest, densification_info,
-                settings: RasterizerSettings, want_radii: bool = False):
+                settings: RasterizerSettings, want_radii: bool = False, capacity: int | None = None,
+                overflow: torch.Tensor | None = None):
         params = [t.contiguous() for t in (means, scales, rotations, opacities, sh0, sh_rest)]
-        image, prim, tile, inst, bucket, m, nb, sel = forward(*params, *settings.as_tuple())
+        image, prim, tile, inst, bucket, m, nb, sel = forward(*params, *settings.as_tuple(), capacity=capacity,
+                                                              overflow=overflow)
         if _Rasterize.track_visibility:
             _Rasterize.last_visibility = n_touched_tiles(prim, params[0].shape[0])
         ctx.settings = settings
@@ -409,18 +411,21 @@ class _Rasterize(torch.autograd.Function):
             pending = backward_blend(ctx.densification_info, grad_image, image, means, scales, rotations, opacities,
                                      sh_rest, prim, tile, inst, bucket, *ctx.settings.as_tuple(), *ctx.buffer_state)
             opt._defer(pending, six)
-            return (None,) * 9
+            return (None,) * 11
         g = backward(ctx.densification_info, grad_image, image, means, scales, rotations, opacities, sh_rest, prim,
                      tile, inst, bucket, *ctx.settings.as_tuple(), *ctx.buffer_state)
         op_shape, sh0_shape, rest_shape = ctx.shapes
         return (g[0], g[1], g[2], g[3].reshape(op_shape), g[4].reshape(sh0_shape), g[5].reshape(rest_shape), None,
-                None, None)
+                None, None, None, None)
 
 
 def diff_rasterize(means, scales, rotations, opacities, sh0, sh_rest, densification_info,
-                   settings: RasterizerSettings) -> torch.Tensor:
-    """Differentiable render of one view: image [3, H, W]."""
-    return _Rasterize.apply(means, scales, rotations, opacities, sh0, sh_rest, densification_info, settings)
+                   settings: RasterizerSettings, *, capacity: int | None = None,
+                   overflow: torch.Tensor | None = None) -> torch.Tensor:
+    """Differentiable render of one view: image [3, H, W]. capacity / overflow (keyword, no counterpart in the
+    reference): the bounded forward (see forward), with no host read."""
+    return _Rasterize.apply(means, scales, rotations, opacities, sh0, sh_rest, densification_info, settings, False,
+                            capacity, overflow)
 
 
 def rasterize_gaussians(means3D, scales, rotations, opacities, shs, viewmatrix, projmatrix, bg, tanfovx, tanfovy,
@@ -445,7 +450,8 @@ def rasterize_gaussians(means3D, scales, rotations, opacities, shs, viewmatrix, 
     log_scales = torch.log(scales * scale_modifier)
     logits = torch.logit(opacities.reshape(-1, 1).clamp(1e-7, 1 - 1e-7))
     sh0, sh_rest = shs[:, :1].contiguous(), shs[:, 1:].contiguous()
-    return _Rasterize.apply(means3D, log_scales, rotations, logits, sh0, sh_rest, torch.empty(0), settings, True)
+    return _Rasterize.apply(means3D, log_scales, rotations, logits, sh0, sh_rest, torch.empty(0), settings, True, None,
+                            None)
 
 
 def check_projmatrix(viewmatrix: torch.Tensor, projmatrix: torch.Tensor, tanfovx: float, tanfovy: float,

@@ -490,9 +490,10 @@ def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
     """The training step through the public API (diff_rasterize + autograd + FusedAdam at N = 1, the exchange's
     optimizer over the ranks at N > 1), over this rank's views of the step (their losses summed, one backward, one
     optimizer step). Every step copies its views' upstream gradients from pinned host memory (on a copy stream,
-    into one of two device buffers per view, issued one step ahead, after the step's first forward has read its
-    instance count, so that the copies overlap the step's kernels) and copies its loss back into pinned host memory;
-    all of those copies sit inside the timed region."""
+    into one of two device buffers per view, issued one step ahead, after the step's first forward is enqueued, so
+    that the copies overlap the step's kernels) and copies its loss back into pinned host memory; all of those copies
+    sit inside the timed region. The forwards are bounded (no host read of the instance count), as in the
+    device-timed run."""
     peer = None
     start = [sc[k].to(dev).contiguous() for k in NAMES]  # the configured scene, as the device-timed run started
     if world > 1:  # the leaves are views of the exchange's parameter buffer; step() takes their .grad
@@ -509,6 +510,13 @@ def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
     hosts = [upstream_gradient(view_seed(args.workload, rank, world, k), c["height"], c["width"]).pin_memory()
              for k, c in enumerate(cams)]
     settings = [gs3d.RasterizerSettings(*scenes.settings_tuple(c, tr.bases, dev)) for c in cams]
+    # bounded forwards, as in the device-timed run: each view's instance count read once here, its forwards then
+    # sized for 1.25 M + 64K instances with the count kept on the device (overflow checked after the timed steps)
+    overflow = torch.zeros(1, dtype=torch.int32, device=dev)
+    caps = []
+    for st in settings:
+        m = gs3d.forward(*[p.detach() for p in leaves], *st.as_tuple())[5]
+        caps.append(m + m // 4 + 65536)
     compute = torch.cuda.current_stream(dev)
     copier = torch.cuda.Stream(dev)
     dbuf = [[torch.empty_like(h, device=dev) for h in hosts] for _ in range(2)]
@@ -531,9 +539,8 @@ def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
         compute.wait_event(copied[b])
         loss = None
         for v, (st, dout) in enumerate(zip(settings, dbuf[b])):
-            img = gs3d.diff_rasterize(*leaves, torch.empty(0), st)
-            # the next step's copies go out once this step's first forward has read its instance count back, so
-            # that the host-to-device copies never sit in front of that small device-to-host read
+            img = gs3d.diff_rasterize(*leaves, torch.empty(0), st, capacity=caps[v], overflow=overflow)
+            # the next step's copies go out once this step's first forward is enqueued
             if v == 0 and k + 1 < total and k + 1 != args.warmup:  # the first timed copy is issued in the region
                 issue_copy(k + 1)
             term = (img * dout).sum()
@@ -576,6 +583,8 @@ def run_e2e(sc, cams, dev, world, args, tr: Trainer) -> dict:
         torch.cuda.synchronize()
         clk.mark_end()
     assert bool(torch.isfinite(losses).all())
+    if int(overflow.item()):
+        raise RuntimeError("an end-to-end forward listed more instances than its capacity; the run is invalid")
     ms = torch.tensor([a.elapsed_time(b)], device=dev)
     if world > 1:
         torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)

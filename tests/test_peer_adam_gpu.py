@@ -162,3 +162,65 @@ def test_compact_exchange_matches_peer(n, views):
         assert err is None, f"rank {rank}: {err}"
         assert exercised, f"rank {rank}: the SH parameters did not move or every Gaussian was seen"
         assert same, f"rank {rank}: compact and full exchanges differ"
+
+
+def _hook_worker(port: int, q, form: str) -> None:
+    """One rank (world size 1): the diff_rasterize backward writes into the exchange's gradient buffer (the autograd
+    hook), so step(grads=[p.grad ...]) finds the leaves' .grad empty and copies nothing; the gradients in the buffer
+    equal gs3d.backward's on the same view to the blend backward's atomic-order noise, and the step moved the
+    parameters."""
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(0)
+        dev = torch.device("cuda", 0)
+        dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=60), device_id=dev)
+        import sys
+        sys.path.insert(0, os.getcwd())
+        import __graft_entry__ as ge
+        ge.load_package()
+        from gs_b200 import dist as D
+        from gs_b200 import gs3d, scenes
+
+        sc = scenes.gs3d_test_scene("tiny", 4)
+        names = ("means", "scales", "rotations", "opacities", "sh0", "sh_rest")
+        tensors = [sc[k].to(dev).contiguous() for k in names]
+        settings = scenes.settings_tuple(sc["cameras"][0], sc["active_sh_bases"], dev)
+        lrs = [1.6e-4, 5e-3, 1e-3, 5e-2, 2.5e-3, 2.5e-3]
+        opt = D.NcclAdam(tensors, lrs) if form == "nccl" else D.PeerAdam(tensors, lrs, nvls=False)
+        leaves = [p.requires_grad_(True) for p in opt.params]
+        img = gs3d.diff_rasterize(*leaves, torch.empty(0), gs3d.RasterizerSettings(*settings))
+        dout = torch.randn(img.shape, device=dev, generator=torch.Generator(device=dev).manual_seed(9)) * 1e-2
+        img.backward(dout)
+        untouched = all(p.grad is None for p in leaves)
+        opt.step(grads=[p.grad for p in leaves])
+        r = gs3d.forward(*tensors, *settings)
+        g = gs3d.backward(None, dout, r[0], tensors[0], tensors[1], tensors[2], tensors[3], tensors[5], *r[1:5],
+                          *settings, *r[5:8])
+        torch.cuda.synchronize()
+        err = max(float((a.flatten() - b.flatten()).norm() / b.flatten().norm().clamp_min(1e-30))
+                  for a, b in zip(opt.grads, g))
+        moved = max(float((a.detach() - b).abs().max()) for a, b in zip(opt.params, tensors))
+        opt.close()
+        dist.destroy_process_group()
+        q.put((untouched, err, moved, None))
+    except Exception as exc:  # report instead of hanging the parent
+        q.put((False, 1.0, 0.0, repr(exc)))
+
+
+@pytest.mark.parametrize("form", ["peer", "nccl"])
+def test_autograd_backward_writes_into_the_exchange(form):
+    if torch.cuda.device_count() < 1:
+        pytest.skip("needs a GPU")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29600 + os.getpid() % 300 + 40 + (form == "nccl")
+    p = ctx.Process(target=_hook_worker, args=(port, q, form))
+    p.start()
+    untouched, err, moved, exc = q.get(timeout=300)
+    p.join(timeout=60)
+    if p.is_alive():
+        p.kill()
+    assert exc is None, exc
+    assert untouched, "the leaves got a .grad: the backward did not write into the exchange's buffer"
+    assert err < 1e-5 and moved > 0, (err, moved)
