@@ -200,7 +200,7 @@ __global__ void __launch_bounds__(kThreads) k_dp_adam_nvls(NvlsArgs a) {
 //   gradients (every rank):  means 3n | scales 3n | rotations 4n | opacities n | records 6n per view
 //   moments (owner):         the parameter layout over the owned Gaussians, with c = hi - lo rounded up to 4
 constexpr int kCompactThreads = 256;
-constexpr int kChunk = 64;       // Gaussians per block iteration
+constexpr int kChunk = 80;       // Gaussians per block iteration (3 x 80 sum threads of the 256)
 constexpr int kRecBatch = 8;     // (rank, view) record blocks staged in shared memory at a time
 constexpr int kMaxBases = 16;
 
