@@ -1,6 +1,7 @@
 """Benchmark of the 3DGS training step on B200, one process per GPU.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--exchange auto|peer|nvls|nccl]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--exchange auto|peer|nvls|compact|nccl]
                     [--workload c3|c2|c4|c1|c5|gs2d|splat2d|blend-bwd|ssim]
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \
         bench.py --gpus N --steps K --warmup W
@@ -10,9 +11,11 @@ synthetic parameters (no dataset is available) - rendered at 1920x1080 / 60 deg.
 training step of one view: forward, backward with dL/dimage ~ N(0, 1e-3) (one fixed seeded image whose sign
 alternates step to step, so that Adam keeps the scene at its configured state), then Adam over the six parameter groups
 (N = 1: one fused Adam launch; N > 1: the gradient exchange and Adam, in the form --exchange names: one peer-memory
-kernel per rank, one NVLink-multicast kernel per rank, or NCCL reduce-scatter + Adam on the slice + all-gather;
-auto takes the fastest measured at that rank count). Each rank renders its own view (a seeded camera at radius 12),
-so the work per GPU is fixed as N grows (weak scaling) and
+kernel per rank, one NVLink-multicast kernel per rank, the peer kernel with compact SH gradients, or NCCL
+reduce-scatter + Adam on the slice + all-gather; auto takes the fastest measured at that rank count). The forwards
+are bounded (a view's instance count is read back once, in a warm-up step; no timed step waits on the host). Each
+rank trains on the configured camera with its own upstream gradient, so the work per GPU is the single-GPU step's
+as N grows (weak scaling) and
     value = N * K / (max over ranks of the device time of K steps)  [views/s],  ms_per_step = that time / K.
 The Gaussian state (2.8 GB with moments) is far larger than the 126 MB L2, so no flush is needed between steps.
 ``e2e`` runs the same step through the public API (diff_rasterize + autograd + FusedAdam, the exchange's optimizer
