@@ -9,7 +9,9 @@
 The reference has no multi-GPU path (every job is single-GPU); this is the sharding the benchmark spec asks
 for: independent views plus one exchange step. PeerAdam below fuses that exchange with the optimizer: one kernel
 per rank reads its slice of every rank's gradients over NVLink, applies Adam, and writes the slice of parameters
-back to every rank (plain peer loads and stores; no multicast loads).
+back to every rank (plain peer loads and stores; no multicast loads), or does the same through NVLink multicast.
+CompactPeerAdam sends each view's SH gradients as six floats per Gaussian (colour gradient and view direction) and
+forms the products on the owner; NcclAdam is the reduce-scatter / all-gather baseline. make_exchange picks one.
 """
 from __future__ import annotations
 
